@@ -1,0 +1,143 @@
+/*
+ * mlxq_b200.h -- C ABI of the B200 group-wise affine quantized matmul library
+ * (libmlxq_b200.so, built from mlx-server-runtime_b200/csrc).
+ *
+ * The reference (huydt84/mlx-server-runtime) reaches these operators through
+ * the third-party MLX package (mlx 0.31.2, python/uv.lock:939-940), whose
+ * Python surface the model graphs call:
+ *   mx.quantize          python/mlx_worker/native_mlx/models/lfm2.py:112-117,142-151
+ *   nn.quantize          python/mlx_worker/native_mlx/models/qwen2.py:318-324
+ *   QuantizedLinear      python/mlx_worker/native_mlx/models/qwen2.py:58-61,123-134,227
+ *   mx.gather_qmm        python/mlx_worker/native_mlx/models/lfm2.py:176-187
+ * Each entry point below replaces one of those operators; the ctypes shim in
+ * mlx-server-runtime_b200/core.py binds them under MLX's names.
+ *
+ * Conventions
+ *  - All pointers are DEVICE pointers to contiguous row-major buffers owned by
+ *    the caller. The library allocates no device memory; kernels that need
+ *    scratch space take a caller-provided workspace.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream). Every call is
+ *    stream-ordered and asynchronous; errors detected on the host are returned
+ *    before anything is enqueued.
+ *  - Return value: MLXQ_OK (0) or a negative MLXQ_ERR_* code; the message of
+ *    the last failure on the calling thread is available from mlxq_last_error().
+ *    The library never aborts the process.
+ *  - dtype codes: MLXQ_F32, MLXQ_BF16, MLXQ_F16.
+ *  - Storage layout (MLX "affine" mode): w_q uint32 [rows, K*bits/32] with code
+ *    k of a row at bits [bits*(k % (32/bits)), +bits) of word k/(32/bits);
+ *    scales/biases [rows, K/group_size]; w ~= scale*q + bias.
+ *  - Supported: bits in {4, 8} for the matmuls, {2, 4, 8} for quantize and
+ *    dequantize; group_size in {32, 64, 128}; K a multiple of group_size.
+ */
+#ifndef MLXQ_B200_H
+#define MLXQ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MLXQ_ABI_VERSION 1
+
+enum {
+    MLXQ_F32 = 0,
+    MLXQ_BF16 = 1,
+    MLXQ_F16 = 2,
+};
+
+enum {
+    MLXQ_OK = 0,
+    MLXQ_ERR_SHAPE = -1,            /* inconsistent or unsupported shape */
+    MLXQ_ERR_DTYPE = -2,            /* unsupported dtype */
+    MLXQ_ERR_ALIGN = -3,            /* pointer not 16-byte aligned */
+    MLXQ_ERR_UNSUPPORTED_BITS = -4, /* bits not supported by this operator */
+    MLXQ_ERR_GROUP_SIZE = -5,       /* group_size not in {32, 64, 128} */
+    MLXQ_ERR_CUDA = -6,             /* a CUDA runtime call failed */
+    MLXQ_ERR_WORKSPACE = -7,        /* workspace missing or too small */
+    MLXQ_ERR_NULL = -8,             /* a required pointer is NULL */
+    MLXQ_ERR_INDEX = -9,            /* index array argument invalid */
+};
+
+/* ABI version of the loaded library (MLXQ_ABI_VERSION at build time). */
+int mlxq_abi_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* mlxq_last_error(void);
+
+/*
+ * quantize: replaces mx.quantize(w, group_size, bits, mode="affine")
+ * (lfm2.py:112-117) and the per-layer quantization nn.quantize performs
+ * (qwen2.py:318-324). w [rows, K] of dtype w_dtype; writes wq
+ * [rows, K*bits/32] uint32 and scales/biases [rows, K/group_size] in w_dtype.
+ */
+int mlxq_quantize(const void* w, int w_dtype, uint32_t* wq, void* scales, void* biases,
+                  int64_t rows, int64_t K, int group_size, int bits, void* stream);
+
+/*
+ * dequantize: replaces mx.dequantize(w, scales, biases, group_size, bits)
+ * (north_star API; MLX public op). out [rows, K] in `dtype` (the dtype of
+ * scales/biases), each element round(round(scale*q) + bias).
+ */
+int mlxq_dequantize(const uint32_t* wq, const void* scales, const void* biases, int dtype,
+                    void* out, int64_t rows, int64_t K, int group_size, int bits,
+                    void* stream);
+
+/*
+ * Bytes of workspace mlxq_quantized_matmul needs for this problem (0 if none).
+ * The workspace must be zero-filled once when first allocated; the kernels
+ * leave it zeroed again at exit, so it can be reused by later calls on the
+ * same stream without clearing. Calls that overlap on the GPU must not share it.
+ */
+size_t mlxq_qmm_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, int bits,
+                               int dtype);
+
+/*
+ * quantized_matmul: replaces mx.quantized_matmul(x, w, scales, biases,
+ * transpose=True, group_size, bits) as called by nn.QuantizedLinear
+ * (qwen2.py:58-61,123-134,227), plus QuantizedLinear's optional bias add.
+ * x [M, K], w [N, K*bits/32], scales/biases [N, K/group_size], bias [N] or
+ * NULL, out [M, N]; x/scales/biases/bias/out all of `dtype` (bf16 or f16).
+ * out = round(x @ dequant(w)^T) with float32 accumulation; with bias,
+ * round(out + bias).
+ */
+int mlxq_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
+                          const void* biases, const void* bias, void* out, int64_t M,
+                          int64_t N, int64_t K, int group_size, int bits, int dtype,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * gather_qmm: replaces mx.gather_qmm(x, w, scales, biases, lhs_indices,
+ * rhs_indices, transpose=True, group_size, bits, sorted_indices) as called by
+ * QuantizedSwitchLinear (lfm2.py:169-190).
+ *   x      [x_batches, M, K]
+ *   w      [num_experts, N, K*bits/32]; scales/biases [num_experts, N, K/group_size]
+ *   out    [batch, M, N], out[b] = x[xi(b)] @ dequant(w[rhs_indices[b]])^T
+ *   xi(b)  = lhs_indices ? lhs_indices[b] : b / lhs_div   (lhs_div >= 1; the
+ *            broadcast of x [T,1,1,K] against indices [T,k] is lhs_div = k)
+ * sorted_indices != 0 promises rhs_indices is non-decreasing (MLX's hint); the
+ * kernels then stream each expert's weights once for all its rows. Results
+ * do not depend on the flag when the promise holds. Rows whose indices are out
+ * of range are left unwritten.
+ */
+int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const void* biases,
+                    const int32_t* lhs_indices, int64_t lhs_div, const int32_t* rhs_indices,
+                    void* out, int64_t batch, int64_t M, int64_t N, int64_t K,
+                    int64_t num_experts, int64_t x_batches, int group_size, int bits,
+                    int dtype, int sorted_indices, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+/*
+ * Bytes of workspace mlxq_gather_qmm needs (the per-expert segment table of
+ * the sorted path; 0 when sorted_indices == 0). No zero-fill is required.
+ */
+size_t mlxq_gather_qmm_workspace_size(int64_t batch, int64_t M, int64_t N, int64_t K,
+                                      int64_t num_experts, int group_size, int bits, int dtype,
+                                      int sorted_indices);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLXQ_B200_H */

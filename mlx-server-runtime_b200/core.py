@@ -1,0 +1,297 @@
+"""MLX-named quantized operators over torch CUDA tensors.
+
+Mirrors the MLX operator surface the reference's model graphs call
+(mlx 0.31.2, python/uv.lock:939-940 of the reference):
+
+  quantize(w, group_size=64, bits=4, mode="affine") -> (w_q, scales, biases)
+      mx.quantize, reference call sites lfm2.py:112-117,142-151
+  dequantize(w_q, scales, biases, group_size=64, bits=4, mode="affine")
+      mx.dequantize (north_star API)
+  quantized_matmul(x, w, scales, biases, transpose=True, group_size=64, bits=4, mode="affine")
+      mx.quantized_matmul via nn.QuantizedLinear, qwen2.py:58-61,123-134,227
+  gather_qmm(x, w, scales, biases, lhs_indices=None, rhs_indices=None, transpose=True,
+             group_size=64, bits=4, mode="affine", sorted_indices=False)
+      mx.gather_qmm via QuantizedSwitchLinear, lfm2.py:176-187
+
+Torch tensors are only device buffers here: every operator is one call into
+libmlxq_b200.so on the tensor's device and current stream. Misuse raises
+ValueError, as MLX does; device failures raise RuntimeError.
+"""
+from __future__ import annotations
+
+import math
+import threading
+
+import torch
+
+from . import _lib
+
+_DT = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
+
+__all__ = ["quantize", "dequantize", "quantized_matmul", "gather_qmm", "Workspace"]
+
+
+def _dtype_code(t: torch.Tensor, what: str, allowed=(torch.bfloat16, torch.float16)) -> int:
+    if t.dtype not in allowed:
+        names = ", ".join(str(a).replace("torch.", "") for a in allowed)
+        raise ValueError(f"{what} must have dtype in ({names}), got {t.dtype}")
+    return _DT[t.dtype]
+
+
+def _cuda(*ts: torch.Tensor) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if t.device.type != "cuda":
+            raise ValueError(f"expected CUDA tensors, got a tensor on {t.device}")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"tensors are on different devices ({dev} and {t.device})")
+    return dev
+
+
+def _mode(mode: str) -> None:
+    if mode != "affine":
+        raise ValueError(f"mode={mode!r} is not supported (only 'affine')")
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+class Workspace:
+    """Per-(device, stream) scratch buffers for the kernels that need them.
+
+    The qmm workspace holds K-split partial sums and tickets that the kernel
+    resets to zero on exit; it is zero-filled once when it is (re)allocated.
+    Work enqueued on different streams never shares a buffer.
+    """
+
+    _lock = threading.Lock()
+    _bufs: dict = {}
+
+    @classmethod
+    def get(cls, device: torch.device, stream: torch.cuda.Stream, nbytes: int) -> torch.Tensor:
+        key = (device.index, stream.cuda_stream)
+        with cls._lock:
+            buf = cls._bufs.get(key)
+            if buf is None or buf.numel() < nbytes:
+                size = max(nbytes, 1 << 20)
+                size = 1 << int(math.ceil(math.log2(size)))
+                with torch.cuda.stream(stream):
+                    buf = torch.zeros(size, dtype=torch.uint8, device=device)
+                cls._bufs[key] = buf
+            return buf
+
+    @classmethod
+    def clear(cls) -> None:
+        with cls._lock:
+            cls._bufs.clear()
+
+
+def quantize(w: torch.Tensor, group_size: int = 64, bits: int = 4, mode: str = "affine"):
+    """Affine group quantization of the last axis: returns (w_q uint32, scales, biases)."""
+    _mode(mode)
+    dev = _cuda(w)
+    dt = _dtype_code(w, "w", (torch.float32, torch.bfloat16, torch.float16))
+    if w.ndim < 2:
+        raise ValueError(f"quantize expects a matrix (ndim >= 2), got shape {tuple(w.shape)}")
+    K = w.shape[-1]
+    if bits not in (2, 4, 8):
+        raise ValueError(f"bits={bits} is not supported (2, 4 or 8)")
+    if group_size not in (32, 64, 128):
+        raise ValueError(f"group_size={group_size} is not one of 32, 64, 128")
+    if K % group_size:
+        raise ValueError(f"the last dimension ({K}) must be divisible by group_size={group_size}")
+    w = w.contiguous()
+    lead = w.shape[:-1]
+    rows = w.numel() // K
+    wq = torch.empty(*lead, K * bits // 32, dtype=torch.uint32, device=dev)
+    s = torch.empty(*lead, K // group_size, dtype=w.dtype, device=dev)
+    b = torch.empty_like(s)
+    with torch.cuda.device(dev):
+        st = torch.cuda.current_stream(dev)
+        rc = _lib.load().mlxq_quantize(_ptr(w), dt, _ptr(wq), _ptr(s), _ptr(b), rows, K,
+                                       group_size, bits, st.cuda_stream)
+    _lib.check(rc, "quantize")
+    return wq, s, b
+
+
+def dequantize(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, group_size: int = 64,
+               bits: int = 4, mode: str = "affine") -> torch.Tensor:
+    """w_hat = scale*q + bias in the dtype of scales (one rounding per operation)."""
+    _mode(mode)
+    dev = _cuda(w, scales, biases)
+    if w.dtype != torch.uint32:
+        raise ValueError(f"w must be uint32 packed codes, got {w.dtype}")
+    dt = _dtype_code(scales, "scales", (torch.float32, torch.bfloat16, torch.float16))
+    if biases.dtype != scales.dtype:
+        raise ValueError("scales and biases must have the same dtype")
+    if bits not in (2, 4, 8):
+        raise ValueError(f"bits={bits} is not supported (2, 4 or 8)")
+    K = w.shape[-1] * 32 // bits
+    if scales.shape != (*w.shape[:-1], K // group_size) or biases.shape != scales.shape:
+        raise ValueError(
+            f"scales/biases shape {tuple(scales.shape)} does not match w {tuple(w.shape)} "
+            f"with group_size={group_size}, bits={bits}")
+    w, scales, biases = w.contiguous(), scales.contiguous(), biases.contiguous()
+    rows = w.numel() // w.shape[-1]
+    out = torch.empty(*w.shape[:-1], K, dtype=scales.dtype, device=dev)
+    with torch.cuda.device(dev):
+        st = torch.cuda.current_stream(dev)
+        rc = _lib.load().mlxq_dequantize(_ptr(w), _ptr(scales), _ptr(biases), dt, _ptr(out),
+                                         rows, K, group_size, bits, st.cuda_stream)
+    _lib.check(rc, "dequantize")
+    return out
+
+
+def _check_qweights(w, scales, biases, group_size, bits, x_dtype):
+    if w.dtype != torch.uint32:
+        raise ValueError(f"w must be uint32 packed codes, got {w.dtype}")
+    if bits not in (4, 8):
+        raise ValueError(f"bits={bits} is not supported by the matmul (4 or 8)")
+    if group_size not in (32, 64, 128):
+        raise ValueError(f"group_size={group_size} is not one of 32, 64, 128")
+    if biases is None:
+        raise ValueError("affine quantization requires biases")
+    if scales.dtype != x_dtype or biases.dtype != x_dtype:
+        raise ValueError(
+            f"scales/biases dtype ({scales.dtype}) must match the activations ({x_dtype})")
+    K = w.shape[-1] * 32 // bits
+    if scales.shape[-1] * group_size != K or scales.shape != biases.shape or \
+            scales.shape[:-1] != w.shape[:-1]:
+        raise ValueError(
+            f"shapes of w {tuple(w.shape)}, scales {tuple(scales.shape)}, biases "
+            f"{tuple(biases.shape)} are inconsistent with group_size={group_size}, bits={bits}")
+    return K
+
+
+def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
+                     biases: torch.Tensor | None = None, transpose: bool = True,
+                     group_size: int = 64, bits: int = 4, mode: str = "affine",
+                     bias: torch.Tensor | None = None) -> torch.Tensor:
+    """x[..., K] @ dequantize(w)^T -> [..., N] (float32 accumulation).
+
+    ``bias`` (not an MLX argument) fuses QuantizedLinear's bias add into the
+    same launch; the result equals ``quantized_matmul(...) + bias``.
+    """
+    _mode(mode)
+    if not transpose:
+        raise ValueError("transpose=False is not supported; the model graphs use transpose=True")
+    dev = _cuda(x, w, scales, biases, bias)
+    dt = _dtype_code(x, "x")
+    if w.ndim != 2:
+        raise ValueError(f"w must be 2-D [N, K*bits/32], got shape {tuple(w.shape)}")
+    K = _check_qweights(w, scales, biases, group_size, bits, x.dtype)
+    if x.shape[-1] != K:
+        raise ValueError(f"x has {x.shape[-1]} features but w expects K={K}")
+    N = w.shape[0]
+    if bias is not None and (bias.shape != (N,) or bias.dtype != x.dtype):
+        raise ValueError(f"bias must be [{N}] of dtype {x.dtype}")
+    lead = x.shape[:-1]
+    x2 = x.contiguous()
+    M = x2.numel() // K
+    out = torch.empty(*lead, N, dtype=x.dtype, device=dev)
+    if M == 0:
+        return out
+    L = _lib.load()
+    w, scales, biases = w.contiguous(), scales.contiguous(), biases.contiguous()
+    with torch.cuda.device(dev):
+        st = torch.cuda.current_stream(dev)
+        need = L.mlxq_qmm_workspace_size(M, N, K, group_size, bits, dt)
+        ws = Workspace.get(dev, st, need) if need else None
+        rc = L.mlxq_quantized_matmul(_ptr(x2), _ptr(w), _ptr(scales), _ptr(biases), _ptr(bias),
+                                     _ptr(out), M, N, K, group_size, bits, dt, _ptr(ws),
+                                     0 if ws is None else ws.numel(), st.cuda_stream)
+    _lib.check(rc, "quantized_matmul")
+    return out
+
+
+def _broadcast_shape(a, b):
+    return tuple(torch.broadcast_shapes(torch.Size(a), torch.Size(b)))
+
+
+def broadcast_divisor(bx: tuple, bshape: tuple) -> int | None:
+    """When x's batch dims ``bx`` broadcast to ``bshape`` only by trailing
+    size-1 dims, output batch entry b reads x batch b // d: return d.
+    Otherwise return None (an explicit index tensor is needed).
+
+    SwitchGLU's unsorted call (x [T,1,1,K] against indices [T,k],
+    lfm2.py:202-214) gives d = k; the sorted call gives d = 1.
+    """
+    pad = (1,) * (len(bshape) - len(bx)) + tuple(bx)
+    tail, k = 1, len(bshape)
+    while k > 0 and pad[k - 1] == 1:
+        tail *= bshape[k - 1]
+        k -= 1
+    return tail if tuple(pad[:k]) == tuple(bshape[:k]) else None
+
+
+def gather_qmm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
+               biases: torch.Tensor | None = None, lhs_indices: torch.Tensor | None = None,
+               rhs_indices: torch.Tensor | None = None, transpose: bool = True,
+               group_size: int = 64, bits: int = 4, mode: str = "affine",
+               sorted_indices: bool = False) -> torch.Tensor:
+    """Batched quantized matmul with index-selected operands (MLX gather_qmm).
+
+    x [..., M, K] with batch dims Bx; w [..., N, K*bits/32] with batch dims Bw.
+    lhs_indices index flattened Bx, rhs_indices flattened Bw; both broadcast to
+    a common shape S and the result is [*S, M, N].
+    """
+    _mode(mode)
+    if not transpose:
+        raise ValueError("transpose=False is not supported; the model graphs use transpose=True")
+    dev = _cuda(x, w, scales, biases, lhs_indices, rhs_indices)
+    dt = _dtype_code(x, "x")
+    if x.ndim < 2 or w.ndim < 2:
+        raise ValueError("gather_qmm expects x [..., M, K] and w [..., N, K*bits/32]")
+    K = _check_qweights(w, scales, biases, group_size, bits, x.dtype)
+    if x.shape[-1] != K:
+        raise ValueError(f"x has {x.shape[-1]} features but w expects K={K}")
+    M, N = x.shape[-2], w.shape[-2]
+    bx, bw = tuple(x.shape[:-2]), tuple(w.shape[:-2])
+    x_batches = math.prod(bx)
+    E = math.prod(bw)
+    for name, idx in (("lhs_indices", lhs_indices), ("rhs_indices", rhs_indices)):
+        if idx is not None and idx.dtype not in (torch.int32, torch.int64, torch.uint32):
+            raise ValueError(f"{name} must be an integer tensor, got {idx.dtype}")
+    lhs_shape = bx if lhs_indices is None else tuple(lhs_indices.shape)
+    rhs_shape = bw if rhs_indices is None else tuple(rhs_indices.shape)
+    try:
+        bshape = _broadcast_shape(lhs_shape, rhs_shape)
+    except RuntimeError as e:
+        raise ValueError(f"cannot broadcast index shapes {lhs_shape} and {rhs_shape}") from e
+    batch = math.prod(bshape)
+    out = torch.empty(*bshape, M, N, dtype=x.dtype, device=dev)
+    if batch == 0 or M == 0:
+        return out
+
+    def _flat(idx, natural):
+        if idx is None:
+            idx = torch.arange(math.prod(natural), device=dev, dtype=torch.int32).reshape(natural)
+        return idx.to(torch.int32).expand(bshape).contiguous().reshape(-1)
+
+    rhs = _flat(rhs_indices, bw)
+    lhs, lhs_div = None, 1
+    if lhs_indices is None:
+        lhs_div = broadcast_divisor(bx, bshape)
+        if lhs_div is None:
+            lhs, lhs_div = _flat(None, bx), 1
+    else:
+        lhs = _flat(lhs_indices, bx)
+    L = _lib.load()
+    x2 = x.contiguous()
+    w, scales, biases = w.contiguous(), scales.contiguous(), biases.contiguous()
+    with torch.cuda.device(dev):
+        st = torch.cuda.current_stream(dev)
+        need = L.mlxq_gather_qmm_workspace_size(batch, M, N, K, E, group_size, bits, dt,
+                                                int(bool(sorted_indices)))
+        ws = Workspace.get(dev, st, need) if need else None
+        rc = L.mlxq_gather_qmm(_ptr(x2), _ptr(w), _ptr(scales), _ptr(biases), _ptr(lhs), lhs_div,
+                               _ptr(rhs), _ptr(out), batch, M, N, K, E, x_batches, group_size,
+                               bits, dt, int(bool(sorted_indices)), _ptr(ws),
+                               0 if ws is None else ws.numel(), st.cuda_stream)
+    _lib.check(rc, "gather_qmm")
+    return out

@@ -1,0 +1,275 @@
+// extern "C" entry points of libmlxq_b200.so (declared in include/mlxq_b200.h).
+// Host-side validation happens before anything is enqueued; every failure
+// returns a negative code and records a message for mlxq_last_error().
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/mlxq_b200.h"
+#include "launch.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(MLXQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+struct DeviceInfo {
+    int num_sms = 0;
+    int max_smem = 0;
+};
+
+// Properties of the calling thread's current device (cached per device).
+int device_info(DeviceInfo* out, cudaStream_t stream) {
+    static DeviceInfo cache[64];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+#if CUDART_VERSION >= 12080
+    if (stream != nullptr) {
+        int sdev = -1;
+        e = cudaStreamGetDevice(stream, &sdev);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaStreamGetDevice");
+        if (sdev != dev)
+            return fail(MLXQ_ERR_CUDA, "stream belongs to device %d but device %d is current",
+                        sdev, dev);
+    }
+#else
+    (void)stream;
+#endif
+    if (dev < 0 || dev >= 64) return fail(MLXQ_ERR_CUDA, "device ordinal %d out of range", dev);
+    if (cache[dev].num_sms == 0) {
+        int sms = 0, smem = 0;
+        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SMs)");
+        e = cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(smem)");
+        cache[dev].max_smem = smem - 1024;  // room for the kernels' static shared memory
+        cache[dev].num_sms = sms;
+    }
+    *out = cache[dev];
+    return MLXQ_OK;
+}
+
+int check_bits_gs(int bits, int group_size, bool matmul) {
+    const bool bits_ok = matmul ? (bits == 4 || bits == 8) : (bits == 2 || bits == 4 || bits == 8);
+    if (!bits_ok)
+        return fail(MLXQ_ERR_UNSUPPORTED_BITS, "bits=%d is not supported (%s)", bits,
+                    matmul ? "4 or 8" : "2, 4 or 8");
+    if (group_size != 32 && group_size != 64 && group_size != 128)
+        return fail(MLXQ_ERR_GROUP_SIZE, "group_size=%d is not one of 32, 64, 128", group_size);
+    return MLXQ_OK;
+}
+
+int check_k(int64_t K, int group_size) {
+    if (K <= 0 || K % group_size != 0)
+        return fail(MLXQ_ERR_SHAPE, "K=%lld must be a positive multiple of group_size=%d",
+                    static_cast<long long>(K), group_size);
+    return MLXQ_OK;
+}
+
+constexpr int64_t kIntMax = 0x7fffffffLL;
+
+size_t dense_plan(int64_t M, int64_t N, int64_t K, int group_size, int bits, int dtype,
+                  const DeviceInfo& di, mlxq::QmvPlan* plan, bool* ok) {
+    *ok = mlxq::qmv_plan(dtype, bits, group_size, static_cast<int>(M), static_cast<int>(N),
+                         static_cast<int>(K), 0, 0, di.num_sms, di.max_smem, plan);
+    return *ok ? plan->ws_bytes : 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mlxq_abi_version(void) { return MLXQ_ABI_VERSION; }
+
+const char* mlxq_last_error(void) { return g_last_error.c_str(); }
+
+int mlxq_quantize(const void* w, int w_dtype, uint32_t* wq, void* scales, void* biases,
+                  int64_t rows, int64_t K, int group_size, int bits, void* stream) {
+    int rc = check_bits_gs(bits, group_size, false);
+    if (rc) return rc;
+    if ((rc = check_k(K, group_size))) return rc;
+    if (rows < 0) return fail(MLXQ_ERR_SHAPE, "rows=%lld must be >= 0", (long long)rows);
+    if (w_dtype != MLXQ_F32 && w_dtype != MLXQ_BF16 && w_dtype != MLXQ_F16)
+        return fail(MLXQ_ERR_DTYPE, "w_dtype=%d is not float32, bfloat16 or float16", w_dtype);
+    if (!w || !wq || !scales || !biases) return fail(MLXQ_ERR_NULL, "quantize: NULL pointer");
+    if (!aligned16(w) || !aligned16(wq) || !aligned16(scales) || !aligned16(biases))
+        return fail(MLXQ_ERR_ALIGN, "quantize: pointers must be 16-byte aligned");
+    if (rows == 0) return MLXQ_OK;
+    cudaError_t e = mlxq::launch_quantize(w, w_dtype, wq, scales, biases, rows, K, group_size, bits,
+                                          static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
+    return MLXQ_OK;
+}
+
+int mlxq_dequantize(const uint32_t* wq, const void* scales, const void* biases, int dtype,
+                    void* out, int64_t rows, int64_t K, int group_size, int bits, void* stream) {
+    int rc = check_bits_gs(bits, group_size, false);
+    if (rc) return rc;
+    if ((rc = check_k(K, group_size))) return rc;
+    if (rows < 0) return fail(MLXQ_ERR_SHAPE, "rows=%lld must be >= 0", (long long)rows);
+    if (dtype != MLXQ_F32 && dtype != MLXQ_BF16 && dtype != MLXQ_F16)
+        return fail(MLXQ_ERR_DTYPE, "dtype=%d is not float32, bfloat16 or float16", dtype);
+    if (!wq || !scales || !biases || !out) return fail(MLXQ_ERR_NULL, "dequantize: NULL pointer");
+    if (!aligned16(wq) || !aligned16(scales) || !aligned16(biases) || !aligned16(out))
+        return fail(MLXQ_ERR_ALIGN, "dequantize: pointers must be 16-byte aligned");
+    if (rows == 0) return MLXQ_OK;
+    cudaError_t e = mlxq::launch_dequantize(wq, scales, biases, dtype, out, rows, K, group_size,
+                                            bits, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "dequantize launch");
+    return MLXQ_OK;
+}
+
+size_t mlxq_qmm_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, int bits,
+                               int dtype) {
+    if (check_bits_gs(bits, group_size, true) || check_k(K, group_size)) return 0;
+    if (M <= 0 || N <= 0 || M > kIntMax || N > kIntMax || K > kIntMax) return 0;
+    DeviceInfo di;
+    if (device_info(&di, nullptr)) return 0;
+    mlxq::QmvPlan plan;
+    bool ok = false;
+    return dense_plan(M, N, K, group_size, bits, dtype, di, &plan, &ok);
+}
+
+int mlxq_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
+                          const void* biases, const void* bias, void* out, int64_t M, int64_t N,
+                          int64_t K, int group_size, int bits, int dtype, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+    int rc = check_bits_gs(bits, group_size, true);
+    if (rc) return rc;
+    if ((rc = check_k(K, group_size))) return rc;
+    if (M < 0 || N <= 0 || M > kIntMax || N > kIntMax || K > kIntMax)
+        return fail(MLXQ_ERR_SHAPE, "quantized_matmul: bad shape M=%lld N=%lld K=%lld",
+                    (long long)M, (long long)N, (long long)K);
+    if (dtype != MLXQ_BF16 && dtype != MLXQ_F16)
+        return fail(MLXQ_ERR_DTYPE, "quantized_matmul: dtype=%d must be bfloat16 or float16", dtype);
+    if (!x || !w || !scales || !biases || !out)
+        return fail(MLXQ_ERR_NULL, "quantized_matmul: NULL pointer");
+    if (!aligned16(x) || !aligned16(w) || !aligned16(scales) || !aligned16(biases) ||
+        !aligned16(out) || (bias && !aligned16(bias)))
+        return fail(MLXQ_ERR_ALIGN, "quantized_matmul: pointers must be 16-byte aligned");
+    if (M == 0) return MLXQ_OK;
+    DeviceInfo di;
+    if ((rc = device_info(&di, static_cast<cudaStream_t>(stream)))) return rc;
+    mlxq::QmvPlan plan;
+    bool ok = false;
+    const size_t need = dense_plan(M, N, K, group_size, bits, dtype, di, &plan, &ok);
+    if (!ok) return fail(MLXQ_ERR_SHAPE, "quantized_matmul: no launch plan fits shared memory");
+    if (need > 0) {
+        if (!workspace || workspace_bytes < need)
+            return fail(MLXQ_ERR_WORKSPACE, "quantized_matmul: needs %zu workspace bytes, got %zu",
+                        need, workspace ? workspace_bytes : (size_t)0);
+        if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+            return fail(MLXQ_ERR_ALIGN, "quantized_matmul: workspace must be 256-byte aligned");
+    }
+    mlxq::QmvParams p{};
+    p.x = x; p.w = w; p.s = scales; p.b = biases; p.bias = bias; p.out = out;
+    p.M = static_cast<int>(M); p.N = static_cast<int>(N); p.K = static_cast<int>(K);
+    p.mode = 0; p.lhs = nullptr; p.lhs_div = 1; p.rhs = nullptr; p.seg = nullptr;
+    p.batch = 0; p.num_experts = 1; p.x_batches = 1; p.w_estride = 0; p.sb_estride = 0;
+    p.splits = plan.splits; p.gps = plan.gps; p.win = plan.win; p.ztotal = plan.ztotal;
+    if (need > 0) {
+        const size_t counters = static_cast<size_t>(plan.ztotal) * plan.rowblocks * 4;
+        p.counter = static_cast<unsigned*>(workspace);
+        p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                             ((counters + 255) / 256) * 256);
+    }
+    cudaError_t e = mlxq::qmv_launch(dtype, bits, group_size, plan, p,
+                                     static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "quantized_matmul launch");
+    return MLXQ_OK;
+}
+
+size_t mlxq_gather_qmm_workspace_size(int64_t batch, int64_t M, int64_t N, int64_t K,
+                                      int64_t num_experts, int group_size, int bits, int dtype,
+                                      int sorted_indices) {
+    (void)batch; (void)M; (void)N; (void)K; (void)group_size; (void)bits; (void)dtype;
+    if (!sorted_indices || num_experts <= 0) return 0;
+    return ((static_cast<size_t>(num_experts) + 1) * 4 + 255) / 256 * 256;
+}
+
+int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const void* biases,
+                    const int32_t* lhs_indices, int64_t lhs_div, const int32_t* rhs_indices,
+                    void* out, int64_t batch, int64_t M, int64_t N, int64_t K,
+                    int64_t num_experts, int64_t x_batches, int group_size, int bits, int dtype,
+                    int sorted_indices, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc = check_bits_gs(bits, group_size, true);
+    if (rc) return rc;
+    if ((rc = check_k(K, group_size))) return rc;
+    if (batch < 0 || M < 0 || N <= 0 || num_experts <= 0 || x_batches <= 0 || batch > kIntMax ||
+        M > kIntMax || N > kIntMax || K > kIntMax || num_experts > kIntMax ||
+        x_batches > kIntMax || batch * M > kIntMax || x_batches * M > kIntMax)
+        return fail(MLXQ_ERR_SHAPE,
+                    "gather_qmm: bad shape batch=%lld M=%lld N=%lld K=%lld E=%lld x_batches=%lld",
+                    (long long)batch, (long long)M, (long long)N, (long long)K,
+                    (long long)num_experts, (long long)x_batches);
+    if (!lhs_indices && lhs_div < 1)
+        return fail(MLXQ_ERR_INDEX, "gather_qmm: lhs_div must be >= 1 without lhs_indices");
+    if (dtype != MLXQ_BF16 && dtype != MLXQ_F16)
+        return fail(MLXQ_ERR_DTYPE, "gather_qmm: dtype=%d must be bfloat16 or float16", dtype);
+    if (!x || !w || !scales || !biases || !out || !rhs_indices)
+        return fail(MLXQ_ERR_NULL, "gather_qmm: NULL pointer");
+    if (!aligned16(x) || !aligned16(w) || !aligned16(scales) || !aligned16(biases) ||
+        !aligned16(out))
+        return fail(MLXQ_ERR_ALIGN, "gather_qmm: pointers must be 16-byte aligned");
+    if (batch == 0 || M == 0) return MLXQ_OK;
+    DeviceInfo di;
+    if ((rc = device_info(&di, static_cast<cudaStream_t>(stream)))) return rc;
+    const int mode = sorted_indices ? 2 : 1;
+    const size_t need = mlxq_gather_qmm_workspace_size(batch, M, N, K, num_experts, group_size,
+                                                       bits, dtype, sorted_indices);
+    if (need > 0) {
+        if (!workspace || workspace_bytes < need)
+            return fail(MLXQ_ERR_WORKSPACE, "gather_qmm: needs %zu workspace bytes, got %zu", need,
+                        workspace ? workspace_bytes : (size_t)0);
+        if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+            return fail(MLXQ_ERR_ALIGN, "gather_qmm: workspace must be 256-byte aligned");
+    }
+    mlxq::QmvPlan plan;
+    const int zhint = (mode == 2) ? static_cast<int>(batch * M / num_experts) : static_cast<int>(batch);
+    if (!mlxq::qmv_plan(dtype, bits, group_size, static_cast<int>(M), static_cast<int>(N),
+                        static_cast<int>(K), mode, zhint, di.num_sms, di.max_smem, &plan))
+        return fail(MLXQ_ERR_SHAPE, "gather_qmm: no launch plan fits shared memory");
+    if (mode == 2) {
+        plan.ztotal = static_cast<int>(num_experts);
+        plan.gridz = plan.ztotal < 65535 ? plan.ztotal : 65535;
+    }
+    mlxq::QmvParams p{};
+    p.x = x; p.w = w; p.s = scales; p.b = biases; p.bias = nullptr; p.out = out;
+    p.M = static_cast<int>(M); p.N = static_cast<int>(N); p.K = static_cast<int>(K);
+    p.mode = mode; p.lhs = lhs_indices; p.lhs_div = static_cast<int>(lhs_div < 1 ? 1 : lhs_div);
+    p.rhs = rhs_indices; p.batch = static_cast<int>(batch);
+    p.num_experts = static_cast<int>(num_experts); p.x_batches = static_cast<int>(x_batches);
+    p.w_estride = N * (K * bits / 32);
+    p.sb_estride = N * (K / group_size);
+    p.splits = 1; p.gps = plan.gps; p.win = plan.win; p.ztotal = plan.ztotal;
+    p.partial = nullptr; p.counter = nullptr;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (mode == 2) {
+        int32_t* seg = static_cast<int32_t*>(workspace);
+        cudaError_t e = mlxq::launch_segments(rhs_indices, static_cast<int>(batch),
+                                              static_cast<int>(num_experts), seg, st);
+        if (e != cudaSuccess) return cuda_fail(e, "gather_qmm segment table");
+        p.seg = seg;
+    }
+    cudaError_t e = mlxq::qmv_launch(dtype, bits, group_size, plan, p, st);
+    if (e != cudaSuccess) return cuda_fail(e, "gather_qmm launch");
+    return MLXQ_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,71 @@
+// Host-side launcher declarations shared by the C-ABI layer (abi.cu) and the
+// kernel translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mlxq {
+
+enum { kF32 = 0, kBF16 = 1, kF16 = 2 };
+
+cudaError_t launch_quantize(const void* w, int dtype, uint32_t* wq, void* s, void* b,
+                            long long rows, long long K, int gs, int bits, cudaStream_t st);
+cudaError_t launch_dequantize(const uint32_t* wq, const void* s, const void* b, int dtype,
+                              void* out, long long rows, long long K, int gs, int bits,
+                              cudaStream_t st);
+
+// One problem for the skinny (decode) tensor-core kernel family.
+//   mode 0: dense  out[M,N] = x[M,K] @ W^T
+//   mode 1: gather, one batch entry per grid z: out[b] = x[xi(b)] @ W[rhs[b]]^T
+//   mode 2: gather with rhs sorted; grid z = expert, rows of expert e are the
+//           batch entries [seg[e], seg[e+1]) of a segment table built on device.
+struct QmvParams {
+    const void* x;
+    const uint32_t* w;
+    const void* s;
+    const void* b;
+    const void* bias;  // optional per-output bias [N] (mode 0 only)
+    void* out;
+    int M, N, K;
+    int mode;
+    const int32_t* lhs;  // optional x-batch index per batch entry
+    int lhs_div;         // xi(b) = b / lhs_div when lhs == nullptr
+    const int32_t* rhs;  // expert per batch entry
+    const int32_t* seg;  // mode 2: [num_experts + 1] row offsets
+    int batch;
+    int num_experts;
+    int x_batches;         // number of [M, K] matrices x holds (gather modes)
+    long long w_estride;   // words per expert
+    long long sb_estride;  // scale/bias elements per expert
+    int splits;            // K splits (mode 0)
+    int gps;               // groups per split
+    int win;               // groups per shared-memory window (multiple of the chunk)
+    int ztotal;            // number of z work items
+    float* partial;        // [splits][M][N] fp32, used when splits > 1
+    unsigned* counter;     // [ztotal][gridDim.x], zero at entry and exit
+};
+
+struct QmvPlan {
+    int nt;       // n-tiles of 8 tokens (1, 2 or 4)
+    int splits;
+    int gps;
+    int win;
+    int rowblocks;
+    int ztotal;
+    int gridz;
+    size_t smem;
+    bool sbvec;
+    size_t ws_bytes;  // workspace the plan needs (0 if none)
+};
+
+// Plans and launches the skinny kernel (defined in qmv_dispatch.cu).
+bool qmv_plan(int dtype, int bits, int gs, int M_tokens_per_item, int N, int K, int mode,
+              int z_items, int num_sms, int max_smem, QmvPlan* plan);
+cudaError_t qmv_launch(int dtype, int bits, int gs, const QmvPlan& plan, const QmvParams& p,
+                       cudaStream_t st);
+
+cudaError_t launch_segments(const int32_t* rhs, int batch, int num_experts, int32_t* seg,
+                            cudaStream_t st);
+
+}  // namespace mlxq

@@ -1,0 +1,70 @@
+// Launch wrapper for one instantiation of the skinny kernel. Each
+// qmv_<dtype>_<bits>.cu translation unit instantiates the wrappers for its
+// (dtype, bits) pair so the kernel family compiles in parallel.
+#pragma once
+
+#include "qmv.cuh"
+
+namespace mlxq {
+
+constexpr int kQmvWarps = 8;
+constexpr int kQmvStages = 4;
+
+template <typename T, int BITS, int GS, int NT, bool SBV>
+cudaError_t qmv_launch_t(const QmvPlan& plan, const QmvParams& p, cudaStream_t st) {
+    auto kern = qmv_kernel<T, BITS, GS, NT, kQmvWarps, kQmvStages, SBV>;
+    static int configured[64] = {0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (configured[dev] < static_cast<int>(plan.smem)) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(plan.smem));
+        if (e != cudaSuccess) return e;
+        configured[dev] = static_cast<int>(plan.smem);
+    }
+    dim3 grid(plan.rowblocks, plan.splits, plan.gridz);
+    kern<<<grid, kQmvWarps * 32, plan.smem, st>>>(p);
+    return cudaGetLastError();
+}
+
+#define MLXQ_INSTANTIATE_QMV(T, BITS)                                                          \
+    template cudaError_t qmv_launch_t<T, BITS, 32, 1, true>(const QmvPlan&, const QmvParams&,  \
+                                                            cudaStream_t);                     \
+    template cudaError_t qmv_launch_t<T, BITS, 32, 2, true>(const QmvPlan&, const QmvParams&,  \
+                                                            cudaStream_t);                     \
+    template cudaError_t qmv_launch_t<T, BITS, 32, 4, true>(const QmvPlan&, const QmvParams&,  \
+                                                            cudaStream_t);                     \
+    template cudaError_t qmv_launch_t<T, BITS, 64, 1, true>(const QmvPlan&, const QmvParams&,  \
+                                                            cudaStream_t);                     \
+    template cudaError_t qmv_launch_t<T, BITS, 64, 2, true>(const QmvPlan&, const QmvParams&,  \
+                                                            cudaStream_t);                     \
+    template cudaError_t qmv_launch_t<T, BITS, 64, 4, true>(const QmvPlan&, const QmvParams&,  \
+                                                            cudaStream_t);                     \
+    template cudaError_t qmv_launch_t<T, BITS, 128, 1, true>(const QmvPlan&, const QmvParams&, \
+                                                             cudaStream_t);                    \
+    template cudaError_t qmv_launch_t<T, BITS, 128, 2, true>(const QmvPlan&, const QmvParams&, \
+                                                             cudaStream_t);                    \
+    template cudaError_t qmv_launch_t<T, BITS, 128, 4, true>(const QmvPlan&, const QmvParams&, \
+                                                             cudaStream_t);                    \
+    template cudaError_t qmv_launch_t<T, BITS, 32, 1, false>(const QmvPlan&, const QmvParams&, \
+                                                             cudaStream_t);                    \
+    template cudaError_t qmv_launch_t<T, BITS, 32, 2, false>(const QmvPlan&, const QmvParams&, \
+                                                             cudaStream_t);                    \
+    template cudaError_t qmv_launch_t<T, BITS, 32, 4, false>(const QmvPlan&, const QmvParams&, \
+                                                             cudaStream_t);                    \
+    template cudaError_t qmv_launch_t<T, BITS, 64, 1, false>(const QmvPlan&, const QmvParams&, \
+                                                             cudaStream_t);                    \
+    template cudaError_t qmv_launch_t<T, BITS, 64, 2, false>(const QmvPlan&, const QmvParams&, \
+                                                             cudaStream_t);                    \
+    template cudaError_t qmv_launch_t<T, BITS, 64, 4, false>(const QmvPlan&, const QmvParams&, \
+                                                             cudaStream_t);                    \
+    template cudaError_t qmv_launch_t<T, BITS, 128, 1, false>(const QmvPlan&, const QmvParams&,\
+                                                              cudaStream_t);                   \
+    template cudaError_t qmv_launch_t<T, BITS, 128, 2, false>(const QmvPlan&, const QmvParams&,\
+                                                              cudaStream_t);                   \
+    template cudaError_t qmv_launch_t<T, BITS, 128, 4, false>(const QmvPlan&, const QmvParams&,\
+                                                              cudaStream_t);
+
+}  // namespace mlxq
