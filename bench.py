@@ -402,8 +402,73 @@ def run(args):
         dist.destroy_process_group()
 
 
+CASES = {"q": (HIDDEN, HIDDEN), "kv": (KV, HIDDEN), "gate": (INTER, HIDDEN),
+         "down": (HIDDEN, INTER), "lm_head": (VOCAB, HIDDEN)}
+
+
+def run_case(args):
+    """A few launches of one projection (small, for ncu captures and sweeps):
+    rotates over enough weight copies that their total exceeds L2."""
+    import torch
+
+    mxq = load_package()
+    dev = torch.device("cuda", 0)
+    N, K = CASES[args.case]
+    M = args.m
+    per = qmm_bytes(M, N, K)
+    copies = max(2, min(16, -(-400_000_000 // (N * K // 2))))
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7)
+    ws = []
+    for _ in range(copies):
+        w = (torch.randn(N, K, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+        ws.append(mxq.quantize(w, GS, BITS))
+        del w
+    x = torch.randn(M, K, device=dev, generator=gen).to(torch.bfloat16)
+    for i in range(max(3, args.warmup)):
+        mxq.quantized_matmul(x, *ws[i % copies], group_size=GS, bits=BITS)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if args.eager:
+        e0.record()
+        for i in range(args.steps):
+            mxq.quantized_matmul(x, *ws[i % copies], group_size=GS, bits=BITS)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / args.steps
+    else:
+        # one graph of `copies` launches (each weight copy once), replayed
+        st = torch.cuda.Stream(device=dev)
+        st.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(st):
+            for i in range(copies):
+                mxq.quantized_matmul(x, *ws[i], group_size=GS, bits=BITS)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            for i in range(copies):
+                mxq.quantized_matmul(x, *ws[i], group_size=GS, bits=BITS)
+        for _ in range(3):
+            g.replay()
+        reps = max(1, args.steps // copies)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * copies)
+    print(json.dumps({"case": args.case, "M": M, "N": N, "K": K, "copies": copies,
+                      "us_per_launch": round(us, 3), "bytes": per,
+                      "GB/s": round(per / (us * 1e-6) / 1e9, 1)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--case", choices=sorted(CASES), default=None,
+                    help="time one projection only (eager launches, for profiling)")
+    ap.add_argument("--m", type=int, default=1, help="tokens for --case")
+    ap.add_argument("--eager", action="store_true", help="--case: plain launches, no graph")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=10)
@@ -413,6 +478,8 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.case:
+        run_case(args)
     else:
         run(args)
 

@@ -62,19 +62,22 @@ def _ptr(t):
 
 
 class Workspace:
-    """Per-(device, stream) scratch buffers for the kernels that need them.
+    """Per-(device, stream, operator) scratch buffers for the kernels that need them.
 
-    The qmm workspace holds K-split partial sums and tickets that the kernel
-    resets to zero on exit; it is zero-filled once when it is (re)allocated.
-    Work enqueued on different streams never shares a buffer.
+    The quantized_matmul workspace holds K-split partial sums and tickets that
+    the kernel resets to zero on exit; it is zero-filled once when it is
+    (re)allocated and is never shared with another operator (gather_qmm writes
+    its expert segment table into its own buffer). Work enqueued on different
+    streams never shares a buffer.
     """
 
     _lock = threading.Lock()
     _bufs: dict = {}
 
     @classmethod
-    def get(cls, device: torch.device, stream: torch.cuda.Stream, nbytes: int) -> torch.Tensor:
-        key = (device.index, stream.cuda_stream)
+    def get(cls, device: torch.device, stream: torch.cuda.Stream, nbytes: int,
+            kind: str = "qmm") -> torch.Tensor:
+        key = (device.index, stream.cuda_stream, kind)
         with cls._lock:
             buf = cls._bufs.get(key)
             if buf is None or buf.numel() < nbytes:
@@ -288,7 +291,7 @@ def gather_qmm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
         st = torch.cuda.current_stream(dev)
         need = L.mlxq_gather_qmm_workspace_size(batch, M, N, K, E, group_size, bits, dt,
                                                 int(bool(sorted_indices)))
-        ws = Workspace.get(dev, st, need) if need else None
+        ws = Workspace.get(dev, st, need, "gather") if need else None
         rc = L.mlxq_gather_qmm(_ptr(x2), _ptr(w), _ptr(scales), _ptr(biases), _ptr(lhs), lhs_div,
                                _ptr(rhs), _ptr(out), batch, M, N, K, E, x_batches, group_size,
                                bits, dt, int(bool(sorted_indices)), _ptr(ws),

@@ -40,7 +40,12 @@ int device_info(DeviceInfo* out, cudaStream_t stream) {
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
 #if CUDART_VERSION >= 12080
-    if (stream != nullptr) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (stream != nullptr) e = cudaStreamIsCapturing(stream, &cap);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
+    // cudaStreamGetDevice is not permitted on a capturing stream; the check is
+    // skipped while a graph is being captured.
+    if (stream != nullptr && cap == cudaStreamCaptureStatusNone) {
         int sdev = -1;
         e = cudaStreamGetDevice(stream, &sdev);
         if (e != cudaSuccess) return cuda_fail(e, "cudaStreamGetDevice");

@@ -9,37 +9,81 @@
 namespace mlxq {
 
 // ---- element types -----------------------------------------------------------------------
-// Per activation type: conversion helpers and the "magic" constants that turn a
-// 4-bit code held in the low mantissa bits of a 16-bit float into an exact value.
-//   bf16: 0x4300 | q   == 128 + q        (bf16 exponent 2^7, mantissa ulp 1)
-//         0x4500 | q   == 2048 + 16*q    (used for the high nibble of 8-bit codes)
-//   f16 : 0x6400 | q   == 1024 + q
-//         0x7400 | q   == 16384 + 16*q
-// A matmul over (magic | q) therefore computes sum x*q + OFF*sum x, and the
-// per-group epilogue removes OFF*sum(x) in float32.
+// Per activation type: conversion helpers and the extraction that turns packed
+// codes into exact 16-bit MMA operands without integer-to-float conversion. A
+// field OR'ed into the mantissa of a 16-bit float with a fixed exponent gives
+// offset + field exactly:
+//   bf16 (7 mantissa bits): a nibble must sit at bits 0-3 of a half, so every
+//     nibble position is shifted there first:  0x4300 | q = 128 + q,
+//     0x4500 | q = 2048 + 16*q  (the high nibble of an 8-bit code).
+//   f16 (10 mantissa bits): bits 0-3 and 4-7 both fit:  0x6400 | q = 1024 + q,
+//     0x5400 | (q << 4) = 64 + q,  0x6400 | (q << 4) = 1024 + 16*q.
+// extract<BITS>(w) returns four operands, each holding a pair of codes, in a
+// fixed order the activation fragments mirror:
+//   4-bit: nibble pairs (0,4) (1,5) (2,6) (3,7)
+//   8-bit: (low nibbles of bytes 0,2) (high nibbles of bytes 0,2)
+//          (low nibbles of bytes 1,3) (high nibbles of bytes 1,3)
+// and the matmul over them equals sum x*q plus offsets times activation sums:
+//   kUniform: every operand carries the same offset kOff (per code);
+//   otherwise even code positions carry kOffE and odd positions kOffO.
 template <typename T>
 struct Elem;
 
 template <>
 struct Elem<__nv_bfloat16> {
-    static constexpr uint32_t kMagicLo = 0x43004300u;
-    static constexpr uint32_t kMagicHi = 0x45004500u;
-    static constexpr float kOff4 = 128.0f;
-    static constexpr float kOff8 = 2176.0f;  // 128 + 2048
+    template <int BITS>
+    static __device__ __forceinline__ void extract(uint32_t w, uint32_t (&t)[4]) {
+        constexpr uint32_t M0 = 0x000F000Fu, LO = 0x43004300u;
+        constexpr uint32_t HI = (BITS == 4) ? 0x43004300u : 0x45004500u;
+        t[0] = (w & M0) | LO;
+        t[1] = ((w >> 4) & M0) | HI;
+        t[2] = ((w >> 8) & M0) | LO;
+        t[3] = ((w >> 12) & M0) | HI;
+    }
+    template <int BITS>
+    struct Off {
+        static constexpr bool kUniform = true;
+        static constexpr float kOff = (BITS == 4) ? 128.0f : 2176.0f;  // 128 + 2048
+        static constexpr float kOffE = kOff, kOffO = kOff;
+    };
     static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
     static __device__ __forceinline__ __nv_bfloat16 from_f(float v) {
         return __float2bfloat16_rn(v);
+    }
+    // the low / high 16-bit halves of a packed pair, as float
+    static __device__ __forceinline__ float lo(uint32_t u) { return __uint_as_float(u << 16); }
+    static __device__ __forceinline__ float hi(uint32_t u) {
+        return __uint_as_float(u & 0xffff0000u);
     }
 };
 
 template <>
 struct Elem<__half> {
-    static constexpr uint32_t kMagicLo = 0x64006400u;
-    static constexpr uint32_t kMagicHi = 0x74007400u;
-    static constexpr float kOff4 = 1024.0f;
-    static constexpr float kOff8 = 17408.0f;  // 1024 + 16384
+    template <int BITS>
+    static __device__ __forceinline__ void extract(uint32_t w, uint32_t (&t)[4]) {
+        constexpr uint32_t M0 = 0x000F000Fu, M1 = 0x00F000F0u, E = 0x64006400u;
+        constexpr uint32_t O = (BITS == 4) ? 0x54005400u : 0x64006400u;
+        const uint32_t h = w >> 8;
+        t[0] = (w & M0) | E;
+        t[1] = (w & M1) | O;
+        t[2] = (h & M0) | E;
+        t[3] = (h & M1) | O;
+    }
+    template <int BITS>
+    struct Off {
+        static constexpr bool kUniform = (BITS == 8);
+        static constexpr float kOffE = 1024.0f;
+        static constexpr float kOffO = (BITS == 4) ? 64.0f : 1024.0f;
+        static constexpr float kOff = (BITS == 4) ? 1024.0f : 2048.0f;  // uniform case only
+    };
     static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
     static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+    static __device__ __forceinline__ float lo(uint32_t u) {
+        return __half2float(__ushort_as_half(static_cast<unsigned short>(u & 0xffffu)));
+    }
+    static __device__ __forceinline__ float hi(uint32_t u) {
+        return __half2float(__ushort_as_half(static_cast<unsigned short>(u >> 16)));
+    }
 };
 
 template <>
@@ -49,30 +93,39 @@ struct Elem<float> {
 };
 
 // ---- tensor-core fragment MMA (m16n8k16, fp32 accumulate) -------------------------------
+// Plain (non-volatile) asm: the instructions have no side effects beyond their
+// outputs, so the compiler may interleave independent accumulation chains.
+// mma16816z starts from a zero accumulator.
+#define MLXQ_MMA_ASM(TY)                                                                         \
+    "mma.sync.aligned.m16n8k16.row.col.f32." TY "." TY ".f32 "
+
 template <typename T>
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                         uint32_t a3, uint32_t b0, uint32_t b1);
-
-template <>
-__device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], uint32_t a0, uint32_t a1,
-                                                        uint32_t a2, uint32_t a3, uint32_t b0,
-                                                        uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
-        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+    if constexpr (__is_same(T, __nv_bfloat16)) {
+        asm(MLXQ_MMA_ASM("bf16") "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    } else {
+        asm(MLXQ_MMA_ASM("f16") "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    }
 }
 
-template <>
-__device__ __forceinline__ void mma16816<__half>(float (&d)[4], uint32_t a0, uint32_t a1,
-                                                 uint32_t a2, uint32_t a3, uint32_t b0,
-                                                 uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
-        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+template <typename T>
+__device__ __forceinline__ void mma16816z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+    const float z = 0.0f;
+    if constexpr (__is_same(T, __nv_bfloat16)) {
+        asm(MLXQ_MMA_ASM("bf16") "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+            : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
+    } else {
+        asm(MLXQ_MMA_ASM("f16") "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+            : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
+    }
 }
 
 // ---- async copies (LDGSTS) ----------------------------------------------------------------

@@ -56,6 +56,7 @@ struct QmvPlan {
     int gridz;
     size_t smem;
     bool sbvec;
+    bool single;  // one token per pass (selects the kernel without odd-column folds)
     size_t ws_bytes;  // workspace the plan needs (0 if none)
 };
 

@@ -7,28 +7,30 @@
 // gather_qmm's per-expert products, lfm2.py:176-187).
 //
 // Work decomposition
-//   * A warp owns 16 weight rows; a CTA of NW warps owns 16*NW rows and a
-//     contiguous range of quantization groups (a K split). Weight rows are
-//     the M side of a m16n8k16 MMA, tokens the N side (8 per n-tile).
+//   * A CTA owns 128 weight rows (8 row tiles of 16) and a contiguous range of
+//     quantization groups (a K split). Weight rows are the M side of an
+//     m16n8k16 MMA, tokens the N side (8 per n-tile).
+//   * Each row tile is served by KSW warps that take alternate 128-byte chunks
+//     of K (KSW = 2 for up to 16 tokens: 16 warps per SM hide the MMA and
+//     shared-memory latencies); their partial sums meet in shared memory at
+//     the end, in a fixed order.
 //   * Weights stream HBM -> shared memory with 16-byte cp.async copies into a
 //     STAGES-deep ring private to each warp: one stage is 16 rows x 128 bytes
-//     (CG groups), plus the matching scales/biases. No block-wide barrier in
+//     (CG groups) plus the matching scales/biases. No block-wide barrier in
 //     the steady state; the hardware wait_group retires copies.
 //   * Activations of the CTA's K window are loaded once and stored in shared
-//     memory already permuted into MMA B fragments, with the per-group sums
-//     sum_k x[t,k] that the affine bias needs.
-//   * A 32-bit word of codes becomes MMA A operands with one shift and one
-//     LOP3 per pair of codes: (word >> s) & 0x000F000F | magic gives two
-//     16-bit floats equal to OFF + q exactly (see Elem<T>). 8-bit codes are
-//     split into nibbles, the high nibble carrying a x16 exponent, so the same
-//     MMA sums both. The K order inside an MMA is permuted to match this
-//     extraction; the B fragments carry the same permutation.
-//   * Each group gets a fresh fp32 accumulator D = sum x*(OFF+q); the
-//     epilogue of the group folds acc += scale*D + (bias - OFF*scale)*sum(x)
-//     in fp32, so no rounded dequantized weight ever exists.
-//   * K splits (small N) write fp32 partials to the workspace; the last CTA of
-//     a row block (atomic ticket, no waiting) sums them in split order, so
-//     results are deterministic, and resets its ticket to zero.
+//     memory already permuted into MMA B fragments (lane-interleaved so the
+//     128-bit fragment loads are conflict free), with two per-group sums per
+//     token: S = sum x and T = sum x * (field offset of its code position).
+//   * Codes become MMA A operands with one LOP3 per pair (plus one shift per
+//     32-bit word): see Elem<T>. The K order inside an MMA is permuted to match
+//     the extraction; the B fragments carry the same permutation.
+//   * Each group gets a fresh fp32 accumulator D = sum x*(offset + q); the
+//     group epilogue folds acc += scale*(D - T) + bias*S in fp32, so no rounded
+//     dequantized weight ever exists.
+//   * K splits across CTAs (small N) write fp32 partials to the workspace; the
+//     last CTA of a row block (atomic ticket, no waiting) sums them in split
+//     order, so results are deterministic, and resets its ticket to zero.
 #pragma once
 
 #include "common.cuh"
@@ -36,46 +38,65 @@
 
 namespace mlxq {
 
-template <int BITS, int GS>
-struct QmvShape {
-    static constexpr int WPG = GS * BITS / 32;  // packed words per group per row
-    static constexpr int WPT = WPG / 4;         // words per thread per group
-    static constexpr int CG = 32 / WPG;         // groups per 128-byte stage row
-    // Row padding (words) that keeps the fragment loads bank-conflict free.
-    static constexpr int PADW = (WPT == 1) ? 4 : (WPT == 2) ? 8 : (WPT == 4) ? 16 : 4;
-    static constexpr int RW = 32 + PADW;        // stage row stride in words
-    static constexpr int FR = GS / 8;           // B-fragment words per (group, n-tile, lane)
-    static_assert(WPT >= 1, "group too small for the 4-lane split");
+constexpr int kRowTiles = 8;  // 16-row warp tiles per CTA: 128 rows
+
+// Geometry shared by the kernel (as constants) and the host planner.
+struct QmvGeom {
+    int wpg;         // packed words per group per row
+    int wpt;         // words per thread per group
+    int cg;          // groups per 128-byte stage row
+    int rw;          // stage row stride in words (padded: conflict-free fragment loads)
+    int fr;          // B-fragment words per (group, n-tile, lane)
+    int sw;          // words per stage
+    int ksw;         // warps per row tile (K interleave)
+    int stages;      // cp.async ring depth
+    int nwarp;       // warps per CTA
+    int stage_bytes; // all warps' rings
+    int per_group;   // shared bytes per group of the activation window
+    int red_bytes;   // cross-warp reduction buffer
 };
 
-template <int BITS, int GS, bool SBV>
-__host__ __device__ constexpr int qmv_stage_words() {
-    return 16 * QmvShape<BITS, GS>::RW + (SBV ? 16 * QmvShape<BITS, GS>::CG : 0);
+// two_sums: per-group activation sums carry (S, T) instead of S alone (f16 4-bit,
+// whose even and odd code positions have different operand offsets).
+__host__ __device__ constexpr QmvGeom qmv_geom(int bits, int gs, int nt, bool sbv,
+                                               bool two_sums) {
+    const int wpg = gs * bits / 32;
+    const int wpt = wpg / 4;
+    const int cg = 32 / wpg;
+    const int padw = (wpt == 1) ? 4 : (wpt == 2) ? 8 : (wpt == 4) ? 16 : 4;
+    const int rw = 32 + padw;
+    const int sw = 16 * rw + (sbv ? 16 * cg : 0);
+    const int ksw = nt <= 2 ? 2 : 1;
+    const int stages = ksw == 2 ? 3 : 4;
+    const int nwarp = kRowTiles * ksw;
+    return QmvGeom{wpg, wpt, cg, rw, gs / 8, sw, ksw, stages, nwarp,
+                   nwarp * stages * sw * 4,
+                   nt * 32 * (gs / 8) * 4 + nt * 8 * (two_sums ? 8 : 4),
+                   (ksw - 1) * kRowTiles * nt * 4 * 32 * 4};
 }
 
-template <int NW, int STAGES, int BITS, int GS, bool SBV>
-__host__ __device__ constexpr int qmv_stage_bytes() {
-    return NW * STAGES * qmv_stage_words<BITS, GS, SBV>() * 4;
+template <typename T, int BITS>
+__host__ __device__ constexpr bool qmv_two_sums() {
+    return !Elem<T>::template Off<BITS>::kUniform;
 }
 
-// Shared memory per group of the activation window for NT n-tiles.
-template <int GS>
-__host__ __device__ constexpr int qmv_win_bytes_per_group(int nt) {
-    return nt * 32 * (GS / 8) * 4 + nt * 8 * 4;
-}
-
-template <typename T, int BITS, int GS, int NT, int NW, int STAGES, bool SBV>
-__global__ void __launch_bounds__(NW * 32, 1) qmv_kernel(const QmvParams p) {
+// ODD = false: every pass has one token, so the fold of odd token columns is
+// skipped (decode at batch 1).
+template <typename T, int BITS, int GS, int NT, bool SBV, bool ODD>
+__global__ void __launch_bounds__(qmv_geom(BITS, GS, NT, SBV, qmv_two_sums<T, BITS>()).nwarp * 32, 1)
+    qmv_kernel(const QmvParams p) {
     using E = Elem<T>;
-    using S = QmvShape<BITS, GS>;
-    constexpr int WPG = S::WPG, WPT = S::WPT, CG = S::CG, RW = S::RW, FR = S::FR;
-    constexpr int STAGE_WORDS = qmv_stage_words<BITS, GS, SBV>();
+    using OFF = typename Elem<T>::template Off<BITS>;
+    constexpr bool TWO = !OFF::kUniform;
+    constexpr QmvGeom GEO = qmv_geom(BITS, GS, NT, SBV, TWO);
+    constexpr int WPG = GEO.wpg, WPT = GEO.wpt, CG = GEO.cg, RW = GEO.rw, FR = GEO.fr;
+    constexpr int SW = GEO.sw, KSW = GEO.ksw, STAGES = GEO.stages, NTHR = GEO.nwarp * 32;
     constexpr int TOK = NT * 8;
-    constexpr float OFF = (BITS == 4) ? E::kOff4 : E::kOff8;
-    constexpr uint32_t MLO = E::kMagicLo, MHI = E::kMagicHi, NIB = 0x000F000Fu;
+    static_assert(WPT >= 1 && FR % 4 == 0, "unsupported group geometry");
 
     extern __shared__ __align__(16) uint32_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int rt = warp % kRowTiles, kh = warp / kRowTiles;
     const int r = lane >> 2, c = lane & 3;
     const int N = p.N, K = p.K;
     const int G = K / GS;
@@ -83,14 +104,16 @@ __global__ void __launch_bounds__(NW * 32, 1) qmv_kernel(const QmvParams p) {
     const int split = blockIdx.y;
     const int g_begin = split * p.gps;
     const int g_end = min(G, g_begin + p.gps);
-    const int row_block0 = blockIdx.x * (NW * 16);
-    const int row0 = row_block0 + warp * 16;
+    const int row_block0 = blockIdx.x * (kRowTiles * 16);
+    const int row0 = row_block0 + rt * 16;
 
-    uint32_t* xfrag = smem;
-    float* sumx = reinterpret_cast<float*>(smem + static_cast<size_t>(p.win) * NT * 32 * FR);
-    uint32_t* stage =
-        reinterpret_cast<uint32_t*>(sumx + static_cast<size_t>(p.win) * TOK) +
-        warp * STAGES * STAGE_WORDS;
+    // shared memory: [win][NT][FR/4][32] uint4 fragments | [win][TOK] sums (float or
+    // float2) | cross-warp reduction | per-warp cp.async rings
+    uint4* xfrag = reinterpret_cast<uint4*>(smem);
+    float* sums = reinterpret_cast<float*>(xfrag + static_cast<size_t>(p.win) * NT * (FR / 4) * 32);
+    float* red = sums + static_cast<size_t>(p.win) * TOK * (TWO ? 2 : 1);
+    uint32_t* stage0 = reinterpret_cast<uint32_t*>(red + (KSW - 1) * kRowTiles * NT * 4 * 32) +
+                       warp * STAGES * SW;
 
     const T* xg = static_cast<const T*>(p.x);
     T* og = static_cast<T*>(p.out);
@@ -143,107 +166,154 @@ __global__ void __launch_bounds__(NW * 32, 1) qmv_kernel(const QmvParams p) {
             for (int w0 = g_begin; w0 < g_end; w0 += p.win) {
                 const int wn = min(p.win, g_end - w0);
                 const int nchunks = (wn + CG - 1) / CG;
+                const int my_n = (nchunks - kh + KSW - 1) / KSW;  // chunks kh, kh+KSW, ...
 
-                auto issue = [&](int ch) {
-                    uint32_t* dst = stage + (ch % STAGES) * STAGE_WORDS;
-                    const int gch = w0 + ch * CG;
+                // Per-lane copy descriptors: lane copies 16-byte column `col` of rows
+                // lane/8 + 4*it of every chunk, and one row of scales or biases. Rows past
+                // N copy zero bytes from a valid address and never advance.
+                const int col = lane & 7;
+                const int grp_in_chunk = (col * 4) / WPG;
+                const uint32_t* wptr[4];
+                int wbytes[4];
+                long long wstep[4];
+#pragma unroll
+                for (int it = 0; it < 4; ++it) {
+                    const int n = row0 + (lane >> 3) + 4 * it;
+                    const bool ok = n < N;
+                    wbytes[it] = ok ? 16 : 0;
+                    wstep[it] = ok ? static_cast<long long>(KSW) * 32 : 0;
+                    wptr[it] = ok ? wbase + static_cast<long long>(n) * kw +
+                                        static_cast<long long>(w0 + kh * CG) * WPG + col * 4
+                                  : wbase;
+                }
+                const int srow = row0 + (lane & 15);
+                const int sbytes = srow < N ? CG * 2 : 0;
+                const T* sb0 = (lane < 16) ? sbase : bbase;
+                const T* sbptr = sbytes ? sb0 + static_cast<long long>(srow) * G + w0 + kh * CG : sb0;
+                const int sbstep = sbytes ? KSW * CG : 0;
+                uint32_t* sdst0 = stage0 + 16 * RW + (lane < 16 ? 0 : 8 * CG) + (lane & 15) * (CG / 2);
+                int issue_i = 0;
+
+                auto issue = [&](int slot) {
+                    uint32_t* dst = stage0 + slot * SW;
+                    const int gch = w0 + (kh + issue_i * KSW) * CG;
 #pragma unroll
                     for (int it = 0; it < 4; ++it) {
-                        const int i = lane + 32 * it;
-                        const int rr = i >> 3, col = i & 7;
-                        const int grp = gch + (col * 4) / WPG;
-                        const int n = row0 + rr;
-                        const bool ok = (n < N) && (grp < w0 + wn);
-                        const uint32_t* src =
-                            ok ? wbase + static_cast<long long>(n) * kw +
-                                     static_cast<long long>(gch) * WPG + col * 4
-                               : wbase;
-                        cp_async16(dst + rr * RW + col * 4, src, ok ? 16 : 0);
+                        int nb = wbytes[it];
+                        if constexpr (!SBV) nb = (gch + grp_in_chunk < w0 + wn) ? nb : 0;
+                        cp_async16(dst + ((lane >> 3) + 4 * it) * RW + col * 4,
+                                   nb ? wptr[it] : wbase, nb);
+                        wptr[it] += wstep[it];
                     }
                     if constexpr (SBV) {
-                        const int rr = lane & 15;
-                        const int n = row0 + rr;
-                        const bool ok = n < N;
-                        const T* base = (lane < 16) ? sbase : bbase;
-                        const T* src = ok ? base + static_cast<long long>(n) * G + gch : base;
-                        uint32_t* sdst = dst + 16 * RW + (lane < 16 ? 0 : 8 * CG) + rr * (CG / 2);
-                        if constexpr (CG == 8) cp_async16(sdst, src, ok ? 16 : 0);
-                        else if constexpr (CG == 4) cp_async8(sdst, src, ok ? 8 : 0);
-                        else cp_async4(sdst, src, ok ? 4 : 0);
+                        uint32_t* sdst = sdst0 + slot * SW;
+                        if constexpr (CG == 8) cp_async16(sdst, sbptr, sbytes);
+                        else if constexpr (CG == 4) cp_async8(sdst, sbptr, sbytes);
+                        else cp_async4(sdst, sbptr, sbytes);
+                        sbptr += sbstep;
                     }
                     cp_async_commit();
+                    ++issue_i;
                 };
 
                 // Start streaming weights before building the activation fragments.
 #pragma unroll
                 for (int i = 0; i < STAGES - 1; ++i) {
-                    if (i < nchunks) issue(i);
+                    if (i < my_n) issue(i);
                     else cp_async_commit();
                 }
 
                 // ---- activation window -> B fragments + per-group sums ---------------------
-                __syncthreads();  // previous window / item finished reading xfrag
-                for (int idx = threadIdx.x; idx < wn * NT * 32; idx += NW * 32) {
+                __syncthreads();  // previous window / item finished reading the window
+                for (int idx = threadIdx.x; idx < wn * NT * 32; idx += NTHR) {
                     const int ln = idx & 31;
                     const int jj = (idx >> 5) % NT;
                     const int gi = (idx >> 5) / NT;
                     const int tt = jj * 8 + (ln >> 2);
                     const int cc = ln & 3;
                     uint32_t fr[FR];
-                    float sum = 0.f;
+#pragma unroll
+                    for (int f = 0; f < FR; ++f) fr[f] = 0u;
+                    float se = 0.f, so = 0.f;
                     long long xrow = 0, orow = 0;
                     if (tt < ntok) rows_of(tc + tt, xrow, orow);
                     if (tt < ntok && xrow >= 0 && xrow < static_cast<long long>(p.x_batches) * p.M) {
                         const T* xr = xg + xrow * K;
 #pragma unroll
                         for (int w = 0; w < WPT; ++w) {
-                            const long long gw =
-                                static_cast<long long>(w0 + gi) * WPG + cc * WPT + w;
+                            const long long gw = static_cast<long long>(w0 + gi) * WPG + cc * WPT + w;
                             if constexpr (BITS == 4) {
                                 const uint4 u = *reinterpret_cast<const uint4*>(xr + gw * 8);
-                                fr[4 * w + 0] = prmt(u.x, u.z, 0x5410);
-                                fr[4 * w + 1] = prmt(u.x, u.z, 0x7632);
-                                fr[4 * w + 2] = prmt(u.y, u.w, 0x5410);
-                                fr[4 * w + 3] = prmt(u.y, u.w, 0x7632);
-                                const T* v = reinterpret_cast<const T*>(&u);
-#pragma unroll
-                                for (int e = 0; e < 8; ++e) sum += E::to_f(v[e]);
+                                fr[4 * w + 0] = prmt(u.x, u.z, 0x5410);  // x0, x4
+                                fr[4 * w + 1] = prmt(u.x, u.z, 0x7632);  // x1, x5
+                                fr[4 * w + 2] = prmt(u.y, u.w, 0x5410);  // x2, x6
+                                fr[4 * w + 3] = prmt(u.y, u.w, 0x7632);  // x3, x7
+                                se += (E::lo(u.x) + E::lo(u.y)) + (E::lo(u.z) + E::lo(u.w));
+                                so += (E::hi(u.x) + E::hi(u.y)) + (E::hi(u.z) + E::hi(u.w));
                             } else {
                                 const uint2 u = *reinterpret_cast<const uint2*>(xr + gw * 4);
-                                fr[2 * w + 0] = prmt(u.x, u.y, 0x5410);
-                                fr[2 * w + 1] = prmt(u.x, u.y, 0x7632);
-                                const T* v = reinterpret_cast<const T*>(&u);
-#pragma unroll
-                                for (int e = 0; e < 4; ++e) sum += E::to_f(v[e]);
+                                fr[2 * w + 0] = prmt(u.x, u.y, 0x5410);  // x0, x2
+                                fr[2 * w + 1] = prmt(u.x, u.y, 0x7632);  // x1, x3
+                                se += (E::lo(u.x) + E::hi(u.x)) + (E::lo(u.y) + E::hi(u.y));
                             }
                         }
-                    } else {
-#pragma unroll
-                        for (int f = 0; f < FR; ++f) fr[f] = 0u;
                     }
-                    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-                    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-                    uint4* dst = reinterpret_cast<uint4*>(
-                        xfrag + (static_cast<size_t>(gi * NT + jj) * 32 + ln) * FR);
+                    se += __shfl_xor_sync(0xffffffffu, se, 1);
+                    se += __shfl_xor_sync(0xffffffffu, se, 2);
+                    so += __shfl_xor_sync(0xffffffffu, so, 1);
+                    so += __shfl_xor_sync(0xffffffffu, so, 2);
+                    uint4* dst = xfrag + static_cast<size_t>(gi * NT + jj) * (FR / 4) * 32 + ln;
 #pragma unroll
                     for (int f = 0; f < FR / 4; ++f)
-                        dst[f] = make_uint4(fr[4 * f], fr[4 * f + 1], fr[4 * f + 2], fr[4 * f + 3]);
-                    if (cc == 0) sumx[gi * TOK + tt] = sum;
+                        dst[f * 32] = make_uint4(fr[4 * f], fr[4 * f + 1], fr[4 * f + 2], fr[4 * f + 3]);
+                    if (cc == 0) {
+                        if constexpr (TWO) {
+                            reinterpret_cast<float2*>(sums)[gi * TOK + tt] =
+                                make_float2(se + so, OFF::kOffE * se + OFF::kOffO * so);
+                        } else {
+                            sums[gi * TOK + tt] = se + so;
+                        }
+                    }
                 }
                 __syncthreads();
 
-                // ---- main loop over 128-byte chunks of the warp's 16 rows ------------------
-                for (int ch = 0; ch < nchunks; ++ch) {
-                    cp_async_wait<STAGES - 2>();
-                    __syncwarp();
-                    if (ch + STAGES - 1 < nchunks) issue(ch + STAGES - 1);
-                    else cp_async_commit();
-
-                    const uint32_t* sw = stage + (ch % STAGES) * STAGE_WORDS;
+                // ---- main loop over this warp's 128-byte chunks ----------------------------
+                // Unrolled by the ring depth so every stage slot is a constant.
+                auto chunk = [&](const int i, const uint32_t* sw) {
+                    const int ch = kh + i * KSW;
+                    // packed scales / biases of this chunk for rows r and r+8
+                    uint32_t sp0[CG / 2 > 0 ? CG / 2 : 1], sp1[CG / 2 > 0 ? CG / 2 : 1];
+                    uint32_t bp0[CG / 2 > 0 ? CG / 2 : 1], bp1[CG / 2 > 0 ? CG / 2 : 1];
+                    if constexpr (SBV) {
+                        const uint32_t* sp = sw + 16 * RW;
+                        const uint32_t* bp = sp + 8 * CG;
+#pragma unroll
+                        for (int q = 0; q < CG / 2; ++q) {
+                            sp0[q] = sp[r * (CG / 2) + q];
+                            sp1[q] = sp[(r + 8) * (CG / 2) + q];
+                            bp0[q] = bp[r * (CG / 2) + q];
+                            bp1[q] = bp[(r + 8) * (CG / 2) + q];
+                        }
+                    }
 #pragma unroll
                     for (int gi = 0; gi < CG; ++gi) {
                         const int gl = ch * CG + gi;  // group index within the window
-                        if (gl >= wn) break;
+                        if (!SBV && gl >= wn) continue;
+                        float s0, s1, b0, b1;
+                        if constexpr (SBV) {
+                            const int q = gi >> 1;
+                            s0 = (gi & 1) ? E::hi(sp0[q]) : E::lo(sp0[q]);
+                            s1 = (gi & 1) ? E::hi(sp1[q]) : E::lo(sp1[q]);
+                            b0 = (gi & 1) ? E::hi(bp0[q]) : E::lo(bp0[q]);
+                            b1 = (gi & 1) ? E::hi(bp1[q]) : E::lo(bp1[q]);
+                        } else {
+                            const int g = w0 + gl;
+                            const int n0 = row0 + r, n1 = row0 + r + 8;
+                            s0 = n0 < N ? E::to_f(sbase[static_cast<long long>(n0) * G + g]) : 0.f;
+                            b0 = n0 < N ? E::to_f(bbase[static_cast<long long>(n0) * G + g]) : 0.f;
+                            s1 = n1 < N ? E::to_f(sbase[static_cast<long long>(n1) * G + g]) : 0.f;
+                            b1 = n1 < N ? E::to_f(bbase[static_cast<long long>(n1) * G + g]) : 0.f;
+                        }
                         uint32_t wa[WPT], wb[WPT];
                         {
                             const uint32_t* pa = sw + r * RW + gi * WPG + c * WPT;
@@ -268,68 +338,82 @@ __global__ void __launch_bounds__(NW * 32, 1) qmv_kernel(const QmvParams p) {
                                 }
                             }
                         }
-                        float s0, s1, b0, b1;
-                        if constexpr (SBV) {
-                            const T* sh = reinterpret_cast<const T*>(sw + 16 * RW);
-                            const T* bh = sh + 16 * CG;
-                            s0 = E::to_f(sh[r * CG + gi]);
-                            s1 = E::to_f(sh[(r + 8) * CG + gi]);
-                            b0 = E::to_f(bh[r * CG + gi]);
-                            b1 = E::to_f(bh[(r + 8) * CG + gi]);
-                        } else {
-                            const int g = w0 + gl;
-                            const int n0 = row0 + r, n1 = row0 + r + 8;
-                            s0 = n0 < N ? E::to_f(sbase[static_cast<long long>(n0) * G + g]) : 0.f;
-                            b0 = n0 < N ? E::to_f(bbase[static_cast<long long>(n0) * G + g]) : 0.f;
-                            s1 = n1 < N ? E::to_f(sbase[static_cast<long long>(n1) * G + g]) : 0.f;
-                            b1 = n1 < N ? E::to_f(bbase[static_cast<long long>(n1) * G + g]) : 0.f;
+                        uint32_t ta[WPT][4], tb[WPT][4];
+#pragma unroll
+                        for (int w = 0; w < WPT; ++w) {
+                            E::template extract<BITS>(wa[w], ta[w]);
+                            E::template extract<BITS>(wb[w], tb[w]);
                         }
-                        const float cr0 = fmaf(-OFF, s0, b0);
-                        const float cr1 = fmaf(-OFF, s1, b1);
+                        float cr0 = 0.f, cr1 = 0.f;
+                        if constexpr (!TWO) {
+                            cr0 = fmaf(-OFF::kOff, s0, b0);
+                            cr1 = fmaf(-OFF::kOff, s1, b1);
+                        }
 #pragma unroll
                         for (int j = 0; j < NT; ++j) {
                             uint32_t X[FR];
-                            const uint4* xf = reinterpret_cast<const uint4*>(
-                                xfrag + (static_cast<size_t>(gl * NT + j) * 32 + lane) * FR);
+                            const uint4* xf = xfrag + static_cast<size_t>(gl * NT + j) * (FR / 4) * 32 + lane;
 #pragma unroll
                             for (int f = 0; f < FR / 4; ++f) {
-                                const uint4 v = xf[f];
+                                const uint4 v = xf[f * 32];
                                 X[4 * f + 0] = v.x; X[4 * f + 1] = v.y;
                                 X[4 * f + 2] = v.z; X[4 * f + 3] = v.w;
                             }
-                            float d[4] = {0.f, 0.f, 0.f, 0.f};
+                            float d[4];
 #pragma unroll
                             for (int w = 0; w < WPT; ++w) {
                                 if constexpr (BITS == 4) {
-                                    const uint32_t a0 = (wa[w] & NIB) | MLO;
-                                    const uint32_t a1 = ((wa[w] >> 4) & NIB) | MLO;
-                                    const uint32_t a2 = ((wa[w] >> 8) & NIB) | MLO;
-                                    const uint32_t a3 = ((wa[w] >> 12) & NIB) | MLO;
-                                    const uint32_t b0_ = (wb[w] & NIB) | MLO;
-                                    const uint32_t b1_ = ((wb[w] >> 4) & NIB) | MLO;
-                                    const uint32_t b2_ = ((wb[w] >> 8) & NIB) | MLO;
-                                    const uint32_t b3_ = ((wb[w] >> 12) & NIB) | MLO;
-                                    mma16816<T>(d, a0, b0_, a1, b1_, X[4 * w + 0], X[4 * w + 1]);
-                                    mma16816<T>(d, a2, b2_, a3, b3_, X[4 * w + 2], X[4 * w + 3]);
+                                    if (w == 0)
+                                        mma16816z<T>(d, ta[w][0], tb[w][0], ta[w][1], tb[w][1],
+                                                     X[4 * w + 0], X[4 * w + 1]);
+                                    else
+                                        mma16816<T>(d, ta[w][0], tb[w][0], ta[w][1], tb[w][1],
+                                                    X[4 * w + 0], X[4 * w + 1]);
+                                    mma16816<T>(d, ta[w][2], tb[w][2], ta[w][3], tb[w][3],
+                                                X[4 * w + 2], X[4 * w + 3]);
                                 } else {
-                                    const uint32_t l0 = (wa[w] & NIB) | MLO;
-                                    const uint32_t h0 = ((wa[w] >> 4) & NIB) | MHI;
-                                    const uint32_t l1 = ((wa[w] >> 8) & NIB) | MLO;
-                                    const uint32_t h1 = ((wa[w] >> 12) & NIB) | MHI;
-                                    const uint32_t m0 = (wb[w] & NIB) | MLO;
-                                    const uint32_t k0 = ((wb[w] >> 4) & NIB) | MHI;
-                                    const uint32_t m1 = ((wb[w] >> 8) & NIB) | MLO;
-                                    const uint32_t k1 = ((wb[w] >> 12) & NIB) | MHI;
-                                    mma16816<T>(d, l0, m0, h0, k0, X[2 * w + 0], X[2 * w + 0]);
-                                    mma16816<T>(d, l1, m1, h1, k1, X[2 * w + 1], X[2 * w + 1]);
+                                    if (w == 0)
+                                        mma16816z<T>(d, ta[w][0], tb[w][0], ta[w][1], tb[w][1],
+                                                     X[2 * w + 0], X[2 * w + 0]);
+                                    else
+                                        mma16816<T>(d, ta[w][0], tb[w][0], ta[w][1], tb[w][1],
+                                                    X[2 * w + 0], X[2 * w + 0]);
+                                    mma16816<T>(d, ta[w][2], tb[w][2], ta[w][3], tb[w][3],
+                                                X[2 * w + 1], X[2 * w + 1]);
                                 }
                             }
-                            const float2 sx =
-                                *reinterpret_cast<const float2*>(sumx + gl * TOK + j * 8 + 2 * c);
-                            acc[j][0] = fmaf(s0, d[0], fmaf(cr0, sx.x, acc[j][0]));
-                            acc[j][1] = fmaf(s0, d[1], fmaf(cr0, sx.y, acc[j][1]));
-                            acc[j][2] = fmaf(s1, d[2], fmaf(cr1, sx.x, acc[j][2]));
-                            acc[j][3] = fmaf(s1, d[3], fmaf(cr1, sx.y, acc[j][3]));
+                            // fold this group into the accumulators of tokens 2c and 2c+1
+                            if constexpr (TWO) {
+                                const float4 st = *reinterpret_cast<const float4*>(
+                                    reinterpret_cast<const float2*>(sums) + gl * TOK + j * 8 + 2 * c);
+                                acc[j][0] = fmaf(s0, d[0] - st.y, fmaf(b0, st.x, acc[j][0]));
+                                acc[j][2] = fmaf(s1, d[2] - st.y, fmaf(b1, st.x, acc[j][2]));
+                                if constexpr (ODD) {
+                                    acc[j][1] = fmaf(s0, d[1] - st.w, fmaf(b0, st.z, acc[j][1]));
+                                    acc[j][3] = fmaf(s1, d[3] - st.w, fmaf(b1, st.z, acc[j][3]));
+                                }
+                            } else {
+                                const float2 sx = *reinterpret_cast<const float2*>(sums + gl * TOK + j * 8 + 2 * c);
+                                acc[j][0] = fmaf(s0, d[0], fmaf(cr0, sx.x, acc[j][0]));
+                                acc[j][2] = fmaf(s1, d[2], fmaf(cr1, sx.x, acc[j][2]));
+                                if constexpr (ODD) {
+                                    acc[j][1] = fmaf(s0, d[1], fmaf(cr0, sx.y, acc[j][1]));
+                                    acc[j][3] = fmaf(s1, d[3], fmaf(cr1, sx.y, acc[j][3]));
+                                }
+                            }
+                        }
+                    }
+                };
+                for (int i0 = 0; i0 < my_n; i0 += STAGES) {
+#pragma unroll
+                    for (int u = 0; u < STAGES; ++u) {
+                        const int i = i0 + u;
+                        if (i < my_n) {
+                            cp_async_wait<STAGES - 2>();
+                            __syncwarp();
+                            if (i + STAGES - 1 < my_n) issue((u + STAGES - 1) % STAGES);
+                            else cp_async_commit();
+                            chunk(i, stage0 + u * SW);
                         }
                     }
                 }
@@ -337,41 +421,68 @@ __global__ void __launch_bounds__(NW * 32, 1) qmv_kernel(const QmvParams p) {
                 __syncwarp();
             }
 
+            // ---- combine the K-interleaved warps of each row tile (fixed order) ----------
+            if constexpr (KSW > 1) {
+                __syncthreads();
+                if (kh > 0) {
+                    float* dst = red + ((kh - 1) * kRowTiles + rt) * NT * 4 * 32 + lane;
+#pragma unroll
+                    for (int j = 0; j < NT; ++j)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) dst[(j * 4 + e) * 32] = acc[j][e];
+                }
+                __syncthreads();
+                if (kh == 0) {
+#pragma unroll
+                    for (int h = 1; h < KSW; ++h) {
+                        const float* src = red + ((h - 1) * kRowTiles + rt) * NT * 4 * 32 + lane;
+#pragma unroll
+                        for (int j = 0; j < NT; ++j)
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) acc[j][e] += src[(j * 4 + e) * 32];
+                    }
+                }
+            }
+
             // ---- epilogue ---------------------------------------------------------------
             const T* biasg = static_cast<const T*>(p.bias);
             if (p.splits == 1) {
+                if (kh == 0) {
 #pragma unroll
-                for (int j = 0; j < NT; ++j) {
+                    for (int j = 0; j < NT; ++j) {
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int n = row0 + r + 8 * h;
+                        for (int h = 0; h < 2; ++h) {
+                            const int n = row0 + r + 8 * h;
 #pragma unroll
-                        for (int q = 0; q < 2; ++q) {
-                            const int t = j * 8 + 2 * c + q;
-                            if (t < ntok && n < N) {
-                                long long xrow, orow;
-                                rows_of(tc + t, xrow, orow);
-                                T y = E::from_f(acc[j][2 * h + q]);
-                                if (biasg) y = E::from_f(E::to_f(y) + E::to_f(biasg[n]));
-                                og[orow * N + n] = y;
+                            for (int q = 0; q < 2; ++q) {
+                                const int t = j * 8 + 2 * c + q;
+                                if (t < ntok && n < N) {
+                                    long long xrow, orow;
+                                    rows_of(tc + t, xrow, orow);
+                                    T y = E::from_f(acc[j][2 * h + q]);
+                                    if (biasg) y = E::from_f(E::to_f(y) + E::to_f(biasg[n]));
+                                    og[orow * N + n] = y;
+                                }
                             }
                         }
                     }
                 }
             } else {
-                // K-split: fp32 partial of this split, then the last CTA reduces.
+                // K split across CTAs: fp32 partial of this split, then the last CTA reduces.
+                if (kh == 0) {
 #pragma unroll
-                for (int j = 0; j < NT; ++j) {
+                    for (int j = 0; j < NT; ++j) {
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int n = row0 + r + 8 * h;
+                        for (int h = 0; h < 2; ++h) {
+                            const int n = row0 + r + 8 * h;
 #pragma unroll
-                        for (int q = 0; q < 2; ++q) {
-                            const int t = j * 8 + 2 * c + q;
-                            if (t < ntok && n < N) {
-                                const long long m = static_cast<long long>(z) * TOK + t;
-                                p.partial[(static_cast<long long>(split) * p.M + m) * N + n] =
-                                    acc[j][2 * h + q];
+                            for (int q = 0; q < 2; ++q) {
+                                const int t = j * 8 + 2 * c + q;
+                                if (t < ntok && n < N) {
+                                    const long long m = static_cast<long long>(z) * TOK + t;
+                                    p.partial[(static_cast<long long>(split) * p.M + m) * N + n] =
+                                        acc[j][2 * h + q];
+                                }
                             }
                         }
                     }
@@ -379,12 +490,13 @@ __global__ void __launch_bounds__(NW * 32, 1) qmv_kernel(const QmvParams p) {
                 __threadfence();
                 __syncthreads();
                 unsigned* ticket = p.counter + static_cast<long long>(z) * gridDim.x + blockIdx.x;
-                if (threadIdx.x == 0) s_last = (atomicAdd(ticket, 1u) == static_cast<unsigned>(p.splits - 1));
+                if (threadIdx.x == 0)
+                    s_last = (atomicAdd(ticket, 1u) == static_cast<unsigned>(p.splits - 1));
                 __syncthreads();
                 if (s_last) {
                     __threadfence();
-                    const int rows_here = min(NW * 16, N - row_block0);
-                    for (int idx = threadIdx.x; idx < ntok * rows_here; idx += NW * 32) {
+                    const int rows_here = min(kRowTiles * 16, N - row_block0);
+                    for (int idx = threadIdx.x; idx < ntok * rows_here; idx += NTHR) {
                         const int t = idx / rows_here;
                         const int n = row_block0 + idx % rows_here;
                         const long long m = static_cast<long long>(z) * TOK + t;

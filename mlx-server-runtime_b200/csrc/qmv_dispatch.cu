@@ -6,28 +6,15 @@
 
 namespace mlxq {
 
-template <typename T, int BITS, int GS, int NT, bool SBV>
+template <typename T, int BITS, int GS, int NT, bool SBV, bool ODD>
 cudaError_t qmv_launch_t(const QmvPlan& plan, const QmvParams& p, cudaStream_t st);
-
-static int words_per_group(int gs, int bits) { return gs * bits / 32; }
-
-static size_t stage_bytes(int bits, int gs, bool sbv) {
-    const int wpg = words_per_group(gs, bits);
-    const int wpt = wpg / 4;
-    const int cg = 32 / wpg;
-    const int padw = (wpt == 1) ? 4 : (wpt == 2) ? 8 : (wpt == 4) ? 16 : 4;
-    const int stage_words = 16 * (32 + padw) + (sbv ? 16 * cg : 0);
-    return static_cast<size_t>(kQmvWarps) * kQmvStages * stage_words * 4;
-}
 
 static int nt_for(long long tokens) { return tokens <= 8 ? 1 : tokens <= 16 ? 2 : 4; }
 
 bool qmv_plan(int dtype, int bits, int gs, int M, int N, int K, int mode, int z_items,
               int num_sms, int max_smem, QmvPlan* plan) {
-    (void)dtype;
     const int G = K / gs;
-    const int wpg = words_per_group(gs, bits);
-    const int cg = 32 / wpg;
+    const int cg = 32 / (gs * bits / 32);
     QmvPlan pl{};
     if (mode == 0) {
         pl.nt = nt_for(M);
@@ -38,9 +25,12 @@ bool qmv_plan(int dtype, int bits, int gs, int M, int N, int K, int mode, int z_
         pl.nt = nt_for(z_items < 1 ? 1 : z_items);
     }
     pl.sbvec = (cg >= 2) && (G % cg == 0);
-    pl.rowblocks = (N + kQmvWarps * 16 - 1) / (kQmvWarps * 16);
-    const size_t sb = stage_bytes(bits, gs, pl.sbvec);
-    const size_t per_group = static_cast<size_t>(pl.nt) * 32 * (gs / 8) * 4 + pl.nt * 8 * 4;
+    // every pass holds exactly one token: dense or per-entry gather with M == 1
+    pl.single = (mode != 2) && M == 1;
+    pl.rowblocks = (N + kRowTiles * 16 - 1) / (kRowTiles * 16);
+    const QmvGeom geo = qmv_geom(bits, gs, pl.nt, pl.sbvec, dtype == kF16 && bits == 4);
+    const size_t sb = static_cast<size_t>(geo.stage_bytes) + geo.red_bytes;
+    const size_t per_group = geo.per_group;
     if (static_cast<size_t>(max_smem) <= sb + per_group * cg) return false;
     int win_max = static_cast<int>((max_smem - sb) / per_group);
     win_max = (win_max / cg) * cg;
@@ -78,9 +68,11 @@ bool qmv_plan(int dtype, int bits, int gs, int M, int N, int K, int mode, int z_
 
 #define QMV_CASE_NT(T, BITS, GS, SBV)                                                    \
     switch (plan.nt) {                                                                   \
-        case 1: return qmv_launch_t<T, BITS, GS, 1, SBV>(plan, p, st);                   \
-        case 2: return qmv_launch_t<T, BITS, GS, 2, SBV>(plan, p, st);                   \
-        default: return qmv_launch_t<T, BITS, GS, 4, SBV>(plan, p, st);                  \
+        case 1:                                                                          \
+            if (plan.single) return qmv_launch_t<T, BITS, GS, 1, SBV, false>(plan, p, st); \
+            return qmv_launch_t<T, BITS, GS, 1, SBV, true>(plan, p, st);                 \
+        case 2: return qmv_launch_t<T, BITS, GS, 2, SBV, true>(plan, p, st);             \
+        default: return qmv_launch_t<T, BITS, GS, 4, SBV, true>(plan, p, st);            \
     }
 
 #define QMV_CASE_GS(T, BITS)                                                             \

@@ -7,12 +7,10 @@
 
 namespace mlxq {
 
-constexpr int kQmvWarps = 8;
-constexpr int kQmvStages = 4;
-
-template <typename T, int BITS, int GS, int NT, bool SBV>
+template <typename T, int BITS, int GS, int NT, bool SBV, bool ODD>
 cudaError_t qmv_launch_t(const QmvPlan& plan, const QmvParams& p, cudaStream_t st) {
-    auto kern = qmv_kernel<T, BITS, GS, NT, kQmvWarps, kQmvStages, SBV>;
+    auto kern = qmv_kernel<T, BITS, GS, NT, SBV, ODD>;
+    constexpr QmvGeom geo = qmv_geom(BITS, GS, NT, SBV, qmv_two_sums<T, BITS>());
     static int configured[64] = {0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -25,46 +23,34 @@ cudaError_t qmv_launch_t(const QmvPlan& plan, const QmvParams& p, cudaStream_t s
         configured[dev] = static_cast<int>(plan.smem);
     }
     dim3 grid(plan.rowblocks, plan.splits, plan.gridz);
-    kern<<<grid, kQmvWarps * 32, plan.smem, st>>>(p);
+    kern<<<grid, geo.nwarp * 32, plan.smem, st>>>(p);
     return cudaGetLastError();
 }
 
-#define MLXQ_INSTANTIATE_QMV(T, BITS)                                                          \
-    template cudaError_t qmv_launch_t<T, BITS, 32, 1, true>(const QmvPlan&, const QmvParams&,  \
-                                                            cudaStream_t);                     \
-    template cudaError_t qmv_launch_t<T, BITS, 32, 2, true>(const QmvPlan&, const QmvParams&,  \
-                                                            cudaStream_t);                     \
-    template cudaError_t qmv_launch_t<T, BITS, 32, 4, true>(const QmvPlan&, const QmvParams&,  \
-                                                            cudaStream_t);                     \
-    template cudaError_t qmv_launch_t<T, BITS, 64, 1, true>(const QmvPlan&, const QmvParams&,  \
-                                                            cudaStream_t);                     \
-    template cudaError_t qmv_launch_t<T, BITS, 64, 2, true>(const QmvPlan&, const QmvParams&,  \
-                                                            cudaStream_t);                     \
-    template cudaError_t qmv_launch_t<T, BITS, 64, 4, true>(const QmvPlan&, const QmvParams&,  \
-                                                            cudaStream_t);                     \
-    template cudaError_t qmv_launch_t<T, BITS, 128, 1, true>(const QmvPlan&, const QmvParams&, \
-                                                             cudaStream_t);                    \
-    template cudaError_t qmv_launch_t<T, BITS, 128, 2, true>(const QmvPlan&, const QmvParams&, \
-                                                             cudaStream_t);                    \
-    template cudaError_t qmv_launch_t<T, BITS, 128, 4, true>(const QmvPlan&, const QmvParams&, \
-                                                             cudaStream_t);                    \
-    template cudaError_t qmv_launch_t<T, BITS, 32, 1, false>(const QmvPlan&, const QmvParams&, \
-                                                             cudaStream_t);                    \
-    template cudaError_t qmv_launch_t<T, BITS, 32, 2, false>(const QmvPlan&, const QmvParams&, \
-                                                             cudaStream_t);                    \
-    template cudaError_t qmv_launch_t<T, BITS, 32, 4, false>(const QmvPlan&, const QmvParams&, \
-                                                             cudaStream_t);                    \
-    template cudaError_t qmv_launch_t<T, BITS, 64, 1, false>(const QmvPlan&, const QmvParams&, \
-                                                             cudaStream_t);                    \
-    template cudaError_t qmv_launch_t<T, BITS, 64, 2, false>(const QmvPlan&, const QmvParams&, \
-                                                             cudaStream_t);                    \
-    template cudaError_t qmv_launch_t<T, BITS, 64, 4, false>(const QmvPlan&, const QmvParams&, \
-                                                             cudaStream_t);                    \
-    template cudaError_t qmv_launch_t<T, BITS, 128, 1, false>(const QmvPlan&, const QmvParams&,\
-                                                              cudaStream_t);                   \
-    template cudaError_t qmv_launch_t<T, BITS, 128, 2, false>(const QmvPlan&, const QmvParams&,\
-                                                              cudaStream_t);                   \
-    template cudaError_t qmv_launch_t<T, BITS, 128, 4, false>(const QmvPlan&, const QmvParams&,\
-                                                              cudaStream_t);
+#define MLXQ_INSTANTIATE_QMV(T, BITS)  \
+    template cudaError_t qmv_launch_t<T, BITS, 32, 1, true, false>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 32, 1, true, true>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 32, 2, true, true>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 32, 4, true, true>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 32, 1, false, false>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 32, 1, false, true>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 32, 2, false, true>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 32, 4, false, true>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 64, 1, true, false>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 64, 1, true, true>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 64, 2, true, true>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 64, 4, true, true>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 64, 1, false, false>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 64, 1, false, true>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 64, 2, false, true>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 64, 4, false, true>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 128, 1, true, false>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 128, 1, true, true>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 128, 2, true, true>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 128, 4, true, true>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 128, 1, false, false>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 128, 1, false, true>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 128, 2, false, true>(const QmvPlan&, const QmvParams&, cudaStream_t);  \
+    template cudaError_t qmv_launch_t<T, BITS, 128, 4, false, true>(const QmvPlan&, const QmvParams&, cudaStream_t);
 
 }  // namespace mlxq
