@@ -258,6 +258,10 @@ def run(args):
         # one flat result buffer (feeds the all-gather and the single D2H copy)
         torch.cat([o.reshape(-1) for o in outs if o is not None], out=out_flat)
 
+    # Launch overlap: the projections' weights are static, so each matmul may start
+    # streaming them while the previous one finishes.
+    overlap = mxq.launch_overlap(not args.no_overlap)
+
     # warm-up eagerly (sets kernel attributes, allocates workspaces), then capture
     for _ in range(2):
         step_eager()
@@ -382,6 +386,7 @@ def run(args):
                        "global_batch": 1, "parallelism": f"n-shard{world}",
                        "step_bytes": total_bytes, "l2": "inputs exceed L2 (3.98 GB/step)",
                        "replay": "cuda graph of public-API calls",
+                       "launch_overlap": not args.no_overlap,
                        "allgather": "one NCCL all-gather of all outputs per step" if world > 1
                        else None,
                        "qmm_only_tok_per_s": round(1000.0 / ms, 1)},
@@ -425,6 +430,7 @@ def run_case(args):
         ws.append(mxq.quantize(w, GS, BITS))
         del w
     x = torch.randn(M, K, device=dev, generator=gen).to(torch.bfloat16)
+    mxq.launch_overlap(not args.no_overlap)
     for i in range(max(3, args.warmup)):
         mxq.quantized_matmul(x, *ws[i % copies], group_size=GS, bits=BITS)
     torch.cuda.synchronize()
@@ -459,6 +465,7 @@ def run_case(args):
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / (reps * copies)
     print(json.dumps({"case": args.case, "M": M, "N": N, "K": K, "copies": copies,
+                      "overlap": not args.no_overlap,
                       "us_per_launch": round(us, 3), "bytes": per,
                       "GB/s": round(per / (us * 1e-6) / 1e9, 1)}), flush=True)
 
@@ -469,6 +476,8 @@ def main():
                     help="time one projection only (eager launches, for profiling)")
     ap.add_argument("--m", type=int, default=1, help="tokens for --case")
     ap.add_argument("--eager", action="store_true", help="--case: plain launches, no graph")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="launch matmuls without programmatic launch overlap")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=10)

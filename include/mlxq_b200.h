@@ -67,6 +67,20 @@ int mlxq_abi_version(void);
 const char* mlxq_last_error(void);
 
 /*
+ * Launch overlap for quantized_matmul (process-wide, default off; returns the
+ * previous setting). When on, each quantized_matmul is launched with CUDA
+ * programmatic stream serialization: it may start streaming its packed weights,
+ * scales and biases while the kernel before it on the stream is still running,
+ * and waits for that kernel before reading activations or writing anything.
+ * This hides the launch and ramp time between the back-to-back projections of
+ * a decode step. Turn it on only when those weight buffers are not being
+ * written by work still executing on the stream (the normal case: weights are
+ * loaded once). No counterpart in the reference (MLX schedules its own graph).
+ */
+int mlxq_set_launch_overlap(int enable);
+int mlxq_get_launch_overlap(void);
+
+/*
  * quantize: replaces mx.quantize(w, group_size, bits, mode="affine")
  * (lfm2.py:112-117) and the per-layer quantization nn.quantize performs
  * (qwen2.py:318-324). w [rows, K] of dtype w_dtype; writes wq

@@ -30,6 +30,8 @@ EXPORTED = (
     "mlxq_quantized_matmul",
     "mlxq_gather_qmm",
     "mlxq_gather_qmm_workspace_size",
+    "mlxq_set_launch_overlap",
+    "mlxq_get_launch_overlap",
 )
 
 _lock = threading.Lock()
@@ -71,6 +73,9 @@ def load(path: str | None = None):
         L.mlxq_gather_qmm.restype = i32
         L.mlxq_gather_qmm_workspace_size.argtypes = [i64, i64, i64, i64, i64, i32, i32, i32, i32]
         L.mlxq_gather_qmm_workspace_size.restype = sz
+        L.mlxq_set_launch_overlap.argtypes = [i32]
+        L.mlxq_set_launch_overlap.restype = i32
+        L.mlxq_get_launch_overlap.restype = i32
         v = L.mlxq_abi_version()
         if v != ABI_VERSION:
             raise LibraryError(f"{p} has ABI version {v}, expected {ABI_VERSION}; rebuild it")

@@ -28,7 +28,8 @@ from . import _lib
 
 _DT = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
 
-__all__ = ["quantize", "dequantize", "quantized_matmul", "gather_qmm", "Workspace"]
+__all__ = ["quantize", "dequantize", "quantized_matmul", "gather_qmm", "Workspace",
+           "launch_overlap"]
 
 
 def _dtype_code(t: torch.Tensor, what: str, allowed=(torch.bfloat16, torch.float16)) -> int:
@@ -92,6 +93,27 @@ class Workspace:
     def clear(cls) -> None:
         with cls._lock:
             cls._bufs.clear()
+
+
+class launch_overlap:
+    """Context manager (or plain call) enabling launch overlap for quantized_matmul.
+
+    While enabled, each quantized_matmul may begin streaming its packed weights,
+    scales and biases before the previous kernel on the stream has finished; it
+    waits for that kernel before touching activations or outputs. Use it for
+    decode loops over weights that were loaded earlier and are not being written
+    by in-flight work.
+    """
+
+    def __init__(self, enable: bool = True):
+        self._prev = _lib.load().mlxq_set_launch_overlap(int(bool(enable)))
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        _lib.load().mlxq_set_launch_overlap(self._prev)
+        return False
 
 
 def quantize(w: torch.Tensor, group_size: int = 64, bits: int = 4, mode: str = "affine"):

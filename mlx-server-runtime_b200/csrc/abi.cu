@@ -1,6 +1,7 @@
 // extern "C" entry points of libmlxq_b200.so (declared in include/mlxq_b200.h).
 // Host-side validation happens before anything is enqueued; every failure
 // returns a negative code and records a message for mlxq_last_error().
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <string>
@@ -11,6 +12,7 @@
 namespace {
 
 thread_local std::string g_last_error;
+std::atomic<int> g_overlap{0};
 
 int fail(int code, const char* fmt, ...) {
     char buf[512];
@@ -98,7 +100,18 @@ size_t dense_plan(int64_t M, int64_t N, int64_t K, int group_size, int bits, int
 
 }  // namespace
 
+namespace mlxq {
+bool launch_overlap_enabled() { return g_overlap.load(std::memory_order_relaxed) != 0; }
+}  // namespace mlxq
+
 extern "C" {
+
+int mlxq_set_launch_overlap(int enable) {
+    const int prev = g_overlap.exchange(enable ? 1 : 0);
+    return prev;
+}
+
+int mlxq_get_launch_overlap(void) { return g_overlap.load(); }
 
 int mlxq_abi_version(void) { return MLXQ_ABI_VERSION; }
 
@@ -194,6 +207,7 @@ int mlxq_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
         p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) +
                                              ((counters + 255) / 256) * 256);
     }
+    plan.overlap = mlxq::launch_overlap_enabled();
     cudaError_t e = mlxq::qmv_launch(dtype, bits, group_size, plan, p,
                                      static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "quantized_matmul launch");
@@ -272,6 +286,7 @@ int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const 
         if (e != cudaSuccess) return cuda_fail(e, "gather_qmm segment table");
         p.seg = seg;
     }
+    plan.overlap = false;  // index arrays come from the kernels just before
     cudaError_t e = mlxq::qmv_launch(dtype, bits, group_size, plan, p, st);
     if (e != cudaSuccess) return cuda_fail(e, "gather_qmm launch");
     return MLXQ_OK;

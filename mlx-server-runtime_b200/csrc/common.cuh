@@ -26,19 +26,39 @@ namespace mlxq {
 // and the matmul over them equals sum x*q plus offsets times activation sums:
 //   kUniform: every operand carries the same offset kOff (per code);
 //   otherwise even code positions carry kOffE and odd positions kOffO.
+// (a & MASK) | c as one LOP3 with the mask as its immediate and c a register.
+template <uint32_t MASK>
+__device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t c) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "n"(MASK), "r"(c));
+    return r;
+}
+
+// A value the compiler cannot treat as a constant, so it stays in one register
+// instead of being rebuilt from an immediate before every use.
+__device__ __forceinline__ uint32_t opaque(uint32_t v) {
+    asm volatile("" : "+r"(v));
+    return v;
+}
+
 template <typename T>
 struct Elem;
 
 template <>
 struct Elem<__nv_bfloat16> {
+    // magic operands for extract(): kept in registers by the caller (see opaque())
     template <int BITS>
-    static __device__ __forceinline__ void extract(uint32_t w, uint32_t (&t)[4]) {
-        constexpr uint32_t M0 = 0x000F000Fu, LO = 0x43004300u;
-        constexpr uint32_t HI = (BITS == 4) ? 0x43004300u : 0x45004500u;
-        t[0] = (w & M0) | LO;
-        t[1] = ((w >> 4) & M0) | HI;
-        t[2] = ((w >> 8) & M0) | LO;
-        t[3] = ((w >> 12) & M0) | HI;
+    struct Magic {
+        static constexpr uint32_t kA = 0x43004300u;
+        static constexpr uint32_t kB = (BITS == 4) ? 0x43004300u : 0x45004500u;
+    };
+    template <int BITS>
+    static __device__ __forceinline__ void extract(uint32_t w, uint32_t (&t)[4], uint32_t ma,
+                                                   uint32_t mb) {
+        t[0] = lop_and_or<0x000F000Fu>(w, ma);
+        t[1] = lop_and_or<0x000F000Fu>(w >> 4, mb);
+        t[2] = lop_and_or<0x000F000Fu>(w >> 8, ma);
+        t[3] = lop_and_or<0x000F000Fu>(w >> 12, mb);
     }
     template <int BITS>
     struct Off {
@@ -60,14 +80,18 @@ struct Elem<__nv_bfloat16> {
 template <>
 struct Elem<__half> {
     template <int BITS>
-    static __device__ __forceinline__ void extract(uint32_t w, uint32_t (&t)[4]) {
-        constexpr uint32_t M0 = 0x000F000Fu, M1 = 0x00F000F0u, E = 0x64006400u;
-        constexpr uint32_t O = (BITS == 4) ? 0x54005400u : 0x64006400u;
+    struct Magic {
+        static constexpr uint32_t kA = 0x64006400u;
+        static constexpr uint32_t kB = (BITS == 4) ? 0x54005400u : 0x64006400u;
+    };
+    template <int BITS>
+    static __device__ __forceinline__ void extract(uint32_t w, uint32_t (&t)[4], uint32_t ma,
+                                                   uint32_t mb) {
         const uint32_t h = w >> 8;
-        t[0] = (w & M0) | E;
-        t[1] = (w & M1) | O;
-        t[2] = (h & M0) | E;
-        t[3] = (h & M1) | O;
+        t[0] = lop_and_or<0x000F000Fu>(w, ma);
+        t[1] = lop_and_or<0x00F000F0u>(w, mb);
+        t[2] = lop_and_or<0x000F000Fu>(h, ma);
+        t[3] = lop_and_or<0x00F000F0u>(h, mb);
     }
     template <int BITS>
     struct Off {

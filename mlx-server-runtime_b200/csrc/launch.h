@@ -56,7 +56,8 @@ struct QmvPlan {
     int gridz;
     size_t smem;
     bool sbvec;
-    bool single;  // one token per pass (selects the kernel without odd-column folds)
+    bool single;   // one token per pass (selects the kernel without odd-column folds)
+    bool overlap;  // launch with programmatic stream serialization (launch overlap)
     size_t ws_bytes;  // workspace the plan needs (0 if none)
 };
 
@@ -65,6 +66,9 @@ bool qmv_plan(int dtype, int bits, int gs, int M_tokens_per_item, int N, int K, 
               int z_items, int num_sms, int max_smem, QmvPlan* plan);
 cudaError_t qmv_launch(int dtype, int bits, int gs, const QmvPlan& plan, const QmvParams& p,
                        cudaStream_t st);
+
+// Process-wide launch-overlap switch (mlxq_set_launch_overlap).
+bool launch_overlap_enabled();
 
 cudaError_t launch_segments(const int32_t* rhs, int batch, int num_experts, int32_t* seg,
                             cudaStream_t st);

@@ -118,6 +118,22 @@ __global__ void __launch_bounds__(qmv_geom(BITS, GS, NT, SBV, qmv_two_sums<T, BI
     const T* xg = static_cast<const T*>(p.x);
     T* og = static_cast<T*>(p.out);
     __shared__ int s_last;
+    const uint32_t magic_a = opaque(E::template Magic<BITS>::kA);
+    const uint32_t magic_b = opaque(E::template Magic<BITS>::kB);
+
+    // Launch-overlap protocol (griddepcontrol is a no-op when the launch did not opt
+    // in): the next kernel on the stream may start as soon as SMs free up; this
+    // kernel reads only weights, scales and biases before griddepcontrol.wait, and
+    // activations, index arrays and every global write come after it.
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+    bool waited = false;
+    auto wait_prior = [&]() {
+        if (!waited) {
+            asm volatile("griddepcontrol.wait;\n" ::: "memory");
+            waited = true;
+        }
+    };
+    if (p.mode != 0) wait_prior();  // gather modes read index arrays first
 
     for (int z = blockIdx.z; z < p.ztotal; z += gridDim.z) {
         // ---- resolve the work item: expert, token rows ------------------------------
@@ -199,10 +215,15 @@ __global__ void __launch_bounds__(qmv_geom(BITS, GS, NT, SBV, qmv_two_sums<T, BI
                     const int gch = w0 + (kh + issue_i * KSW) * CG;
 #pragma unroll
                     for (int it = 0; it < 4; ++it) {
-                        int nb = wbytes[it];
-                        if constexpr (!SBV) nb = (gch + grp_in_chunk < w0 + wn) ? nb : 0;
-                        cp_async16(dst + ((lane >> 3) + 4 * it) * RW + col * 4,
-                                   nb ? wptr[it] : wbase, nb);
+                        if constexpr (SBV) {
+                            // invalid rows keep a valid source address and copy 0 bytes
+                            cp_async16(dst + ((lane >> 3) + 4 * it) * RW + col * 4, wptr[it],
+                                       wbytes[it]);
+                        } else {
+                            const int nb = (gch + grp_in_chunk < w0 + wn) ? wbytes[it] : 0;
+                            cp_async16(dst + ((lane >> 3) + 4 * it) * RW + col * 4,
+                                       nb ? wptr[it] : wbase, nb);
+                        }
                         wptr[it] += wstep[it];
                     }
                     if constexpr (SBV) {
@@ -222,56 +243,89 @@ __global__ void __launch_bounds__(qmv_geom(BITS, GS, NT, SBV, qmv_two_sums<T, BI
                     if (i < my_n) issue(i);
                     else cp_async_commit();
                 }
+                wait_prior();
 
                 // ---- activation window -> B fragments + per-group sums ---------------------
                 __syncthreads();  // previous window / item finished reading the window
-                for (int idx = threadIdx.x; idx < wn * NT * 32; idx += NTHR) {
-                    const int ln = idx & 31;
-                    const int jj = (idx >> 5) % NT;
-                    const int gi = (idx >> 5) / NT;
-                    const int tt = jj * 8 + (ln >> 2);
-                    const int cc = ln & 3;
-                    uint32_t fr[FR];
+                {
+                    // Loads of PB entries are issued before any is used, so a thread
+                    // pays one memory round trip per PB entries.
+                    constexpr int PB = (WPT <= 2) ? 4 : 2;
+                    constexpr int XW = (BITS == 4) ? 4 : 2;  // activation words per packed word
+                    const int total = wn * NT * 32;
+                    for (int base = threadIdx.x; base < total; base += PB * NTHR) {
+                        uint32_t raw[PB][WPT][XW];
 #pragma unroll
-                    for (int f = 0; f < FR; ++f) fr[f] = 0u;
-                    float se = 0.f, so = 0.f;
-                    long long xrow = 0, orow = 0;
-                    if (tt < ntok) rows_of(tc + tt, xrow, orow);
-                    if (tt < ntok && xrow >= 0 && xrow < static_cast<long long>(p.x_batches) * p.M) {
-                        const T* xr = xg + xrow * K;
+                        for (int b = 0; b < PB; ++b) {
+                            const int idx = base + b * NTHR;
+                            const int ln = idx & 31;
+                            const int jj = (idx >> 5) % NT;
+                            const int gi = (idx >> 5) / NT;
+                            const int tt = jj * 8 + (ln >> 2);
+                            const int cc = ln & 3;
+                            long long xrow = -1, orow = 0;
+                            if (idx < total && tt < ntok) rows_of(tc + tt, xrow, orow);
+                            const bool live =
+                                xrow >= 0 && xrow < static_cast<long long>(p.x_batches) * p.M;
 #pragma unroll
-                        for (int w = 0; w < WPT; ++w) {
-                            const long long gw = static_cast<long long>(w0 + gi) * WPG + cc * WPT + w;
-                            if constexpr (BITS == 4) {
-                                const uint4 u = *reinterpret_cast<const uint4*>(xr + gw * 8);
-                                fr[4 * w + 0] = prmt(u.x, u.z, 0x5410);  // x0, x4
-                                fr[4 * w + 1] = prmt(u.x, u.z, 0x7632);  // x1, x5
-                                fr[4 * w + 2] = prmt(u.y, u.w, 0x5410);  // x2, x6
-                                fr[4 * w + 3] = prmt(u.y, u.w, 0x7632);  // x3, x7
-                                se += (E::lo(u.x) + E::lo(u.y)) + (E::lo(u.z) + E::lo(u.w));
-                                so += (E::hi(u.x) + E::hi(u.y)) + (E::hi(u.z) + E::hi(u.w));
-                            } else {
-                                const uint2 u = *reinterpret_cast<const uint2*>(xr + gw * 4);
-                                fr[2 * w + 0] = prmt(u.x, u.y, 0x5410);  // x0, x2
-                                fr[2 * w + 1] = prmt(u.x, u.y, 0x7632);  // x1, x3
-                                se += (E::lo(u.x) + E::hi(u.x)) + (E::lo(u.y) + E::hi(u.y));
+                            for (int w = 0; w < WPT; ++w) {
+                                const long long gw =
+                                    static_cast<long long>(w0 + gi) * WPG + cc * WPT + w;
+                                if constexpr (BITS == 4) {
+                                    uint4 u = make_uint4(0u, 0u, 0u, 0u);
+                                    if (live) u = *reinterpret_cast<const uint4*>(xg + xrow * K + gw * 8);
+                                    raw[b][w][0] = u.x; raw[b][w][1] = u.y;
+                                    raw[b][w][2] = u.z; raw[b][w][3] = u.w;
+                                } else {
+                                    uint2 u = make_uint2(0u, 0u);
+                                    if (live) u = *reinterpret_cast<const uint2*>(xg + xrow * K + gw * 4);
+                                    raw[b][w][0] = u.x; raw[b][w][1] = u.y;
+                                }
                             }
                         }
-                    }
-                    se += __shfl_xor_sync(0xffffffffu, se, 1);
-                    se += __shfl_xor_sync(0xffffffffu, se, 2);
-                    so += __shfl_xor_sync(0xffffffffu, so, 1);
-                    so += __shfl_xor_sync(0xffffffffu, so, 2);
-                    uint4* dst = xfrag + static_cast<size_t>(gi * NT + jj) * (FR / 4) * 32 + ln;
 #pragma unroll
-                    for (int f = 0; f < FR / 4; ++f)
-                        dst[f * 32] = make_uint4(fr[4 * f], fr[4 * f + 1], fr[4 * f + 2], fr[4 * f + 3]);
-                    if (cc == 0) {
-                        if constexpr (TWO) {
-                            reinterpret_cast<float2*>(sums)[gi * TOK + tt] =
-                                make_float2(se + so, OFF::kOffE * se + OFF::kOffO * so);
-                        } else {
-                            sums[gi * TOK + tt] = se + so;
+                        for (int b = 0; b < PB; ++b) {
+                            const int idx = base + b * NTHR;
+                            if (idx >= total) break;  // warp-uniform: total is a multiple of 32
+                            const int ln = idx & 31;
+                            const int jj = (idx >> 5) % NT;
+                            const int gi = (idx >> 5) / NT;
+                            const int tt = jj * 8 + (ln >> 2);
+                            const int cc = ln & 3;
+                            uint32_t fr[FR];
+                            float se = 0.f, so = 0.f;
+#pragma unroll
+                            for (int w = 0; w < WPT; ++w) {
+                                const uint32_t* u = raw[b][w];
+                                if constexpr (BITS == 4) {
+                                    fr[4 * w + 0] = prmt(u[0], u[2], 0x5410);  // x0, x4
+                                    fr[4 * w + 1] = prmt(u[0], u[2], 0x7632);  // x1, x5
+                                    fr[4 * w + 2] = prmt(u[1], u[3], 0x5410);  // x2, x6
+                                    fr[4 * w + 3] = prmt(u[1], u[3], 0x7632);  // x3, x7
+                                    se += (E::lo(u[0]) + E::lo(u[1])) + (E::lo(u[2]) + E::lo(u[3]));
+                                    so += (E::hi(u[0]) + E::hi(u[1])) + (E::hi(u[2]) + E::hi(u[3]));
+                                } else {
+                                    fr[2 * w + 0] = prmt(u[0], u[1], 0x5410);  // x0, x2
+                                    fr[2 * w + 1] = prmt(u[0], u[1], 0x7632);  // x1, x3
+                                    se += (E::lo(u[0]) + E::hi(u[0])) + (E::lo(u[1]) + E::hi(u[1]));
+                                }
+                            }
+                            se += __shfl_xor_sync(0xffffffffu, se, 1);
+                            se += __shfl_xor_sync(0xffffffffu, se, 2);
+                            so += __shfl_xor_sync(0xffffffffu, so, 1);
+                            so += __shfl_xor_sync(0xffffffffu, so, 2);
+                            uint4* dst = xfrag + static_cast<size_t>(gi * NT + jj) * (FR / 4) * 32 + ln;
+#pragma unroll
+                            for (int f = 0; f < FR / 4; ++f)
+                                dst[f * 32] = make_uint4(fr[4 * f], fr[4 * f + 1], fr[4 * f + 2], fr[4 * f + 3]);
+                            if (cc == 0) {
+                                if constexpr (TWO) {
+                                    reinterpret_cast<float2*>(sums)[gi * TOK + tt] =
+                                        make_float2(se + so, OFF::kOffE * se + OFF::kOffO * so);
+                                } else {
+                                    sums[gi * TOK + tt] = se + so;
+                                }
+                            }
                         }
                     }
                 }
@@ -287,13 +341,21 @@ __global__ void __launch_bounds__(qmv_geom(BITS, GS, NT, SBV, qmv_two_sums<T, BI
                     if constexpr (SBV) {
                         const uint32_t* sp = sw + 16 * RW;
                         const uint32_t* bp = sp + 8 * CG;
-#pragma unroll
-                        for (int q = 0; q < CG / 2; ++q) {
-                            sp0[q] = sp[r * (CG / 2) + q];
-                            sp1[q] = sp[(r + 8) * (CG / 2) + q];
-                            bp0[q] = bp[r * (CG / 2) + q];
-                            bp1[q] = bp[(r + 8) * (CG / 2) + q];
-                        }
+                        auto ld = [](const uint32_t* a, uint32_t* dst) {
+                            if constexpr (CG == 8) {
+                                const uint4 v = *reinterpret_cast<const uint4*>(a);
+                                dst[0] = v.x; dst[1] = v.y; dst[2] = v.z; dst[3] = v.w;
+                            } else if constexpr (CG == 4) {
+                                const uint2 v = *reinterpret_cast<const uint2*>(a);
+                                dst[0] = v.x; dst[1] = v.y;
+                            } else {
+                                dst[0] = a[0];
+                            }
+                        };
+                        ld(sp + r * (CG / 2), sp0);
+                        ld(sp + (r + 8) * (CG / 2), sp1);
+                        ld(bp + r * (CG / 2), bp0);
+                        ld(bp + (r + 8) * (CG / 2), bp1);
                     }
 #pragma unroll
                     for (int gi = 0; gi < CG; ++gi) {
@@ -341,8 +403,8 @@ __global__ void __launch_bounds__(qmv_geom(BITS, GS, NT, SBV, qmv_two_sums<T, BI
                         uint32_t ta[WPT][4], tb[WPT][4];
 #pragma unroll
                         for (int w = 0; w < WPT; ++w) {
-                            E::template extract<BITS>(wa[w], ta[w]);
-                            E::template extract<BITS>(wb[w], tb[w]);
+                            E::template extract<BITS>(wa[w], ta[w], magic_a, magic_b);
+                            E::template extract<BITS>(wb[w], tb[w], magic_a, magic_b);
                         }
                         float cr0 = 0.f, cr1 = 0.f;
                         if constexpr (!TWO) {

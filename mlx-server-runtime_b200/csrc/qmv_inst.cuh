@@ -23,8 +23,21 @@ cudaError_t qmv_launch_t(const QmvPlan& plan, const QmvParams& p, cudaStream_t s
         configured[dev] = static_cast<int>(plan.smem);
     }
     dim3 grid(plan.rowblocks, plan.splits, plan.gridz);
-    kern<<<grid, geo.nwarp * 32, plan.smem, st>>>(p);
-    return cudaGetLastError();
+    if (!plan.overlap) {
+        kern<<<grid, geo.nwarp * 32, plan.smem, st>>>(p);
+        return cudaGetLastError();
+    }
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(geo.nwarp * 32);
+    cfg.dynamicSmemBytes = plan.smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
 #define MLXQ_INSTANTIATE_QMV(T, BITS)  \

@@ -333,3 +333,38 @@ def test_split_k_after_sorted_gather_same_stream():
                    rhs_indices=sel, sorted_indices=True)
     y, ref = _qmm_case("bfloat16", 4, 64, 2, 512, 3584, seed=77)
     close(y, ref, "bfloat16")
+
+
+def test_launch_overlap_dependent_chain():
+    """With launch overlap on, a chain of matmuls where each consumes the previous
+    output (and a K split that uses tickets) gives the same bits as without."""
+    rng = np.random.default_rng(41)
+    dims = [3584, 512, 3584, 18944, 3584]
+    layers = []
+    for k, n in zip(dims[:-1], dims[1:]):
+        w = to_dev(rand_weights(rng, (n, k), "bfloat16"), "bfloat16")
+        layers.append(mxq.quantize(w, 64, 4))
+    x0 = to_dev(rand_x(rng, (1, dims[0]), "bfloat16"), "bfloat16")
+
+    def chain():
+        h = x0
+        outs = []
+        for wq, s, b in layers:
+            h = mxq.quantized_matmul(h, wq, s, b)
+            outs.append(h)
+        return outs
+
+    ref = chain()
+    torch.cuda.synchronize()
+    with mxq.launch_overlap(True):
+        for _ in range(3):
+            got = chain()
+        torch.cuda.synchronize()
+    assert _lib_overlap_state() == 0
+    for a, b in zip(ref, got):
+        assert torch.equal(a, b)
+
+
+def _lib_overlap_state():
+    from mlx_server_runtime_b200 import _lib as L
+    return L.load().mlxq_get_launch_overlap()
