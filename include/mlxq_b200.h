@@ -143,6 +143,28 @@ int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const 
                     void* stream);
 
 /*
+ * quantized_matmul_noalloc: the same operation as mlxq_quantized_matmul, for
+ * callers that cannot allocate device memory -- a host that binds this C ABI
+ * without a device allocator of its own, or a plugin inside a serving engine
+ * whose memory manager owns all device memory and where a cudaMalloc in the
+ * middle of a decode step may synchronize the device. It takes no workspace:
+ * the K-split scratch is a fixed MLXQ_NOALLOC_SCRATCH_BYTES (2 MiB) array
+ * compiled into the library, held by every GPU that loads the library until the
+ * process exits. Shapes whose scratch need exceeds it return MLXQ_ERR_WORKSPACE
+ * with the required size. The first call on a device looks up the array's
+ * device address and sets kernel attributes; make that first call before any
+ * stream capture. All calls share the one array: calls that overlap on the GPU
+ * (different streams, or concurrent host threads) race and must be serialized
+ * by the caller. It calls no cudaMalloc, cudaFree or allocating routine.
+ * No counterpart in the reference (MLX allocates its own buffers).
+ */
+#define MLXQ_NOALLOC_SCRATCH_BYTES (2u * 1024u * 1024u)
+int mlxq_quantized_matmul_noalloc(const void* x, const uint32_t* w, const void* scales,
+                                  const void* biases, const void* bias, void* out, int64_t M,
+                                  int64_t N, int64_t K, int group_size, int bits, int dtype,
+                                  void* stream);
+
+/*
  * Bytes of workspace mlxq_gather_qmm needs (the per-expert segment table of
  * the sorted path; 0 when sorted_indices == 0). No zero-fill is required.
  */

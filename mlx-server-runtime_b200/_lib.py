@@ -32,6 +32,7 @@ EXPORTED = (
     "mlxq_gather_qmm_workspace_size",
     "mlxq_set_launch_overlap",
     "mlxq_get_launch_overlap",
+    "mlxq_quantized_matmul_noalloc",
 )
 
 _lock = threading.Lock()
@@ -76,6 +77,9 @@ def load(path: str | None = None):
         L.mlxq_set_launch_overlap.argtypes = [i32]
         L.mlxq_set_launch_overlap.restype = i32
         L.mlxq_get_launch_overlap.restype = i32
+        L.mlxq_quantized_matmul_noalloc.argtypes = [vp, vp, vp, vp, vp, vp, i64, i64, i64, i32,
+                                                    i32, i32, vp]
+        L.mlxq_quantized_matmul_noalloc.restype = i32
         v = L.mlxq_abi_version()
         if v != ABI_VERSION:
             raise LibraryError(f"{p} has ABI version {v}, expected {ABI_VERSION}; rebuild it")

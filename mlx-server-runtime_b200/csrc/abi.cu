@@ -102,6 +102,13 @@ size_t dense_plan(int64_t M, int64_t N, int64_t K, int group_size, int bits, int
 
 namespace mlxq {
 bool launch_overlap_enabled() { return g_overlap.load(std::memory_order_relaxed) != 0; }
+
+// Records the message mlxq_last_error() returns; for entry points defined in
+// other translation units.
+int set_last_error(int code, const char* msg) {
+    g_last_error = msg;
+    return code;
+}
 }  // namespace mlxq
 
 extern "C" {

@@ -70,6 +70,9 @@ cudaError_t qmv_launch(int dtype, int bits, int gs, const QmvPlan& plan, const Q
 // Process-wide launch-overlap switch (mlxq_set_launch_overlap).
 bool launch_overlap_enabled();
 
+// Sets the thread's mlxq_last_error() message and returns `code`.
+int set_last_error(int code, const char* msg);
+
 cudaError_t launch_segments(const int32_t* rhs, int batch, int num_experts, int32_t* seg,
                             cudaStream_t st);
 
