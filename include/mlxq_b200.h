@@ -81,6 +81,14 @@ int mlxq_set_launch_overlap(int enable);
 int mlxq_get_launch_overlap(void);
 
 /*
+ * Reads and clears the current device's kernel error code (0 = none). Kernels
+ * that wait on hardware barriers give up after a bounded number of polls
+ * instead of hanging; they then record a nonzero code here, skip their output
+ * and exit. Synchronous (reads device memory). No counterpart in the reference.
+ */
+int mlxq_device_error(int* code);
+
+/*
  * quantize: replaces mx.quantize(w, group_size, bits, mode="affine")
  * (lfm2.py:112-117) and the per-layer quantization nn.quantize performs
  * (qwen2.py:318-324). w [rows, K] of dtype w_dtype; writes wq
@@ -111,6 +119,9 @@ size_t mlxq_qmm_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, 
  * quantized_matmul: replaces mx.quantized_matmul(x, w, scales, biases,
  * transpose=True, group_size, bits) as called by nn.QuantizedLinear
  * (qwen2.py:58-61,123-134,227), plus QuantizedLinear's optional bias add.
+ * Up to 32 rows of x use the decode kernel (HBM-bound); more rows with K a
+ * multiple of 64 use the tcgen05 prefill kernel (weights dequantized into
+ * shared memory, rounded once to the activation dtype, fp32 accumulation).
  * x [M, K], w [N, K*bits/32], scales/biases [N, K/group_size], bias [N] or
  * NULL, out [M, N]; x/scales/biases/bias/out all of `dtype` (bf16 or f16).
  * out = round(x @ dequant(w)^T) with float32 accumulation; with bias,

@@ -33,6 +33,7 @@ EXPORTED = (
     "mlxq_set_launch_overlap",
     "mlxq_get_launch_overlap",
     "mlxq_quantized_matmul_noalloc",
+    "mlxq_device_error",
 )
 
 _lock = threading.Lock()
@@ -80,12 +81,21 @@ def load(path: str | None = None):
         L.mlxq_quantized_matmul_noalloc.argtypes = [vp, vp, vp, vp, vp, vp, i64, i64, i64, i32,
                                                     i32, i32, vp]
         L.mlxq_quantized_matmul_noalloc.restype = i32
+        L.mlxq_device_error.argtypes = [ctypes.POINTER(ctypes.c_int)]
+        L.mlxq_device_error.restype = i32
         v = L.mlxq_abi_version()
         if v != ABI_VERSION:
             raise LibraryError(f"{p} has ABI version {v}, expected {ABI_VERSION}; rebuild it")
         if path is None:
             _lib = L
         return L
+
+
+def device_error() -> int:
+    """Read and clear the current device's kernel error code (0 = none)."""
+    code = ctypes.c_int(0)
+    check(load().mlxq_device_error(ctypes.byref(code)), "device_error")
+    return code.value
 
 
 def last_error() -> str:

@@ -120,6 +120,14 @@ int mlxq_set_launch_overlap(int enable) {
 
 int mlxq_get_launch_overlap(void) { return g_overlap.load(); }
 
+int mlxq_device_error(int* code) {
+    if (!code) return fail(MLXQ_ERR_NULL, "device_error: NULL pointer");
+    *code = 0;
+    cudaError_t e = mlxq::qgemm_read_error(code);
+    if (e != cudaSuccess) return cuda_fail(e, "device_error");
+    return MLXQ_OK;
+}
+
 int mlxq_abi_version(void) { return MLXQ_ABI_VERSION; }
 
 const char* mlxq_last_error(void) { return g_last_error.c_str(); }
@@ -164,6 +172,9 @@ size_t mlxq_qmm_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, 
                                int dtype) {
     if (check_bits_gs(bits, group_size, true) || check_k(K, group_size)) return 0;
     if (M <= 0 || N <= 0 || M > kIntMax || N > kIntMax || K > kIntMax) return 0;
+    if (mlxq::qgemm_supported(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                              bits, group_size))
+        return 0;  // the tensor-core prefill kernel needs no workspace
     DeviceInfo di;
     if (device_info(&di, nullptr)) return 0;
     mlxq::QmvPlan plan;
@@ -191,6 +202,17 @@ int mlxq_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
     if (M == 0) return MLXQ_OK;
     DeviceInfo di;
     if ((rc = device_info(&di, static_cast<cudaStream_t>(stream)))) return rc;
+    if (mlxq::qgemm_supported(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), bits,
+                              group_size)) {
+        // prefill: dequantize into shared memory + tcgen05 tensor cores
+        mlxq::QgemmParams q{};
+        q.x = x; q.w = w; q.s = scales; q.b = biases; q.bias = bias; q.out = out;
+        q.M = static_cast<int>(M); q.N = static_cast<int>(N); q.K = static_cast<int>(K);
+        cudaError_t e = mlxq::qgemm_launch(dtype, bits, group_size, q,
+                                           static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return cuda_fail(e, "quantized_matmul (prefill) launch");
+        return MLXQ_OK;
+    }
     mlxq::QmvPlan plan;
     bool ok = false;
     const size_t need = dense_plan(M, N, K, group_size, bits, dtype, di, &plan, &ok);

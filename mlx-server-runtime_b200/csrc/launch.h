@@ -67,6 +67,22 @@ bool qmv_plan(int dtype, int bits, int gs, int M_tokens_per_item, int N, int K, 
 cudaError_t qmv_launch(int dtype, int bits, int gs, const QmvPlan& plan, const QmvParams& p,
                        cudaStream_t st);
 
+// One dense problem for the tcgen05 prefill kernel (qgemm_sm100.cu).
+struct QgemmParams {
+    const void* x;
+    const uint32_t* w;
+    const void* s;
+    const void* b;
+    const void* bias;  // optional per-output bias [N]
+    void* out;
+    int M, N, K;
+};
+
+bool qgemm_supported(int M, int N, int K, int bits, int gs);
+cudaError_t qgemm_launch(int dtype, int bits, int gs, const QgemmParams& p, cudaStream_t st);
+// Reads (and clears) the error code a kernel recorded after a bounded wait gave up.
+cudaError_t qgemm_read_error(int* out_code);
+
 // Process-wide launch-overlap switch (mlxq_set_launch_overlap).
 bool launch_overlap_enabled();
 
