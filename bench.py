@@ -390,11 +390,11 @@ def run(args):
                        "allgather": "one NCCL all-gather of all outputs per step" if world > 1
                        else None,
                        "qmm_only_tok_per_s": round(1000.0 / ms, 1)},
-            "gpu_launches": (launches_per_step + 1) * args.steps,
-            "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak,
-                         "unit": "GB/s", "frac": round(value / peak, 4),
-                         "peak_source": peak_src,
-                         "frac_of_8TBs_nominal": round(value / 8000.0, 4),
+            "gpu_launches": launches_per_step * args.steps,
+            "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak * world,
+                         "unit": "GB/s", "frac": round(value / (peak * world), 4),
+                         "peak_source": peak_src + (f" (per GPU x {world})" if world > 1 else ""),
+                         "frac_of_8TBs_nominal": round(value / (8000.0 * world), 4),
                          "traffic": traffic},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
@@ -464,10 +464,12 @@ def run_case(args):
         e1.record()
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / (reps * copies)
+    flops = 2.0 * M * N * K
     print(json.dumps({"case": args.case, "M": M, "N": N, "K": K, "copies": copies,
                       "overlap": not args.no_overlap,
                       "us_per_launch": round(us, 3), "bytes": per,
-                      "GB/s": round(per / (us * 1e-6) / 1e9, 1)}), flush=True)
+                      "GB/s": round(per / (us * 1e-6) / 1e9, 1),
+                      "TFLOP/s": round(flops / (us * 1e-6) / 1e12, 1)}), flush=True)
 
 
 def main():

@@ -1,0 +1,109 @@
+"""Two-GPU NCCL tests of the sharded forms with the CUDA operators as the
+per-rank compute: N-sharded QuantizedLinear + all-gather, and the
+expert-parallel SwitchGLU. Checked against the oracle within the matmul
+tolerance. Skipped with fewer than two GPUs."""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    try:
+        sys.path.insert(0, ROOT)
+        sys.path.insert(0, os.path.join(ROOT, "tests"))
+        import datetime
+
+        import conftest
+        conftest.load_package()
+        import torch.distributed as dist
+
+        import mlx_server_runtime_b200 as mxq
+        from mlx_server_runtime_b200.distributed import (ExpertParallelSwitchGLU,
+                                                         ShardedQuantizedLinear)
+        from gpu_util import close, rand_weights, rand_x, to_dev, to_np
+        from oracle import oracle_np
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        dev = torch.device("cuda", rank)
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=60))
+
+        # N-sharded linear: same full weights on both ranks, each keeps its rows
+        rng = np.random.default_rng(5)
+        N, K, M = 3000, 1024, 4
+        w_np = rand_weights(rng, (N, K), "bfloat16")
+        x_np = rand_x(rng, (M, K), "bfloat16")
+        wq, s, b = mxq.quantize(to_dev(w_np, "bfloat16", dev), 64, 4)
+        lin = ShardedQuantizedLinear.from_full(wq, s, b, group_size=64, bits=4)
+        got = lin(to_dev(x_np, "bfloat16", dev))
+        torch.cuda.synchronize()
+        ref = oracle_np.quantized_matmul(x_np, to_np(wq), to_np(s), to_np(b), "bfloat16", 64, 4)
+        close(to_np(got), ref, "bfloat16")
+
+        # expert parallel: 8 experts, 4 per rank, top-2 routing of each rank's tokens
+        E, D, I, T, k = 8, 512, 256, 24 + 8 * rank, 2
+        rng = np.random.default_rng(9)
+        full = []
+        for n, kk in ((I, D), (I, D), (D, I)):
+            w = to_dev(rand_weights(rng, (E, n, kk), "bfloat16"), "bfloat16", dev)
+            full.append(mxq.quantize(w, 64, 4))
+        el = E // world
+        local = [tuple(a[rank * el:(rank + 1) * el].contiguous() for a in t) for t in full]
+        rr = np.random.default_rng(40 + rank)
+        x_np = rand_x(rr, (T, D), "bfloat16")
+        idx_np = np.array([rr.choice(E, size=k, replace=False) for _ in range(T)], np.int32)
+        moe = ExpertParallelSwitchGLU(*local, num_experts=E, group_size=64, bits=4)
+        got = moe(to_dev(x_np, "bfloat16", dev), torch.from_numpy(idx_np).to(dev))
+        torch.cuda.synchronize()
+        # reference: the same expert chain on this rank's GPU without any exchange
+        x_d = to_dev(x_np, "bfloat16", dev)
+        ref = torch.empty(T, k, D, dtype=torch.bfloat16, device=dev)
+        for t in range(T):
+            for j in range(k):
+                e = int(idx_np[t, j])
+                g = mxq.quantized_matmul(x_d[t:t + 1], *(a[e] for a in full[0]), group_size=64)
+                u = mxq.quantized_matmul(x_d[t:t + 1], *(a[e] for a in full[1]), group_size=64)
+                h = torch.nn.functional.silu(g) * u
+                ref[t, j] = mxq.quantized_matmul(h, *(a[e] for a in full[2]), group_size=64)[0]
+        torch.cuda.synchronize()
+        close(to_np(got), to_np(ref), "bfloat16")
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, True, ""))
+    except Exception as e:
+        q.put((rank, False, repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_sharded_linear_and_expert_parallel_on_two_gpus():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    for rank, ok, info in sorted(res):
+        assert ok, f"rank {rank}: {info}"
