@@ -123,8 +123,11 @@ int mlxq_get_launch_overlap(void) { return g_overlap.load(); }
 int mlxq_device_error(int* code) {
     if (!code) return fail(MLXQ_ERR_NULL, "device_error: NULL pointer");
     *code = 0;
-    cudaError_t e = mlxq::qgemm_read_error(code);
+    int a = 0, b = 0;
+    cudaError_t e = mlxq::qgemm_read_error(&a);
+    if (e == cudaSuccess) e = mlxq::qmv_tma_read_error(&b);
     if (e != cudaSuccess) return cuda_fail(e, "device_error");
+    *code = a ? a : b;
     return MLXQ_OK;
 }
 
@@ -177,6 +180,10 @@ size_t mlxq_qmm_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, 
         return 0;  // the tensor-core prefill kernel needs no workspace
     DeviceInfo di;
     if (device_info(&di, nullptr)) return 0;
+    mlxq::QtPlan tplan;
+    if (mlxq::qmv_tma_plan(dtype, bits, group_size, static_cast<int>(M), static_cast<int>(N),
+                           static_cast<int>(K), di.num_sms, di.max_smem, &tplan))
+        return tplan.ws_bytes;
     mlxq::QmvPlan plan;
     bool ok = false;
     return dense_plan(M, N, K, group_size, bits, dtype, di, &plan, &ok);
@@ -213,6 +220,25 @@ int mlxq_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
         if (e != cudaSuccess) return cuda_fail(e, "quantized_matmul (prefill) launch");
         return MLXQ_OK;
     }
+    mlxq::QtPlan tplan;
+    if (mlxq::qmv_tma_plan(dtype, bits, group_size, static_cast<int>(M), static_cast<int>(N),
+                           static_cast<int>(K), di.num_sms, di.max_smem, &tplan)) {
+        // decode, M <= 8: TMA-fed stream-K kernel
+        if (tplan.ws_bytes > 0) {
+            if (!workspace || workspace_bytes < tplan.ws_bytes)
+                return fail(MLXQ_ERR_WORKSPACE,
+                            "quantized_matmul: needs %zu workspace bytes, got %zu",
+                            tplan.ws_bytes, workspace ? workspace_bytes : (size_t)0);
+            if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+                return fail(MLXQ_ERR_ALIGN, "quantized_matmul: workspace must be 256-byte aligned");
+        }
+        cudaError_t e = mlxq::qmv_tma_launch(
+            dtype, bits, group_size, tplan, x, w, scales, biases, bias, out, static_cast<int>(M),
+            static_cast<int>(N), static_cast<int>(K), workspace, mlxq::launch_overlap_enabled(),
+            static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return cuda_fail(e, "quantized_matmul (decode) launch");
+        return MLXQ_OK;
+    }
     mlxq::QmvPlan plan;
     bool ok = false;
     const size_t need = dense_plan(M, N, K, group_size, bits, dtype, di, &plan, &ok);
@@ -231,10 +257,8 @@ int mlxq_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
     p.batch = 0; p.num_experts = 1; p.x_batches = 1; p.w_estride = 0; p.sb_estride = 0;
     p.splits = plan.splits; p.gps = plan.gps; p.win = plan.win; p.ztotal = plan.ztotal;
     if (need > 0) {
-        const size_t counters = static_cast<size_t>(plan.ztotal) * plan.rowblocks * 4;
         p.counter = static_cast<unsigned*>(workspace);
-        p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) +
-                                             ((counters + 255) / 256) * 256);
+        p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + mlxq::kTicketBytes);
     }
     plan.overlap = mlxq::launch_overlap_enabled();
     cudaError_t e = mlxq::qmv_launch(dtype, bits, group_size, plan, p,

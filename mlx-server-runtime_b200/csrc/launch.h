@@ -9,6 +9,13 @@ namespace mlxq {
 
 enum { kF32 = 0, kBF16 = 1, kF16 = 2 };
 
+// Layout of the quantized_matmul workspace shared by the decode kernels: a fixed
+// ticket region (one counter per row block, zero between calls) followed by the
+// fp32 partial sums of the current call. The ticket region never moves, so
+// partial sums written by one call can never land where a later call, planned
+// with more row blocks, expects zeroed tickets.
+constexpr size_t kTicketBytes = 64 * 1024;
+
 cudaError_t launch_quantize(const void* w, int dtype, uint32_t* wq, void* s, void* b,
                             long long rows, long long K, int gs, int bits, cudaStream_t st);
 cudaError_t launch_dequantize(const uint32_t* wq, const void* s, const void* b, int dtype,
@@ -66,6 +73,26 @@ bool qmv_plan(int dtype, int bits, int gs, int M_tokens_per_item, int N, int K, 
               int z_items, int num_sms, int max_smem, QmvPlan* plan);
 cudaError_t qmv_launch(int dtype, int bits, int gs, const QmvPlan& plan, const QmvParams& p,
                        cudaStream_t st);
+
+// Plan of the TMA-fed decode kernel (qmv_tma.cu): M <= 8 tokens, K/group_size a
+// multiple of 8. Units of 64 rows x 8 groups, split evenly over P CTAs.
+struct QtPlan {
+    int RB;        // 64-row blocks
+    int S;         // units per row block
+    long long U;   // units
+    int P;         // CTAs
+    int stages;    // ring depth
+    int maxc;      // most CTAs sharing one row block
+    size_t smem;
+    size_t ws_bytes;  // workspace (tickets + partials) when a row block is shared
+};
+bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms, int max_smem,
+                  QtPlan* plan);
+cudaError_t qmv_tma_launch(int dtype, int bits, int gs, const QtPlan& plan, const void* x,
+                           const uint32_t* w, const void* s, const void* b, const void* bias,
+                           void* out, int M, int N, int K, void* workspace, bool overlap,
+                           cudaStream_t st);
+cudaError_t qmv_tma_read_error(int* out_code);
 
 // One dense problem for the tcgen05 prefill kernel (qgemm_sm100.cu).
 struct QgemmParams {

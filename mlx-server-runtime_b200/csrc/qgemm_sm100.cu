@@ -28,6 +28,7 @@
 // frees its tensor memory and returns.
 #include "common.cuh"
 #include "launch.h"
+#include "sm100.cuh"
 
 namespace mlxq {
 
@@ -48,10 +49,6 @@ template <int BITS>
 constexpr int smem_bytes() { return STAGES * stage_bytes<BITS>() + 1024 + 128; }
 }  // namespace qg
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart.
 __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
     uint64_t d = 0;
@@ -69,29 +66,6 @@ __host__ __device__ constexpr uint32_t qgemm_idesc() {
     constexpr uint32_t ab = __is_same(T, __nv_bfloat16) ? 1u : 0u;
     return (1u << 4) | (ab << 7) | (ab << 10) | (static_cast<uint32_t>(qg::BN >> 3) << 17) |
            (static_cast<uint32_t>(qg::BM >> 4) << 24);
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count));
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.b32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// Bounded wait; false after kSpinLimit polls.
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
-    for (uint32_t i = 0; i < qg::kSpinLimit; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    return false;
 }
 
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
@@ -355,7 +329,7 @@ __global__ void __launch_bounds__(qg::THREADS, 1) qgemm_kernel(const QgemmParams
         if (kb + STAGES - 1 < KB) {
             if (kb >= 1) {
                 const int ps = (kb - 1) % STAGES;
-                if (!mbar_wait_bounded(smem_u32(bars + ps), ((kb - 1) / STAGES) & 1)) {
+                if (!mbar_wait_bounded(smem_u32(bars + ps), ((kb - 1) / STAGES) & 1, kSpinLimit)) {
                     *s_abort = 1;
                     atomicCAS(&g_qgemm_error, 0, kErrTimeout);
                 }
@@ -372,7 +346,7 @@ __global__ void __launch_bounds__(qg::THREADS, 1) qgemm_kernel(const QgemmParams
     bool done = !aborted && KB > 0;
     if (done) {
         const int ls = (KB - 1) % STAGES;
-        if (!mbar_wait_bounded(smem_u32(bars + ls), ((KB - 1) / STAGES) & 1)) {
+        if (!mbar_wait_bounded(smem_u32(bars + ls), ((KB - 1) / STAGES) & 1, kSpinLimit)) {
             atomicCAS(&g_qgemm_error, 0, kErrTimeout);
             done = false;
         }

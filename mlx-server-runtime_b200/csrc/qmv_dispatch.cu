@@ -59,7 +59,8 @@ bool qmv_plan(int dtype, int bits, int gs, int M, int N, int K, int mode, int z_
     pl.ws_bytes = 0;
     if (pl.splits > 1) {
         const size_t counters = static_cast<size_t>(pl.ztotal) * pl.rowblocks * 4;
-        pl.ws_bytes = ((counters + 255) / 256) * 256 +
+        if (counters > kTicketBytes) return false;
+        pl.ws_bytes = kTicketBytes +
                       static_cast<size_t>(pl.splits) * M * static_cast<size_t>(N) * 4;
     }
     *plan = pl;

@@ -1,0 +1,173 @@
+// Planning, tensor maps and dispatch for the TMA-fed decode kernel (qmv_tma.cuh).
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "qmv_tma.cuh"
+
+namespace mlxq {
+
+__device__ int g_qmv_tma_error;
+
+template <typename T, int BITS, int GS, int TM>
+cudaError_t qt_launch_t(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tb,
+                        const QtParams& p, int grid, size_t smem, bool overlap, cudaStream_t st);
+
+namespace {
+
+int stage_bytes(int bits, int gs) {
+    const int boxes = gs * bits / 128;
+    return boxes * qt::BR * 128 + 2 * qt::BR * qt::SG * 2;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 2-D map over a row-major [rows, cols] array of `esize`-byte elements, box
+// [box_rows, box_cols].
+bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esize,
+              unsigned long long cols, unsigned long long rows, unsigned box_cols,
+              unsigned box_rows, CUtensorMapSwizzle swz) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * static_cast<cuuint64_t>(esize)};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms, int max_smem,
+                  QtPlan* plan) {
+    if (M < 1 || M > qt::MAXM || N < 1 || K < 1 || K % gs) return false;
+    if (bits != 4 && bits != 8) return false;
+    if (gs != 32 && gs != 64 && gs != 128) return false;
+    if (bits == 8 && gs == 128) return false;  // 64 KB stages: too shallow a ring
+    const int G = K / gs;
+    if (G % qt::SG) return false;  // scale/bias rows must be whole 16-byte TMA boxes
+    if (!encode_fn()) return false;
+    const int TM = qt::token_slots(M);
+    const int stage = stage_bytes(bits, gs);
+    const int fixed = qt::layout(stage, 0, G, TM, gs * 2).total + 1024;  // + alignment slack
+    if (fixed + 2 * stage > max_smem) return false;
+    QtPlan pl{};
+    pl.RB = (N + qt::BR - 1) / qt::BR;
+    if (static_cast<size_t>(pl.RB) * 4 > kTicketBytes) return false;
+    pl.S = G / qt::SG;
+    pl.U = static_cast<long long>(pl.RB) * pl.S;
+    pl.P = static_cast<int>(std::min<long long>(pl.U, num_sms));
+    const long long per_cta = (pl.U + pl.P - 1) / pl.P;
+    int stages = std::min((max_smem - fixed) / stage, qt::MAX_STAGES);
+    stages = static_cast<int>(std::min<long long>(stages, std::max<long long>(2, per_cta)));
+    pl.stages = std::max(2, stages);
+    pl.smem = static_cast<size_t>(qt::layout(stage, pl.stages, G, TM, gs * 2).total) + 1024;
+    int maxc = 1;
+    for (int rb = 0; rb < pl.RB; ++rb) {
+        const long long ub = static_cast<long long>(rb) * pl.S;
+        const int nc = qt::owner(ub + pl.S - 1, pl.U, pl.P) - qt::owner(ub, pl.U, pl.P) + 1;
+        maxc = std::max(maxc, nc);
+    }
+    pl.maxc = maxc;
+    pl.ws_bytes = 0;
+    if (maxc > 1)
+        pl.ws_bytes = kTicketBytes +
+                      static_cast<size_t>(pl.RB) * maxc * M * qt::BR * 4;
+    *plan = pl;
+    return true;
+}
+
+#define QT_CASE(T, BITS, GS)                                                                    \
+    switch (qt::token_slots(M)) {                                                               \
+        case 1: return qt_launch_t<T, BITS, GS, 1>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
+        case 2: return qt_launch_t<T, BITS, GS, 2>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
+        case 4: return qt_launch_t<T, BITS, GS, 4>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
+        default: return qt_launch_t<T, BITS, GS, 8>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
+    }
+
+template <typename T>
+static cudaError_t qt_dispatch(int bits, int gs, int M, const CUtensorMap& tw,
+                               const CUtensorMap& ts, const CUtensorMap& tb, const QtParams& p,
+                               const QtPlan& plan, bool overlap, cudaStream_t st) {
+    if (bits == 4) {
+        if (gs == 32) { QT_CASE(T, 4, 32) }
+        if (gs == 64) { QT_CASE(T, 4, 64) }
+        if (gs == 128) { QT_CASE(T, 4, 128) }
+    } else if (bits == 8) {
+        if (gs == 32) { QT_CASE(T, 8, 32) }
+        if (gs == 64) { QT_CASE(T, 8, 64) }
+    }
+    return cudaErrorInvalidValue;
+}
+
+// Device address of g_qmv_tma_error, looked up once per device (kernels in other
+// translation units reach the flag through this pointer).
+static int* error_flag() {
+    static int* addr[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (!addr[dev]) {
+        void* a = nullptr;
+        if (cudaGetSymbolAddress(&a, g_qmv_tma_error) != cudaSuccess) return nullptr;
+        addr[dev] = static_cast<int*>(a);
+    }
+    return addr[dev];
+}
+
+cudaError_t qmv_tma_launch(int dtype, int bits, int gs, const QtPlan& plan, const void* x,
+                           const uint32_t* w, const void* s, const void* b, const void* bias,
+                           void* out, int M, int N, int K, void* workspace, bool overlap,
+                           cudaStream_t st) {
+    const int G = K / gs;
+    const unsigned long long kw = static_cast<unsigned long long>(K) * bits / 32;
+    CUtensorMap tw, ts, tb;
+    if (!make_map(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, kw, N, 32, qt::BR,
+                  CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&ts, s, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, G, N, qt::SG, qt::BR,
+                  CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map(&tb, b, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, G, N, qt::SG, qt::BR,
+                  CU_TENSOR_MAP_SWIZZLE_NONE))
+        return cudaErrorInvalidValue;
+    QtParams p{};
+    p.err = error_flag();
+    if (!p.err) return cudaErrorInvalidSymbol;
+    p.x = x; p.bias = bias; p.out = out;
+    p.M = M; p.N = N; p.K = K; p.G = G;
+    p.S = plan.S; p.RB = plan.RB; p.U = plan.U; p.stages = plan.stages; p.maxc = plan.maxc;
+    if (plan.ws_bytes) {
+        p.counter = static_cast<unsigned*>(workspace);
+        p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kTicketBytes);
+    }
+    if (dtype == kBF16) return qt_dispatch<__nv_bfloat16>(bits, gs, M, tw, ts, tb, p, plan, overlap, st);
+    if (dtype == kF16) return qt_dispatch<__half>(bits, gs, M, tw, ts, tb, p, plan, overlap, st);
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t qmv_tma_read_error(int* code) {
+    int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_qmv_tma_error, sizeof(int));
+    if (e != cudaSuccess) return e;
+    if (v) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbol(g_qmv_tma_error, &zero, sizeof(int));
+    }
+    *code = v;
+    return e;
+}
+
+}  // namespace mlxq

@@ -1,0 +1,541 @@
+// Decode-shaped group-wise affine quantized matmul fed by TMA (sm_100a):
+//
+//   out[t, n] = sum_k x[t, k] * (scale[n, k/g] * q[n, k] + bias[n, k/g]),  t < M <= 8
+//
+// MLX's quantized_matmul with transpose=True as QuantizedLinear calls it at
+// decode (qwen2.py:58-61,123-134 of the reference).
+//
+// Work: the weight matrix is cut into units of 64 rows x 8 quantization groups
+// (one pipeline stage). Units are numbered row-block-major and each CTA takes a
+// contiguous, equal share (stream-K): every SM streams the same number of
+// bytes whatever N and K are. A row block whose units span several CTAs is
+// finished by the last of them (atomic ticket, no waiting), which adds the fp32
+// partials in CTA order, so results are deterministic.
+//
+// Per CTA: one producer warp and 16 consumer warps.
+//   * Producer (one thread): for every unit, 2-D TMA loads of the packed
+//     weights [64 rows x 128 B] per box (128-byte swizzle) plus one box each of
+//     scales and biases [64 rows x 8 groups], into a ring of `stages` slots with
+//     full/empty mbarriers. The ring holds most of the CTA's share, so nearly
+//     all of it is requested from HBM at kernel start.
+//   * Consumers: warp (rt, kq) owns row tile rt (16 rows) and groups 2kq, 2kq+1
+//     of every stage. ldmatrix reads the swizzled tiles without bank conflicts
+//     and hands lane (r, c) words c, c+4, ... of the group for rows r and r+8.
+//     Codes become exact f16 MMA operands with one LOP3 per pair (see
+//     Elem<__half>::extract); one m16n8k16 MMA covers 16 codes x 8 token slots
+//     into a fresh fp32 accumulator per group.
+//   * Activations: x[M, K] is staged once as f16 MMA B fragments. Each (group,
+//     token) slice is multiplied by a power of two 2^e that brings its largest
+//     magnitude into [2^14, 2^15), which makes the bf16 (or f16) values exact in
+//     f16, so bf16 activations use the cheaper f16 extraction too. A record
+//     {sum x, sum offset * x 2^e, 2^-e} per slice turns the MMA result D into
+//       acc += (scale * 2^-e) * (D - sum offset * x 2^e) + bias * sum x.
+//     The token count is a compile-time slot count TM in {1, 2, 4, 8} (M rounded
+//     up; absent tokens are zero), so every shared-memory address in the main
+//     loop is a per-lane base plus a constant.
+// Every wait is bounded: a timeout records an error in *p.err, sets a CTA-wide
+// abort flag that turns the remaining waits and all global writes off, and
+// lets every warp run to the end (so the named barriers still meet).
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+#include "launch.h"
+#include "sm100.cuh"
+
+namespace mlxq {
+
+namespace qt {
+constexpr int BR = 64;                   // weight rows per unit
+constexpr int SG = 8;                    // quantization groups per unit (stage)
+constexpr int RT = BR / 16;              // 16-row MMA tiles per unit
+constexpr int KSW = SG / 2;              // consumer warps per row tile (2 groups each)
+constexpr int CWARPS = RT * KSW;         // 16 consumer warps
+constexpr int CTHREADS = CWARPS * 32;
+constexpr int THREADS = CTHREADS + 32;   // + producer warp
+constexpr int MAXM = 8;                  // tokens per launch
+constexpr int MAX_STAGES = 16;
+constexpr uint32_t kSpinLimit = 1u << 22;
+constexpr int kErrTimeout = 2;
+
+// Token slots a kernel instance is compiled for; M is rounded up to one of them.
+__host__ __device__ constexpr int token_slots(int M) {
+    return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8;
+}
+
+template <int BITS, int GS>
+struct Geo {
+    static constexpr int WPG = GS * BITS / 32;     // packed words per group per row
+    static constexpr int CPG = WPG / 4;            // 16-byte chunks per group per row
+    static constexpr int BOXES = SG * WPG / 32;    // 128-byte TMA boxes per stage
+    static constexpr int W_BYTES = BOXES * BR * 128;
+    static constexpr int SB_BYTES = BR * SG * 2;   // scales (or biases) of one stage
+    static constexpr int STAGE = W_BYTES + 2 * SB_BYTES;
+    static constexpr int FR = (BITS == 4) ? 4 * CPG : 2 * CPG;  // B-fragment words per lane
+    static constexpr int XG = GS * 2;              // fragment bytes per (group, token slot)
+    static_assert(CPG >= 1 && BOXES >= 1 && STAGE % 1024 == 0, "unsupported geometry");
+};
+
+// Shared-memory layout (from a 1024-byte aligned base), in bytes.
+struct Layout {
+    int ring, xf, rec, red, bars, flags, total;
+};
+__host__ __device__ inline Layout layout(int stage_bytes, int stages, int G, int TM, int xg) {
+    Layout L;
+    L.ring = 0;
+    L.xf = stages * stage_bytes;               // [G][FR/4][TM][4 lanes] x 16 B
+    L.rec = L.xf + G * TM * xg;                // [G][TM] float4 records
+    L.red = L.rec + G * TM * 16;               // cross-warp reduction
+    L.bars = (L.red + (KSW - 1) * RT * 4 * 32 * 4 + 7) & ~7;
+    L.flags = (L.bars + 2 * stages * 8 + 15) & ~15;  // abort, last
+    L.total = L.flags + 16;
+    return L;
+}
+
+// Owner CTA of unit u when U units are split in P contiguous shares
+// [floor(U*i/P), floor(U*(i+1)/P)).
+__host__ __device__ inline int owner(long long u, long long U, int P) {
+    return static_cast<int>(((u + 1) * P - 1) / U);
+}
+
+// 2^e as a float for integer e in [-126, 127] (exact).
+__device__ __forceinline__ float pow2i(int e) {
+    return __uint_as_float(static_cast<uint32_t>(127 + e) << 23);
+}
+
+// The e that brings a finite m > 0 into [2^14, 2^15) (clamped so 2^e and 2^-e
+// stay normal floats); 0 for zero, infinite or NaN m.
+__device__ __forceinline__ int slice_exponent(float m) {
+    const uint32_t bits = __float_as_uint(m);
+    const int ef = static_cast<int>((bits >> 23) & 0xffu);
+    if (!(m > 0.f) || ef == 0xff) return 0;
+    const int e = 14 - (ef - 127);  // subnormal m (ef == 0) gives the clamp below
+    return e > 126 ? 126 : (e < -126 ? -126 : e);
+}
+
+// Slow path of a full-barrier wait (the first poll usually succeeds).
+static __device__ __noinline__ bool wait_slow(uint32_t bar, uint32_t parity) {
+    return mbar_wait_bounded(bar, parity, kSpinLimit);
+}
+}  // namespace qt
+
+struct QtParams {
+    const void* x;
+    const void* bias;
+    void* out;
+    int M, N, K, G;
+    int S;          // stages (units) per row block = G / 8
+    int RB;         // row blocks
+    long long U;    // units
+    int stages;     // ring depth
+    int maxc;       // most CTAs contributing to one row block
+    unsigned* counter;  // [RB], zero at entry and exit
+    float* partial;     // [RB][maxc][M][64]
+    int* err;           // device error flag
+};
+
+template <typename T, int BITS, int GS, int TM>
+__global__ void __launch_bounds__(qt::THREADS, 1)
+    qmv_tma_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ts,
+                   const __grid_constant__ CUtensorMap tb, const QtParams p) {
+    using namespace qt;
+    using ET = Elem<T>;        // activation / output type
+    using EH = Elem<__half>;   // MMA operand type
+    using OFF = typename EH::template Off<BITS>;
+    using GEO = Geo<BITS, GS>;
+    constexpr int WPG = GEO::WPG, CPG = GEO::CPG, FR = GEO::FR, XG = GEO::XG;
+    constexpr int STAGE = GEO::STAGE, W_BYTES = GEO::W_BYTES, SB_BYTES = GEO::SB_BYTES;
+    constexpr bool ODD = TM > 1;
+
+    extern __shared__ __align__(16) uint8_t qt_smem_raw[];
+    // 1024-byte aligned base (128-byte swizzled TMA boxes), derived from the shared
+    // array by pointer arithmetic so every access stays a shared-memory access
+    uint8_t* base = qt_smem_raw + ((1024u - (smem_u32(qt_smem_raw) & 1023u)) & 1023u);
+    const int M = p.M, N = p.N, G = p.G, S = p.S, stages = p.stages;
+    const Layout L = layout(STAGE, stages, G, TM, XG);
+    uint8_t* ring = base + L.ring;
+    uint8_t* xf = base + L.xf;
+    float4* rec = reinterpret_cast<float4*>(base + L.rec);
+    float* red = reinterpret_cast<float*>(base + L.red);
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + L.bars);
+    uint64_t* empty = full + stages;
+    volatile int* s_abort = reinterpret_cast<volatile int*>(base + L.flags);
+    volatile int* s_last = s_abort + 1;
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const long long U = p.U;
+    const int P = gridDim.x;
+    const long long u_lo = U * blockIdx.x / P, u_hi = U * (blockIdx.x + 1) / P;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(smem_u32(full + s), 1);
+            mbar_init(smem_u32(empty + s), CWARPS);
+        }
+        *s_abort = 0;
+        *s_last = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    __syncthreads();
+    // Launch overlap: the next kernel may start once every CTA got here. Weights,
+    // scales and biases are read before griddepcontrol.wait; x, the workspace and
+    // every global write come after it.
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+
+    if (warp == CWARPS) {
+        // ------------------------------ producer ------------------------------------
+        if (lane == 0) {
+            tma_prefetch_map(&tw);
+            tma_prefetch_map(&ts);
+            tma_prefetch_map(&tb);
+            uint32_t it = 0;
+            int slot = 0;
+            uint32_t phase = 0;  // parity of the empty-barrier phase to wait for
+            int rb = static_cast<int>(u_lo / S), st = static_cast<int>(u_lo % S);
+            for (long long u = u_lo; u < u_hi; ++u, ++it) {
+                if (it >= static_cast<uint32_t>(stages)) {
+                    if (*s_abort) break;
+                    if (!mbar_wait_bounded(smem_u32(empty + slot), phase, kSpinLimit)) {
+                        atomicCAS(p.err, 0, kErrTimeout);
+                        *s_abort = 1;
+                        break;
+                    }
+                }
+                const uint32_t dst = smem_u32(ring + slot * STAGE);
+                const uint32_t bar = smem_u32(full + slot);
+                mbar_arrive_expect_tx(bar, STAGE);
+#pragma unroll
+                for (int b = 0; b < GEO::BOXES; ++b)
+                    tma_load_2d(dst + b * (BR * 128), &tw, bar, (st * SG * WPG) + b * 32, rb * BR);
+                tma_load_2d(dst + W_BYTES, &ts, bar, st * SG, rb * BR);
+                tma_load_2d(dst + W_BYTES + SB_BYTES, &tb, bar, st * SG, rb * BR);
+                if (++slot == stages) {
+                    slot = 0;
+                    if (it >= static_cast<uint32_t>(stages)) phase ^= 1u;  // not after the first pass
+                }
+                if (++st == S) {
+                    st = 0;
+                    ++rb;
+                }
+            }
+            if (*s_abort) {
+                // let the copies already issued land before the CTA can exit
+                const uint32_t n = it < static_cast<uint32_t>(stages) ? it : stages;
+                for (uint32_t j = it - n; j < it; ++j)
+                    mbar_wait_bounded(smem_u32(full + j % stages), (j / stages) & 1, kSpinLimit);
+            }
+        }
+        return;
+    }
+
+    // -------------------------------- consumers ------------------------------------
+    const int rt = warp % RT, kq = warp / RT;
+    const int r = lane >> 2, c = lane & 3;
+    const int ctid = threadIdx.x;  // 0 .. CTHREADS-1
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+
+    // x[M, K] -> f16 B fragments and records. Item i = ((g * TM + t) * 4 + c): lane
+    // c of token slot t in group g holds words c, c+4, ... of the group (the words
+    // ldmatrix gives that lane). G*TM*4 is a multiple of 32 (G % 8 == 0), so every
+    // warp runs whole iterations and the 4 lanes of an item share a warp.
+    {
+        const T* xg = static_cast<const T*>(p.x);
+        constexpr int XW = BITS == 4 ? 8 : 4;  // activations per packed word
+        constexpr int PB = (CPG * XW / 2 <= 8) ? 4 : 2;  // items with loads in flight together
+        const int total = G * TM * 4;
+        for (int i0 = ctid; i0 < total; i0 += PB * CTHREADS) {
+          uint32_t raw[PB][CPG][XW / 2];
+#pragma unroll
+          for (int b = 0; b < PB; ++b) {
+            const int i = i0 + b * CTHREADS;
+            const int cc = i & 3, t = (i >> 2) % TM, g = (i >> 2) / TM;
+#pragma unroll
+            for (int w = 0; w < CPG; ++w) {
+                const long long off = static_cast<long long>(t) * p.K + g * GS + (4 * w + cc) * XW;
+                if constexpr (BITS == 4) {
+                    uint4 q = make_uint4(0u, 0u, 0u, 0u);
+                    if (i < total && t < M) q = *reinterpret_cast<const uint4*>(xg + off);
+                    raw[b][w][0] = q.x; raw[b][w][1] = q.y; raw[b][w][2] = q.z; raw[b][w][3] = q.w;
+                } else {
+                    uint2 q = make_uint2(0u, 0u);
+                    if (i < total && t < M) q = *reinterpret_cast<const uint2*>(xg + off);
+                    raw[b][w][0] = q.x; raw[b][w][1] = q.y;
+                }
+            }
+          }
+#pragma unroll
+          for (int b = 0; b < PB; ++b) {
+            const int i = i0 + b * CTHREADS;
+            if (i >= total) break;  // warp-uniform: total and CTHREADS are multiples of 32
+            const int cc = i & 3, t = (i >> 2) % TM, g = (i >> 2) / TM;
+            float v[CPG][XW];
+            float m = 0.f;
+#pragma unroll
+            for (int w = 0; w < CPG; ++w) {
+#pragma unroll
+                for (int k = 0; k < XW / 2; ++k) {
+                    v[w][2 * k] = ET::lo(raw[b][w][k]);
+                    v[w][2 * k + 1] = ET::hi(raw[b][w][k]);
+                    m = fmaxf(m, fmaxf(fabsf(v[w][2 * k]), fabsf(v[w][2 * k + 1])));
+                }
+            }
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+            // fmaxf drops NaN, and an infinite maximum keeps e = 0: NaN and inf
+            // activations reach D unchanged and propagate to the output.
+            const int e = slice_exponent(m);
+            const float sc = pow2i(e);
+            uint32_t fr[FR];
+            float s_all = 0.f, s_even = 0.f, s_odd = 0.f;
+#pragma unroll
+            for (int w = 0; w < CPG; ++w) {
+                float y[XW];
+#pragma unroll
+                for (int k = 0; k < XW; ++k) {
+                    y[k] = v[w][k] * sc;
+                    s_all += v[w][k];
+                    if (k & 1) s_odd += y[k]; else s_even += y[k];
+                }
+                if constexpr (BITS == 4) {
+                    // operands pair nibbles (0,4) (1,5) (2,6) (3,7) of the word
+                    fr[4 * w + 0] = pack_half2(y[0], y[4]);
+                    fr[4 * w + 1] = pack_half2(y[1], y[5]);
+                    fr[4 * w + 2] = pack_half2(y[2], y[6]);
+                    fr[4 * w + 3] = pack_half2(y[3], y[7]);
+                } else {
+                    // operands pair bytes (0,2) and (1,3) of the word
+                    fr[2 * w + 0] = pack_half2(y[0], y[2]);
+                    fr[2 * w + 1] = pack_half2(y[1], y[3]);
+                }
+            }
+#pragma unroll
+            for (int o = 1; o <= 2; o <<= 1) {
+                s_all += __shfl_xor_sync(0xffffffffu, s_all, o);
+                s_even += __shfl_xor_sync(0xffffffffu, s_even, o);
+                s_odd += __shfl_xor_sync(0xffffffffu, s_odd, o);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(xf + static_cast<size_t>(g) * TM * XG);
+#pragma unroll
+            for (int f = 0; f < FR / 4; ++f)
+                dst[(f * TM + t) * 4 + cc] =
+                    make_uint4(fr[4 * f], fr[4 * f + 1], fr[4 * f + 2], fr[4 * f + 3]);
+            if (cc == 0) {
+                // 4-bit: even code positions carry offset kOffE, odd ones kOffO (per
+                // MMA slot); 8-bit: every activation meets both nibble operands.
+                const float toff = (BITS == 4) ? OFF::kOffE * s_even + OFF::kOffO * s_odd
+                                               : OFF::kOff * (s_even + s_odd);
+                rec[g * TM + t] = make_float4(s_all, toff, pow2i(-e), 0.f);
+            }
+          }
+        }
+    }
+    named_bar_sync(1, CTHREADS);
+
+    const uint32_t magic_a = opaque(EH::template Magic<BITS>::kA);
+    const uint32_t magic_b = opaque(EH::template Magic<BITS>::kB);
+    const T* biasg = static_cast<const T*>(p.bias);
+    T* og = static_cast<T*>(p.out);
+
+    // Per-lane offsets, fixed for the whole kernel. Group gi = 2kq + h of a stage:
+    //   ldmatrix row addresses (relative to the stage) of its CPG chunks,
+    constexpr int NLD = CPG > 1 ? CPG / 2 : 1;
+    uint32_t lmo[2][NLD];
+    {
+        const int row = 16 * rt + (lane & 15);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int gi = 2 * kq + h;
+            const int box = (gi * WPG) >> 5;
+            const int cbase = ((gi * WPG) & 31) >> 2;
+#pragma unroll
+            for (int j = 0; j < NLD; ++j) {
+                const int ch = cbase + 2 * j + (CPG > 1 ? (lane >> 4) : 0);
+                lmo[h][j] = box * (BR * 128) + row * 128 + ((ch ^ (row & 7)) << 4);
+            }
+        }
+    }
+    //   packed (scale, scale) / (bias, bias) words of groups 2kq, 2kq+1, rows r and r+8,
+    const int rr = 16 * rt + r;
+    const int so0 = W_BYTES + (rr * 4 + kq) * 4, so1 = so0 + 8 * 16;
+    //   the B fragments of token slot r (lanes past the last slot repeat a slot:
+    //   their MMA columns are never read),
+    const int tr = r & (TM - 1);
+    const uint8_t* xl = xf + (tr * 4 + c) * 16 + 2 * kq * TM * XG;
+    //   and the records of tokens 2c, 2c+1 (wrapped into the slots likewise).
+    const float4* rl = rec + ((2 * c) & (TM - 1)) + 2 * kq * TM;
+
+    uint32_t it = 0;
+    int slot = 0;
+    uint32_t phase = 0;  // parity of the full-barrier phase to wait for
+    long long u = u_lo;
+    while (u < u_hi) {
+        const int rb = static_cast<int>(u / S);
+        const int st0 = static_cast<int>(u % S);
+        const int st_end = static_cast<int>(st0 + (u_hi - u) < S ? st0 + (u_hi - u) : S);
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint8_t* xs = xl + static_cast<size_t>(st0) * SG * TM * XG;
+        const float4* rs = rl + st0 * SG * TM;
+
+        for (int st = st0; st < st_end; ++st, ++it) {
+            if (!*s_abort) {
+                const uint32_t fb = smem_u32(full + slot);
+                if (!mbar_try_wait(fb, phase) && !wait_slow(fb, phase)) {
+                    atomicCAS(p.err, 0, kErrTimeout);
+                    *s_abort = 1;
+                }
+            }
+            const uint8_t* stg = ring + slot * STAGE;
+            const uint32_t stg_s = smem_u32(stg);
+            const uint32_t s_r0 = *reinterpret_cast<const uint32_t*>(stg + so0);
+            const uint32_t s_r1 = *reinterpret_cast<const uint32_t*>(stg + so1);
+            const uint32_t b_r0 = *reinterpret_cast<const uint32_t*>(stg + so0 + SB_BYTES);
+            const uint32_t b_r1 = *reinterpret_cast<const uint32_t*>(stg + so1 + SB_BYTES);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                uint32_t wa[CPG], wb[CPG];
+                if constexpr (CPG == 1) {
+                    ldmatrix_x2(stg_s + lmo[h][0], wa[0], wb[0]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < NLD; ++j)
+                        ldmatrix_x4(stg_s + lmo[h][j], wa[2 * j], wb[2 * j], wa[2 * j + 1],
+                                    wb[2 * j + 1]);
+                }
+                const float s0 = h ? ET::hi(s_r0) : ET::lo(s_r0);
+                const float s1 = h ? ET::hi(s_r1) : ET::lo(s_r1);
+                const float b0 = h ? ET::hi(b_r0) : ET::lo(b_r0);
+                const float b1 = h ? ET::hi(b_r1) : ET::lo(b_r1);
+                uint32_t ta[CPG][4], tb[CPG][4];
+#pragma unroll
+                for (int w = 0; w < CPG; ++w) {
+                    EH::template extract<BITS>(wa[w], ta[w], magic_a, magic_b);
+                    EH::template extract<BITS>(wb[w], tb[w], magic_a, magic_b);
+                }
+                uint32_t X[FR];
+#pragma unroll
+                for (int f = 0; f < FR / 4; ++f) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(xs + h * TM * XG + f * TM * 64);
+                    X[4 * f + 0] = v.x; X[4 * f + 1] = v.y;
+                    X[4 * f + 2] = v.z; X[4 * f + 3] = v.w;
+                }
+                float d[4];
+#pragma unroll
+                for (int w = 0; w < CPG; ++w) {
+                    if constexpr (BITS == 4) {
+                        if (w == 0)
+                            mma16816z<__half>(d, ta[w][0], tb[w][0], ta[w][1], tb[w][1],
+                                              X[4 * w + 0], X[4 * w + 1]);
+                        else
+                            mma16816<__half>(d, ta[w][0], tb[w][0], ta[w][1], tb[w][1],
+                                             X[4 * w + 0], X[4 * w + 1]);
+                        mma16816<__half>(d, ta[w][2], tb[w][2], ta[w][3], tb[w][3], X[4 * w + 2],
+                                         X[4 * w + 3]);
+                    } else {
+                        if (w == 0)
+                            mma16816z<__half>(d, ta[w][0], tb[w][0], ta[w][1], tb[w][1],
+                                              X[2 * w + 0], X[2 * w + 0]);
+                        else
+                            mma16816<__half>(d, ta[w][0], tb[w][0], ta[w][1], tb[w][1],
+                                             X[2 * w + 0], X[2 * w + 0]);
+                        mma16816<__half>(d, ta[w][2], tb[w][2], ta[w][3], tb[w][3], X[2 * w + 1],
+                                         X[2 * w + 1]);
+                    }
+                }
+                // fold this group into tokens 2c, 2c+1 of rows r, r+8
+                const float4 q0 = rs[h * TM];
+                acc[0] = fmaf(s0 * q0.z, d[0] - q0.y, fmaf(b0, q0.x, acc[0]));
+                acc[2] = fmaf(s1 * q0.z, d[2] - q0.y, fmaf(b1, q0.x, acc[2]));
+                if constexpr (ODD) {
+                    const float4 q1 = rs[h * TM + 1];
+                    acc[1] = fmaf(s0 * q1.z, d[1] - q1.y, fmaf(b0, q1.x, acc[1]));
+                    acc[3] = fmaf(s1 * q1.z, d[3] - q1.y, fmaf(b1, q1.x, acc[3]));
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(empty + slot));
+            xs += SG * TM * XG;
+            rs += SG * TM;
+            if (++slot == stages) {
+                slot = 0;
+                phase ^= 1u;
+            }
+        }
+
+        // ---- combine the four group-interleaved warps of each row tile (fixed order)
+        named_bar_sync(1, CTHREADS);
+        if (kq > 0) {
+            float* dst = red + ((kq - 1) * RT + rt) * 4 * 32 + lane;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) dst[e * 32] = acc[e];
+        }
+        named_bar_sync(1, CTHREADS);
+        if (kq == 0) {
+#pragma unroll
+            for (int h = 1; h < KSW; ++h) {
+                const float* src = red + ((h - 1) * RT + rt) * 4 * 32 + lane;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[e] += src[e * 32];
+            }
+        }
+        const bool abort = *s_abort != 0;
+        const int row0 = rb * BR;
+        if (st0 == 0 && st_end == S) {
+            // the whole row block is this CTA's: write the outputs
+            if (kq == 0 && !abort) {
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    const int n = row0 + 16 * rt + r + 8 * hh;
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        const int t = 2 * c + q;
+                        if (t < M && n < N) {
+                            T y = ET::from_f(acc[2 * hh + q]);
+                            if (biasg) y = ET::from_f(ET::to_f(y) + ET::to_f(biasg[n]));
+                            og[static_cast<long long>(t) * N + n] = y;
+                        }
+                    }
+                }
+            }
+        } else {
+            // part of a row block: fp32 partial, then the last contributor reduces
+            const long long ub = static_cast<long long>(rb) * S;
+            const int first = owner(ub, U, P);
+            const int nc = owner(ub + S - 1, U, P) - first + 1;
+            const int ci = blockIdx.x - first;
+            float* part = p.partial + static_cast<long long>(rb) * p.maxc * M * BR;
+            if (kq == 0 && !abort) {
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    const int rw = 16 * rt + r + 8 * hh;
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        const int t = 2 * c + q;
+                        if (t < M && row0 + rw < N) part[(ci * M + t) * BR + rw] = acc[2 * hh + q];
+                    }
+                }
+                __threadfence();
+            }
+            named_bar_sync(1, CTHREADS);
+            if (ctid == 0)
+                *s_last = (!abort && atomicAdd(p.counter + rb, 1u) == static_cast<unsigned>(nc - 1));
+            named_bar_sync(1, CTHREADS);
+            if (*s_last) {
+                __threadfence();
+                const int rows_here = min(BR, N - row0);
+                for (int idx = ctid; idx < M * rows_here; idx += CTHREADS) {
+                    const int t = idx / rows_here, rw = idx % rows_here;
+                    float v = 0.f;
+                    for (int k = 0; k < nc; ++k) v += __ldcg(part + (k * M + t) * BR + rw);
+                    T y = ET::from_f(v);
+                    if (biasg) y = ET::from_f(ET::to_f(y) + ET::to_f(biasg[row0 + rw]));
+                    og[static_cast<long long>(t) * N + row0 + rw] = y;
+                }
+                if (ctid == 0) p.counter[rb] = 0u;
+            }
+        }
+        u += st_end - st0;
+    }
+}
+
+}  // namespace mlxq
