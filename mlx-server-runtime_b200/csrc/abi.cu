@@ -32,7 +32,8 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 struct DeviceInfo {
     int num_sms = 0;
-    int max_smem = 0;
+    int max_smem = 0;  // usable dynamic shared memory per CTA
+    int sm_smem = 0;   // shared memory per SM
 };
 
 // Properties of the calling thread's current device (cached per device).
@@ -65,7 +66,11 @@ int device_info(DeviceInfo* out, cudaStream_t stream) {
         if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SMs)");
         e = cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
         if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(smem)");
+        int sm_smem = 0;
+        e = cudaDeviceGetAttribute(&sm_smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(smem per SM)");
         cache[dev].max_smem = smem - 1024;  // room for the kernels' static shared memory
+        cache[dev].sm_smem = sm_smem;
         cache[dev].num_sms = sms;
     }
     *out = cache[dev];
@@ -182,7 +187,7 @@ size_t mlxq_qmm_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, 
     if (device_info(&di, nullptr)) return 0;
     mlxq::QtPlan tplan;
     if (mlxq::qmv_tma_plan(dtype, bits, group_size, static_cast<int>(M), static_cast<int>(N),
-                           static_cast<int>(K), di.num_sms, di.max_smem, &tplan))
+                           static_cast<int>(K), di.num_sms, di.max_smem, di.sm_smem, &tplan))
         return tplan.ws_bytes;
     mlxq::QmvPlan plan;
     bool ok = false;
@@ -222,7 +227,7 @@ int mlxq_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
     }
     mlxq::QtPlan tplan;
     if (mlxq::qmv_tma_plan(dtype, bits, group_size, static_cast<int>(M), static_cast<int>(N),
-                           static_cast<int>(K), di.num_sms, di.max_smem, &tplan)) {
+                           static_cast<int>(K), di.num_sms, di.max_smem, di.sm_smem, &tplan)) {
         // decode, M <= 8: TMA-fed stream-K kernel
         if (tplan.ws_bytes > 0) {
             if (!workspace || workspace_bytes < tplan.ws_bytes)

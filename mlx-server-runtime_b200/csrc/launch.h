@@ -87,7 +87,7 @@ struct QtPlan {
     size_t ws_bytes;  // workspace (tickets + partials) when a row block is shared
 };
 bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms, int max_smem,
-                  QtPlan* plan);
+                  int sm_smem, QtPlan* plan);
 cudaError_t qmv_tma_launch(int dtype, int bits, int gs, const QtPlan& plan, const void* x,
                            const uint32_t* w, const void* s, const void* b, const void* bias,
                            void* out, int M, int N, int K, void* workspace, bool overlap,

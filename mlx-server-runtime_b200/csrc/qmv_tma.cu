@@ -53,8 +53,15 @@ bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esiz
 
 }  // namespace
 
+// CTAs of this kernel meant to fit on one SM together: with 2, the shared memory
+// of a CTA is capped at half the SM's, so under launch overlap the next matmul's
+// CTAs can start streaming their weights while this one finishes.
+constexpr int kCtasPerSm = 2;
+// CTAs launched per SM (stream-K shares = kGridPerSm x SMs).
+constexpr int kGridPerSm = 1;
+
 bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms, int max_smem,
-                  QtPlan* plan) {
+                  int sm_smem, QtPlan* plan) {
     if (M < 1 || M > qt::MAXM || N < 1 || K < 1 || K % gs) return false;
     if (bits != 4 && bits != 8) return false;
     if (gs != 32 && gs != 64 && gs != 128) return false;
@@ -62,6 +69,8 @@ bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms,
     const int G = K / gs;
     if (G % qt::SG) return false;  // scale/bias rows must be whole 16-byte TMA boxes
     if (!encode_fn()) return false;
+    // the driver reserves 1 KB of shared memory per CTA
+    max_smem = std::min(max_smem, sm_smem / kCtasPerSm - 1024);
     const int TM = qt::token_slots(M);
     const int stage = stage_bytes(bits, gs);
     const int fixed = qt::layout(stage, 0, G, TM, gs * 2).total + 1024;  // + alignment slack
@@ -71,7 +80,7 @@ bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms,
     if (static_cast<size_t>(pl.RB) * 4 > kTicketBytes) return false;
     pl.S = G / qt::SG;
     pl.U = static_cast<long long>(pl.RB) * pl.S;
-    pl.P = static_cast<int>(std::min<long long>(pl.U, num_sms));
+    pl.P = static_cast<int>(std::min<long long>(pl.U, static_cast<long long>(num_sms) * kGridPerSm));
     const long long per_cta = (pl.U + pl.P - 1) / pl.P;
     int stages = std::min((max_smem - fixed) / stage, qt::MAX_STAGES);
     stages = static_cast<int>(std::min<long long>(stages, std::max<long long>(2, per_cta)));

@@ -12,13 +12,13 @@
 // finished by the last of them (atomic ticket, no waiting), which adds the fp32
 // partials in CTA order, so results are deterministic.
 //
-// Per CTA: one producer warp and 16 consumer warps.
+// Per CTA: one producer warp and 8 consumer warps.
 //   * Producer (one thread): for every unit, 2-D TMA loads of the packed
 //     weights [64 rows x 128 B] per box (128-byte swizzle) plus one box each of
 //     scales and biases [64 rows x 8 groups], into a ring of `stages` slots with
 //     full/empty mbarriers. The ring holds most of the CTA's share, so nearly
 //     all of it is requested from HBM at kernel start.
-//   * Consumers: warp (rt, kq) owns row tile rt (16 rows) and groups 2kq, 2kq+1
+//   * Consumers: warp (rt, kq) owns row tile rt (16 rows) and GPW groups, GPW*kq..,
 //     of every stage. ldmatrix reads the swizzled tiles without bank conflicts
 //     and hands lane (r, c) words c, c+4, ... of the group for rows r and r+8.
 //     Codes become exact f16 MMA operands with one LOP3 per pair (see
@@ -50,8 +50,9 @@ namespace qt {
 constexpr int BR = 64;                   // weight rows per unit
 constexpr int SG = 8;                    // quantization groups per unit (stage)
 constexpr int RT = BR / 16;              // 16-row MMA tiles per unit
-constexpr int KSW = SG / 2;              // consumer warps per row tile (2 groups each)
-constexpr int CWARPS = RT * KSW;         // 16 consumer warps
+constexpr int GPW = 4;                   // groups of a stage per consumer warp (even)
+constexpr int KSW = SG / GPW;            // consumer warps per row tile
+constexpr int CWARPS = RT * KSW;         // consumer warps
 constexpr int CTHREADS = CWARPS * 32;
 constexpr int THREADS = CTHREADS + 32;   // + producer warp
 constexpr int MAXM = 8;                  // tokens per launch
@@ -337,15 +338,15 @@ __global__ void __launch_bounds__(qt::THREADS, 1)
     const T* biasg = static_cast<const T*>(p.bias);
     T* og = static_cast<T*>(p.out);
 
-    // Per-lane offsets, fixed for the whole kernel. Group gi = 2kq + h of a stage:
+    // Per-lane offsets, fixed for the whole kernel. Group gi = GPW*kq + h of a stage:
     //   ldmatrix row addresses (relative to the stage) of its CPG chunks,
     constexpr int NLD = CPG > 1 ? CPG / 2 : 1;
-    uint32_t lmo[2][NLD];
+    uint32_t lmo[GPW][NLD];
     {
         const int row = 16 * rt + (lane & 15);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int gi = 2 * kq + h;
+        for (int h = 0; h < GPW; ++h) {
+            const int gi = GPW * kq + h;
             const int box = (gi * WPG) >> 5;
             const int cbase = ((gi * WPG) & 31) >> 2;
 #pragma unroll
@@ -355,15 +356,15 @@ __global__ void __launch_bounds__(qt::THREADS, 1)
             }
         }
     }
-    //   packed (scale, scale) / (bias, bias) words of groups 2kq, 2kq+1, rows r and r+8,
+    //   packed (scale, scale) / (bias, bias) words of the warp's group pairs, rows r, r+8,
     const int rr = 16 * rt + r;
-    const int so0 = W_BYTES + (rr * 4 + kq) * 4, so1 = so0 + 8 * 16;
+    const int so0 = W_BYTES + (rr * 4 + GPW / 2 * kq) * 4, so1 = so0 + 8 * 16;
     //   the B fragments of token slot r (lanes past the last slot repeat a slot:
     //   their MMA columns are never read),
     const int tr = r & (TM - 1);
-    const uint8_t* xl = xf + (tr * 4 + c) * 16 + 2 * kq * TM * XG;
+    const uint8_t* xl = xf + (tr * 4 + c) * 16 + GPW * kq * TM * XG;
     //   and the records of tokens 2c, 2c+1 (wrapped into the slots likewise).
-    const float4* rl = rec + ((2 * c) & (TM - 1)) + 2 * kq * TM;
+    const float4* rl = rec + ((2 * c) & (TM - 1)) + GPW * kq * TM;
 
     uint32_t it = 0;
     int slot = 0;
@@ -387,12 +388,16 @@ __global__ void __launch_bounds__(qt::THREADS, 1)
             }
             const uint8_t* stg = ring + slot * STAGE;
             const uint32_t stg_s = smem_u32(stg);
-            const uint32_t s_r0 = *reinterpret_cast<const uint32_t*>(stg + so0);
-            const uint32_t s_r1 = *reinterpret_cast<const uint32_t*>(stg + so1);
-            const uint32_t b_r0 = *reinterpret_cast<const uint32_t*>(stg + so0 + SB_BYTES);
-            const uint32_t b_r1 = *reinterpret_cast<const uint32_t*>(stg + so1 + SB_BYTES);
+            uint32_t s_r0[GPW / 2], s_r1[GPW / 2], b_r0[GPW / 2], b_r1[GPW / 2];
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
+            for (int q = 0; q < GPW / 2; ++q) {
+                s_r0[q] = *reinterpret_cast<const uint32_t*>(stg + so0 + 4 * q);
+                s_r1[q] = *reinterpret_cast<const uint32_t*>(stg + so1 + 4 * q);
+                b_r0[q] = *reinterpret_cast<const uint32_t*>(stg + so0 + 4 * q + SB_BYTES);
+                b_r1[q] = *reinterpret_cast<const uint32_t*>(stg + so1 + 4 * q + SB_BYTES);
+            }
+#pragma unroll
+            for (int h = 0; h < GPW; ++h) {
                 uint32_t wa[CPG], wb[CPG];
                 if constexpr (CPG == 1) {
                     ldmatrix_x2(stg_s + lmo[h][0], wa[0], wb[0]);
@@ -402,10 +407,11 @@ __global__ void __launch_bounds__(qt::THREADS, 1)
                         ldmatrix_x4(stg_s + lmo[h][j], wa[2 * j], wb[2 * j], wa[2 * j + 1],
                                     wb[2 * j + 1]);
                 }
-                const float s0 = h ? ET::hi(s_r0) : ET::lo(s_r0);
-                const float s1 = h ? ET::hi(s_r1) : ET::lo(s_r1);
-                const float b0 = h ? ET::hi(b_r0) : ET::lo(b_r0);
-                const float b1 = h ? ET::hi(b_r1) : ET::lo(b_r1);
+                const int hq = h >> 1;
+                const float s0 = (h & 1) ? ET::hi(s_r0[hq]) : ET::lo(s_r0[hq]);
+                const float s1 = (h & 1) ? ET::hi(s_r1[hq]) : ET::lo(s_r1[hq]);
+                const float b0 = (h & 1) ? ET::hi(b_r0[hq]) : ET::lo(b_r0[hq]);
+                const float b1 = (h & 1) ? ET::hi(b_r1[hq]) : ET::lo(b_r1[hq]);
                 uint32_t ta[CPG][4], tb[CPG][4];
 #pragma unroll
                 for (int w = 0; w < CPG; ++w) {
