@@ -7,25 +7,28 @@
 // for M > 32 tokens (MLX's quantized_matmul as QuantizedLinear calls it during
 // prefill, qwen2.py:58-61,123-134 of the reference).
 //
-// CTA tile: BM = 128 tokens x BN = 256 weight rows, K blocks of BK = 64, a
-// 3-stage pipeline, 256 threads:
-//   * x tiles [128 x 64] bf16 arrive by 16-byte cp.async into the canonical
-//     K-major 128-byte-swizzled layout (8-row x 128-byte atoms, chunk c of row r
-//     stored at chunk c ^ (r % 8)).
-//   * Packed weight rows arrive by cp.async; thread t dequantizes row t of the
-//     block: codes become exact 16-bit values with byte permutes and a magic
-//     exponent (no integer-to-float conversion), then w = scale*q + bias with one
-//     packed FMA (one rounding, like MLX's dequantize-in-kernel), stored in the
-//     same swizzled layout.
-//   * One thread issues tcgen05.mma (M=128, N=256, K=16) x 4 per K block from
-//     shared-memory descriptors into a 128 x 256 fp32 accumulator in tensor
-//     memory, then tcgen05.commit arrives on the stage's mbarrier; a stage is
-//     refilled only after that barrier shows its MMAs finished.
-//   * Epilogue: tcgen05.ld (32 lanes x 32 columns per warp) -> bf16/f16 ->
-//     global, optional per-row bias added as a second rounding.
+// Output tiles BM = 128 tokens x BN = 256 weight rows, K blocks of BK = 64; one
+// persistent CTA per SM with specialized warps (see qgemm_kernel):
+//   * TMA brings the activation tile in the canonical K-major 128-byte-swizzled
+//     layout (8-row x 128-byte atoms, chunk c of row r at chunk c ^ (r % 8)) that
+//     the MMA reads directly, and the raw packed codes of the 256 weight rows.
+//   * One thread per weight row dequantizes: codes become exact 16-bit values with
+//     byte permutes and a magic exponent (no integer-to-float conversion), then
+//     w = scale*q + bias with one packed FMA (one rounding, like MLX's
+//     dequantize-in-kernel), stored in the same swizzled layout.
+//   * One thread issues tcgen05.mma (M=128, N=256, K=16) from shared-memory
+//     descriptors into one of two 128 x 256 fp32 accumulators in tensor memory;
+//     tcgen05.commit hands each stage and B tile back to its producer.
+//   * Epilogue warps read the finished accumulator (tcgen05.ld, 32 lanes x 32
+//     columns) while the other one fills: bf16/f16, optional per-row bias added
+//     as a second rounding.
 // Every mbarrier wait is bounded: on timeout the CTA records an error in
-// g_qgemm_error, stops issuing work, waits (bounded) for what is in flight,
-// frees its tensor memory and returns.
+// g_qgemm_error, its roles stop issuing work, the loads and MMAs in flight are
+// waited for (bounded), tensor memory is freed and the kernel returns.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "common.cuh"
 #include "launch.h"
 #include "sm100.cuh"
@@ -35,18 +38,26 @@ namespace mlxq {
 __device__ int g_qgemm_error;  // 0, or the first error code a kernel recorded
 
 namespace qg {
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 3, THREADS = 256;
+constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int BSTAGES = 3;                      // dequantized B tiles in flight
+constexpr int NDEQ = 8, NEPI = 4;               // dequant / epilogue warps
+constexpr int WARP_TMA = 0, WARP_MMA = 1, WARP_EPI0 = 2, WARP_DEQ0 = WARP_EPI0 + NEPI;
+constexpr int THREADS = (WARP_DEQ0 + NDEQ) * 32;  // 448: one dequant thread per weight row
+static_assert(NDEQ * 32 == BN, "one dequant thread per weight row of the tile");
 constexpr int A_BYTES = BM * BK * 2;  // 16 KB
 constexpr int B_BYTES = BN * BK * 2;  // 32 KB
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kSpinLimit = 1u << 20;
+constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
+constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr int kErrTimeout = 1;
 template <int BITS>
-constexpr int raw_row_bytes() { return BK * BITS / 8; }  // 32 (4-bit) / 64 (8-bit)
+constexpr int raw_bytes() { return BN * BK * BITS / 8; }  // 8 KB (4-bit) / 16 KB (8-bit)
 template <int BITS>
-constexpr int stage_bytes() { return A_BYTES + B_BYTES + BN * raw_row_bytes<BITS>(); }
+constexpr int load_stages() { return BITS == 4 ? 4 : 3; }
 template <int BITS>
-constexpr int smem_bytes() { return STAGES * stage_bytes<BITS>() + 1024 + 128; }
+constexpr int smem_bytes() {
+    return load_stages<BITS>() * (A_BYTES + raw_bytes<BITS>()) + BSTAGES * B_BYTES +
+           (2 * load_stages<BITS>() + 2 * BSTAGES + 5) * 8 + 16 + 1024;
+}
 }  // namespace qg
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart.
@@ -190,40 +201,70 @@ __device__ __forceinline__ uint4 dequant_chunk(const uint32_t* wds, uint32_t s2,
     return r;
 }
 
+// Persistent, warp-specialized prefill kernel. One CTA per SM walks its share of
+// the [BM x BN] output tiles; per K block of 64:
+//   warp 0  (TMA)      x tile [128 x 64] (128-byte swizzle, the MMA's A layout)
+//                      and the raw packed weights [256 rows x 64 codes] of the
+//                      tile into a ring of load stages;
+//   warps 6-13 (dequant, thread = weight row) turn the raw codes of their row
+//                      into bf16/f16 values w = scale*q + bias in a ring of
+//                      B tiles (the MMA's K-major, 128-byte swizzled layout);
+//   warp 1  (MMA)      one thread issues tcgen05.mma M=128 N=256 K=16 x 4 into
+//                      one of two 256-column TMEM accumulators and commits the
+//                      stage and the B tile back to their producers;
+//   warps 2-5 (epilogue) drain the other accumulator with tcgen05.ld while the
+//                      next tile accumulates, add the optional bias as a second
+//                      rounding, and store.
 template <typename T, int BITS, int GS>
-__global__ void __launch_bounds__(qg::THREADS, 1) qgemm_kernel(const QgemmParams p) {
+__global__ void __launch_bounds__(qg::THREADS, 1)
+    qgemm_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw,
+                 const QgemmParams p) {
     using namespace qg;
-    constexpr int SB = stage_bytes<BITS>();
-    constexpr int RAWB = raw_row_bytes<BITS>();
-    constexpr int WPR = RAWB / 4;  // packed words per row per K block
+    constexpr int LS = load_stages<BITS>();
+    constexpr int RAW = raw_bytes<BITS>();
+    constexpr int LSB = A_BYTES + RAW;    // bytes of one load stage
+    constexpr int WPR = BK * BITS / 32;   // packed words per row per K block
     constexpr uint32_t IDESC = qgemm_idesc<T>();
 
     extern __shared__ uint8_t qg_smem_raw[];
-    const uint32_t raw_base = smem_u32(qg_smem_raw);
-    const uint32_t base = (raw_base + 1023u) & ~1023u;
-    uint8_t* smem = qg_smem_raw + (base - raw_base);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * SB);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + STAGES);
+    uint8_t* smem = qg_smem_raw + ((1024u - (smem_u32(qg_smem_raw) & 1023u)) & 1023u);
+    uint8_t* bbuf = smem + LS * LSB;
+    uint64_t* load_full = reinterpret_cast<uint64_t*>(bbuf + BSTAGES * B_BYTES);
+    uint64_t* load_empty = load_full + LS;
+    uint64_t* b_full = load_empty + LS;
+    uint64_t* b_empty = b_full + BSTAGES;
+    uint64_t* acc_full = b_empty + BSTAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* mma_done = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
     const int M = p.M, N = p.N, K = p.K;
-    const long long kw = static_cast<long long>(K) * BITS / 32;
     const int KB = K / BK;
-    const int G = K / GS;
-    const T* xg = static_cast<const T*>(p.x);
-    const T* sg = static_cast<const T*>(p.s);
-    const T* bg = static_cast<const T*>(p.b);
+    const int MB = (M + BM - 1) / BM, NB = (N + BN - 1) / BN;
+    const int tiles = MB * NB;
 
-    if (warp == 0) {
+    if (warp == WARP_MMA) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
                          smem_u32(tmem_slot)),
                      "r"(kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
     }
     if (tid == 0) {
-        for (int s = 0; s < STAGES; ++s) mbar_init(smem_u32(bars + s), 1);
+        for (int s = 0; s < LS; ++s) {
+            mbar_init(smem_u32(load_full + s), 1);
+            mbar_init(smem_u32(load_empty + s), NDEQ + 1);
+        }
+        for (int b = 0; b < BSTAGES; ++b) {
+            mbar_init(smem_u32(b_full + b), NDEQ);
+            mbar_init(smem_u32(b_empty + b), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(smem_u32(acc_full + a), 1);
+            mbar_init(smem_u32(acc_empty + a), NEPI);
+        }
+        mbar_init(smem_u32(mma_done), 1);
         *s_abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
@@ -232,173 +273,236 @@ __global__ void __launch_bounds__(qg::THREADS, 1) qgemm_kernel(const QgemmParams
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
     const uint32_t tmem = *tmem_slot;
 
-    // this thread's weight row
-    const int wn = n0 + tid;
-    const bool wrow_ok = wn < N;
-    const uint32_t* wrow = p.w + (wrow_ok ? static_cast<long long>(wn) * kw : 0);
-
-    auto load_stage = [&](int kb, int s) {
-        uint8_t* st = smem + s * SB;
-        // x tile: 1024 16-byte units, 4 per thread, swizzled
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int u = tid + THREADS * i;
-            const int row = u >> 3, c = u & 7;
-            const int tok = m0 + row;
-            const bool ok = tok < M;
-            const T* src = ok ? xg + static_cast<long long>(tok) * K + kb * BK + c * 8 : xg;
-            cp_async16(st + (row >> 3) * 1024 + (row & 7) * 128 + ((c ^ (row & 7)) << 4), src,
-                       ok ? 16 : 0);
-        }
-        // packed weights of this thread's row
-        uint8_t* rdst = st + A_BYTES + B_BYTES + tid * RAWB;
-        const uint32_t* rsrc = wrow + static_cast<long long>(kb) * WPR;
-#pragma unroll
-        for (int j = 0; j < RAWB / 16; ++j)
-            cp_async16(rdst + 16 * j, wrow_ok ? rsrc + 4 * j : p.w, wrow_ok ? 16 : 0);
-        cp_async_commit();
+    // bounded wait shared by every role: false (and the CTA marked aborted) on timeout
+    auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+        if (*s_abort) return false;
+        if (mbar_try_wait(smem_u32(bar), parity)) return true;
+        if (mbar_wait_bounded(smem_u32(bar), parity, kSpinLimit)) return true;
+        atomicCAS(&g_qgemm_error, 0, kErrTimeout);
+        *s_abort = 1;
+        return false;
     };
 
-    // scales / biases of this thread's row for K block kb (one or two groups)
-    auto load_sb = [&](int kb, uint32_t (&s2)[2], uint32_t (&b2)[2]) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int g = (kb * BK + h * 32) / GS;
-            T sv = T(0.0f), bv = T(0.0f);
-            if (wrow_ok && kb < KB) {
-                sv = sg[static_cast<long long>(wn) * G + g];
-                bv = bg[static_cast<long long>(wn) * G + g];
-            }
-            s2[h] = splat(sv);
-            b2[h] = splat(bv);
-        }
-    };
-
-#pragma unroll
-    for (int i = 0; i < STAGES - 1; ++i) {
-        if (i < KB) load_stage(i, i);
-        else cp_async_commit();
-    }
-    uint32_t s2[2], b2[2];
-    load_sb(0, s2, b2);
-    const uint32_t mlo = opaque(Pair<T>::kMagicLo), mhi = opaque(Pair<T>::kMagicHi);
-    bool aborted = false;
-
-    for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % STAGES;
-        uint8_t* st = smem + s * SB;
-        uint32_t ns2[2], nb2[2];
-        load_sb(kb + 1, ns2, nb2);  // next block's scales, hidden behind this block
-
-        cp_async_wait<STAGES - 2>();
-        // dequantize this thread's row into the swizzled B tile
-        {
-            uint32_t raw[WPR];
-            const uint4* rsrc = reinterpret_cast<const uint4*>(st + A_BYTES + B_BYTES + tid * RAWB);
-#pragma unroll
-            for (int j = 0; j < WPR / 4; ++j) {
-                const uint4 v = rsrc[j];
-                raw[4 * j] = v.x; raw[4 * j + 1] = v.y; raw[4 * j + 2] = v.z; raw[4 * j + 3] = v.w;
-            }
-            uint8_t* bdst = st + A_BYTES + (tid >> 3) * 1024 + (tid & 7) * 128;
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                const int h = (c * 8 >= 32) ? 1 : 0;  // which half of the block (group for g32)
-                const uint4 v = dequant_chunk<T, BITS>(&raw[c * (BITS == 4 ? 1 : 2)], s2[h], b2[h],
-                                                      mlo, mhi);
-                *reinterpret_cast<uint4*>(bdst + ((c ^ (tid & 7)) << 4)) = v;
-            }
-        }
-        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-        asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
-        __syncthreads();
-        if (*s_abort) {
-            aborted = true;
-            break;
-        }
-        if (tid == 0) {
-            asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-            const uint64_t adesc = sw128_kmajor_desc(smem_u32(st));
-            const uint64_t bdesc = sw128_kmajor_desc(smem_u32(st + A_BYTES));
-#pragma unroll
-            for (int j = 0; j < BK / 16; ++j)  // advance 32 bytes (16 elements) per step
-                umma_f16(tmem, adesc + 2 * j, bdesc + 2 * j, IDESC, (kb > 0 || j > 0) ? 1u : 0u);
-            umma_commit(smem_u32(bars + s));
-        }
-        // refill the stage MMA(kb-1) used with K block kb + STAGES - 1
-        if (kb + STAGES - 1 < KB) {
-            if (kb >= 1) {
-                const int ps = (kb - 1) % STAGES;
-                if (!mbar_wait_bounded(smem_u32(bars + ps), ((kb - 1) / STAGES) & 1, kSpinLimit)) {
-                    *s_abort = 1;
-                    atomicCAS(&g_qgemm_error, 0, kErrTimeout);
+    if (warp == WARP_TMA) {
+        // ------------------------------ loads -------------------------------------
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&tx)) : "memory");
+            asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&tw)) : "memory");
+            uint32_t li = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                const int mb = t % MB, nb = t / MB;
+                for (int kb = 0; kb < KB; ++kb, ++li) {
+                    const int s = li % LS;
+                    if (li >= LS && !wait(load_empty + s, (li / LS - 1) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t dst = smem_u32(smem + s * LSB);
+                    const uint32_t bar = smem_u32(load_full + s);
+                    mbar_arrive_expect_tx(bar, LSB);
+                    tma_load_2d(dst, &tx, bar, kb * BK, mb * BM);
+                    tma_load_2d(dst + A_BYTES, &tw, bar, kb * WPR, nb * BN);
                 }
             }
-            load_stage(kb + STAGES - 1, (kb + STAGES - 1) % STAGES);
-        } else {
-            cp_async_commit();
+            if (!ok) {
+                // let the copies already issued land before the CTA can exit
+                const uint32_t n = li < static_cast<uint32_t>(LS) ? li : LS;
+                for (uint32_t j = li - n; j < li; ++j)
+                    mbar_wait_bounded(smem_u32(load_full + j % LS), (j / LS) & 1, kSpinLimit);
+            }
         }
-        s2[0] = ns2[0]; s2[1] = ns2[1];
-        b2[0] = nb2[0]; b2[1] = nb2[1];
-    }
-
-    // wait for the last MMA, then read the accumulator out of tensor memory
-    bool done = !aborted && KB > 0;
-    if (done) {
-        const int ls = (KB - 1) % STAGES;
-        if (!mbar_wait_bounded(smem_u32(bars + ls), ((KB - 1) / STAGES) & 1, kSpinLimit)) {
-            atomicCAS(&g_qgemm_error, 0, kErrTimeout);
-            done = false;
+    } else if (warp == WARP_MMA) {
+        // ------------------------------ MMA issue ---------------------------------
+        if (lane == 0) {
+            uint32_t li = 0, bi = 0, ai = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++ai) {
+                const uint32_t a = ai & 1;
+                if (ai >= 2 && !wait(acc_empty + a, (ai / 2 - 1) & 1)) {
+                    ok = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+                for (int kb = 0; kb < KB; ++kb, ++li, ++bi) {
+                    const int s = li % LS, b = bi % BSTAGES;
+                    if (!wait(load_full + s, (li / LS) & 1) || !wait(b_full + b, (bi / BSTAGES) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+                    const uint64_t adesc = sw128_kmajor_desc(smem_u32(smem + s * LSB));
+                    const uint64_t bdesc = sw128_kmajor_desc(smem_u32(bbuf + b * B_BYTES));
+#pragma unroll
+                    for (int j = 0; j < BK / 16; ++j)  // 32 bytes (16 elements) per step
+                        umma_f16(tmem + a * BN, adesc + 2 * j, bdesc + 2 * j, IDESC,
+                                 (kb > 0 || j > 0) ? 1u : 0u);
+                    umma_commit(smem_u32(load_empty + s));
+                    umma_commit(smem_u32(b_empty + b));
+                }
+                if (ok) umma_commit(smem_u32(acc_full + a));
+            }
+            // every MMA issued so far has finished before tensor memory is freed
+            umma_commit(smem_u32(mma_done));
+            mbar_wait_bounded(smem_u32(mma_done), 0, kSpinLimit);
         }
-    }
-    cp_async_wait<0>();
-    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-    done = __syncthreads_and(done ? 1 : 0) != 0;
-    if (done) {
-        const int quarter = warp & 3, half = warp >> 2;
-        const int tok = m0 + quarter * 32 + lane;
+    } else if (warp >= WARP_DEQ0) {
+        // ------------------------------ dequantize ---------------------------------
+        const int d = tid - WARP_DEQ0 * 32;  // weight row within the tile
+        const int G = K / GS;
+        const T* sg = static_cast<const T*>(p.s);
+        const T* bg = static_cast<const T*>(p.b);
+        const uint32_t mlo = opaque(Pair<T>::kMagicLo), mhi = opaque(Pair<T>::kMagicHi);
+        // packed (value, value) scale and bias of the two 32-wide halves of block kb
+        auto load_sb = [&](int n, int kb, uint32_t (&s2)[2], uint32_t (&b2)[2]) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int g = (kb * BK + h * 32) / GS;
+                T sv = T(0.0f), bv = T(0.0f);
+                if (n < N) {
+                    sv = sg[static_cast<long long>(n) * G + g];
+                    bv = bg[static_cast<long long>(n) * G + g];
+                }
+                s2[h] = splat(sv);
+                b2[h] = splat(bv);
+            }
+        };
+        uint32_t li = 0, bi = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            const int n = (t / MB) * BN + d;
+            uint32_t s2[2], b2[2];
+            load_sb(n, 0, s2, b2);
+            for (int kb = 0; kb < KB; ++kb, ++li, ++bi) {
+                const int s = li % LS, b = bi % BSTAGES;
+                uint32_t ns2[2], nb2[2];
+                load_sb(n, kb + 1 < KB ? kb + 1 : kb, ns2, nb2);  // next block, hidden behind this one
+                if (!wait(load_full + s, (li / LS) & 1) ||
+                    (bi >= BSTAGES && !wait(b_empty + b, (bi / BSTAGES - 1) & 1))) {
+                    ok = false;
+                    break;
+                }
+                // raw row d of the stage (TMA 32-/64-byte swizzle: 16-byte chunk c of
+                // row d sits at chunk c ^ (d >> 2 & 1) / c ^ (d >> 1 & 3))
+                uint32_t raw[WPR];
+                const uint8_t* rrow = smem + s * LSB + A_BYTES + d * (WPR * 4);
+#pragma unroll
+                for (int c = 0; c < WPR / 4; ++c) {
+                    const int pc = (BITS == 4) ? (c ^ ((d >> 2) & 1)) : (c ^ ((d >> 1) & 3));
+                    const uint4 v = *reinterpret_cast<const uint4*>(rrow + pc * 16);
+                    raw[4 * c] = v.x; raw[4 * c + 1] = v.y; raw[4 * c + 2] = v.z; raw[4 * c + 3] = v.w;
+                }
+                uint8_t* bdst = bbuf + b * B_BYTES + (d >> 3) * 1024 + (d & 7) * 128;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const int h = (c * 8 >= 32) ? 1 : 0;
+                    const uint4 v = dequant_chunk<T, BITS>(&raw[c * (BITS == 4 ? 1 : 2)], s2[h], b2[h],
+                                                          mlo, mhi);
+                    *reinterpret_cast<uint4*>(bdst + ((c ^ (d & 7)) << 4)) = v;
+                }
+                asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(smem_u32(b_full + b));
+                    mbar_arrive(smem_u32(load_empty + s));
+                }
+                s2[0] = ns2[0]; s2[1] = ns2[1];
+                b2[0] = nb2[0]; b2[1] = nb2[1];
+            }
+        }
+    } else {
+        // ------------------------------ epilogue -----------------------------------
+        const int quarter = warp & 3;  // TMEM lanes this warp may read
         T* og = static_cast<T*>(p.out);
         const T* biasg = static_cast<const T*>(p.bias);
+        uint32_t ai = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++ai) {
+            const uint32_t a = ai & 1;
+            if (!wait(acc_full + a, (ai / 2) & 1)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+            const int mb = t % MB, nb = t / MB;
+            const int tok = mb * BM + quarter * 32 + lane;
 #pragma unroll 1
-        for (int i = 0; i < 4; ++i) {
-            const int col = half * 128 + i * 32;
-            uint32_t r[32];
-            tmem_ld32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + col, r);
-            const int n = n0 + col;
-            if (tok < M && n < N) {
-                T y[32];
+            for (int i = 0; i < BN / 32; ++i) {
+                uint32_t r[32];
+                tmem_ld32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN + i * 32, r);
+                const int n = nb * BN + i * 32;
+                if (tok < M && n < N) {
+                    // round once, add the bias as a second rounding, pack pairs
+                    uint32_t pk[16];
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    y[e] = Elem<T>::from_f(__uint_as_float(r[e]));
-                    if (biasg && n + e < N)
-                        y[e] = Elem<T>::from_f(Elem<T>::to_f(y[e]) + Elem<T>::to_f(biasg[n + e]));
-                }
-                T* dst = og + static_cast<long long>(tok) * N + n;
-                if ((N & 7) == 0 && n + 32 <= N) {
+                    for (int e = 0; e < 32; ++e) {
+                        T y = Elem<T>::from_f(__uint_as_float(r[e]));
+                        if (biasg && n + e < N)
+                            y = Elem<T>::from_f(Elem<T>::to_f(y) + Elem<T>::to_f(biasg[n + e]));
+                        const uint32_t bits = *reinterpret_cast<const uint16_t*>(&y);
+                        pk[e >> 1] = (e & 1) ? (pk[e >> 1] | (bits << 16)) : bits;
+                    }
+                    T* dst = og + static_cast<long long>(tok) * N + n;
+                    if ((N & 7) == 0 && n + 32 <= N) {
 #pragma unroll
-                    for (int v = 0; v < 4; ++v)
-                        reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(y)[v];
-                } else {
-                    for (int e = 0; e < 32 && n + e < N; ++e) dst[e] = y[e];
+                        for (int v = 0; v < 4; ++v)
+                            reinterpret_cast<uint4*>(dst)[v] =
+                                make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+                    } else {
+                        uint16_t* d16 = reinterpret_cast<uint16_t*>(dst);
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            if (n + e < N) d16[e] = static_cast<uint16_t>(pk[e >> 1] >> ((e & 1) * 16));
+                    }
                 }
             }
+            asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(acc_empty + a));
         }
-    } else if (!aborted) {
-        // nothing to read (K == 0 is rejected on the host) or the last wait timed out
     }
+
     asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
     __syncthreads();
-    if (warp == 0) {
+    if (warp == WARP_MMA) {
+        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem),
                      "r"(kTmemCols));
     }
 }
+
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 qg_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+bool qg_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esize,
+            unsigned long long cols, unsigned long long rows, unsigned box_cols, unsigned box_rows,
+            CUtensorMapSwizzle swz) {
+    auto fn = qg_encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * static_cast<cuuint64_t>(esize)};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace
 
 template <typename T, int BITS, int GS>
 static cudaError_t qgemm_launch_t(const QgemmParams& p, cudaStream_t st) {
     auto kern = qgemm_kernel<T, BITS, GS>;
     constexpr int smem = qg::smem_bytes<BITS>();
     static int configured[64] = {0};
+    static int num_sms[64] = {0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -406,10 +510,21 @@ static cudaError_t qgemm_launch_t(const QgemmParams& p, cudaStream_t st) {
     if (!configured[dev]) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
+        e = cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
         configured[dev] = 1;
     }
-    dim3 grid((p.M + qg::BM - 1) / qg::BM, (p.N + qg::BN - 1) / qg::BN, 1);
-    kern<<<grid, qg::THREADS, smem, st>>>(p);
+    CUtensorMap tx, tw;
+    const unsigned long long kw = static_cast<unsigned long long>(p.K) * BITS / 32;
+    if (!qg_map(&tx, p.x, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, p.K, p.M, qg::BK, qg::BM,
+                CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !qg_map(&tw, p.w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, kw, p.N, qg::BK * BITS / 32, qg::BN,
+                BITS == 4 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
+        return cudaErrorInvalidValue;
+    const long long tiles = static_cast<long long>((p.M + qg::BM - 1) / qg::BM) *
+                            ((p.N + qg::BN - 1) / qg::BN);
+    const int grid = static_cast<int>(tiles < num_sms[dev] ? tiles : num_sms[dev]);
+    kern<<<grid, qg::THREADS, smem, st>>>(tx, tw, p);
     return cudaGetLastError();
 }
 
