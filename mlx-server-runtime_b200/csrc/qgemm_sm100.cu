@@ -41,14 +41,17 @@ namespace qg {
 constexpr int BM = 128, BN = 256, BK = 64;
 constexpr int BSTAGES = 3;                      // dequantized B tiles in flight
 constexpr int NDEQ = 8, NEPI = 4;               // dequant / epilogue warps
+constexpr int DPR = NDEQ * 32 / BN;             // dequant threads per weight row
 constexpr int WARP_TMA = 0, WARP_MMA = 1, WARP_EPI0 = 2, WARP_DEQ0 = WARP_EPI0 + NEPI;
-constexpr int THREADS = (WARP_DEQ0 + NDEQ) * 32;  // 448: one dequant thread per weight row
-static_assert(NDEQ * 32 == BN, "one dequant thread per weight row of the tile");
+constexpr int THREADS = (WARP_DEQ0 + NDEQ) * 32;
+static_assert(DPR == 1 || DPR == 2, "one or two dequant threads per weight row");
 constexpr int A_BYTES = BM * BK * 2;  // 16 KB
 constexpr int B_BYTES = BN * BK * 2;  // 32 KB
 constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
 constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr int kErrTimeout = 1;
+// suspending barrier waits: up to kParkLimit waits of about kParkNs each (~4 s)
+constexpr uint32_t kParkNs = 2000, kParkLimit = 1u << 21;
 template <int BITS>
 constexpr int raw_bytes() { return BN * BK * BITS / 8; }  // 8 KB (4-bit) / 16 KB (8-bit)
 template <int BITS>
@@ -274,10 +277,10 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
     const uint32_t tmem = *tmem_slot;
 
     // bounded wait shared by every role: false (and the CTA marked aborted) on timeout
+    // (a suspending wait: the hardware parks the thread until the phase completes)
     auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
         if (*s_abort) return false;
-        if (mbar_try_wait(smem_u32(bar), parity)) return true;
-        if (mbar_wait_bounded(smem_u32(bar), parity, kSpinLimit)) return true;
+        if (mbar_wait_park(smem_u32(bar), parity, kParkLimit, kParkNs)) return true;
         atomicCAS(&g_qgemm_error, 0, kErrTimeout);
         *s_abort = 1;
         return false;
@@ -326,7 +329,8 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
                 asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
                 for (int kb = 0; kb < KB; ++kb, ++li, ++bi) {
                     const int s = li % LS, b = bi % BSTAGES;
-                    if (!wait(load_full + s, (li / LS) & 1) || !wait(b_full + b, (bi / BSTAGES) & 1)) {
+                    if (!wait(load_full + s, (li / LS) & 1) ||
+                        !wait(b_full + b, (bi / BSTAGES) & 1)) {
                         ok = false;
                         break;
                     }
@@ -348,7 +352,9 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
         }
     } else if (warp >= WARP_DEQ0) {
         // ------------------------------ dequantize ---------------------------------
-        const int d = tid - WARP_DEQ0 * 32;  // weight row within the tile
+        const int dq = tid - WARP_DEQ0 * 32;
+        const int d = dq % BN;   // weight row within the tile
+        const int hh = dq / BN;  // which part of the row's 64 codes this thread converts
         const int G = K / GS;
         const T* sg = static_cast<const T*>(p.s);
         const T* bg = static_cast<const T*>(p.b);
@@ -367,16 +373,64 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
                 b2[h] = splat(bv);
             }
         };
+        // Scales and biases by 16-byte chunks of 8 groups (when rows are 16-byte
+        // aligned): `cur` holds the chunk in use, `nxt` the following one of this
+        // CTA's (tile, chunk) sequence, loaded a whole chunk (4-16 K blocks) early.
+        const bool vec = (G % 8) == 0;
+        const int nch = G / 8;
+        auto load_chunk = [&](int tt, int cc, uint4& sv, uint4& bv) {
+            const int n = (tt / MB) * BN + d;
+            sv = make_uint4(0u, 0u, 0u, 0u);
+            bv = sv;
+            if (tt < tiles && n < N) {
+                const long long off = static_cast<long long>(n) * G + cc * 8;
+                sv = *reinterpret_cast<const uint4*>(sg + off);
+                bv = *reinterpret_cast<const uint4*>(bg + off);
+            }
+        };
+        uint4 sc = make_uint4(0u, 0u, 0u, 0u), bc = sc, sn = sc, bn = sc;
+        int cur_t = blockIdx.x, cur_c = 0, tn = blockIdx.x, cn = 0;
+        auto advance = [&]() {  // nxt becomes cur; fetch the chunk after it
+            sc = sn;
+            bc = bn;
+            cur_t = tn;
+            cur_c = cn;
+            if (++cn == nch) {
+                cn = 0;
+                tn += gridDim.x;
+            }
+            load_chunk(tn, cn, sn, bn);
+        };
+        if (vec) {
+            load_chunk(tn, cn, sn, bn);
+            advance();
+        }
+        auto pick = [](const uint4& v, int g) -> uint32_t {  // halfword g % 8, splatted
+            const int q = (g >> 1) & 3;
+            const uint32_t w = (q & 2) ? ((q & 1) ? v.w : v.z) : ((q & 1) ? v.y : v.x);
+            const uint32_t h = (g & 1) ? (w >> 16) : (w & 0xffffu);
+            return h | (h << 16);
+        };
         uint32_t li = 0, bi = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
             const int n = (t / MB) * BN + d;
             uint32_t s2[2], b2[2];
-            load_sb(n, 0, s2, b2);
+            if (!vec) load_sb(n, 0, s2, b2);
             for (int kb = 0; kb < KB; ++kb, ++li, ++bi) {
                 const int s = li % LS, b = bi % BSTAGES;
                 uint32_t ns2[2], nb2[2];
-                load_sb(n, kb + 1 < KB ? kb + 1 : kb, ns2, nb2);  // next block, hidden behind this one
+                if (vec) {
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int g = (kb * BK + h * 32) / GS;
+                        if ((g >> 3) != cur_c || t != cur_t) advance();
+                        s2[h] = pick(sc, g);
+                        b2[h] = pick(bc, g);
+                    }
+                } else {
+                    load_sb(n, kb + 1 < KB ? kb + 1 : kb, ns2, nb2);  // next block, hidden behind this one
+                }
                 if (!wait(load_full + s, (li / LS) & 1) ||
                     (bi >= BSTAGES && !wait(b_empty + b, (bi / BSTAGES - 1) & 1))) {
                     ok = false;
@@ -384,21 +438,25 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
                 }
                 // raw row d of the stage (TMA 32-/64-byte swizzle: 16-byte chunk c of
                 // row d sits at chunk c ^ (d >> 2 & 1) / c ^ (d >> 1 & 3))
-                uint32_t raw[WPR];
+                constexpr int RW = WPR / DPR;  // this thread's packed words
+                uint32_t raw[RW];
                 const uint8_t* rrow = smem + s * LSB + A_BYTES + d * (WPR * 4);
 #pragma unroll
-                for (int c = 0; c < WPR / 4; ++c) {
-                    const int pc = (BITS == 4) ? (c ^ ((d >> 2) & 1)) : (c ^ ((d >> 1) & 3));
+                for (int c = 0; c < RW / 4; ++c) {
+                    const int lc = hh * (RW / 4) + c;  // logical 16-byte chunk of the row
+                    const int pc = (BITS == 4) ? (lc ^ ((d >> 2) & 1)) : (lc ^ ((d >> 1) & 3));
                     const uint4 v = *reinterpret_cast<const uint4*>(rrow + pc * 16);
                     raw[4 * c] = v.x; raw[4 * c + 1] = v.y; raw[4 * c + 2] = v.z; raw[4 * c + 3] = v.w;
                 }
                 uint8_t* bdst = bbuf + b * B_BYTES + (d >> 3) * 1024 + (d & 7) * 128;
+                constexpr int CPT = 8 / DPR;  // 8-element output chunks per thread
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const int h = (c * 8 >= 32) ? 1 : 0;
+                for (int c = 0; c < CPT; ++c) {
+                    const int oc = CPT * hh + c;
+                    const int h = (oc * 8 >= 32) ? 1 : 0;  // which 32-wide half (group for g32)
                     const uint4 v = dequant_chunk<T, BITS>(&raw[c * (BITS == 4 ? 1 : 2)], s2[h], b2[h],
                                                           mlo, mhi);
-                    *reinterpret_cast<uint4*>(bdst + ((c ^ (d & 7)) << 4)) = v;
+                    *reinterpret_cast<uint4*>(bdst + ((oc ^ (d & 7)) << 4)) = v;
                 }
                 asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
                 __syncwarp();
@@ -406,8 +464,10 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
                     mbar_arrive(smem_u32(b_full + b));
                     mbar_arrive(smem_u32(load_empty + s));
                 }
-                s2[0] = ns2[0]; s2[1] = ns2[1];
-                b2[0] = nb2[0]; b2[1] = nb2[1];
+                if (!vec) {
+                    s2[0] = ns2[0]; s2[1] = ns2[1];
+                    b2[0] = nb2[0]; b2[1] = nb2[1];
+                }
             }
         }
     } else {
@@ -418,7 +478,11 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
         uint32_t ai = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++ai) {
             const uint32_t a = ai & 1;
-            if (!wait(acc_full + a, (ai / 2) & 1)) break;
+            int okw = 1;
+            if (lane == 0) okw = wait(acc_full + a, (ai / 2) & 1) ? 1 : 0;
+            okw = __shfl_sync(0xffffffffu, okw, 0);
+            __syncwarp();
+            if (!okw) break;
             asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
             const int mb = t % MB, nb = t / MB;
             const int tok = mb * BM + quarter * 32 + lane;

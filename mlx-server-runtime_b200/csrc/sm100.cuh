@@ -34,6 +34,29 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
     return false;
 }
 
+// try_wait with a suspend-time hint: the thread is parked by the hardware until
+// the phase completes or about `hint_ns` nanoseconds pass, so a waiting warp
+// takes no issue slots from the warps doing work.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded suspending wait: at most `limit` hinted waits of `hint_ns` each.
+__device__ __forceinline__ bool mbar_wait_park(uint32_t bar, uint32_t parity, uint32_t limit,
+                                               uint32_t hint_ns) {
+    for (uint32_t i = 0; i < limit; ++i)
+        if (mbar_try_wait_hint(bar, parity, hint_ns)) return true;
+    return false;
+}
+
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
 }
