@@ -472,9 +472,57 @@ def run_case(args):
                       "TFLOP/s": round(flops / (us * 1e-6) / 1e12, 1)}), flush=True)
 
 
+MOE_CASES = {"moe_gate": (768, 2048), "moe_down": (2048, 768)}  # (N, K), 128 experts
+MOE_E, MOE_TOPK = 128, 8
+
+
+def run_moe_case(args):
+    """Sorted gather_qmm of one Qwen3-30B-A3B-shaped MoE projection: T tokens x top-8
+    of 128 experts (uniform random routing, seeded), rows sorted by expert."""
+    import torch
+
+    mxq = load_package()
+    dev = torch.device("cuda", 0)
+    N, K = MOE_CASES[args.case]
+    T = args.m
+    rows = T * MOE_TOPK
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(11)
+    w = (torch.randn(MOE_E, N, K, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+    wq, s, b = mxq.quantize(w, GS, BITS)
+    del w
+    x = torch.randn(rows, 1, K, device=dev, generator=gen).to(torch.bfloat16)
+    idx = torch.stack([torch.randperm(MOE_E, device=dev, generator=gen)[:MOE_TOPK]
+                       for _ in range(T)]).reshape(-1).to(torch.int32)
+    rhs = torch.sort(idx).values
+
+    def call():
+        return mxq.gather_qmm(x, wq, s, b, rhs_indices=rhs, group_size=GS, bits=BITS,
+                              sorted_indices=True)
+
+    for _ in range(max(3, args.warmup)):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    used = int(torch.unique(rhs).numel())
+    wbytes = used * (N * K * BITS // 8 + 4 * N * K // GS)
+    byts = wbytes + 2 * rows * K + 2 * rows * N
+    flops = 2.0 * rows * N * K
+    print(json.dumps({"case": args.case, "T": T, "rows": rows, "N": N, "K": K, "experts": MOE_E,
+                      "experts_used": used, "us_per_call": round(us, 3), "bytes": byts,
+                      "GB/s": round(byts / (us * 1e-6) / 1e9, 1),
+                      "TFLOP/s": round(flops / (us * 1e-6) / 1e12, 2)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", choices=sorted(CASES), default=None,
+    ap.add_argument("--case", choices=sorted(CASES) + sorted(MOE_CASES), default=None,
                     help="time one projection only (eager launches, for profiling)")
     ap.add_argument("--m", type=int, default=1, help="tokens for --case")
     ap.add_argument("--eager", action="store_true", help="--case: plain launches, no graph")
@@ -489,6 +537,8 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.case in MOE_CASES:
+        run_moe_case(args)
     elif args.case:
         run_case(args)
     else:

@@ -95,6 +95,9 @@ int check_k(int64_t K, int group_size) {
 }
 
 constexpr int64_t kIntMax = 0x7fffffffLL;
+// Sorted gather_qmm goes to the grouped tensor-core kernel from this many rows per
+// expert on average (below it, the weight-streaming decode kernel is as fast).
+constexpr int64_t kGroupedMinRows = 24;
 
 size_t dense_plan(int64_t M, int64_t N, int64_t K, int group_size, int bits, int dtype,
                   const DeviceInfo& di, mlxq::QmvPlan* plan, bool* ok) {
@@ -277,7 +280,8 @@ size_t mlxq_gather_qmm_workspace_size(int64_t batch, int64_t M, int64_t N, int64
                                       int sorted_indices) {
     (void)batch; (void)M; (void)N; (void)K; (void)group_size; (void)bits; (void)dtype;
     if (!sorted_indices || num_experts <= 0) return 0;
-    return ((static_cast<size_t>(num_experts) + 1) * 4 + 255) / 256 * 256;
+    // expert segment table [E+1], then the grouped kernel's tile offsets [E+1]
+    return (2 * (static_cast<size_t>(num_experts) + 1) * 4 + 255) / 256 * 256;
 }
 
 int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const void* biases,
@@ -317,6 +321,30 @@ int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const 
         if (reinterpret_cast<uintptr_t>(workspace) & 255u)
             return fail(MLXQ_ERR_ALIGN, "gather_qmm: workspace must be 256-byte aligned");
     }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // Sorted, one x row block per entry, enough rows per expert: grouped tcgen05 GEMM
+    // over the experts' contiguous row segments.
+    if (mode == 2 && !lhs_indices && lhs_div == 1 && x_batches == batch &&
+        batch * M >= kGroupedMinRows * num_experts &&
+        mlxq::qgemm_supported(static_cast<int>(batch * M), static_cast<int>(N),
+                              static_cast<int>(K), bits, group_size)) {
+        int32_t* seg = static_cast<int32_t*>(workspace);
+        int32_t* tile_start = seg + (num_experts + 1);
+        cudaError_t e = mlxq::launch_segments(rhs_indices, static_cast<int>(batch),
+                                              static_cast<int>(num_experts), seg, st);
+        if (e == cudaSuccess)
+            e = mlxq::launch_group_tiles(seg, static_cast<int>(num_experts), static_cast<int>(M),
+                                         static_cast<int>(N), tile_start, st);
+        if (e != cudaSuccess) return cuda_fail(e, "gather_qmm segment table");
+        mlxq::QgemmParams q{};
+        q.x = x; q.w = w; q.s = scales; q.b = biases; q.bias = nullptr; q.out = out;
+        q.M = static_cast<int>(batch * M); q.N = static_cast<int>(N); q.K = static_cast<int>(K);
+        q.E = static_cast<int>(num_experts); q.rpe = static_cast<int>(M);
+        q.seg = seg; q.tile_start = tile_start;
+        e = mlxq::qgemm_launch(dtype, bits, group_size, q, st);
+        if (e != cudaSuccess) return cuda_fail(e, "gather_qmm (grouped) launch");
+        return MLXQ_OK;
+    }
     mlxq::QmvPlan plan;
     const int zhint = (mode == 2) ? static_cast<int>(batch * M / num_experts) : static_cast<int>(batch);
     if (!mlxq::qmv_plan(dtype, bits, group_size, static_cast<int>(M), static_cast<int>(N),
@@ -336,7 +364,6 @@ int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const 
     p.sb_estride = N * (K / group_size);
     p.splits = 1; p.gps = plan.gps; p.win = plan.win; p.ztotal = plan.ztotal;
     p.partial = nullptr; p.counter = nullptr;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (mode == 2) {
         int32_t* seg = static_cast<int32_t*>(workspace);
         cudaError_t e = mlxq::launch_segments(rhs_indices, static_cast<int>(batch),

@@ -94,18 +94,28 @@ cudaError_t qmv_tma_launch(int dtype, int bits, int gs, const QtPlan& plan, cons
                            cudaStream_t st);
 cudaError_t qmv_tma_read_error(int* out_code);
 
-// One dense problem for the tcgen05 prefill kernel (qgemm_sm100.cu).
+// One problem for the tcgen05 prefill kernel (qgemm_sm100.cu): dense, or grouped by
+// expert (sorted gather_qmm) when E > 0: rows [seg[e]*rpe, seg[e+1]*rpe) of x and out
+// use expert e's weights (w, s, b hold E stacked [N, ...] matrices); tile_start[e]
+// is the first output tile of expert e and tile_start[E] the tile count.
 struct QgemmParams {
     const void* x;
     const uint32_t* w;
     const void* s;
     const void* b;
-    const void* bias;  // optional per-output bias [N]
+    const void* bias;  // optional per-output bias [N] (dense only)
     void* out;
-    int M, N, K;
+    int M, N, K;       // M: rows of x and out (all experts' rows when grouped)
+    int E;             // 0: dense
+    int rpe;           // rows per batch entry (grouped)
+    const int32_t* seg;
+    const int32_t* tile_start;
 };
 
 bool qgemm_supported(int M, int N, int K, int bits, int gs);
+// Builds tile_start[0..E] for a grouped problem from seg (qgemm_sm100.cu).
+cudaError_t launch_group_tiles(const int32_t* seg, int E, int rpe, int N, int32_t* tile_start,
+                               cudaStream_t st);
 cudaError_t qgemm_launch(int dtype, int bits, int gs, const QgemmParams& p, cudaStream_t st);
 // Reads (and clears) the error code a kernel recorded after a bounded wait gave up.
 cudaError_t qgemm_read_error(int* out_code);

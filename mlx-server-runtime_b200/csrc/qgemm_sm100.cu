@@ -246,7 +246,26 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
     const int M = p.M, N = p.N, K = p.K;
     const int KB = K / BK;
     const int MB = (M + BM - 1) / BM, NB = (N + BN - 1) / BN;
-    const int tiles = MB * NB;
+    const bool grouped = p.E > 0;
+    const int tiles = grouped ? p.tile_start[p.E] : MB * NB;
+    // Output tile t: expert, first row, end of the expert's rows, column block.
+    struct Tile {
+        int e, row0, row_end, nb;
+    };
+    auto tile_of = [&](int t) -> Tile {
+        if (!grouped) return Tile{0, (t % MB) * BM, M, t / MB};
+        int lo = 0, hi = p.E - 1;  // last expert whose first tile is <= t
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (p.tile_start[mid] <= t) lo = mid;
+            else hi = mid - 1;
+        }
+        const int lt = t - p.tile_start[lo];
+        const int r0 = p.seg[lo] * p.rpe;
+        const int rows = max(0, p.seg[lo + 1] * p.rpe - r0);
+        const int mbe = max(1, (rows + BM - 1) / BM);
+        return Tile{lo, r0 + (lt % mbe) * BM, r0 + rows, lt / mbe};
+    };
 
     if (warp == WARP_MMA) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
@@ -294,7 +313,7 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
             uint32_t li = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-                const int mb = t % MB, nb = t / MB;
+                const Tile tl = tile_of(t);
                 for (int kb = 0; kb < KB; ++kb, ++li) {
                     const int s = li % LS;
                     if (li >= LS && !wait(load_empty + s, (li / LS - 1) & 1)) {
@@ -304,8 +323,8 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
                     const uint32_t dst = smem_u32(smem + s * LSB);
                     const uint32_t bar = smem_u32(load_full + s);
                     mbar_arrive_expect_tx(bar, LSB);
-                    tma_load_2d(dst, &tx, bar, kb * BK, mb * BM);
-                    tma_load_2d(dst + A_BYTES, &tw, bar, kb * WPR, nb * BN);
+                    tma_load_2d(dst, &tx, bar, kb * BK, tl.row0);
+                    tma_load_2d(dst + A_BYTES, &tw, bar, kb * WPR, tl.e * N + tl.nb * BN);
                 }
             }
             if (!ok) {
@@ -360,14 +379,14 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
         const T* bg = static_cast<const T*>(p.b);
         const uint32_t mlo = opaque(Pair<T>::kMagicLo), mhi = opaque(Pair<T>::kMagicHi);
         // packed (value, value) scale and bias of the two 32-wide halves of block kb
-        auto load_sb = [&](int n, int kb, uint32_t (&s2)[2], uint32_t (&b2)[2]) {
+        auto load_sb = [&](int e, int n, int kb, uint32_t (&s2)[2], uint32_t (&b2)[2]) {
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const int g = (kb * BK + h * 32) / GS;
                 T sv = T(0.0f), bv = T(0.0f);
                 if (n < N) {
-                    sv = sg[static_cast<long long>(n) * G + g];
-                    bv = bg[static_cast<long long>(n) * G + g];
+                    sv = sg[(static_cast<long long>(e) * N + n) * G + g];
+                    bv = bg[(static_cast<long long>(e) * N + n) * G + g];
                 }
                 s2[h] = splat(sv);
                 b2[h] = splat(bv);
@@ -379,11 +398,13 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
         const bool vec = (G % 8) == 0;
         const int nch = G / 8;
         auto load_chunk = [&](int tt, int cc, uint4& sv, uint4& bv) {
-            const int n = (tt / MB) * BN + d;
             sv = make_uint4(0u, 0u, 0u, 0u);
             bv = sv;
-            if (tt < tiles && n < N) {
-                const long long off = static_cast<long long>(n) * G + cc * 8;
+            if (tt >= tiles) return;
+            const Tile tl = tile_of(tt);
+            const int n = tl.nb * BN + d;
+            if (n < N) {
+                const long long off = (static_cast<long long>(tl.e) * N + n) * G + cc * 8;
                 sv = *reinterpret_cast<const uint4*>(sg + off);
                 bv = *reinterpret_cast<const uint4*>(bg + off);
             }
@@ -414,9 +435,10 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
         uint32_t li = 0, bi = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-            const int n = (t / MB) * BN + d;
+            const Tile tl = tile_of(t);
+            const int n = tl.nb * BN + d;  // row within expert tl.e (n >= N: none)
             uint32_t s2[2], b2[2];
-            if (!vec) load_sb(n, 0, s2, b2);
+            if (!vec) load_sb(tl.e, n, 0, s2, b2);
             for (int kb = 0; kb < KB; ++kb, ++li, ++bi) {
                 const int s = li % LS, b = bi % BSTAGES;
                 uint32_t ns2[2], nb2[2];
@@ -429,7 +451,7 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
                         b2[h] = pick(bc, g);
                     }
                 } else {
-                    load_sb(n, kb + 1 < KB ? kb + 1 : kb, ns2, nb2);  // next block, hidden behind this one
+                    load_sb(tl.e, n, kb + 1 < KB ? kb + 1 : kb, ns2, nb2);  // next block, hidden behind this one
                 }
                 if (!wait(load_full + s, (li / LS) & 1) ||
                     (bi >= BSTAGES && !wait(b_empty + b, (bi / BSTAGES - 1) & 1))) {
@@ -484,14 +506,15 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
             __syncwarp();
             if (!okw) break;
             asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-            const int mb = t % MB, nb = t / MB;
-            const int tok = mb * BM + quarter * 32 + lane;
+            const Tile tl = tile_of(t);
+            const int tok = tl.row0 + quarter * 32 + lane;
+            const int nb = tl.nb;
 #pragma unroll 1
             for (int i = 0; i < BN / 32; ++i) {
                 uint32_t r[32];
                 tmem_ld32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN + i * 32, r);
                 const int n = nb * BN + i * 32;
-                if (tok < M && n < N) {
+                if (tok < tl.row_end && n < N) {
                     // round once, add the bias as a second rounding, pack pairs
                     uint32_t pk[16];
 #pragma unroll
@@ -582,13 +605,54 @@ static cudaError_t qgemm_launch_t(const QgemmParams& p, cudaStream_t st) {
     const unsigned long long kw = static_cast<unsigned long long>(p.K) * BITS / 32;
     if (!qg_map(&tx, p.x, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, p.K, p.M, qg::BK, qg::BM,
                 CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !qg_map(&tw, p.w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, kw, p.N, qg::BK * BITS / 32, qg::BN,
+        !qg_map(&tw, p.w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, kw,
+                static_cast<unsigned long long>(p.N) * (p.E > 0 ? p.E : 1), qg::BK * BITS / 32, qg::BN,
                 BITS == 4 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
         return cudaErrorInvalidValue;
-    const long long tiles = static_cast<long long>((p.M + qg::BM - 1) / qg::BM) *
-                            ((p.N + qg::BN - 1) / qg::BN);
+    // grouped: the tile count lives on the device; ceil(rows_e / BM) summed over experts
+    // is at most ceil(M / BM) + E
+    const long long mblocks = (p.M + qg::BM - 1) / qg::BM + (p.E > 0 ? p.E : 0);
+    const long long tiles = mblocks * ((p.N + qg::BN - 1) / qg::BN);
     const int grid = static_cast<int>(tiles < num_sms[dev] ? tiles : num_sms[dev]);
     kern<<<grid, qg::THREADS, smem, st>>>(tx, tw, p);
+    return cudaGetLastError();
+}
+
+// tile_start[e + 1] = tile_start[e] + ceil(rows_e / BM) * NB, one block, E in chunks
+__global__ void group_tiles_kernel(const int32_t* __restrict__ seg, int E, int rpe, int NB,
+                                   int32_t* __restrict__ tile_start) {
+    __shared__ int scan[1024];
+    __shared__ int carry;
+    if (threadIdx.x == 0) {
+        carry = 0;
+        tile_start[0] = 0;
+    }
+    __syncthreads();
+    for (int base = 0; base < E; base += 1024) {
+        const int e = base + threadIdx.x;
+        int c = 0;
+        if (e < E) {
+            const int rows = max(0, (seg[e + 1] - seg[e]) * rpe);
+            c = (rows + qg::BM - 1) / qg::BM * NB;
+        }
+        scan[threadIdx.x] = c;
+        __syncthreads();
+        for (int off = 1; off < 1024; off <<= 1) {  // inclusive scan
+            const int v = threadIdx.x >= off ? scan[threadIdx.x - off] : 0;
+            __syncthreads();
+            scan[threadIdx.x] += v;
+            __syncthreads();
+        }
+        if (e < E) tile_start[e + 1] = carry + scan[threadIdx.x];
+        __syncthreads();
+        if (threadIdx.x == 0) carry += scan[1023];
+        __syncthreads();
+    }
+}
+
+cudaError_t launch_group_tiles(const int32_t* seg, int E, int rpe, int N, int32_t* tile_start,
+                               cudaStream_t st) {
+    group_tiles_kernel<<<1, 1024, 0, st>>>(seg, E, rpe, (N + qg::BN - 1) / qg::BN, tile_start);
     return cudaGetLastError();
 }
 
