@@ -7,20 +7,20 @@
 // for M > 32 tokens (MLX's quantized_matmul as QuantizedLinear calls it during
 // prefill, qwen2.py:58-61,123-134 of the reference).
 //
-// Output tiles BM = 128 tokens x BN = 256 weight rows, K blocks of BK = 64; one
+// Output tiles BW = 128 weight rows x BT = 192 tokens, K blocks of BK = 64; one
 // persistent CTA per SM with specialized warps (see qgemm_kernel):
 //   * TMA brings the activation tile in the canonical K-major 128-byte-swizzled
-//     layout (8-row x 128-byte atoms, chunk c of row r at chunk c ^ (r % 8)) that
-//     the MMA reads directly, and the raw packed codes of the 256 weight rows.
-//   * One thread per weight row dequantizes: codes become exact 16-bit values with
-//     byte permutes and a magic exponent (no integer-to-float conversion), then
-//     w = scale*q + bias with one packed FMA (one rounding, like MLX's
-//     dequantize-in-kernel), stored in the same swizzled layout.
-//   * One thread issues tcgen05.mma (M=128, N=256, K=16) from shared-memory
-//     descriptors into one of two 128 x 256 fp32 accumulators in tensor memory;
-//     tcgen05.commit hands each stage and B tile back to its producer.
-//   * Epilogue warps read the finished accumulator (tcgen05.ld, 32 lanes x 32
-//     columns) while the other one fills: bf16/f16, optional per-row bias added
+//     layout (8-row x 128-byte atoms, chunk c of row r at chunk c ^ (r % 8)) that the
+//     MMA reads as its B operand, and the raw packed codes of the 128 weight rows.
+//   * Two threads per weight row dequantize 32 codes each: codes become exact 16-bit
+//     values with byte permutes and a magic exponent (no integer-to-float
+//     conversion), then w = scale*q + bias with one packed FMA (one rounding, like
+//     MLX's dequantize-in-kernel), stored straight into tensor memory as the MMA's
+//     A operand (weight row = lane).
+//   * One thread issues tcgen05.mma (M=128, N=192, K=16; A from tensor memory, B
+//     from a shared-memory descriptor) into one of two 128 x 192 fp32 accumulators.
+//   * Epilogue warps read the finished accumulator (tcgen05.ld; thread = weight row,
+//     32 tokens per load) while the other one fills: bf16/f16, optional bias added
 //     as a second rounding.
 // Every mbarrier wait is bounded: on timeout the CTA records an error in
 // g_qgemm_error, its roles stop issuing work, the loads and MMAs in flight are
@@ -38,28 +38,31 @@ namespace mlxq {
 __device__ int g_qgemm_error;  // 0, or the first error code a kernel recorded
 
 namespace qg {
-constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int BSTAGES = 3;                      // dequantized B tiles in flight
+constexpr int BW = 128;  // weight rows per tile: MMA M, tensor-memory lanes
+constexpr int BT = 192;  // tokens per tile: MMA N
+constexpr int BK = 64;
+constexpr int ASTAGES = 4;                      // dequantized weight tiles in tensor memory
 constexpr int NDEQ = 8, NEPI = 4;               // dequant / epilogue warps
-constexpr int DPR = NDEQ * 32 / BN;             // dequant threads per weight row
 constexpr int WARP_TMA = 0, WARP_MMA = 1, WARP_EPI0 = 2, WARP_DEQ0 = WARP_EPI0 + NEPI;
-constexpr int THREADS = (WARP_DEQ0 + NDEQ) * 32;
-static_assert(DPR == 1 || DPR == 2, "one or two dequant threads per weight row");
-constexpr int A_BYTES = BM * BK * 2;  // 16 KB
-constexpr int B_BYTES = BN * BK * 2;  // 32 KB
-constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
+constexpr int THREADS = (WARP_DEQ0 + NDEQ) * 32;  // 448
+static_assert(NDEQ == 8, "two dequant warps per tensor-memory lane quarter (32 codes each)");
+constexpr int X_BYTES = BT * BK * 2;    // 24 KB activation tile
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kACol0 = 2 * BT;     // first A stage column (after two accumulators)
+constexpr uint32_t kACols = BK / 2;     // 32-bit columns per A stage (two 16-bit values each)
+static_assert(kACol0 + ASTAGES * kACols <= kTmemCols, "tensor memory budget");
 constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr int kErrTimeout = 1;
 // suspending barrier waits: up to kParkLimit waits of about kParkNs each (~4 s)
 constexpr uint32_t kParkNs = 2000, kParkLimit = 1u << 21;
 template <int BITS>
-constexpr int raw_bytes() { return BN * BK * BITS / 8; }  // 8 KB (4-bit) / 16 KB (8-bit)
+constexpr int raw_bytes() { return BW * BK * BITS / 8; }  // 4 KB (4-bit) / 8 KB (8-bit)
 template <int BITS>
-constexpr int load_stages() { return BITS == 4 ? 4 : 3; }
+constexpr int load_stages() { return BITS == 4 ? 6 : 5; }
 template <int BITS>
 constexpr int smem_bytes() {
-    return load_stages<BITS>() * (A_BYTES + raw_bytes<BITS>()) + BSTAGES * B_BYTES +
-           (2 * load_stages<BITS>() + 2 * BSTAGES + 5) * 8 + 16 + 1024;
+    return load_stages<BITS>() * (X_BYTES + raw_bytes<BITS>()) +
+           (2 * load_stages<BITS>() + 2 * ASTAGES + 5) * 8 + 16 + 1024;
 }
 }  // namespace qg
 
@@ -74,21 +77,34 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
     return d;
 }
 
-// Instruction descriptor, kind::f16: fp32 accumulate, A/B bf16 or f16, both K-major.
+// Instruction descriptor, kind::f16: fp32 accumulate, A/B bf16 or f16, both K-major,
+// M = BW, N = BT.
 template <typename T>
 __host__ __device__ constexpr uint32_t qgemm_idesc() {
     constexpr uint32_t ab = __is_same(T, __nv_bfloat16) ? 1u : 0u;
-    return (1u << 4) | (ab << 7) | (ab << 10) | (static_cast<uint32_t>(qg::BN >> 3) << 17) |
-           (static_cast<uint32_t>(qg::BM >> 4) << 24);
+    return (1u << 4) | (ab << 7) | (ab << 10) | (static_cast<uint32_t>(qg::BT >> 3) << 17) |
+           (static_cast<uint32_t>(qg::BW >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                         uint32_t idesc, uint32_t accumulate) {
+// D (tensor memory) (+)= A (tensor memory) * B (shared-memory descriptor)
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// 16 consecutive 32-bit columns of this thread's tensor-memory lane
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+        "r"(v[15])
+        : "memory");
 }
 
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
@@ -205,19 +221,20 @@ __device__ __forceinline__ uint4 dequant_chunk(const uint32_t* wds, uint32_t s2,
 }
 
 // Persistent, warp-specialized prefill kernel. One CTA per SM walks its share of
-// the [BM x BN] output tiles; per K block of 64:
-//   warp 0  (TMA)      x tile [128 x 64] (128-byte swizzle, the MMA's A layout)
-//                      and the raw packed weights [256 rows x 64 codes] of the
-//                      tile into a ring of load stages;
-//   warps 6-13 (dequant, thread = weight row) turn the raw codes of their row
-//                      into bf16/f16 values w = scale*q + bias in a ring of
-//                      B tiles (the MMA's K-major, 128-byte swizzled layout);
-//   warp 1  (MMA)      one thread issues tcgen05.mma M=128 N=256 K=16 x 4 into
-//                      one of two 256-column TMEM accumulators and commits the
-//                      stage and the B tile back to their producers;
-//   warps 2-5 (epilogue) drain the other accumulator with tcgen05.ld while the
-//                      next tile accumulates, add the optional bias as a second
-//                      rounding, and store.
+// the output tiles (BW = 128 weight rows x BT = 192 tokens); per K block of 64:
+//   warp 0  (TMA)      the activation tile [192 tokens x 64] (128-byte swizzle: the
+//                      MMA's K-major B layout) and the raw packed codes of the tile's
+//                      128 weight rows, into a ring of load stages;
+//   warps 6-13 (dequant) thread = weight row: warps w and w+4 share tensor-memory lane
+//                      quarter w % 4 and take 32 codes each; w = scale*q + bias goes
+//                      straight into a ring of A tiles in tensor memory (tcgen05.st),
+//                      never through shared memory;
+//   warp 1  (MMA)      one thread issues tcgen05.mma M=128 N=192 K=16 x 4 with A from
+//                      tensor memory into one of two accumulators and commits the load
+//                      stage and the A tile back to their producers;
+//   warps 2-5 (epilogue) drain the other accumulator (thread = weight row, columns =
+//                      tokens) while the next tile accumulates; optional bias as a
+//                      second rounding.
 template <typename T, int BITS, int GS>
 __global__ void __launch_bounds__(qg::THREADS, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw,
@@ -225,18 +242,17 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
     using namespace qg;
     constexpr int LS = load_stages<BITS>();
     constexpr int RAW = raw_bytes<BITS>();
-    constexpr int LSB = A_BYTES + RAW;    // bytes of one load stage
+    constexpr int LSB = X_BYTES + RAW;    // bytes of one load stage
     constexpr int WPR = BK * BITS / 32;   // packed words per row per K block
     constexpr uint32_t IDESC = qgemm_idesc<T>();
 
     extern __shared__ uint8_t qg_smem_raw[];
     uint8_t* smem = qg_smem_raw + ((1024u - (smem_u32(qg_smem_raw) & 1023u)) & 1023u);
-    uint8_t* bbuf = smem + LS * LSB;
-    uint64_t* load_full = reinterpret_cast<uint64_t*>(bbuf + BSTAGES * B_BYTES);
+    uint64_t* load_full = reinterpret_cast<uint64_t*>(smem + LS * LSB);
     uint64_t* load_empty = load_full + LS;
-    uint64_t* b_full = load_empty + LS;
-    uint64_t* b_empty = b_full + BSTAGES;
-    uint64_t* acc_full = b_empty + BSTAGES;
+    uint64_t* a_full = load_empty + LS;
+    uint64_t* a_empty = a_full + ASTAGES;
+    uint64_t* acc_full = a_empty + ASTAGES;
     uint64_t* acc_empty = acc_full + 2;
     uint64_t* mma_done = acc_empty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
@@ -245,15 +261,15 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int M = p.M, N = p.N, K = p.K;
     const int KB = K / BK;
-    const int MB = (M + BM - 1) / BM, NB = (N + BN - 1) / BN;
+    const int MB = (M + BT - 1) / BT, NB = (N + BW - 1) / BW;
     const bool grouped = p.E > 0;
     const int tiles = grouped ? p.tile_start[p.E] : MB * NB;
-    // Output tile t: expert, first row, end of the expert's rows, column block.
+    // Output tile t: expert, first token row, end of the expert's rows, weight block.
     struct Tile {
         int e, row0, row_end, nb;
     };
     auto tile_of = [&](int t) -> Tile {
-        if (!grouped) return Tile{0, (t % MB) * BM, M, t / MB};
+        if (!grouped) return Tile{0, (t % MB) * BT, M, t / MB};
         int lo = 0, hi = p.E - 1;  // last expert whose first tile is <= t
         while (lo < hi) {
             const int mid = (lo + hi + 1) >> 1;
@@ -263,8 +279,8 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
         const int lt = t - p.tile_start[lo];
         const int r0 = p.seg[lo] * p.rpe;
         const int rows = max(0, p.seg[lo + 1] * p.rpe - r0);
-        const int mbe = max(1, (rows + BM - 1) / BM);
-        return Tile{lo, r0 + (lt % mbe) * BM, r0 + rows, lt / mbe};
+        const int mbe = max(1, (rows + BT - 1) / BT);
+        return Tile{lo, r0 + (lt % mbe) * BT, r0 + rows, lt / mbe};
     };
 
     if (warp == WARP_MMA) {
@@ -278,9 +294,9 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
             mbar_init(smem_u32(load_full + s), 1);
             mbar_init(smem_u32(load_empty + s), NDEQ + 1);
         }
-        for (int b = 0; b < BSTAGES; ++b) {
-            mbar_init(smem_u32(b_full + b), NDEQ);
-            mbar_init(smem_u32(b_empty + b), 1);
+        for (int a = 0; a < ASTAGES; ++a) {
+            mbar_init(smem_u32(a_full + a), NDEQ);
+            mbar_init(smem_u32(a_empty + a), 1);
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(smem_u32(acc_full + a), 1);
@@ -295,7 +311,6 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
     const uint32_t tmem = *tmem_slot;
 
-    // bounded wait shared by every role: false (and the CTA marked aborted) on timeout
     // (a suspending wait: the hardware parks the thread until the phase completes)
     auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
         if (*s_abort) return false;
@@ -324,7 +339,7 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
                     const uint32_t bar = smem_u32(load_full + s);
                     mbar_arrive_expect_tx(bar, LSB);
                     tma_load_2d(dst, &tx, bar, kb * BK, tl.row0);
-                    tma_load_2d(dst + A_BYTES, &tw, bar, kb * WPR, tl.e * N + tl.nb * BN);
+                    tma_load_2d(dst + X_BYTES, &tw, bar, kb * WPR, tl.e * N + tl.nb * BW);
                 }
             }
             if (!ok) {
@@ -337,7 +352,7 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
     } else if (warp == WARP_MMA) {
         // ------------------------------ MMA issue ---------------------------------
         if (lane == 0) {
-            uint32_t li = 0, bi = 0, ai = 0;
+            uint32_t li = 0, ai_k = 0, ai = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++ai) {
                 const uint32_t a = ai & 1;
@@ -346,22 +361,22 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
                     break;
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-                for (int kb = 0; kb < KB; ++kb, ++li, ++bi) {
-                    const int s = li % LS, b = bi % BSTAGES;
+                for (int kb = 0; kb < KB; ++kb, ++li, ++ai_k) {
+                    const int s = li % LS, as = ai_k % ASTAGES;
                     if (!wait(load_full + s, (li / LS) & 1) ||
-                        !wait(b_full + b, (bi / BSTAGES) & 1)) {
+                        !wait(a_full + as, (ai_k / ASTAGES) & 1)) {
                         ok = false;
                         break;
                     }
                     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-                    const uint64_t adesc = sw128_kmajor_desc(smem_u32(smem + s * LSB));
-                    const uint64_t bdesc = sw128_kmajor_desc(smem_u32(bbuf + b * B_BYTES));
+                    const uint64_t bdesc = sw128_kmajor_desc(smem_u32(smem + s * LSB));
+                    const uint32_t acol = tmem + kACol0 + as * kACols;
 #pragma unroll
-                    for (int j = 0; j < BK / 16; ++j)  // 32 bytes (16 elements) per step
-                        umma_f16(tmem + a * BN, adesc + 2 * j, bdesc + 2 * j, IDESC,
-                                 (kb > 0 || j > 0) ? 1u : 0u);
+                    for (int j = 0; j < BK / 16; ++j)  // 16 elements: 8 A columns, 32 B of B
+                        umma_f16_ts(tmem + a * BT, acol + 8 * j, bdesc + 2 * j, IDESC,
+                                    (kb > 0 || j > 0) ? 1u : 0u);
                     umma_commit(smem_u32(load_empty + s));
-                    umma_commit(smem_u32(b_empty + b));
+                    umma_commit(smem_u32(a_empty + as));
                 }
                 if (ok) umma_commit(smem_u32(acc_full + a));
             }
@@ -371,30 +386,17 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
         }
     } else if (warp >= WARP_DEQ0) {
         // ------------------------------ dequantize ---------------------------------
-        const int dq = tid - WARP_DEQ0 * 32;
-        const int d = dq % BN;   // weight row within the tile
-        const int hh = dq / BN;  // which part of the row's 64 codes this thread converts
+        const int q = warp & 3;                       // tensor-memory lane quarter
+        const int r = q * 32 + lane;                  // weight row within the tile
+        const int hh = (warp - WARP_DEQ0) / 4;        // which 32 codes of the K block
         const int G = K / GS;
         const T* sg = static_cast<const T*>(p.s);
         const T* bg = static_cast<const T*>(p.b);
         const uint32_t mlo = opaque(Pair<T>::kMagicLo), mhi = opaque(Pair<T>::kMagicHi);
-        // packed (value, value) scale and bias of the two 32-wide halves of block kb
-        auto load_sb = [&](int e, int n, int kb, uint32_t (&s2)[2], uint32_t (&b2)[2]) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int g = (kb * BK + h * 32) / GS;
-                T sv = T(0.0f), bv = T(0.0f);
-                if (n < N) {
-                    sv = sg[(static_cast<long long>(e) * N + n) * G + g];
-                    bv = bg[(static_cast<long long>(e) * N + n) * G + g];
-                }
-                s2[h] = splat(sv);
-                b2[h] = splat(bv);
-            }
-        };
-        // Scales and biases by 16-byte chunks of 8 groups (when rows are 16-byte
-        // aligned): `cur` holds the chunk in use, `nxt` the following one of this
-        // CTA's (tile, chunk) sequence, loaded a whole chunk (4-16 K blocks) early.
+        const uint32_t tq = tmem + (static_cast<uint32_t>(q * 32) << 16) + kACol0 + 16 * hh;
+        // Scales and biases by 16-byte chunks of 8 groups (rows 16-byte aligned):
+        // `cur` is the chunk in use, `nxt` the next one this thread will need along its
+        // (tile, chunk) sequence, loaded a whole chunk (4-16 K blocks) early.
         const bool vec = (G % 8) == 0;
         const int nch = G / 8;
         auto load_chunk = [&](int tt, int cc, uint4& sv, uint4& bv) {
@@ -402,7 +404,7 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
             bv = sv;
             if (tt >= tiles) return;
             const Tile tl = tile_of(tt);
-            const int n = tl.nb * BN + d;
+            const int n = tl.nb * BW + r;
             if (n < N) {
                 const long long off = (static_cast<long long>(tl.e) * N + n) * G + cc * 8;
                 sv = *reinterpret_cast<const uint4*>(sg + off);
@@ -427,115 +429,96 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
             advance();
         }
         auto pick = [](const uint4& v, int g) -> uint32_t {  // halfword g % 8, splatted
-            const int q = (g >> 1) & 3;
-            const uint32_t w = (q & 2) ? ((q & 1) ? v.w : v.z) : ((q & 1) ? v.y : v.x);
+            const int w4 = (g >> 1) & 3;
+            const uint32_t w = (w4 & 2) ? ((w4 & 1) ? v.w : v.z) : ((w4 & 1) ? v.y : v.x);
             const uint32_t h = (g & 1) ? (w >> 16) : (w & 0xffffu);
             return h | (h << 16);
         };
-        uint32_t li = 0, bi = 0;
+        uint32_t li = 0, ai_k = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
             const Tile tl = tile_of(t);
-            const int n = tl.nb * BN + d;  // row within expert tl.e (n >= N: none)
-            uint32_t s2[2], b2[2];
-            if (!vec) load_sb(tl.e, n, 0, s2, b2);
-            for (int kb = 0; kb < KB; ++kb, ++li, ++bi) {
-                const int s = li % LS, b = bi % BSTAGES;
-                uint32_t ns2[2], nb2[2];
+            const int n = tl.nb * BW + r;  // row within expert tl.e (n >= N: none)
+            for (int kb = 0; kb < KB; ++kb, ++li, ++ai_k) {
+                const int s = li % LS, as = ai_k % ASTAGES;
+                const int g = (kb * BK + hh * 32) / GS;  // this thread's group
+                uint32_t s2, b2;
                 if (vec) {
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int g = (kb * BK + h * 32) / GS;
-                        if ((g >> 3) != cur_c || t != cur_t) advance();
-                        s2[h] = pick(sc, g);
-                        b2[h] = pick(bc, g);
-                    }
+                    if ((g >> 3) != cur_c || t != cur_t) advance();
+                    s2 = pick(sc, g);
+                    b2 = pick(bc, g);
                 } else {
-                    load_sb(tl.e, n, kb + 1 < KB ? kb + 1 : kb, ns2, nb2);  // next block, hidden behind this one
+                    T sv = T(0.0f), bv = T(0.0f);
+                    if (n < N) {
+                        sv = sg[(static_cast<long long>(tl.e) * N + n) * G + g];
+                        bv = bg[(static_cast<long long>(tl.e) * N + n) * G + g];
+                    }
+                    s2 = splat(sv);
+                    b2 = splat(bv);
                 }
                 if (!wait(load_full + s, (li / LS) & 1) ||
-                    (bi >= BSTAGES && !wait(b_empty + b, (bi / BSTAGES - 1) & 1))) {
+                    (ai_k >= ASTAGES && !wait(a_empty + as, (ai_k / ASTAGES - 1) & 1))) {
                     ok = false;
                     break;
                 }
-                // raw row d of the stage (TMA 32-/64-byte swizzle: 16-byte chunk c of
-                // row d sits at chunk c ^ (d >> 2 & 1) / c ^ (d >> 1 & 3))
-                constexpr int RW = WPR / DPR;  // this thread's packed words
+                // this thread's half of row r (TMA 32-/64-byte swizzle: 16-byte chunk c
+                // of row r sits at chunk c ^ (r >> 2 & 1) / c ^ (r >> 1 & 3))
+                constexpr int RW = WPR / 2;
                 uint32_t raw[RW];
-                const uint8_t* rrow = smem + s * LSB + A_BYTES + d * (WPR * 4);
+                const uint8_t* rrow = smem + s * LSB + X_BYTES + r * (WPR * 4);
 #pragma unroll
                 for (int c = 0; c < RW / 4; ++c) {
-                    const int lc = hh * (RW / 4) + c;  // logical 16-byte chunk of the row
-                    const int pc = (BITS == 4) ? (lc ^ ((d >> 2) & 1)) : (lc ^ ((d >> 1) & 3));
+                    const int lc = hh * (RW / 4) + c;
+                    const int pc = (BITS == 4) ? (lc ^ ((r >> 2) & 1)) : (lc ^ ((r >> 1) & 3));
                     const uint4 v = *reinterpret_cast<const uint4*>(rrow + pc * 16);
                     raw[4 * c] = v.x; raw[4 * c + 1] = v.y; raw[4 * c + 2] = v.z; raw[4 * c + 3] = v.w;
                 }
-                uint8_t* bdst = bbuf + b * B_BYTES + (d >> 3) * 1024 + (d & 7) * 128;
-                constexpr int CPT = 8 / DPR;  // 8-element output chunks per thread
+                uint32_t out16[16];
 #pragma unroll
-                for (int c = 0; c < CPT; ++c) {
-                    const int oc = CPT * hh + c;
-                    const int h = (oc * 8 >= 32) ? 1 : 0;  // which 32-wide half (group for g32)
-                    const uint4 v = dequant_chunk<T, BITS>(&raw[c * (BITS == 4 ? 1 : 2)], s2[h], b2[h],
+                for (int c = 0; c < 4; ++c) {
+                    const uint4 v = dequant_chunk<T, BITS>(&raw[c * (BITS == 4 ? 1 : 2)], s2, b2,
                                                           mlo, mhi);
-                    *reinterpret_cast<uint4*>(bdst + ((oc ^ (d & 7)) << 4)) = v;
+                    out16[4 * c] = v.x; out16[4 * c + 1] = v.y;
+                    out16[4 * c + 2] = v.z; out16[4 * c + 3] = v.w;
                 }
-                asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+                tmem_st16(tq + as * kACols, out16);
+                asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+                asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive(smem_u32(b_full + b));
+                    mbar_arrive(smem_u32(a_full + as));
                     mbar_arrive(smem_u32(load_empty + s));
-                }
-                if (!vec) {
-                    s2[0] = ns2[0]; s2[1] = ns2[1];
-                    b2[0] = nb2[0]; b2[1] = nb2[1];
                 }
             }
         }
     } else {
         // ------------------------------ epilogue -----------------------------------
-        const int quarter = warp & 3;  // TMEM lanes this warp may read
+        const int q = warp & 3;  // tensor-memory lanes this warp may read
         T* og = static_cast<T*>(p.out);
         const T* biasg = static_cast<const T*>(p.bias);
         uint32_t ai = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++ai) {
             const uint32_t a = ai & 1;
-            int okw = 1;
-            if (lane == 0) okw = wait(acc_full + a, (ai / 2) & 1) ? 1 : 0;
-            okw = __shfl_sync(0xffffffffu, okw, 0);
-            __syncwarp();
-            if (!okw) break;
+            if (!wait(acc_full + a, (ai / 2) & 1)) break;
             asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
             const Tile tl = tile_of(t);
-            const int tok = tl.row0 + quarter * 32 + lane;
-            const int nb = tl.nb;
+            const int n = tl.nb * BW + q * 32 + lane;  // this thread's output column
+            const bool col_ok = n < N;
+            const float bsum = (biasg && col_ok) ? Elem<T>::to_f(biasg[n]) : 0.f;
 #pragma unroll 1
-            for (int i = 0; i < BN / 32; ++i) {
-                uint32_t r[32];
-                tmem_ld32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN + i * 32, r);
-                const int n = nb * BN + i * 32;
-                if (tok < tl.row_end && n < N) {
-                    // round once, add the bias as a second rounding, pack pairs
-                    uint32_t pk[16];
+            for (int i = 0; i < BT / 32; ++i) {
+                uint32_t v[32];
+                tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + a * BT + i * 32, v);
+                const int tok0 = tl.row0 + i * 32;
+                if (col_ok) {
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        T y = Elem<T>::from_f(__uint_as_float(r[e]));
-                        if (biasg && n + e < N)
-                            y = Elem<T>::from_f(Elem<T>::to_f(y) + Elem<T>::to_f(biasg[n + e]));
-                        const uint32_t bits = *reinterpret_cast<const uint16_t*>(&y);
-                        pk[e >> 1] = (e & 1) ? (pk[e >> 1] | (bits << 16)) : bits;
-                    }
-                    T* dst = og + static_cast<long long>(tok) * N + n;
-                    if ((N & 7) == 0 && n + 32 <= N) {
-#pragma unroll
-                        for (int v = 0; v < 4; ++v)
-                            reinterpret_cast<uint4*>(dst)[v] =
-                                make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
-                    } else {
-                        uint16_t* d16 = reinterpret_cast<uint16_t*>(dst);
-#pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            if (n + e < N) d16[e] = static_cast<uint16_t>(pk[e >> 1] >> ((e & 1) * 16));
+                    for (int j = 0; j < 32; ++j) {
+                        const int tok = tok0 + j;
+                        if (tok < tl.row_end) {
+                            T y = Elem<T>::from_f(__uint_as_float(v[j]));
+                            if (biasg) y = Elem<T>::from_f(Elem<T>::to_f(y) + bsum);
+                            og[static_cast<long long>(tok) * N + n] = y;
+                        }
                     }
                 }
             }
@@ -603,22 +586,22 @@ static cudaError_t qgemm_launch_t(const QgemmParams& p, cudaStream_t st) {
     }
     CUtensorMap tx, tw;
     const unsigned long long kw = static_cast<unsigned long long>(p.K) * BITS / 32;
-    if (!qg_map(&tx, p.x, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, p.K, p.M, qg::BK, qg::BM,
+    if (!qg_map(&tx, p.x, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, p.K, p.M, qg::BK, qg::BT,
                 CU_TENSOR_MAP_SWIZZLE_128B) ||
         !qg_map(&tw, p.w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, kw,
-                static_cast<unsigned long long>(p.N) * (p.E > 0 ? p.E : 1), qg::BK * BITS / 32, qg::BN,
+                static_cast<unsigned long long>(p.N) * (p.E > 0 ? p.E : 1), qg::BK * BITS / 32, qg::BW,
                 BITS == 4 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
         return cudaErrorInvalidValue;
-    // grouped: the tile count lives on the device; ceil(rows_e / BM) summed over experts
-    // is at most ceil(M / BM) + E
-    const long long mblocks = (p.M + qg::BM - 1) / qg::BM + (p.E > 0 ? p.E : 0);
-    const long long tiles = mblocks * ((p.N + qg::BN - 1) / qg::BN);
+    // grouped: the tile count lives on the device; ceil(rows_e / BT) summed over experts
+    // is at most ceil(M / BT) + E
+    const long long mblocks = (p.M + qg::BT - 1) / qg::BT + (p.E > 0 ? p.E : 0);
+    const long long tiles = mblocks * ((p.N + qg::BW - 1) / qg::BW);
     const int grid = static_cast<int>(tiles < num_sms[dev] ? tiles : num_sms[dev]);
     kern<<<grid, qg::THREADS, smem, st>>>(tx, tw, p);
     return cudaGetLastError();
 }
 
-// tile_start[e + 1] = tile_start[e] + ceil(rows_e / BM) * NB, one block, E in chunks
+// tile_start[e + 1] = tile_start[e] + ceil(rows_e / BT) * NB, one block, E in chunks
 __global__ void group_tiles_kernel(const int32_t* __restrict__ seg, int E, int rpe, int NB,
                                    int32_t* __restrict__ tile_start) {
     __shared__ int scan[1024];
@@ -633,7 +616,7 @@ __global__ void group_tiles_kernel(const int32_t* __restrict__ seg, int E, int r
         int c = 0;
         if (e < E) {
             const int rows = max(0, (seg[e + 1] - seg[e]) * rpe);
-            c = (rows + qg::BM - 1) / qg::BM * NB;
+            c = (rows + qg::BT - 1) / qg::BT * NB;
         }
         scan[threadIdx.x] = c;
         __syncthreads();
@@ -652,7 +635,7 @@ __global__ void group_tiles_kernel(const int32_t* __restrict__ seg, int E, int r
 
 cudaError_t launch_group_tiles(const int32_t* seg, int E, int rpe, int N, int32_t* tile_start,
                                cudaStream_t st) {
-    group_tiles_kernel<<<1, 1024, 0, st>>>(seg, E, rpe, (N + qg::BN - 1) / qg::BN, tile_start);
+    group_tiles_kernel<<<1, 1024, 0, st>>>(seg, E, rpe, (N + qg::BW - 1) / qg::BW, tile_start);
     return cudaGetLastError();
 }
 
