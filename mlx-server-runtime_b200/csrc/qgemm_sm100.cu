@@ -7,12 +7,13 @@
 // for M > 32 tokens (MLX's quantized_matmul as QuantizedLinear calls it during
 // prefill, qwen2.py:58-61,123-134 of the reference).
 //
-// Output tiles BW = 128 weight rows x BT = 192 tokens, K blocks of BK = 64; one
+// Output tiles BW = 128 weight rows x BT = 192 tokens (128 for experts' row segments),
+// K blocks of BK = 64; one
 // persistent CTA per SM with specialized warps (see qgemm_kernel):
 //   * TMA brings the activation tile in the canonical K-major 128-byte-swizzled
 //     layout (8-row x 128-byte atoms, chunk c of row r at chunk c ^ (r % 8)) that the
 //     MMA reads as its B operand, and the raw packed codes of the 128 weight rows.
-//   * Two threads per weight row dequantize 32 codes each: codes become exact 16-bit
+//   * DQ threads per weight row dequantize 64/DQ codes each: codes become exact 16-bit
 //     values with byte permutes and a magic exponent (no integer-to-float
 //     conversion), then w = scale*q + bias with one packed FMA (one rounding, like
 //     MLX's dequantize-in-kernel), stored straight into tensor memory as the MMA's
@@ -39,18 +40,16 @@ __device__ int g_qgemm_error;  // 0, or the first error code a kernel recorded
 
 namespace qg {
 constexpr int BW = 128;  // weight rows per tile: MMA M, tensor-memory lanes
-constexpr int BT = 192;  // tokens per tile: MMA N
+constexpr int BT_DENSE = 192, BT_GROUPED = 128;  // tokens per tile (MMA N): dense / experts
 constexpr int BK = 64;
 constexpr int ASTAGES = 4;                      // dequantized weight tiles in tensor memory
-constexpr int NDEQ = 8, NEPI = 4;               // dequant / epilogue warps
+constexpr int DQ = 2;                           // dequant warps per tensor-memory lane quarter
+constexpr int NDEQ = 4 * DQ, NEPI = 4;          // dequant / epilogue warps
 constexpr int WARP_TMA = 0, WARP_MMA = 1, WARP_EPI0 = 2, WARP_DEQ0 = WARP_EPI0 + NEPI;
-constexpr int THREADS = (WARP_DEQ0 + NDEQ) * 32;  // 448
-static_assert(NDEQ == 8, "two dequant warps per tensor-memory lane quarter (32 codes each)");
-constexpr int X_BYTES = BT * BK * 2;    // 24 KB activation tile
+constexpr int THREADS = (WARP_DEQ0 + NDEQ) * 32;
+static_assert(DQ == 2 || DQ == 4, "each dequant thread converts 64 / DQ codes of its row");
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kACol0 = 2 * BT;     // first A stage column (after two accumulators)
 constexpr uint32_t kACols = BK / 2;     // 32-bit columns per A stage (two 16-bit values each)
-static_assert(kACol0 + ASTAGES * kACols <= kTmemCols, "tensor memory budget");
 constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr int kErrTimeout = 1;
 // suspending barrier waits: up to kParkLimit waits of about kParkNs each (~4 s)
@@ -59,9 +58,9 @@ template <int BITS>
 constexpr int raw_bytes() { return BW * BK * BITS / 8; }  // 4 KB (4-bit) / 8 KB (8-bit)
 template <int BITS>
 constexpr int load_stages() { return BITS == 4 ? 6 : 5; }
-template <int BITS>
+template <int BITS, int BT>
 constexpr int smem_bytes() {
-    return load_stages<BITS>() * (X_BYTES + raw_bytes<BITS>()) +
+    return load_stages<BITS>() * (BT * BK * 2 + raw_bytes<BITS>()) +
            (2 * load_stages<BITS>() + 2 * ASTAGES + 5) * 8 + 16 + 1024;
 }
 }  // namespace qg
@@ -79,10 +78,10 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
 
 // Instruction descriptor, kind::f16: fp32 accumulate, A/B bf16 or f16, both K-major,
 // M = BW, N = BT.
-template <typename T>
+template <typename T, int BT>
 __host__ __device__ constexpr uint32_t qgemm_idesc() {
     constexpr uint32_t ab = __is_same(T, __nv_bfloat16) ? 1u : 0u;
-    return (1u << 4) | (ab << 7) | (ab << 10) | (static_cast<uint32_t>(qg::BT >> 3) << 17) |
+    return (1u << 4) | (ab << 7) | (ab << 10) | (static_cast<uint32_t>(BT >> 3) << 17) |
            (static_cast<uint32_t>(qg::BW >> 4) << 24);
 }
 
@@ -96,8 +95,16 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, ui
         "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
+// 8 consecutive 32-bit columns of this thread's tensor-memory lane
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+        : "memory");
+}
+
 // 16 consecutive 32-bit columns of this thread's tensor-memory lane
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
         "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(taddr),
@@ -221,30 +228,33 @@ __device__ __forceinline__ uint4 dequant_chunk(const uint32_t* wds, uint32_t s2,
 }
 
 // Persistent, warp-specialized prefill kernel. One CTA per SM walks its share of
-// the output tiles (BW = 128 weight rows x BT = 192 tokens); per K block of 64:
-//   warp 0  (TMA)      the activation tile [192 tokens x 64] (128-byte swizzle: the
+// the output tiles (BW = 128 weight rows x BT tokens); per K block of 64:
+//   warp 0  (TMA)      the activation tile [BT tokens x 64] (128-byte swizzle: the
 //                      MMA's K-major B layout) and the raw packed codes of the tile's
 //                      128 weight rows, into a ring of load stages;
-//   warps 6-13 (dequant) thread = weight row: warps w and w+4 share tensor-memory lane
-//                      quarter w % 4 and take 32 codes each; w = scale*q + bias goes
+//   dequant warps      thread = weight row: DQ warps share each tensor-memory lane
+//                      quarter (w % 4) and take 64/DQ codes each; w = scale*q + bias goes
 //                      straight into a ring of A tiles in tensor memory (tcgen05.st),
 //                      never through shared memory;
-//   warp 1  (MMA)      one thread issues tcgen05.mma M=128 N=192 K=16 x 4 with A from
+//   warp 1  (MMA)      one thread issues tcgen05.mma M=128 N=BT K=16 x 4 with A from
 //                      tensor memory into one of two accumulators and commits the load
 //                      stage and the A tile back to their producers;
 //   warps 2-5 (epilogue) drain the other accumulator (thread = weight row, columns =
 //                      tokens) while the next tile accumulates; optional bias as a
 //                      second rounding.
-template <typename T, int BITS, int GS>
+template <typename T, int BITS, int GS, int BT>
 __global__ void __launch_bounds__(qg::THREADS, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw,
                  const QgemmParams p) {
     using namespace qg;
     constexpr int LS = load_stages<BITS>();
     constexpr int RAW = raw_bytes<BITS>();
+    constexpr int X_BYTES = BT * BK * 2;  // activation tile
     constexpr int LSB = X_BYTES + RAW;    // bytes of one load stage
+    constexpr uint32_t kACol0 = 2 * BT;   // first A stage column (after two accumulators)
+    static_assert(kACol0 + ASTAGES * kACols <= kTmemCols, "tensor memory budget");
     constexpr int WPR = BK * BITS / 32;   // packed words per row per K block
-    constexpr uint32_t IDESC = qgemm_idesc<T>();
+    constexpr uint32_t IDESC = qgemm_idesc<T, BT>();
 
     extern __shared__ uint8_t qg_smem_raw[];
     uint8_t* smem = qg_smem_raw + ((1024u - (smem_u32(qg_smem_raw) & 1023u)) & 1023u);
@@ -363,8 +373,11 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
                 asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
                 for (int kb = 0; kb < KB; ++kb, ++li, ++ai_k) {
                     const int s = li % LS, as = ai_k % ASTAGES;
-                    if (!wait(load_full + s, (li / LS) & 1) ||
-                        !wait(a_full + as, (ai_k / ASTAGES) & 1)) {
+                    // (the single MMA thread polls without parking: it wakes fastest)
+                    if (!mbar_wait_bounded(smem_u32(load_full + s), (li / LS) & 1, kSpinLimit) ||
+                        !mbar_wait_bounded(smem_u32(a_full + as), (ai_k / ASTAGES) & 1, kSpinLimit)) {
+                        atomicCAS(&g_qgemm_error, 0, kErrTimeout);
+                        *s_abort = 1;
                         ok = false;
                         break;
                     }
@@ -388,12 +401,14 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
         // ------------------------------ dequantize ---------------------------------
         const int q = warp & 3;                       // tensor-memory lane quarter
         const int r = q * 32 + lane;                  // weight row within the tile
-        const int hh = (warp - WARP_DEQ0) / 4;        // which 32 codes of the K block
+        const int hh = (warp - WARP_DEQ0) / 4;        // which 64/DQ codes of the K block
+        constexpr int CPTH = BK / DQ;                 // codes per thread per K block
+        constexpr int TCOLS = CPTH / 2;               // tensor-memory columns per thread
         const int G = K / GS;
         const T* sg = static_cast<const T*>(p.s);
         const T* bg = static_cast<const T*>(p.b);
         const uint32_t mlo = opaque(Pair<T>::kMagicLo), mhi = opaque(Pair<T>::kMagicHi);
-        const uint32_t tq = tmem + (static_cast<uint32_t>(q * 32) << 16) + kACol0 + 16 * hh;
+        const uint32_t tq = tmem + (static_cast<uint32_t>(q * 32) << 16) + kACol0 + TCOLS * hh;
         // Scales and biases by 16-byte chunks of 8 groups (rows 16-byte aligned):
         // `cur` is the chunk in use, `nxt` the next one this thread will need along its
         // (tile, chunk) sequence, loaded a whole chunk (4-16 K blocks) early.
@@ -441,7 +456,7 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
             const int n = tl.nb * BW + r;  // row within expert tl.e (n >= N: none)
             for (int kb = 0; kb < KB; ++kb, ++li, ++ai_k) {
                 const int s = li % LS, as = ai_k % ASTAGES;
-                const int g = (kb * BK + hh * 32) / GS;  // this thread's group
+                const int g = (kb * BK + hh * CPTH) / GS;  // this thread's group
                 uint32_t s2, b2;
                 if (vec) {
                     if ((g >> 3) != cur_c || t != cur_t) advance();
@@ -461,27 +476,36 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
                     ok = false;
                     break;
                 }
-                // this thread's half of row r (TMA 32-/64-byte swizzle: 16-byte chunk c
+                // this thread's codes of row r (TMA 32-/64-byte swizzle: 16-byte chunk c
                 // of row r sits at chunk c ^ (r >> 2 & 1) / c ^ (r >> 1 & 3))
-                constexpr int RW = WPR / 2;
+                constexpr int RW = WPR / DQ;  // packed words (1 word = 8 codes / 4 codes)
                 uint32_t raw[RW];
                 const uint8_t* rrow = smem + s * LSB + X_BYTES + r * (WPR * 4);
+                auto phys = [&](int lc) {
+                    return (BITS == 4) ? (lc ^ ((r >> 2) & 1)) : (lc ^ ((r >> 1) & 3));
+                };
+                if constexpr (RW >= 4) {
 #pragma unroll
-                for (int c = 0; c < RW / 4; ++c) {
-                    const int lc = hh * (RW / 4) + c;
-                    const int pc = (BITS == 4) ? (lc ^ ((r >> 2) & 1)) : (lc ^ ((r >> 1) & 3));
-                    const uint4 v = *reinterpret_cast<const uint4*>(rrow + pc * 16);
-                    raw[4 * c] = v.x; raw[4 * c + 1] = v.y; raw[4 * c + 2] = v.z; raw[4 * c + 3] = v.w;
+                    for (int c = 0; c < RW / 4; ++c) {
+                        const uint4 v = *reinterpret_cast<const uint4*>(
+                            rrow + phys(hh * (RW / 4) + c) * 16);
+                        raw[4 * c] = v.x; raw[4 * c + 1] = v.y; raw[4 * c + 2] = v.z; raw[4 * c + 3] = v.w;
+                    }
+                } else {  // 8 bytes: half of a 16-byte chunk
+                    const uint2 v = *reinterpret_cast<const uint2*>(
+                        rrow + phys(hh >> 1) * 16 + (hh & 1) * 8);
+                    raw[0] = v.x; raw[1] = v.y;
                 }
-                uint32_t out16[16];
+                uint32_t outv[TCOLS];
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
+                for (int c = 0; c < CPTH / 8; ++c) {
                     const uint4 v = dequant_chunk<T, BITS>(&raw[c * (BITS == 4 ? 1 : 2)], s2, b2,
                                                           mlo, mhi);
-                    out16[4 * c] = v.x; out16[4 * c + 1] = v.y;
-                    out16[4 * c + 2] = v.z; out16[4 * c + 3] = v.w;
+                    outv[4 * c] = v.x; outv[4 * c + 1] = v.y;
+                    outv[4 * c + 2] = v.z; outv[4 * c + 3] = v.w;
                 }
-                tmem_st16(tq + as * kACols, out16);
+                if constexpr (TCOLS == 16) tmem_st16(tq + as * kACols, outv);
+                else tmem_st8(tq + as * kACols, outv);
                 asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
                 asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
                 __syncwarp();
@@ -567,10 +591,10 @@ bool qg_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esize,
 }
 }  // namespace
 
-template <typename T, int BITS, int GS>
-static cudaError_t qgemm_launch_t(const QgemmParams& p, cudaStream_t st) {
-    auto kern = qgemm_kernel<T, BITS, GS>;
-    constexpr int smem = qg::smem_bytes<BITS>();
+template <typename T, int BITS, int GS, int BT>
+static cudaError_t qgemm_launch_bt(const QgemmParams& p, cudaStream_t st) {
+    auto kern = qgemm_kernel<T, BITS, GS, BT>;
+    constexpr int smem = qg::smem_bytes<BITS, BT>();
     static int configured[64] = {0};
     static int num_sms[64] = {0};
     int dev = 0;
@@ -586,7 +610,7 @@ static cudaError_t qgemm_launch_t(const QgemmParams& p, cudaStream_t st) {
     }
     CUtensorMap tx, tw;
     const unsigned long long kw = static_cast<unsigned long long>(p.K) * BITS / 32;
-    if (!qg_map(&tx, p.x, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, p.K, p.M, qg::BK, qg::BT,
+    if (!qg_map(&tx, p.x, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, p.K, p.M, qg::BK, BT,
                 CU_TENSOR_MAP_SWIZZLE_128B) ||
         !qg_map(&tw, p.w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, kw,
                 static_cast<unsigned long long>(p.N) * (p.E > 0 ? p.E : 1), qg::BK * BITS / 32, qg::BW,
@@ -594,14 +618,21 @@ static cudaError_t qgemm_launch_t(const QgemmParams& p, cudaStream_t st) {
         return cudaErrorInvalidValue;
     // grouped: the tile count lives on the device; ceil(rows_e / BT) summed over experts
     // is at most ceil(M / BT) + E
-    const long long mblocks = (p.M + qg::BT - 1) / qg::BT + (p.E > 0 ? p.E : 0);
+    const long long mblocks = (p.M + BT - 1) / BT + (p.E > 0 ? p.E : 0);
     const long long tiles = mblocks * ((p.N + qg::BW - 1) / qg::BW);
     const int grid = static_cast<int>(tiles < num_sms[dev] ? tiles : num_sms[dev]);
     kern<<<grid, qg::THREADS, smem, st>>>(tx, tw, p);
     return cudaGetLastError();
 }
 
-// tile_start[e + 1] = tile_start[e] + ceil(rows_e / BT) * NB, one block, E in chunks
+// Experts' row segments are short (a few hundred rows): 128-token tiles waste less.
+template <typename T, int BITS, int GS>
+static cudaError_t qgemm_launch_t(const QgemmParams& p, cudaStream_t st) {
+    if (p.E > 0) return qgemm_launch_bt<T, BITS, GS, qg::BT_GROUPED>(p, st);
+    return qgemm_launch_bt<T, BITS, GS, qg::BT_DENSE>(p, st);
+}
+
+// tile_start[e + 1] = tile_start[e] + ceil(rows_e / BT_GROUPED) * NB, one block, E in chunks
 __global__ void group_tiles_kernel(const int32_t* __restrict__ seg, int E, int rpe, int NB,
                                    int32_t* __restrict__ tile_start) {
     __shared__ int scan[1024];
@@ -616,7 +647,7 @@ __global__ void group_tiles_kernel(const int32_t* __restrict__ seg, int E, int r
         int c = 0;
         if (e < E) {
             const int rows = max(0, (seg[e + 1] - seg[e]) * rpe);
-            c = (rows + qg::BT - 1) / qg::BT * NB;
+            c = (rows + qg::BT_GROUPED - 1) / qg::BT_GROUPED * NB;
         }
         scan[threadIdx.x] = c;
         __syncthreads();
