@@ -236,21 +236,34 @@ __global__ void __launch_bounds__(qt::THREADS, 1)
     const int ctid = threadIdx.x;  // 0 .. CTHREADS-1
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
 
-    // x[M, K] -> f16 B fragments and records. Item i = ((g * TM + t) * 4 + c): lane
-    // c of token slot t in group g holds words c, c+4, ... of the group (the words
-    // ldmatrix gives that lane). G*TM*4 is a multiple of 32 (G % 8 == 0), so every
-    // warp runs whole iterations and the 4 lanes of an item share a warp.
+    // x[M, K] -> f16 B fragments and records, for the groups this CTA's units use:
+    // stages u % S of its share, at most two ranges [ga0, ga1) and [gb0, gb1) of
+    // groups. Item i = ((j * TM + t) * 4 + c), j the group's position in those ranges:
+    // lane c of token slot t holds words c, c+4, ... of the group (the words ldmatrix
+    // gives that lane). The ranges are whole stages (8 groups), so the item count is
+    // a multiple of 32: every warp runs whole iterations and the 4 lanes of an item
+    // share a warp.
     {
         const T* xg = static_cast<const T*>(p.x);
         constexpr int XW = BITS == 4 ? 8 : 4;  // activations per packed word
         constexpr int PB = (CPG * XW / 2 <= 8) ? 4 : 2;  // items with loads in flight together
-        const int total = G * TM * 4;
+        int ga0 = 0, ga1 = G, gb0 = 0, gb1 = 0;
+        if (u_hi - u_lo < S) {
+            const int s0 = static_cast<int>(u_lo % S);
+            const int s1 = s0 + static_cast<int>(u_hi - u_lo);
+            ga0 = s0 * SG;
+            ga1 = min(s1, S) * SG;
+            gb1 = s1 > S ? (s1 - S) * SG : 0;
+        }
+        const int na = ga1 - ga0;
+        const int total = (na + gb1 - gb0) * TM * 4;
         for (int i0 = ctid; i0 < total; i0 += PB * CTHREADS) {
           uint32_t raw[PB][CPG][XW / 2];
 #pragma unroll
           for (int b = 0; b < PB; ++b) {
             const int i = i0 + b * CTHREADS;
-            const int cc = i & 3, t = (i >> 2) % TM, g = (i >> 2) / TM;
+            const int cc = i & 3, t = (i >> 2) % TM, j = (i >> 2) / TM;
+            const int g = j < na ? ga0 + j : gb0 + (j - na);
 #pragma unroll
             for (int w = 0; w < CPG; ++w) {
                 const long long off = static_cast<long long>(t) * p.K + g * GS + (4 * w + cc) * XW;
@@ -269,7 +282,8 @@ __global__ void __launch_bounds__(qt::THREADS, 1)
           for (int b = 0; b < PB; ++b) {
             const int i = i0 + b * CTHREADS;
             if (i >= total) break;  // warp-uniform: total and CTHREADS are multiples of 32
-            const int cc = i & 3, t = (i >> 2) % TM, g = (i >> 2) / TM;
+            const int cc = i & 3, t = (i >> 2) % TM, j = (i >> 2) / TM;
+            const int g = j < na ? ga0 + j : gb0 + (j - na);
             float v[CPG][XW];
             float m = 0.f;
 #pragma unroll
