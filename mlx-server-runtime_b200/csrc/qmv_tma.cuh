@@ -534,14 +534,16 @@ __global__ void __launch_bounds__(qt::THREADS, 1)
                         if (t < M && row0 + rw < N) part[(ci * M + t) * BR + rw] = acc[2 * hh + q];
                     }
                 }
-                __threadfence();
             }
+            // The barrier orders every thread's partial before thread 0's acq_rel
+            // ticket; its release makes them visible GPU-wide (cumulatively) and its
+            // acquire, with the second barrier, the other CTAs' partials to this one.
             named_bar_sync(1, CTHREADS);
             if (ctid == 0)
-                *s_last = (!abort && atomicAdd(p.counter + rb, 1u) == static_cast<unsigned>(nc - 1));
+                *s_last = (!abort && atom_add_acq_rel_gpu(p.counter + rb, 1u) ==
+                                         static_cast<unsigned>(nc - 1));
             named_bar_sync(1, CTHREADS);
             if (*s_last) {
-                __threadfence();
                 const int rows_here = min(BR, N - row0);
                 for (int idx = ctid; idx < M * rows_here; idx += CTHREADS) {
                     const int t = idx / rows_here, rw = idx % rows_here;

@@ -95,6 +95,16 @@ __device__ __forceinline__ void ldmatrix_x2(uint32_t addr, uint32_t& r0, uint32_
                  : "r"(addr));
 }
 
+// atomicAdd with acquire-release semantics at GPU scope; returns the old value.
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* addr, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;\n"
+                 : "=r"(old)
+                 : "l"(addr), "r"(v)
+                 : "memory");
+    return old;
+}
+
 // Barrier over a subset of the CTA's warps (id 1..15; `threads` a multiple of 32).
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(threads) : "memory");
