@@ -59,6 +59,8 @@ bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esiz
 constexpr int kCtasPerSm = 2;
 // CTAs launched per SM (stream-K shares = kGridPerSm x SMs).
 constexpr int kGridPerSm = 1;
+// Row blocks of at most this many units go whole to one CTA when they fit on the SMs.
+constexpr int kWholeRowBlockStages = 8;
 
 bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms, int max_smem,
                   int sm_smem, QtPlan* plan) {
@@ -81,6 +83,9 @@ bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms,
     pl.S = G / qt::SG;
     pl.U = static_cast<long long>(pl.RB) * pl.S;
     pl.P = static_cast<int>(std::min<long long>(pl.U, static_cast<long long>(num_sms) * kGridPerSm));
+    // Short row blocks that fit on the SMs are not split at all: one CTA per row block
+    // needs no ticket reduction, which costs more than the extra units per CTA.
+    if (pl.RB <= num_sms && pl.S <= kWholeRowBlockStages) pl.P = pl.RB;
     const long long per_cta = (pl.U + pl.P - 1) / pl.P;
     int stages = std::min((max_smem - fixed) / stage, qt::MAX_STAGES);
     stages = static_cast<int>(std::min<long long>(stages, std::max<long long>(2, per_cta)));
