@@ -75,9 +75,10 @@ cudaError_t qmv_launch(int dtype, int bits, int gs, const QmvPlan& plan, const Q
                        cudaStream_t st);
 
 // Plan of the TMA-fed decode kernel (qmv_tma.cu): M <= 8 tokens, K/group_size a
-// multiple of 8. Units of 64 rows x 8 groups, split evenly over P CTAs.
+// multiple of 8. Units of BR rows x 8 groups, split evenly over P CTAs.
 struct QtPlan {
-    int RB;        // 64-row blocks
+    int BR;        // rows per unit (64 or 16)
+    int RB;        // row blocks of BR rows
     int S;         // units per row block
     long long U;   // units
     int P;         // CTAs

@@ -2,6 +2,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "qmv_tma.cuh"
@@ -10,16 +11,11 @@ namespace mlxq {
 
 __device__ int g_qmv_tma_error;
 
-template <typename T, int BITS, int GS, int TM>
+template <typename T, int BITS, int GS, int TM, int BR>
 cudaError_t qt_launch_t(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tb,
                         const QtParams& p, int grid, size_t smem, bool overlap, cudaStream_t st);
 
 namespace {
-
-int stage_bytes(int bits, int gs) {
-    const int boxes = gs * bits / 128;
-    return boxes * qt::BR * 128 + 2 * qt::BR * qt::SG * 2;
-}
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -59,8 +55,19 @@ bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esiz
 constexpr int kCtasPerSm = 2;
 // CTAs launched per SM (stream-K shares = kGridPerSm x SMs).
 constexpr int kGridPerSm = 1;
-// Row blocks of at most this many units go whole to one CTA when they fit on the SMs.
+// 64-row blocks of at most this many units go whole to one CTA when they fit on the SMs.
 constexpr int kWholeRowBlockStages = 8;
+
+// Unit rows forced by the MLXQ_DECODE_ROWS environment variable (16 or 64; read
+// once), else 0: the plan chooses.
+static int rows_override() {
+    static int v = [] {
+        const char* e = std::getenv("MLXQ_DECODE_ROWS");
+        const int r = e ? std::atoi(e) : 0;
+        return (r == 16 || r == 64) ? r : 0;
+    }();
+    return v;
+}
 
 bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms, int max_smem,
                   int sm_smem, QtPlan* plan) {
@@ -74,23 +81,36 @@ bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms,
     // the driver reserves 1 KB of shared memory per CTA
     max_smem = std::min(max_smem, sm_smem / kCtasPerSm - 1024);
     const int TM = qt::token_slots(M);
-    const int stage = stage_bytes(bits, gs);
-    const int fixed = qt::layout(stage, 0, G, TM, gs * 2).total + 1024;  // + alignment slack
+    // Unit rows: a matrix with short rows (at most kWholeRowBlockStages stages) whose
+    // 16-row blocks all fit on the SMs at kCtasPerSm CTAs per SM takes one CTA per
+    // 16-row block: no split row block, hence no ticket reduction, and a short chain
+    // of stages per CTA. Everything else streams 64-row units.
+    int br = rows_override();
+    if (!br)
+        br = ((N + 15) / 16 <= kCtasPerSm * num_sms && G / qt::SG <= kWholeRowBlockStages)
+                 ? 16 : 64;
+    const int rt = br / 16;
+    const int stage = qt::stage_stride(bits, gs, br);
+    const int fixed = qt::layout(stage, 0, G, TM, gs * 2, rt).total + 1024;  // + alignment slack
     if (fixed + 2 * stage > max_smem) return false;
     QtPlan pl{};
-    pl.RB = (N + qt::BR - 1) / qt::BR;
+    pl.BR = br;
+    pl.RB = (N + br - 1) / br;
     if (static_cast<size_t>(pl.RB) * 4 > kTicketBytes) return false;
     pl.S = G / qt::SG;
     pl.U = static_cast<long long>(pl.RB) * pl.S;
     pl.P = static_cast<int>(std::min<long long>(pl.U, static_cast<long long>(num_sms) * kGridPerSm));
-    // Short row blocks that fit on the SMs are not split at all: one CTA per row block
-    // needs no ticket reduction, which costs more than the extra units per CTA.
-    if (pl.RB <= num_sms && pl.S <= kWholeRowBlockStages) pl.P = pl.RB;
+    // Row blocks that fit on the SMs are not split at all: one CTA per row block needs
+    // no ticket reduction, which costs more than the extra units per CTA. (64-row
+    // blocks only when short: one CTA per SM, the chain of stages grows with K.)
+    if (br < 64 ? pl.RB <= kCtasPerSm * num_sms
+                : (pl.RB <= num_sms && pl.S <= kWholeRowBlockStages))
+        pl.P = pl.RB;
     const long long per_cta = (pl.U + pl.P - 1) / pl.P;
     int stages = std::min((max_smem - fixed) / stage, qt::MAX_STAGES);
     stages = static_cast<int>(std::min<long long>(stages, std::max<long long>(2, per_cta)));
     pl.stages = std::max(2, stages);
-    pl.smem = static_cast<size_t>(qt::layout(stage, pl.stages, G, TM, gs * 2).total) + 1024;
+    pl.smem = static_cast<size_t>(qt::layout(stage, pl.stages, G, TM, gs * 2, rt).total) + 1024;
     int maxc = 1;
     for (int rb = 0; rb < pl.RB; ++rb) {
         const long long ub = static_cast<long long>(rb) * pl.S;
@@ -101,17 +121,22 @@ bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms,
     pl.ws_bytes = 0;
     if (maxc > 1)
         pl.ws_bytes = kTicketBytes +
-                      static_cast<size_t>(pl.RB) * maxc * M * qt::BR * 4;
+                      static_cast<size_t>(pl.RB) * maxc * M * br * 4;
     *plan = pl;
     return true;
 }
 
-#define QT_CASE(T, BITS, GS)                                                                    \
+#define QT_CASE_TM(T, BITS, GS, BR)                                                            \
     switch (qt::token_slots(M)) {                                                               \
-        case 1: return qt_launch_t<T, BITS, GS, 1>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
-        case 2: return qt_launch_t<T, BITS, GS, 2>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
-        case 4: return qt_launch_t<T, BITS, GS, 4>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
-        default: return qt_launch_t<T, BITS, GS, 8>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
+        case 1: return qt_launch_t<T, BITS, GS, 1, BR>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
+        case 2: return qt_launch_t<T, BITS, GS, 2, BR>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
+        case 4: return qt_launch_t<T, BITS, GS, 4, BR>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
+        default: return qt_launch_t<T, BITS, GS, 8, BR>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
+    }
+#define QT_CASE(T, BITS, GS)                                     \
+    switch (plan.BR) {                                           \
+        case 16: QT_CASE_TM(T, BITS, GS, 16)                     \
+        default: QT_CASE_TM(T, BITS, GS, 64)                     \
     }
 
 template <typename T>
@@ -150,11 +175,12 @@ cudaError_t qmv_tma_launch(int dtype, int bits, int gs, const QtPlan& plan, cons
     const int G = K / gs;
     const unsigned long long kw = static_cast<unsigned long long>(K) * bits / 32;
     CUtensorMap tw, ts, tb;
-    if (!make_map(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, kw, N, 32, qt::BR,
+    const unsigned br = static_cast<unsigned>(plan.BR);
+    if (!make_map(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, kw, N, 32, br,
                   CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map(&ts, s, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, G, N, qt::SG, qt::BR,
+        !make_map(&ts, s, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, G, N, qt::SG, br,
                   CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_map(&tb, b, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, G, N, qt::SG, qt::BR,
+        !make_map(&tb, b, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, G, N, qt::SG, br,
                   CU_TENSOR_MAP_SWIZZLE_NONE))
         return cudaErrorInvalidValue;
     QtParams p{};

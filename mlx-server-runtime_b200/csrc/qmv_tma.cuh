@@ -5,25 +5,28 @@
 // MLX's quantized_matmul with transpose=True as QuantizedLinear calls it at
 // decode (qwen2.py:58-61,123-134 of the reference).
 //
-// Work: the weight matrix is cut into units of 64 rows x 8 quantization groups
-// (one pipeline stage). Units are numbered row-block-major and each CTA takes a
-// contiguous, equal share (stream-K): every SM streams the same number of
-// bytes whatever N and K are. A row block whose units span several CTAs is
-// finished by the last of them (atomic ticket, no waiting), which adds the fp32
-// partials in CTA order, so results are deterministic.
+// Work: the weight matrix is cut into units of BR rows x 8 quantization groups
+// (one pipeline stage), BR = 64, or 16 for matrices with few, short rows. Units
+// are numbered row-block-major and each CTA takes a contiguous, equal share
+// (stream-K): every SM streams the same number of bytes whatever N and K are. A
+// row block whose units span several CTAs is finished by the last of them (atomic
+// ticket, no waiting), which adds the fp32 partials in CTA order, so results are
+// deterministic. When every row block fits on the SMs, each CTA takes one whole
+// row block instead and no ticket is needed.
 //
 // Per CTA: one producer warp and 8 consumer warps.
 //   * Producer (one thread): for every unit, 2-D TMA loads of the packed
-//     weights [64 rows x 128 B] per box (128-byte swizzle) plus one box each of
-//     scales and biases [64 rows x 8 groups], into a ring of `stages` slots with
+//     weights [BR rows x 128 B] per box (128-byte swizzle) plus one box each of
+//     scales and biases [BR rows x 8 groups], into a ring of `stages` slots with
 //     full/empty mbarriers. The ring holds most of the CTA's share, so nearly
 //     all of it is requested from HBM at kernel start.
 //   * Consumers: warp (rt, kq) owns row tile rt (16 rows) and GPW groups, GPW*kq..,
-//     of every stage. ldmatrix reads the swizzled tiles without bank conflicts
-//     and hands lane (r, c) words c, c+4, ... of the group for rows r and r+8.
-//     Codes become exact f16 MMA operands with one LOP3 per pair (see
-//     Elem<__half>::extract); one m16n8k16 MMA covers 16 codes x 8 token slots
-//     into a fresh fp32 accumulator per group.
+//     of every stage (64-row units: 4 row tiles x 2 warps of 4 groups; 16-row
+//     units: 1 row tile x 8 warps of 1 group). ldmatrix reads the swizzled tiles
+//     without bank conflicts and hands lane (r, c) words c, c+4, ... of the group
+//     for rows r and r+8. Codes become exact f16 MMA operands with one LOP3 per
+//     pair (see Elem<__half>::extract); one m16n8k16 MMA covers 16 codes x 8
+//     token slots into a fresh fp32 accumulator per group.
 //   * Activations: x[M, K] is staged once as f16 MMA B fragments. Each (group,
 //     token) slice is multiplied by a power of two 2^e that brings its largest
 //     magnitude into [2^14, 2^15), which makes the bf16 (or f16) values exact in
@@ -47,14 +50,21 @@
 namespace mlxq {
 
 namespace qt {
-constexpr int BR = 64;                   // weight rows per unit
 constexpr int SG = 8;                    // quantization groups per unit (stage)
-constexpr int RT = BR / 16;              // 16-row MMA tiles per unit
-constexpr int GPW = 4;                   // groups of a stage per consumer warp (even)
-constexpr int KSW = SG / GPW;            // consumer warps per row tile
-constexpr int CWARPS = RT * KSW;         // consumer warps
+constexpr int CWARPS = 8;                // consumer warps
 constexpr int CTHREADS = CWARPS * 32;
 constexpr int THREADS = CTHREADS + 32;   // + producer warp
+// Split of the 8 consumer warps over a unit of BR weight rows (64 or 16): RT
+// row tiles of 16 rows times KSW warps along K, each warp taking GPW of the
+// stage's 8 groups. Shorter units put more CTAs on a matrix with few rows and
+// shorten each CTA's chain of stages when its row blocks are not split.
+template <int BR>
+struct Rows {
+    static_assert(BR == 16 || BR == 64, "unit rows");
+    static constexpr int RT = BR / 16;
+    static constexpr int KSW = CWARPS / RT;
+    static constexpr int GPW = SG / KSW;
+};
 constexpr int MAXM = 8;                  // tokens per launch
 constexpr int MAX_STAGES = 16;
 constexpr uint32_t kSpinLimit = 1u << 22;
@@ -65,30 +75,44 @@ __host__ __device__ constexpr int token_slots(int M) {
     return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8;
 }
 
-template <int BITS, int GS>
+// Bytes one stage's TMA copies deliver (packed codes, scales, biases) and the
+// stage's stride in the ring (rounded up to the 1024-byte period of the 128-byte
+// swizzle, so every stage's boxes start on it).
+__host__ __device__ constexpr int stage_tx(int bits, int gs, int br) {
+    return (SG * gs * bits / 32 / 32) * br * 128 + 2 * br * SG * 2;
+}
+__host__ __device__ constexpr int stage_stride(int bits, int gs, int br) {
+    return (stage_tx(bits, gs, br) + 1023) / 1024 * 1024;
+}
+
+template <int BITS, int GS, int BR>
 struct Geo {
     static constexpr int WPG = GS * BITS / 32;     // packed words per group per row
     static constexpr int CPG = WPG / 4;            // 16-byte chunks per group per row
     static constexpr int BOXES = SG * WPG / 32;    // 128-byte TMA boxes per stage
     static constexpr int W_BYTES = BOXES * BR * 128;
     static constexpr int SB_BYTES = BR * SG * 2;   // scales (or biases) of one stage
-    static constexpr int STAGE = W_BYTES + 2 * SB_BYTES;
+    static constexpr int STAGE_TX = W_BYTES + 2 * SB_BYTES;
+    static constexpr int STAGE = stage_stride(BITS, GS, BR);
     static constexpr int FR = (BITS == 4) ? 4 * CPG : 2 * CPG;  // B-fragment words per lane
     static constexpr int XG = GS * 2;              // fragment bytes per (group, token slot)
-    static_assert(CPG >= 1 && BOXES >= 1 && STAGE % 1024 == 0, "unsupported geometry");
+    static_assert(CPG >= 1 && BOXES >= 1 && STAGE_TX == stage_tx(BITS, GS, BR),
+                  "unsupported geometry");
 };
 
-// Shared-memory layout (from a 1024-byte aligned base), in bytes.
+// Shared-memory layout (from a 1024-byte aligned base), in bytes; rt = row tiles
+// per unit (the cross-warp reduction holds (KSW - 1) * RT = 8 - rt warp tiles).
 struct Layout {
     int ring, xf, rec, red, bars, flags, total;
 };
-__host__ __device__ inline Layout layout(int stage_bytes, int stages, int G, int TM, int xg) {
+__host__ __device__ inline Layout layout(int stage_bytes, int stages, int G, int TM, int xg,
+                                         int rt) {
     Layout L;
     L.ring = 0;
     L.xf = stages * stage_bytes;               // [G][FR/4][TM][4 lanes] x 16 B
     L.rec = L.xf + G * TM * xg;                // [G][TM] float4 records
     L.red = L.rec + G * TM * 16;               // cross-warp reduction
-    L.bars = (L.red + (KSW - 1) * RT * 4 * 32 * 4 + 7) & ~7;
+    L.bars = (L.red + (CWARPS - rt) * 4 * 32 * 4 + 7) & ~7;
     L.flags = (L.bars + 2 * stages * 8 + 15) & ~15;  // abort, last
     L.total = L.flags + 16;
     return L;
@@ -136,7 +160,7 @@ struct QtParams {
     int* err;           // device error flag
 };
 
-template <typename T, int BITS, int GS, int TM>
+template <typename T, int BITS, int GS, int TM, int BR>
 __global__ void __launch_bounds__(qt::THREADS, 1)
     qmv_tma_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ts,
                    const __grid_constant__ CUtensorMap tb, const QtParams p) {
@@ -144,9 +168,10 @@ __global__ void __launch_bounds__(qt::THREADS, 1)
     using ET = Elem<T>;        // activation / output type
     using EH = Elem<__half>;   // MMA operand type
     using OFF = typename EH::template Off<BITS>;
-    using GEO = Geo<BITS, GS>;
+    using GEO = Geo<BITS, GS, BR>;
     constexpr int WPG = GEO::WPG, CPG = GEO::CPG, FR = GEO::FR, XG = GEO::XG;
     constexpr int STAGE = GEO::STAGE, W_BYTES = GEO::W_BYTES, SB_BYTES = GEO::SB_BYTES;
+    constexpr int RT = Rows<BR>::RT, KSW = Rows<BR>::KSW, GPW = Rows<BR>::GPW;
     constexpr bool ODD = TM > 1;
 
     extern __shared__ __align__(16) uint8_t qt_smem_raw[];
@@ -154,7 +179,7 @@ __global__ void __launch_bounds__(qt::THREADS, 1)
     // array by pointer arithmetic so every access stays a shared-memory access
     uint8_t* base = qt_smem_raw + ((1024u - (smem_u32(qt_smem_raw) & 1023u)) & 1023u);
     const int M = p.M, N = p.N, G = p.G, S = p.S, stages = p.stages;
-    const Layout L = layout(STAGE, stages, G, TM, XG);
+    const Layout L = layout(STAGE, stages, G, TM, XG, RT);
     uint8_t* ring = base + L.ring;
     uint8_t* xf = base + L.xf;
     float4* rec = reinterpret_cast<float4*>(base + L.rec);
@@ -205,7 +230,7 @@ __global__ void __launch_bounds__(qt::THREADS, 1)
                 }
                 const uint32_t dst = smem_u32(ring + slot * STAGE);
                 const uint32_t bar = smem_u32(full + slot);
-                mbar_arrive_expect_tx(bar, STAGE);
+                mbar_arrive_expect_tx(bar, GEO::STAGE_TX);
 #pragma unroll
                 for (int b = 0; b < GEO::BOXES; ++b)
                     tma_load_2d(dst + b * (BR * 128), &tw, bar, (st * SG * WPG) + b * 32, rb * BR);
@@ -372,7 +397,10 @@ __global__ void __launch_bounds__(qt::THREADS, 1)
     }
     //   packed (scale, scale) / (bias, bias) words of the warp's group pairs, rows r, r+8,
     const int rr = 16 * rt + r;
-    const int so0 = W_BYTES + (rr * 4 + GPW / 2 * kq) * 4, so1 = so0 + 8 * 16;
+    //   (a warp with one group reads the word holding it and shifts it down),
+    constexpr int SBW = GPW >= 2 ? GPW / 2 : 1;
+    const int so0 = W_BYTES + rr * 16 + ((GPW * kq) & ~1) * 2, so1 = so0 + 8 * 16;
+    const int sb_sh = GPW == 1 ? 16 * (kq & 1) : 0;
     //   the B fragments of token slot r (lanes past the last slot repeat a slot:
     //   their MMA columns are never read),
     const int tr = r & (TM - 1);
@@ -402,13 +430,17 @@ __global__ void __launch_bounds__(qt::THREADS, 1)
             }
             const uint8_t* stg = ring + slot * STAGE;
             const uint32_t stg_s = smem_u32(stg);
-            uint32_t s_r0[GPW / 2], s_r1[GPW / 2], b_r0[GPW / 2], b_r1[GPW / 2];
+            uint32_t s_r0[SBW], s_r1[SBW], b_r0[SBW], b_r1[SBW];
 #pragma unroll
-            for (int q = 0; q < GPW / 2; ++q) {
+            for (int q = 0; q < SBW; ++q) {
                 s_r0[q] = *reinterpret_cast<const uint32_t*>(stg + so0 + 4 * q);
                 s_r1[q] = *reinterpret_cast<const uint32_t*>(stg + so1 + 4 * q);
                 b_r0[q] = *reinterpret_cast<const uint32_t*>(stg + so0 + 4 * q + SB_BYTES);
                 b_r1[q] = *reinterpret_cast<const uint32_t*>(stg + so1 + 4 * q + SB_BYTES);
+            }
+            if constexpr (GPW == 1) {
+                s_r0[0] >>= sb_sh; s_r1[0] >>= sb_sh;
+                b_r0[0] >>= sb_sh; b_r1[0] >>= sb_sh;
             }
 #pragma unroll
             for (int h = 0; h < GPW; ++h) {

@@ -6,10 +6,10 @@
 
 namespace mlxq {
 
-template <typename T, int BITS, int GS, int TM>
+template <typename T, int BITS, int GS, int TM, int BR>
 cudaError_t qt_launch_t(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tb,
                         const QtParams& p, int grid, size_t smem, bool overlap, cudaStream_t st) {
-    auto kern = qmv_tma_kernel<T, BITS, GS, TM>;
+    auto kern = qmv_tma_kernel<T, BITS, GS, TM, BR>;
     static int configured[64] = {0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -34,21 +34,22 @@ cudaError_t qt_launch_t(const CUtensorMap& tw, const CUtensorMap& ts, const CUte
     return cudaLaunchKernelEx(&cfg, kern, tw, ts, tb, p);
 }
 
-#define MLXQ_QT_INST0(T, BITS, GS, TM)                                                          \
-    template cudaError_t qt_launch_t<T, BITS, GS, TM>(const CUtensorMap&, const CUtensorMap&,    \
-                                                      const CUtensorMap&, const QtParams&, int,  \
-                                                      size_t, bool, cudaStream_t);
-#define MLXQ_QT_INST1(T, BITS, GS) \
-    MLXQ_QT_INST0(T, BITS, GS, 1)  \
-    MLXQ_QT_INST0(T, BITS, GS, 2)  \
-    MLXQ_QT_INST0(T, BITS, GS, 4)  \
-    MLXQ_QT_INST0(T, BITS, GS, 8)
+#define MLXQ_QT_INST0(T, BITS, GS, TM, BR)                                                      \
+    template cudaError_t qt_launch_t<T, BITS, GS, TM, BR>(                                       \
+        const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const QtParams&, int, size_t, \
+        bool, cudaStream_t);
+#define MLXQ_QT_INST1(T, BITS, GS, BR) \
+    MLXQ_QT_INST0(T, BITS, GS, 1, BR)  \
+    MLXQ_QT_INST0(T, BITS, GS, 2, BR)  \
+    MLXQ_QT_INST0(T, BITS, GS, 4, BR)  \
+    MLXQ_QT_INST0(T, BITS, GS, 8, BR)
 
-#define MLXQ_INSTANTIATE_QT(T)  \
-    MLXQ_QT_INST1(T, 4, 32)     \
-    MLXQ_QT_INST1(T, 4, 64)     \
-    MLXQ_QT_INST1(T, 4, 128)    \
-    MLXQ_QT_INST1(T, 8, 32)     \
-    MLXQ_QT_INST1(T, 8, 64)
+// Every (bits, group size) the plan accepts, for activation type T and BR-row units.
+#define MLXQ_INSTANTIATE_QT(T, BR)  \
+    MLXQ_QT_INST1(T, 4, 32, BR)     \
+    MLXQ_QT_INST1(T, 4, 64, BR)     \
+    MLXQ_QT_INST1(T, 4, 128, BR)    \
+    MLXQ_QT_INST1(T, 8, 32, BR)     \
+    MLXQ_QT_INST1(T, 8, 64, BR)
 
 }  // namespace mlxq
