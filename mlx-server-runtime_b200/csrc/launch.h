@@ -84,6 +84,7 @@ struct QtPlan {
     int P;         // CTAs
     int stages;    // ring depth
     int maxc;      // most CTAs sharing one row block
+    bool heads;    // a ticket warp takes the head row blocks' tickets (64-row units)
     size_t smem;
     size_t ws_bytes;  // workspace (tickets + partials) when a row block is shared
 };

@@ -11,7 +11,7 @@ namespace mlxq {
 
 __device__ int g_qmv_tma_error;
 
-template <typename T, int BITS, int GS, int TM, int BR>
+template <typename T, int BITS, int GS, int TM, int BR, bool HEADS>
 cudaError_t qt_launch_t(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tb,
                         const QtParams& p, int grid, size_t smem, bool overlap, cudaStream_t st);
 
@@ -57,6 +57,9 @@ constexpr int kCtasPerSm = 2;
 constexpr int kGridPerSm = 1;
 // 64-row blocks of at most this many units go whole to one CTA when they fit on the SMs.
 constexpr int kWholeRowBlockStages = 8;
+// Shares of at most this many units hand their head row block's ticket to a ticket
+// warp: the consumers' wait for the atomic is then a large part of a short share.
+constexpr int kHeadTicketUnits = 32;
 
 // Unit rows forced by the MLXQ_DECODE_ROWS environment variable (16 or 64; read
 // once), else 0: the plan chooses.
@@ -118,6 +121,13 @@ bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms,
         maxc = std::max(maxc, nc);
     }
     pl.maxc = maxc;
+    pl.heads = false;
+    if (br == 64 && maxc > 1 && per_cta <= kHeadTicketUnits) {
+        for (int b = 0; b < pl.P && !pl.heads; ++b) {
+            const long long lo = pl.U * b / pl.P, hi = pl.U * (b + 1) / pl.P;
+            pl.heads = (lo % pl.S) != 0 && hi > (lo / pl.S + 1) * pl.S;
+        }
+    }
     pl.ws_bytes = 0;
     if (maxc > 1)
         pl.ws_bytes = kTicketBytes +
@@ -126,18 +136,17 @@ bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms,
     return true;
 }
 
-#define QT_CASE_TM(T, BITS, GS, BR)                                                            \
-    switch (qt::token_slots(M)) {                                                               \
-        case 1: return qt_launch_t<T, BITS, GS, 1, BR>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
-        case 2: return qt_launch_t<T, BITS, GS, 2, BR>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
-        case 4: return qt_launch_t<T, BITS, GS, 4, BR>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
-        default: return qt_launch_t<T, BITS, GS, 8, BR>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
+#define QT_CASE_TM(T, BITS, GS, BR, H)                                                          \
+    switch (qt::token_slots(M)) {                                                                \
+        case 1: return qt_launch_t<T, BITS, GS, 1, BR, H>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
+        case 2: return qt_launch_t<T, BITS, GS, 2, BR, H>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
+        case 4: return qt_launch_t<T, BITS, GS, 4, BR, H>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
+        default: return qt_launch_t<T, BITS, GS, 8, BR, H>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
     }
-#define QT_CASE(T, BITS, GS)                                     \
-    switch (plan.BR) {                                           \
-        case 16: QT_CASE_TM(T, BITS, GS, 16)                     \
-        default: QT_CASE_TM(T, BITS, GS, 64)                     \
-    }
+#define QT_CASE(T, BITS, GS)                                                  \
+    if (plan.BR == 16) { QT_CASE_TM(T, BITS, GS, 16, false) }                 \
+    if (plan.heads) { QT_CASE_TM(T, BITS, GS, 64, true) }                     \
+    QT_CASE_TM(T, BITS, GS, 64, false)
 
 template <typename T>
 static cudaError_t qt_dispatch(int bits, int gs, int M, const CUtensorMap& tw,

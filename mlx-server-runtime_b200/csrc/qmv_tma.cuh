@@ -53,7 +53,8 @@ namespace qt {
 constexpr int SG = 8;                    // quantization groups per unit (stage)
 constexpr int CWARPS = 8;                // consumer warps
 constexpr int CTHREADS = CWARPS * 32;
-constexpr int THREADS = CTHREADS + 32;   // + producer warp
+// + producer warp (+ ticket warp in the kernels that hand off head tickets)
+__host__ __device__ constexpr int threads(bool heads) { return CTHREADS + (heads ? 64 : 32); }
 // Split of the 8 consumer warps over a unit of BR weight rows (64 or 16): RT
 // row tiles of 16 rows times KSW warps along K, each warp taking GPW of the
 // stage's 8 groups. Shorter units put more CTAs on a matrix with few rows and
@@ -69,6 +70,9 @@ constexpr int MAXM = 8;                  // tokens per launch
 constexpr int MAX_STAGES = 16;
 constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr int kErrTimeout = 2;
+// The ticket warp parks (suspend-time hint) while the consumers finish a head row block.
+constexpr uint32_t kTicketParkNs = 1000;
+constexpr uint32_t kTicketParkLimit = 1u << 20;
 
 // Token slots a kernel instance is compiled for; M is rounded up to one of them.
 __host__ __device__ constexpr int token_slots(int M) {
@@ -113,7 +117,8 @@ __host__ __device__ inline Layout layout(int stage_bytes, int stages, int G, int
     L.rec = L.xf + G * TM * xg;                // [G][TM] float4 records
     L.red = L.rec + G * TM * 16;               // cross-warp reduction
     L.bars = (L.red + (CWARPS - rt) * 4 * 32 * 4 + 7) & ~7;
-    L.flags = (L.bars + 2 * stages * 8 + 15) & ~15;  // abort, last
+    // full[stages], empty[stages], head_done, ticket_done
+    L.flags = (L.bars + (2 * stages + 2) * 8 + 15) & ~15;  // abort, last, head_last
     L.total = L.flags + 16;
     return L;
 }
@@ -160,8 +165,8 @@ struct QtParams {
     int* err;           // device error flag
 };
 
-template <typename T, int BITS, int GS, int TM, int BR>
-__global__ void __launch_bounds__(qt::THREADS, 1)
+template <typename T, int BITS, int GS, int TM, int BR, bool HEADS>
+__global__ void __launch_bounds__(qt::threads(HEADS), 1)
     qmv_tma_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ts,
                    const __grid_constant__ CUtensorMap tb, const QtParams p) {
     using namespace qt;
@@ -186,21 +191,36 @@ __global__ void __launch_bounds__(qt::THREADS, 1)
     float* red = reinterpret_cast<float*>(base + L.red);
     uint64_t* full = reinterpret_cast<uint64_t*>(base + L.bars);
     uint64_t* empty = full + stages;
+    uint64_t* head_done = empty + stages;
+    uint64_t* ticket_done = head_done + 1;
     volatile int* s_abort = reinterpret_cast<volatile int*>(base + L.flags);
     volatile int* s_last = s_abort + 1;
+    volatile int* s_head_last = s_abort + 2;
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const long long U = p.U;
     const int P = gridDim.x;
     const long long u_lo = U * blockIdx.x / P, u_hi = U * (blockIdx.x + 1) / P;
+    // A share that starts inside a row block and runs past its end has a head row
+    // block shared with the previous CTA(s). Its ticket is taken by the ticket warp
+    // while the consumers go on with the rest of the share; whether this CTA came
+    // last to it (and so reduces it) is looked at once the share is done.
+    const int head_rb = static_cast<int>(u_lo / S);
+    const bool has_head =
+        HEADS && (u_lo % S) != 0 && u_hi > static_cast<long long>(head_rb + 1) * S;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
             mbar_init(smem_u32(full + s), 1);
             mbar_init(smem_u32(empty + s), CWARPS);
         }
+        if constexpr (HEADS) {
+            mbar_init(smem_u32(head_done), CWARPS);
+            mbar_init(smem_u32(ticket_done), 1);
+        }
         *s_abort = 0;
         *s_last = 0;
+        *s_head_last = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     __syncthreads();
@@ -251,6 +271,29 @@ __global__ void __launch_bounds__(qt::THREADS, 1)
                 for (uint32_t j = it - n; j < it; ++j)
                     mbar_wait_bounded(smem_u32(full + j % stages), (j / stages) & 1, kSpinLimit);
             }
+        }
+        return;
+    }
+    if (HEADS && warp == CWARPS + 1) {
+        // ---------------------------- ticket warp ------------------------------------
+        // Takes the head row block's ticket once every consumer warp has stored its
+        // partials (head_done), so the consumers never wait for the atomic's round trip.
+        if (lane == 0 && has_head) {
+            asm volatile("griddepcontrol.wait;\n" ::: "memory");
+            int last = 0;
+            if (!mbar_wait_park(smem_u32(head_done), 0, kTicketParkLimit, kTicketParkNs)) {
+                atomicCAS(p.err, 0, kErrTimeout);
+                *s_abort = 1;
+            } else if (!*s_abort) {
+                const long long ub = static_cast<long long>(head_rb) * S;
+                const int nc = owner(ub + S - 1, U, P) - owner(ub, U, P) + 1;
+                // acq_rel: releases the partials the consumers stored (observed through
+                // head_done) and acquires the other contributors' for the reduction
+                last = atom_add_acq_rel_gpu(p.counter + head_rb, 1u) ==
+                       static_cast<unsigned>(nc - 1);
+            }
+            *s_head_last = last;
+            mbar_arrive(smem_u32(ticket_done));
         }
         return;
     }
@@ -408,6 +451,25 @@ __global__ void __launch_bounds__(qt::THREADS, 1)
     //   and the records of tokens 2c, 2c+1 (wrapped into the slots likewise).
     const float4* rl = rec + ((2 * c) & (TM - 1)) + GPW * kq * TM;
 
+    // Last contributor to row block rb_: adds the contributors' fp32 partials in CTA
+    // order, writes the outputs and re-arms the ticket.
+    auto reduce_row_block = [&](int rb_) {
+        const long long ub = static_cast<long long>(rb_) * S;
+        const int nc = owner(ub + S - 1, U, P) - owner(ub, U, P) + 1;
+        const float* part = p.partial + static_cast<long long>(rb_) * p.maxc * M * BR;
+        const int row0 = rb_ * BR;
+        const int rows_here = min(BR, N - row0);
+        for (int idx = ctid; idx < M * rows_here; idx += CTHREADS) {
+            const int t = idx / rows_here, rw = idx % rows_here;
+            float v = 0.f;
+            for (int k = 0; k < nc; ++k) v += __ldcg(part + (k * M + t) * BR + rw);
+            T y = ET::from_f(v);
+            if (biasg) y = ET::from_f(ET::to_f(y) + ET::to_f(biasg[row0 + rw]));
+            og[static_cast<long long>(t) * N + row0 + rw] = y;
+        }
+        if (ctid == 0) p.counter[rb_] = 0u;
+    };
+
     uint32_t it = 0;
     int slot = 0;
     uint32_t phase = 0;  // parity of the full-barrier phase to wait for
@@ -551,9 +613,7 @@ __global__ void __launch_bounds__(qt::THREADS, 1)
             }
         } else {
             // part of a row block: fp32 partial, then the last contributor reduces
-            const long long ub = static_cast<long long>(rb) * S;
-            const int first = owner(ub, U, P);
-            const int nc = owner(ub + S - 1, U, P) - first + 1;
+            const int first = owner(static_cast<long long>(rb) * S, U, P);
             const int ci = blockIdx.x - first;
             float* part = p.partial + static_cast<long long>(rb) * p.maxc * M * BR;
             if (kq == 0 && !abort) {
@@ -567,28 +627,38 @@ __global__ void __launch_bounds__(qt::THREADS, 1)
                     }
                 }
             }
-            // The barrier orders every thread's partial before thread 0's acq_rel
-            // ticket; its release makes them visible GPU-wide (cumulatively) and its
-            // acquire, with the second barrier, the other CTAs' partials to this one.
-            named_bar_sync(1, CTHREADS);
-            if (ctid == 0)
-                *s_last = (!abort && atom_add_acq_rel_gpu(p.counter + rb, 1u) ==
-                                         static_cast<unsigned>(nc - 1));
-            named_bar_sync(1, CTHREADS);
-            if (*s_last) {
-                const int rows_here = min(BR, N - row0);
-                for (int idx = ctid; idx < M * rows_here; idx += CTHREADS) {
-                    const int t = idx / rows_here, rw = idx % rows_here;
-                    float v = 0.f;
-                    for (int k = 0; k < nc; ++k) v += __ldcg(part + (k * M + t) * BR + rw);
-                    T y = ET::from_f(v);
-                    if (biasg) y = ET::from_f(ET::to_f(y) + ET::to_f(biasg[row0 + rw]));
-                    og[static_cast<long long>(t) * N + row0 + rw] = y;
+            if (HEADS && has_head && u == u_lo) {
+                // head row block, more units follow: hand the ticket to the ticket warp
+                // (mbarrier arrive: release of this warp's partials at CTA scope)
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(head_done));
+            } else {
+                // The barrier orders every thread's partial before thread 0's acq_rel
+                // ticket; its release makes them visible GPU-wide (cumulatively) and its
+                // acquire, with the second barrier, the other CTAs' partials to this one.
+                named_bar_sync(1, CTHREADS);
+                if (ctid == 0) {
+                    const int nc = owner(static_cast<long long>(rb) * S + S - 1, U, P) - first + 1;
+                    *s_last = (!abort && atom_add_acq_rel_gpu(p.counter + rb, 1u) ==
+                                             static_cast<unsigned>(nc - 1));
                 }
-                if (ctid == 0) p.counter[rb] = 0u;
+                named_bar_sync(1, CTHREADS);
+                if (*s_last) reduce_row_block(rb);
             }
         }
         u += st_end - st0;
+    }
+    if constexpr (HEADS) {
+        if (has_head) {
+            // the head row block's ticket (taken by the ticket warp)
+            const uint32_t tb_bar = smem_u32(ticket_done);
+            if (!mbar_try_wait(tb_bar, 0) && !wait_slow(tb_bar, 0)) {
+                atomicCAS(p.err, 0, kErrTimeout);
+                *s_abort = 1;
+            } else if (*s_head_last) {
+                reduce_row_block(head_rb);
+            }
+        }
     }
 }
 

@@ -6,10 +6,10 @@
 
 namespace mlxq {
 
-template <typename T, int BITS, int GS, int TM, int BR>
+template <typename T, int BITS, int GS, int TM, int BR, bool HEADS>
 cudaError_t qt_launch_t(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tb,
                         const QtParams& p, int grid, size_t smem, bool overlap, cudaStream_t st) {
-    auto kern = qmv_tma_kernel<T, BITS, GS, TM, BR>;
+    auto kern = qmv_tma_kernel<T, BITS, GS, TM, BR, HEADS>;
     static int configured[64] = {0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -26,7 +26,7 @@ cudaError_t qt_launch_t(const CUtensorMap& tw, const CUtensorMap& ts, const CUte
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(qt::THREADS);
+    cfg.blockDim = dim3(qt::threads(HEADS));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cfg.attrs = overlap ? attr : nullptr;
@@ -34,22 +34,23 @@ cudaError_t qt_launch_t(const CUtensorMap& tw, const CUtensorMap& ts, const CUte
     return cudaLaunchKernelEx(&cfg, kern, tw, ts, tb, p);
 }
 
-#define MLXQ_QT_INST0(T, BITS, GS, TM, BR)                                                      \
-    template cudaError_t qt_launch_t<T, BITS, GS, TM, BR>(                                       \
+#define MLXQ_QT_INST0(T, BITS, GS, TM, BR, H)                                                   \
+    template cudaError_t qt_launch_t<T, BITS, GS, TM, BR, H>(                                    \
         const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const QtParams&, int, size_t, \
         bool, cudaStream_t);
-#define MLXQ_QT_INST1(T, BITS, GS, BR) \
-    MLXQ_QT_INST0(T, BITS, GS, 1, BR)  \
-    MLXQ_QT_INST0(T, BITS, GS, 2, BR)  \
-    MLXQ_QT_INST0(T, BITS, GS, 4, BR)  \
-    MLXQ_QT_INST0(T, BITS, GS, 8, BR)
+#define MLXQ_QT_INST1(T, BITS, GS, BR, H) \
+    MLXQ_QT_INST0(T, BITS, GS, 1, BR, H)  \
+    MLXQ_QT_INST0(T, BITS, GS, 2, BR, H)  \
+    MLXQ_QT_INST0(T, BITS, GS, 4, BR, H)  \
+    MLXQ_QT_INST0(T, BITS, GS, 8, BR, H)
 
-// Every (bits, group size) the plan accepts, for activation type T and BR-row units.
-#define MLXQ_INSTANTIATE_QT(T, BR)  \
-    MLXQ_QT_INST1(T, 4, 32, BR)     \
-    MLXQ_QT_INST1(T, 4, 64, BR)     \
-    MLXQ_QT_INST1(T, 4, 128, BR)    \
-    MLXQ_QT_INST1(T, 8, 32, BR)     \
-    MLXQ_QT_INST1(T, 8, 64, BR)
+// Every (bits, group size) the plan accepts, for activation type T, BR-row units
+// and ticket warp or not.
+#define MLXQ_INSTANTIATE_QT(T, BR, H)  \
+    MLXQ_QT_INST1(T, 4, 32, BR, H)     \
+    MLXQ_QT_INST1(T, 4, 64, BR, H)     \
+    MLXQ_QT_INST1(T, 4, 128, BR, H)    \
+    MLXQ_QT_INST1(T, 8, 32, BR, H)     \
+    MLXQ_QT_INST1(T, 8, 64, BR, H)
 
 }  // namespace mlxq
