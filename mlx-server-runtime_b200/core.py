@@ -28,8 +28,8 @@ from . import _lib
 
 _DT = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
 
-__all__ = ["quantize", "dequantize", "quantized_matmul", "gather_qmm", "Workspace",
-           "launch_overlap"]
+__all__ = ["quantize", "dequantize", "quantized_matmul", "gather_qmm", "concat_quantized",
+           "Workspace", "launch_overlap"]
 
 
 def _dtype_code(t: torch.Tensor, what: str, allowed=(torch.bfloat16, torch.float16)) -> int:
@@ -232,6 +232,36 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
                                      0 if ws is None else ws.numel(), st.cuda_stream)
     _lib.check(rc, "quantized_matmul")
     return out
+
+
+def concat_quantized(parts, group_size: int = 64, bits: int = 4):
+    """Stack quantized matrices that share K, group_size and bits along their
+    output features: returns (w, scales, biases) holding every part's rows
+    unchanged, in order.
+
+    One quantized_matmul over the result computes the outputs of all parts in a
+    single launch; split its last dimension at the parts' N to get each one.
+    This is the fused q/k/v and gate/up projection of a decoder layer, whose
+    layers read the same input (qwen2.py:58-60,133-134 of the reference). The
+    packed words, scales and biases are copied bit for bit, so each part's
+    outputs equal its own quantized_matmul up to the fp32 summation order.
+    """
+    parts = list(parts)
+    if not parts:
+        raise ValueError("concat_quantized needs at least one (w, scales, biases)")
+    w0, s0, b0 = parts[0]
+    for w, s, b in parts:
+        if w.ndim != 2 or s.ndim != 2 or b.ndim != 2:
+            raise ValueError("every part must be 2-D (w [N, K*bits/32], scales/biases [N, K/g])")
+        if w.shape[1] != w0.shape[1] or s.shape[1] != s0.shape[1] or b.shape != s.shape:
+            raise ValueError("parts must share K, group_size and bits")
+        if w.dtype != w0.dtype or s.dtype != s0.dtype or b.dtype != b0.dtype:
+            raise ValueError("parts must share dtypes")
+        if w.shape[0] != s.shape[0]:
+            raise ValueError("w and scales disagree on N")
+    _check_qweights(w0, s0, b0, group_size, bits, s0.dtype)
+    return (torch.cat([p[0] for p in parts], 0), torch.cat([p[1] for p in parts], 0),
+            torch.cat([p[2] for p in parts], 0))
 
 
 def _broadcast_shape(a, b):

@@ -14,7 +14,10 @@
 // deterministic. When every row block fits on the SMs, each CTA takes one whole
 // row block instead and no ticket is needed.
 //
-// Per CTA: one producer warp and 8 consumer warps.
+// Per CTA: one producer warp and 8 consumer warps (plus, in kernels built with
+// HEADS, a ticket warp: a share that starts inside a row block stores that head
+// row block's partials and goes on at once, while the ticket warp takes its
+// ticket; whether the CTA came last to it is read when the share is done).
 //   * Producer (one thread): for every unit, 2-D TMA loads of the packed
 //     weights [BR rows x 128 B] per box (128-byte swizzle) plus one box each of
 //     scales and biases [BR rows x 8 groups], into a ring of `stages` slots with

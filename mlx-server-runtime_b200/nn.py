@@ -22,8 +22,9 @@ import torch
 from . import core
 
 __all__ = [
-    "Module", "Linear", "QuantizedLinear", "Embedding", "QuantizedEmbedding", "SwitchLinear",
-    "QuantizedSwitchLinear", "SwitchGLU", "quantize", "silu",
+    "Module", "Linear", "QuantizedLinear", "FusedQuantizedLinear", "Embedding",
+    "QuantizedEmbedding", "SwitchLinear", "QuantizedSwitchLinear", "SwitchGLU", "quantize",
+    "silu",
 ]
 
 
@@ -124,6 +125,52 @@ class QuantizedLinear(Module):
         return core.quantized_matmul(x, self.weight, self.scales, self.biases, transpose=True,
                                      group_size=self.group_size, bits=self.bits, mode=self.mode,
                                      bias=getattr(self, "bias", None))
+
+
+class FusedQuantizedLinear(Module):
+    """QuantizedLinear layers that read the same input, computed in one launch.
+
+    A decoder layer's q/k/v projections (qwen2.py:58-60, with bias) and its
+    gate/up projections (qwen2.py:133-134) each take the same activations; their
+    packed weights, scales, biases (and bias, zeros for a part without one) are
+    stacked along the output features once, and a call returns one output per
+    part, split from a single quantized_matmul. Each part's outputs equal its
+    own layer's up to the fp32 summation order.
+    """
+
+    def __init__(self, layers):
+        layers = list(layers)
+        if not layers or not all(isinstance(m, QuantizedLinear) for m in layers):
+            raise ValueError("FusedQuantizedLinear takes one or more QuantizedLinear layers")
+        q0 = layers[0]
+        for m in layers:
+            if (m.group_size, m.bits, m.mode) != (q0.group_size, q0.bits, q0.mode):
+                raise ValueError("fused layers must share group_size, bits and mode")
+            if m.input_dims != q0.input_dims:
+                raise ValueError("fused layers must share input_dims")
+        self.group_size, self.bits, self.mode = q0.group_size, q0.bits, q0.mode
+        self.weight, self.scales, self.biases = core.concat_quantized(
+            [(m.weight, m.scales, m.biases) for m in layers], q0.group_size, q0.bits)
+        self.splits = [m.output_dims for m in layers]
+        if any(hasattr(m, "bias") for m in layers):
+            self.bias = torch.cat([
+                m.bias if hasattr(m, "bias") else
+                torch.zeros(m.output_dims, dtype=q0.scales.dtype, device=q0.scales.device)
+                for m in layers])
+
+    @property
+    def input_dims(self) -> int:
+        return self.scales.shape[-1] * self.group_size
+
+    @property
+    def output_dims(self) -> int:
+        return self.weight.shape[0]
+
+    def __call__(self, x):
+        y = core.quantized_matmul(x, self.weight, self.scales, self.biases, transpose=True,
+                                  group_size=self.group_size, bits=self.bits, mode=self.mode,
+                                  bias=getattr(self, "bias", None))
+        return tuple(torch.split(y, self.splits, dim=-1))
 
 
 class Embedding(Module):
