@@ -13,7 +13,9 @@
 //   * TMA brings the activation tile in the canonical K-major 128-byte-swizzled
 //     layout (8-row x 128-byte atoms, chunk c of row r at chunk c ^ (r % 8)) that the
 //     MMA reads as its B operand, and the raw packed codes of the 128 weight rows.
-//   * DQ threads per weight row dequantize 64/DQ codes each: codes become exact 16-bit
+//   * DQ warps per tensor-memory lane quarter take turns by K block (one K block each,
+//     all 64 codes of a row per thread, so DQ K blocks are dequantized at once): codes
+//     become exact 16-bit
 //     values with byte permutes and a magic exponent (no integer-to-float
 //     conversion), then w = scale*q + bias with one packed FMA (one rounding, like
 //     MLX's dequantize-in-kernel), stored straight into tensor memory as the MMA's
@@ -47,7 +49,7 @@ constexpr int DQ = 2;                           // dequant warps per tensor-memo
 constexpr int NDEQ = 4 * DQ, NEPI = 4;          // dequant / epilogue warps
 constexpr int WARP_TMA = 0, WARP_MMA = 1, WARP_EPI0 = 2, WARP_DEQ0 = WARP_EPI0 + NEPI;
 constexpr int THREADS = (WARP_DEQ0 + NDEQ) * 32;
-static_assert(DQ == 2 || DQ == 4, "each dequant thread converts 64 / DQ codes of its row");
+static_assert(DQ == 1 || DQ == 2 || DQ == 4, "dequant warps per lane quarter (a K block each)");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kACols = BK / 2;     // 32-bit columns per A stage (two 16-bit values each)
 constexpr uint32_t kSpinLimit = 1u << 22;
@@ -57,7 +59,12 @@ constexpr uint32_t kParkNs = 2000, kParkLimit = 1u << 21;
 template <int BITS>
 constexpr int raw_bytes() { return BW * BK * BITS / 8; }  // 4 KB (4-bit) / 8 KB (8-bit)
 template <int BITS>
-constexpr int load_stages() { return BITS == 4 ? 6 : 5; }
+constexpr int load_stages() { return 6; }
+// A dequant warp waits on the load stages (and A stages) of its own K blocks only
+// (K block index % DQ == its turn); with both rings multiples of DQ, the stage of its
+// next K block last held one of its own, whose phase it has seen complete, so its
+// parity wait can never match an older phase.
+static_assert(6 % DQ == 0 && ASTAGES % DQ == 0, "load and A rings must be multiples of DQ");
 template <int BITS, int BT>
 constexpr int smem_bytes() {
     return load_stages<BITS>() * (BT * BK * 2 + raw_bytes<BITS>()) +
@@ -114,6 +121,20 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
         : "memory");
 }
 
+// 32 consecutive 32-bit columns of this thread's tensor-memory lane
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+        "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
+        "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
+        "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
                      bar)
@@ -133,6 +154,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
           "=r"(r[31])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+}
+
+// 16-byte read-only global load issued exactly here (volatile asm: the compiler
+// may not sink it to the first use, so a prefetch made a whole chunk ahead keeps
+// its distance).
+__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
 }
 
 // Packed-pair helpers for the dequantization (T = bf16 or f16).
@@ -233,9 +265,10 @@ __device__ __forceinline__ uint4 dequant_chunk(const uint32_t* wds, uint32_t s2,
 //                      MMA's K-major B layout) and the raw packed codes of the tile's
 //                      128 weight rows, into a ring of load stages;
 //   dequant warps      thread = weight row: DQ warps share each tensor-memory lane
-//                      quarter (w % 4) and take 64/DQ codes each; w = scale*q + bias goes
-//                      straight into a ring of A tiles in tensor memory (tcgen05.st),
-//                      never through shared memory;
+//                      quarter (w % 4) and take its K blocks in turn (warp j: blocks
+//                      j, j + DQ, ...), so DQ K blocks are in flight at once; w =
+//                      scale*q + bias goes straight into a ring of A tiles in tensor
+//                      memory (tcgen05.st), never through shared memory;
 //   warp 1  (MMA)      one thread issues tcgen05.mma M=128 N=BT K=16 x 4 with A from
 //                      tensor memory into one of two accumulators and commits the load
 //                      stage and the A tile back to their producers;
@@ -302,10 +335,10 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
     if (tid == 0) {
         for (int s = 0; s < LS; ++s) {
             mbar_init(smem_u32(load_full + s), 1);
-            mbar_init(smem_u32(load_empty + s), NDEQ + 1);
+            mbar_init(smem_u32(load_empty + s), 4 + 1);  // its K block's 4 dequant warps + MMA
         }
         for (int a = 0; a < ASTAGES; ++a) {
-            mbar_init(smem_u32(a_full + a), NDEQ);
+            mbar_init(smem_u32(a_full + a), 4);  // one dequant warp per lane quarter
             mbar_init(smem_u32(a_empty + a), 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -401,14 +434,14 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
         // ------------------------------ dequantize ---------------------------------
         const int q = warp & 3;                       // tensor-memory lane quarter
         const int r = q * 32 + lane;                  // weight row within the tile
-        const int hh = (warp - WARP_DEQ0) / 4;        // which 64/DQ codes of the K block
-        constexpr int CPTH = BK / DQ;                 // codes per thread per K block
-        constexpr int TCOLS = CPTH / 2;               // tensor-memory columns per thread
+        const int ph = (warp - WARP_DEQ0) / 4;        // this warp's K blocks: index % DQ == ph
+        constexpr int TCOLS = BK / 2;                 // tensor-memory columns per thread
+        constexpr int NGK = BK >= GS ? BK / GS : 1;   // quantization groups per K block
         const int G = K / GS;
         const T* sg = static_cast<const T*>(p.s);
         const T* bg = static_cast<const T*>(p.b);
         const uint32_t mlo = opaque(Pair<T>::kMagicLo), mhi = opaque(Pair<T>::kMagicHi);
-        const uint32_t tq = tmem + (static_cast<uint32_t>(q * 32) << 16) + kACol0 + TCOLS * hh;
+        const uint32_t tq = tmem + (static_cast<uint32_t>(q * 32) << 16) + kACol0;
         // Scales and biases by 16-byte chunks of 8 groups (rows 16-byte aligned):
         // `cur` is the chunk in use, `nxt` the next one this thread will need along its
         // (tile, chunk) sequence, loaded a whole chunk (4-16 K blocks) early.
@@ -422,8 +455,8 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
             const int n = tl.nb * BW + r;
             if (n < N) {
                 const long long off = (static_cast<long long>(tl.e) * N + n) * G + cc * 8;
-                sv = *reinterpret_cast<const uint4*>(sg + off);
-                bv = *reinterpret_cast<const uint4*>(bg + off);
+                sv = ldg_nc_v4(sg + off);
+                bv = ldg_nc_v4(bg + off);
             }
         };
         uint4 sc = make_uint4(0u, 0u, 0u, 0u), bc = sc, sn = sc, bn = sc;
@@ -449,63 +482,61 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
             const uint32_t h = (g & 1) ? (w >> 16) : (w & 0xffffu);
             return h | (h << 16);
         };
-        uint32_t li = 0, ai_k = 0;
+        uint32_t lb = 0;  // K blocks of this CTA's earlier tiles
         bool ok = true;
-        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, lb += KB) {
             const Tile tl = tile_of(t);
             const int n = tl.nb * BW + r;  // row within expert tl.e (n >= N: none)
-            for (int kb = 0; kb < KB; ++kb, ++li, ++ai_k) {
-                const int s = li % LS, as = ai_k % ASTAGES;
-                const int g = (kb * BK + hh * CPTH) / GS;  // this thread's group
-                uint32_t s2, b2;
-                if (vec) {
-                    if ((g >> 3) != cur_c || t != cur_t) advance();
-                    s2 = pick(sc, g);
-                    b2 = pick(bc, g);
-                } else {
-                    T sv = T(0.0f), bv = T(0.0f);
-                    if (n < N) {
-                        sv = sg[(static_cast<long long>(tl.e) * N + n) * G + g];
-                        bv = bg[(static_cast<long long>(tl.e) * N + n) * G + g];
+            // K blocks are dealt by their index along the CTA's whole sequence, so a
+            // stage's previous K block (LS back, LS a multiple of DQ) was this warp's too
+            for (int kb = static_cast<int>((ph + DQ - lb % DQ) % DQ); kb < KB; kb += DQ) {
+                const uint32_t li = lb + kb;  // K block index along the CTA's tiles
+                const int s = li % LS, as = li % ASTAGES;
+                uint32_t s2[NGK], b2[NGK];
+#pragma unroll
+                for (int j = 0; j < NGK; ++j) {
+                    const int g = (kb * BK) / GS + j;  // this row's groups in the K block
+                    if (vec) {
+                        // every warp meets each chunk of 8 groups (a chunk spans at
+                        // least 4 K blocks and DQ <= 4), so one step at a time suffices
+                        if ((g >> 3) != cur_c || t != cur_t) advance();
+                        s2[j] = pick(sc, g);
+                        b2[j] = pick(bc, g);
+                    } else {
+                        T sv = T(0.0f), bv = T(0.0f);
+                        if (n < N) {
+                            sv = sg[(static_cast<long long>(tl.e) * N + n) * G + g];
+                            bv = bg[(static_cast<long long>(tl.e) * N + n) * G + g];
+                        }
+                        s2[j] = splat(sv);
+                        b2[j] = splat(bv);
                     }
-                    s2 = splat(sv);
-                    b2 = splat(bv);
                 }
                 if (!wait(load_full + s, (li / LS) & 1) ||
-                    (ai_k >= ASTAGES && !wait(a_empty + as, (ai_k / ASTAGES - 1) & 1))) {
+                    (li >= ASTAGES && !wait(a_empty + as, (li / ASTAGES - 1) & 1))) {
                     ok = false;
                     break;
                 }
-                // this thread's codes of row r (TMA 32-/64-byte swizzle: 16-byte chunk c
+                // row r's codes of the K block (TMA 32-/64-byte swizzle: 16-byte chunk c
                 // of row r sits at chunk c ^ (r >> 2 & 1) / c ^ (r >> 1 & 3))
-                constexpr int RW = WPR / DQ;  // packed words (1 word = 8 codes / 4 codes)
-                uint32_t raw[RW];
+                uint32_t raw[WPR];
                 const uint8_t* rrow = smem + s * LSB + X_BYTES + r * (WPR * 4);
-                auto phys = [&](int lc) {
-                    return (BITS == 4) ? (lc ^ ((r >> 2) & 1)) : (lc ^ ((r >> 1) & 3));
-                };
-                if constexpr (RW >= 4) {
 #pragma unroll
-                    for (int c = 0; c < RW / 4; ++c) {
-                        const uint4 v = *reinterpret_cast<const uint4*>(
-                            rrow + phys(hh * (RW / 4) + c) * 16);
-                        raw[4 * c] = v.x; raw[4 * c + 1] = v.y; raw[4 * c + 2] = v.z; raw[4 * c + 3] = v.w;
-                    }
-                } else {  // 8 bytes: half of a 16-byte chunk
-                    const uint2 v = *reinterpret_cast<const uint2*>(
-                        rrow + phys(hh >> 1) * 16 + (hh & 1) * 8);
-                    raw[0] = v.x; raw[1] = v.y;
+                for (int c = 0; c < WPR / 4; ++c) {
+                    const int pc = (BITS == 4) ? (c ^ ((r >> 2) & 1)) : (c ^ ((r >> 1) & 3));
+                    const uint4 v = *reinterpret_cast<const uint4*>(rrow + pc * 16);
+                    raw[4 * c] = v.x; raw[4 * c + 1] = v.y; raw[4 * c + 2] = v.z; raw[4 * c + 3] = v.w;
                 }
                 uint32_t outv[TCOLS];
 #pragma unroll
-                for (int c = 0; c < CPTH / 8; ++c) {
-                    const uint4 v = dequant_chunk<T, BITS>(&raw[c * (BITS == 4 ? 1 : 2)], s2, b2,
-                                                          mlo, mhi);
+                for (int c = 0; c < BK / 8; ++c) {
+                    const int j = NGK > 1 ? (c * 8) / GS : 0;
+                    const uint4 v = dequant_chunk<T, BITS>(&raw[c * (BITS == 4 ? 1 : 2)], s2[j],
+                                                          b2[j], mlo, mhi);
                     outv[4 * c] = v.x; outv[4 * c + 1] = v.y;
                     outv[4 * c + 2] = v.z; outv[4 * c + 3] = v.w;
                 }
-                if constexpr (TCOLS == 16) tmem_st16(tq + as * kACols, outv);
-                else tmem_st8(tq + as * kACols, outv);
+                tmem_st32(tq + as * kACols, outv);
                 asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
                 asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
                 __syncwarp();
