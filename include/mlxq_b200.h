@@ -111,6 +111,11 @@ int mlxq_dequantize(const uint32_t* wq, const void* scales, const void* biases, 
  * The workspace must be zero-filled once when first allocated; the kernels
  * leave it zeroed again at exit, so it can be reused by later calls on the
  * same stream without clearing. Calls that overlap on the GPU must not share it.
+ * Decode shapes whose row blocks are split over CTAs need it for their partial
+ * sums; prefill shapes whose whole tiles would leave much of the GPU idle (few
+ * output tiles: the q/o, k/v and down projections at a few thousand tokens)
+ * use it for stream-K partial tiles (about 29 MB on 148 SMs). A prefill call
+ * given no workspace, or too small a one, runs whole tiles instead.
  */
 size_t mlxq_qmm_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, int bits,
                                int dtype);

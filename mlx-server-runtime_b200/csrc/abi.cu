@@ -183,11 +183,16 @@ size_t mlxq_qmm_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, 
                                int dtype) {
     if (check_bits_gs(bits, group_size, true) || check_k(K, group_size)) return 0;
     if (M <= 0 || N <= 0 || M > kIntMax || N > kIntMax || K > kIntMax) return 0;
-    if (mlxq::qgemm_supported(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
-                              bits, group_size))
-        return 0;  // the tensor-core prefill kernel needs no workspace
     DeviceInfo di;
     if (device_info(&di, nullptr)) return 0;
+    if (mlxq::qgemm_supported(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                              bits, group_size)) {
+        // the tensor-core prefill kernel: tickets + partial tiles when it runs stream-K
+        mlxq::QgemmPlan gp;
+        mlxq::qgemm_plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                         di.num_sms, &gp);
+        return gp.ws_bytes;
+    }
     mlxq::QtPlan tplan;
     if (mlxq::qmv_tma_plan(dtype, bits, group_size, static_cast<int>(M), static_cast<int>(N),
                            static_cast<int>(K), di.num_sms, di.max_smem, di.sm_smem, &tplan))
@@ -223,6 +228,16 @@ int mlxq_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
         mlxq::QgemmParams q{};
         q.x = x; q.w = w; q.s = scales; q.b = biases; q.bias = bias; q.out = out;
         q.M = static_cast<int>(M); q.N = static_cast<int>(N); q.K = static_cast<int>(K);
+        // Stream-K (shapes whose whole tiles leave much of the last wave idle) needs the
+        // workspace; without one (or too small) the kernel runs whole tiles instead.
+        mlxq::QgemmPlan gp;
+        mlxq::qgemm_plan(q.M, q.N, q.K, di.num_sms, &gp);
+        if (gp.stream_k && workspace && workspace_bytes >= gp.ws_bytes &&
+            !(reinterpret_cast<uintptr_t>(workspace) & 255u)) {
+            q.sk = 1;
+            q.counter = static_cast<unsigned*>(workspace);
+            q.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + mlxq::kTicketBytes);
+        }
         cudaError_t e = mlxq::qgemm_launch(dtype, bits, group_size, q,
                                            static_cast<cudaStream_t>(stream));
         if (e != cudaSuccess) return cuda_fail(e, "quantized_matmul (prefill) launch");

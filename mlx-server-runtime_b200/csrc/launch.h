@@ -112,7 +112,18 @@ struct QgemmParams {
     int rpe;           // rows per batch entry (grouped)
     const int32_t* seg;
     const int32_t* tile_start;
+    int sk;            // stream-K (dense only): CTAs take equal shares of tiles x K blocks
+    unsigned* counter; // stream-K tickets, one per tile, zero at entry and exit
+    float* partial;    // stream-K fp32 partial tiles, two slots per CTA
 };
+
+// Plan of the prefill kernel for a dense problem: data-parallel whole tiles, or
+// stream-K when whole tiles would leave a large part of the last wave idle.
+struct QgemmPlan {
+    bool stream_k;
+    size_t ws_bytes;  // workspace (tickets + partial tiles) for stream-K, else 0
+};
+bool qgemm_plan(int M, int N, int K, int num_sms, QgemmPlan* plan);
 
 bool qgemm_supported(int M, int N, int K, int bits, int gs);
 // Builds tile_start[0..E] for a grouped problem from seg (qgemm_sm100.cu).

@@ -64,11 +64,12 @@ constexpr int load_stages() { return 6; }
 // (K block index % DQ == its turn); with both rings multiples of DQ, the stage of its
 // next K block last held one of its own, whose phase it has seen complete, so its
 // parity wait can never match an older phase.
-static_assert(6 % DQ == 0 && ASTAGES % DQ == 0, "load and A rings must be multiples of DQ");
+static_assert(load_stages<4>() % DQ == 0 && load_stages<8>() % DQ == 0 && ASTAGES % DQ == 0,
+              "load and A rings must be multiples of DQ");
 template <int BITS, int BT>
 constexpr int smem_bytes() {
     return load_stages<BITS>() * (BT * BK * 2 + raw_bytes<BITS>()) +
-           (2 * load_stages<BITS>() + 2 * ASTAGES + 5) * 8 + 16 + 1024;
+           (2 * load_stages<BITS>() + 2 * ASTAGES + 7) * 8 + 16 + 1024;
 }
 }  // namespace qg
 
@@ -275,7 +276,7 @@ __device__ __forceinline__ uint4 dequant_chunk(const uint32_t* wds, uint32_t s2,
 //   warps 2-5 (epilogue) drain the other accumulator (thread = weight row, columns =
 //                      tokens) while the next tile accumulates; optional bias as a
 //                      second rounding.
-template <typename T, int BITS, int GS, int BT>
+template <typename T, int BITS, int GS, int BT, bool SK>
 __global__ void __launch_bounds__(qg::THREADS, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw,
                  const QgemmParams p) {
@@ -298,8 +299,11 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
     uint64_t* acc_full = a_empty + ASTAGES;
     uint64_t* acc_empty = acc_full + 2;
     uint64_t* mma_done = acc_empty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+    uint64_t* epi_done = mma_done + 1;  // stream-K: the epilogue warps stored a partial
+    uint64_t* tk_done = epi_done + 1;   // stream-K: the tile's ticket was taken
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tk_done + 1);
     volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* s_last = s_abort + 1;  // stream-K: this CTA finishes the tile
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int M = p.M, N = p.N, K = p.K;
@@ -325,6 +329,34 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
         const int mbe = max(1, (rows + BT - 1) / BT);
         return Tile{lo, r0 + (lt % mbe) * BT, r0 + rows, lt / mbe};
     };
+    // This CTA's work as segments: tile t, K blocks [kb0, kb1). Data-parallel: whole
+    // tiles blockIdx.x, + gridDim.x, ...; stream-K: an equal contiguous share of the
+    // tiles x K blocks, so its first and last tiles may be partial. (32-bit: the host
+    // runs stream-K only while units x CTAs stays below 2^31.)
+    const unsigned U = static_cast<unsigned>(tiles) * static_cast<unsigned>(KB);
+    const unsigned P = gridDim.x;
+    const unsigned u_lo = SK ? U * blockIdx.x / P : 0u;
+    const unsigned u_hi = SK ? U * (blockIdx.x + 1) / P : 0u;
+    struct Seg {
+        int t, kb0, kb1;
+        unsigned u;  // stream-K: index of the segment's first K block
+    };
+    auto sk_seg = [&](unsigned u) -> Seg {
+        const int kb0 = static_cast<int>(u % static_cast<unsigned>(KB));
+        const unsigned left = u_hi - u;
+        return Seg{static_cast<int>(u / static_cast<unsigned>(KB)), kb0,
+                   left < static_cast<unsigned>(KB - kb0) ? kb0 + static_cast<int>(left) : KB, u};
+    };
+    auto seg_first = [&]() -> Seg {
+        return SK ? sk_seg(u_lo) : Seg{static_cast<int>(blockIdx.x), 0, KB, 0u};
+    };
+    auto seg_valid = [&](const Seg& g) -> bool { return SK ? g.u < u_hi : g.t < tiles; };
+    auto seg_next = [&](const Seg& g) -> Seg {
+        return SK ? sk_seg(g.u + static_cast<unsigned>(g.kb1 - g.kb0))
+                    : Seg{g.t + static_cast<int>(P), 0, KB, 0u};
+    };
+    // stream-K: the CTA that owns K block u of the tiles x K blocks sequence
+    auto owner = [&](unsigned u) -> int { return static_cast<int>(((u + 1) * P - 1) / U); };
 
     if (warp == WARP_MMA) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
@@ -346,6 +378,8 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
             mbar_init(smem_u32(acc_empty + a), NEPI);
         }
         mbar_init(smem_u32(mma_done), 1);
+        mbar_init(smem_u32(epi_done), NEPI);
+        mbar_init(smem_u32(tk_done), 1);
         *s_abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
@@ -370,9 +404,9 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
             asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&tw)) : "memory");
             uint32_t li = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-                const Tile tl = tile_of(t);
-                for (int kb = 0; kb < KB; ++kb, ++li) {
+            for (Seg wk = seg_first(); seg_valid(wk) && ok; wk = seg_next(wk)) {
+                const Tile tl = tile_of(wk.t);
+                for (int kb = wk.kb0; kb < wk.kb1; ++kb, ++li) {
                     const int s = li % LS;
                     if (li >= LS && !wait(load_empty + s, (li / LS - 1) & 1)) {
                         ok = false;
@@ -397,14 +431,14 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
         if (lane == 0) {
             uint32_t li = 0, ai_k = 0, ai = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++ai) {
+            for (Seg wk = seg_first(); seg_valid(wk) && ok; wk = seg_next(wk), ++ai) {
                 const uint32_t a = ai & 1;
                 if (ai >= 2 && !wait(acc_empty + a, (ai / 2 - 1) & 1)) {
                     ok = false;
                     break;
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-                for (int kb = 0; kb < KB; ++kb, ++li, ++ai_k) {
+                for (int kb = wk.kb0; kb < wk.kb1; ++kb, ++li, ++ai_k) {
                     const int s = li % LS, as = ai_k % ASTAGES;
                     // (the single MMA thread polls without parking: it wakes fastest)
                     if (!mbar_wait_bounded(smem_u32(load_full + s), (li / LS) & 1, kSpinLimit) ||
@@ -420,7 +454,7 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < BK / 16; ++j)  // 16 elements: 8 A columns, 32 B of B
                         umma_f16_ts(tmem + a * BT, acol + 8 * j, bdesc + 2 * j, IDESC,
-                                    (kb > 0 || j > 0) ? 1u : 0u);
+                                    (kb > wk.kb0 || j > 0) ? 1u : 0u);
                     umma_commit(smem_u32(load_empty + s));
                     umma_commit(smem_u32(a_empty + as));
                 }
@@ -460,7 +494,10 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
             }
         };
         uint4 sc = make_uint4(0u, 0u, 0u, 0u), bc = sc, sn = sc, bn = sc;
-        int cur_t = blockIdx.x, cur_c = 0, tn = blockIdx.x, cn = 0;
+        // the chunk sequence follows the segments: (tile, chunk) in order, the first
+        // chunk being the one of the first segment's first K block
+        const Seg wk0 = seg_first();
+        int cur_t = wk0.t, cur_c = 0, tn = wk0.t, cn = (wk0.kb0 * BK / GS) >> 3;
         auto advance = [&]() {  // nxt becomes cur; fetch the chunk after it
             sc = sn;
             bc = bn;
@@ -468,7 +505,7 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
             cur_c = cn;
             if (++cn == nch) {
                 cn = 0;
-                tn += gridDim.x;
+                tn += SK ? 1 : static_cast<int>(P);
             }
             load_chunk(tn, cn, sn, bn);
         };
@@ -482,24 +519,29 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
             const uint32_t h = (g & 1) ? (w >> 16) : (w & 0xffffu);
             return h | (h << 16);
         };
-        uint32_t lb = 0;  // K blocks of this CTA's earlier tiles
+        uint32_t lb = 0;  // K blocks of this CTA's earlier segments
         bool ok = true;
-        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, lb += KB) {
+        for (Seg wk = seg_first(); seg_valid(wk) && ok; lb += wk.kb1 - wk.kb0, wk = seg_next(wk)) {
+            const int t = wk.t;
             const Tile tl = tile_of(t);
             const int n = tl.nb * BW + r;  // row within expert tl.e (n >= N: none)
             // K blocks are dealt by their index along the CTA's whole sequence, so a
             // stage's previous K block (LS back, LS a multiple of DQ) was this warp's too
-            for (int kb = static_cast<int>((ph + DQ - lb % DQ) % DQ); kb < KB; kb += DQ) {
-                const uint32_t li = lb + kb;  // K block index along the CTA's tiles
+            for (int kb = wk.kb0 + static_cast<int>((ph + DQ - lb % DQ) % DQ); kb < wk.kb1;
+                 kb += DQ) {
+                const uint32_t li = lb + (kb - wk.kb0);  // K block index along the CTA's work
                 const int s = li % LS, as = li % ASTAGES;
                 uint32_t s2[NGK], b2[NGK];
 #pragma unroll
                 for (int j = 0; j < NGK; ++j) {
                     const int g = (kb * BK) / GS + j;  // this row's groups in the K block
                     if (vec) {
-                        // every warp meets each chunk of 8 groups (a chunk spans at
-                        // least 4 K blocks and DQ <= 4), so one step at a time suffices
-                        if ((g >> 3) != cur_c || t != cur_t) advance();
+                        // a warp meets every chunk of 8 groups (a chunk spans at least 4
+                        // K blocks, DQ <= 4) except perhaps the tail of a stream-K share's
+                        // first chunk: at most one extra step, bounded all the same
+#pragma unroll 1
+                        for (int k = 0; k < 4 && ((g >> 3) != cur_c || t != cur_t); ++k)
+                            advance();
                         s2[j] = pick(sc, g);
                         b2[j] = pick(bc, g);
                     } else {
@@ -551,35 +593,118 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
         const int q = warp & 3;  // tensor-memory lanes this warp may read
         T* og = static_cast<T*>(p.out);
         const T* biasg = static_cast<const T*>(p.bias);
-        uint32_t ai = 0;
-        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++ai) {
+        const int row = q * 32 + lane;  // this thread's weight row in the tile
+        uint32_t ai = 0, np = 0;  // np: partial tiles handled so far (handshake parity)
+        for (Seg wk = seg_first(); seg_valid(wk); wk = seg_next(wk), ++ai) {
             const uint32_t a = ai & 1;
             if (!wait(acc_full + a, (ai / 2) & 1)) break;
             asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-            const Tile tl = tile_of(t);
-            const int n = tl.nb * BW + q * 32 + lane;  // this thread's output column
+            const Tile tl = tile_of(wk.t);
+            const int n = tl.nb * BW + row;  // this thread's output column
             const bool col_ok = n < N;
             const float bsum = (biasg && col_ok) ? Elem<T>::to_f(biasg[n]) : 0.f;
+            const uint32_t tacc = tmem + (static_cast<uint32_t>(q * 32) << 16) + a * BT;
+            if (wk.kb0 == 0 && wk.kb1 == KB) {
+                // the whole tile: straight to the output
 #pragma unroll 1
-            for (int i = 0; i < BT / 32; ++i) {
-                uint32_t v[32];
-                tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + a * BT + i * 32, v);
-                const int tok0 = tl.row0 + i * 32;
-                if (col_ok) {
+                for (int i = 0; i < BT / 32; ++i) {
+                    uint32_t v[32];
+                    tmem_ld32(tacc + i * 32, v);
+                    const int tok0 = tl.row0 + i * 32;
+                    if (col_ok) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int tok = tok0 + j;
-                        if (tok < tl.row_end) {
-                            T y = Elem<T>::from_f(__uint_as_float(v[j]));
-                            if (biasg) y = Elem<T>::from_f(Elem<T>::to_f(y) + bsum);
-                            og[static_cast<long long>(tok) * N + n] = y;
+                        for (int j = 0; j < 32; ++j) {
+                            const int tok = tok0 + j;
+                            if (tok < tl.row_end) {
+                                T y = Elem<T>::from_f(__uint_as_float(v[j]));
+                                if (biasg) y = Elem<T>::from_f(Elem<T>::to_f(y) + bsum);
+                                og[static_cast<long long>(tok) * N + n] = y;
+                            }
                         }
                     }
                 }
+                asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(acc_empty + a));
+                continue;
+            }
+            // Stream-K, part of a tile: the fp32 partial goes to this CTA's slot (0: its
+            // first segment, 1: its last); the last of the tile's contributors (atomic
+            // ticket) adds all partials in CTA order and writes the tile.
+            // (token-major: a warp writes, and later reads, 32 consecutive rows of a token)
+            float* mine = p.partial +
+                          static_cast<size_t>(blockIdx.x * 2 + (wk.u == u_lo ? 0 : 1)) * BT * BW + row;
+#pragma unroll 1
+            for (int i = 0; i < BT / 32; ++i) {
+                uint32_t v[32];
+                tmem_ld32(tacc + i * 32, v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) mine[(i * 32 + j) * BW] = __uint_as_float(v[j]);
             }
             asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(acc_empty + a));
+            if (lane == 0) {
+                mbar_arrive(smem_u32(acc_empty + a));  // the accumulator is free
+                mbar_arrive(smem_u32(epi_done));       // this warp's partials are stored
+            }
+            const unsigned ub = static_cast<unsigned>(wk.t) * static_cast<unsigned>(KB);
+            const int first = owner(ub), nc = owner(ub + KB - 1) - first + 1;
+            // Once all epilogue warps have stored (epi_done: release/acquire at CTA scope),
+            // one thread takes the acq_rel ticket: its release publishes them GPU-wide
+            // (cumulatively), its acquire, passed on through tk_done, orders the other
+            // contributors' partials before the reads below. Bounded waits and no named
+            // barrier: a warp that stops early cannot leave the others blocked.
+            const uint32_t par = np & 1u;
+            ++np;
+            if (row == 0) {
+                int last = 0;
+                if (!mbar_wait_park(smem_u32(epi_done), par, kParkLimit, kParkNs)) {
+                    atomicCAS(&g_qgemm_error, 0, kErrTimeout);
+                    *s_abort = 1;
+                } else if (!*s_abort) {
+                    last = atom_add_acq_rel_gpu(p.counter + wk.t, 1u) ==
+                           static_cast<unsigned>(nc - 1);
+                }
+                *s_last = last;
+                mbar_arrive(smem_u32(tk_done));
+            }
+            if (!mbar_wait_park(smem_u32(tk_done), par, kParkLimit, kParkNs)) {
+                atomicCAS(&g_qgemm_error, 0, kErrTimeout);
+                *s_abort = 1;
+                break;
+            }
+            if (!*s_last) continue;
+            if (row == 0) p.counter[wk.t] = 0u;  // re-armed (every contributor has ticked)
+            if (!col_ok) continue;
+#pragma unroll 1
+            for (int i = 0; i < BT / 32; ++i) {
+                float f[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) f[j] = 0.f;
+#pragma unroll 1
+                for (int c = 0; c < nc; ++c) {
+                    const unsigned b = static_cast<unsigned>(first + c);
+                    // slot 0 if this tile is where CTA b's share starts, else slot 1
+                    const int slot = static_cast<int>(U * b / P / static_cast<unsigned>(KB)) == wk.t ? 0 : 1;
+                    const float* src = p.partial +
+                                       static_cast<size_t>(b * 2 + slot) * BT * BW + i * 32 * BW + row;
+                    float w[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) w[j] = __ldcg(src + j * BW);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) f[j] += w[j];
+                }
+                const int tok0 = tl.row0 + i * 32;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int tok = tok0 + j;
+                    if (tok < tl.row_end) {
+                        T y = Elem<T>::from_f(f[j]);
+                        if (biasg) y = Elem<T>::from_f(Elem<T>::to_f(y) + bsum);
+                        og[static_cast<long long>(tok) * N + n] = y;
+                    }
+                }
+            }
         }
     }
 
@@ -622,10 +747,13 @@ bool qg_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esize,
 }
 }  // namespace
 
-template <typename T, int BITS, int GS, int BT>
+// SK: the stream-K instance (a separate kernel, so the whole-tile one keeps its
+// registers and schedule).
+template <typename T, int BITS, int GS, int BT, bool SK>
 static cudaError_t qgemm_launch_bt(const QgemmParams& p, cudaStream_t st) {
-    auto kern = qgemm_kernel<T, BITS, GS, BT>;
+    auto kern = qgemm_kernel<T, BITS, GS, BT, SK>;
     constexpr int smem = qg::smem_bytes<BITS, BT>();
+    static_assert(smem <= 232448, "at most 227 KB of dynamic shared memory per CTA");
     static int configured[64] = {0};
     static int num_sms[64] = {0};
     int dev = 0;
@@ -651,7 +779,8 @@ static cudaError_t qgemm_launch_bt(const QgemmParams& p, cudaStream_t st) {
     // is at most ceil(M / BT) + E
     const long long mblocks = (p.M + BT - 1) / BT + (p.E > 0 ? p.E : 0);
     const long long tiles = mblocks * ((p.N + qg::BW - 1) / qg::BW);
-    const int grid = static_cast<int>(tiles < num_sms[dev] ? tiles : num_sms[dev]);
+    const int grid = SK ? num_sms[dev]
+                        : static_cast<int>(tiles < num_sms[dev] ? tiles : num_sms[dev]);
     kern<<<grid, qg::THREADS, smem, st>>>(tx, tw, p);
     return cudaGetLastError();
 }
@@ -659,8 +788,9 @@ static cudaError_t qgemm_launch_bt(const QgemmParams& p, cudaStream_t st) {
 // Experts' row segments are short (a few hundred rows): 128-token tiles waste less.
 template <typename T, int BITS, int GS>
 static cudaError_t qgemm_launch_t(const QgemmParams& p, cudaStream_t st) {
-    if (p.E > 0) return qgemm_launch_bt<T, BITS, GS, qg::BT_GROUPED>(p, st);
-    return qgemm_launch_bt<T, BITS, GS, qg::BT_DENSE>(p, st);
+    if (p.E > 0) return qgemm_launch_bt<T, BITS, GS, qg::BT_GROUPED, false>(p, st);
+    if (p.sk) return qgemm_launch_bt<T, BITS, GS, qg::BT_DENSE, true>(p, st);
+    return qgemm_launch_bt<T, BITS, GS, qg::BT_DENSE, false>(p, st);
 }
 
 // tile_start[e + 1] = tile_start[e] + ceil(rows_e / BT_GROUPED) * NB, one block, E in chunks
@@ -713,6 +843,32 @@ static cudaError_t qgemm_dtype(int bits, int gs, const QgemmParams& p, cudaStrea
         if (gs == 128) return qgemm_launch_t<T, 8, 128>(p, st);
     }
     return cudaErrorInvalidValue;
+}
+
+// Stream-K is used when whole tiles would fill less than this share of the CTA slots
+// of their waves (q/o and down projections at a few thousand tokens), as long as each
+// CTA's share is at least a third of a tile: more contributors per tile make the last
+// one's pass over their partials cost more than the idle SMs (k/v at 512 tokens: 12
+// tiles split 12 ways ran at 32 TFLOP/s).
+constexpr double kStreamKBelow = 0.85;
+
+bool qgemm_plan(int M, int N, int K, int num_sms, QgemmPlan* plan) {
+    QgemmPlan pl{};
+    const long long tiles = static_cast<long long>((M + qg::BT_DENSE - 1) / qg::BT_DENSE) *
+                            ((N + qg::BW - 1) / qg::BW);
+    const long long KB = K / qg::BK;
+    const long long waves = (tiles + num_sms - 1) / num_sms;
+    const double fill = static_cast<double>(tiles) / static_cast<double>(waves * num_sms);
+    const long long units = tiles * KB;
+    if (num_sms > 0 && fill < kStreamKBelow && units >= num_sms && 3 * units >= KB * num_sms &&
+        tiles * 4 <= static_cast<long long>(kTicketBytes) &&
+        units * (num_sms + 1) < (1LL << 31)) {
+        pl.stream_k = true;
+        pl.ws_bytes = kTicketBytes + static_cast<size_t>(num_sms) * 2 * qg::BW *
+                                         qg::BT_DENSE * sizeof(float);
+    }
+    *plan = pl;
+    return true;
 }
 
 bool qgemm_supported(int M, int N, int K, int bits, int gs) {

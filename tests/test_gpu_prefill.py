@@ -65,3 +65,43 @@ def test_prefill_deterministic():
     outs = [mxq.quantized_matmul(x, wq, s, b) for _ in range(3)]
     assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
     assert _lib.device_error() == 0
+
+
+# Stream-K: shapes whose whole tiles fill few SMs' worth of waves (here 52-84 tiles on
+# 148 SMs) split tiles x K blocks evenly over the CTAs; a tile shared by several CTAs
+# is finished by the last of them from fp32 partials in the workspace.
+@pytest.mark.parametrize("dt", ["bfloat16", "float16"])
+@pytest.mark.parametrize("bits,gs", [(4, 32), (4, 64), (4, 128), (8, 32), (8, 64)])
+def test_prefill_stream_k_types(dt, bits, gs):
+    y, ref = _case(dt, bits, gs, 200, 3584, 2048, seed=bits * 11 + gs, bias=True)
+    close(y, ref, dt)
+
+
+@pytest.mark.parametrize("M,N,K", [(450, 3328, 1024), (1000, 1280, 2048), (257, 3584, 8192),
+                                   (300, 3584, 4096)])
+def test_prefill_stream_k_shapes(M, N, K):
+    y, ref = _case("bfloat16", 4, 64, M, N, K, seed=M + N + K, bias=(M % 2 == 0))
+    close(y, ref, "bfloat16")
+
+
+def test_prefill_stream_k_repeat_and_whole_tiles_agree():
+    """Three stream-K calls in a row (the tickets must be back at zero) give the
+    same bits; the whole-tile form (no workspace passed) agrees within tolerance."""
+    import ctypes
+    rng = np.random.default_rng(21)
+    M, N, K = 600, 1664, 2048
+    w = to_dev(rand_weights(rng, (N, K), "bfloat16"), "bfloat16")
+    wq, s, b = mxq.quantize(w)
+    x = to_dev(rand_x(rng, (M, K), "bfloat16"), "bfloat16")
+    L = _lib.load()
+    assert L.mlxq_qmm_workspace_size(M, N, K, 64, 4, _lib.BF16) > 0
+    outs = [mxq.quantized_matmul(x, wq, s, b) for _ in range(3)]
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+    whole = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    rc = L.mlxq_quantized_matmul(x.data_ptr(), wq.data_ptr(), s.data_ptr(), b.data_ptr(), None,
+                                 whole.data_ptr(), M, N, K, 64, 4, _lib.BF16, None, 0,
+                                 ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0, _lib.last_error()
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    close(to_np(outs[0]), to_np(whole), "bfloat16")
