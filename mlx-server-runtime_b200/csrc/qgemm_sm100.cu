@@ -316,7 +316,12 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
         int e, row0, row_end, nb;
     };
     auto tile_of = [&](int t) -> Tile {
-        if (!grouped) return Tile{0, (t % MB) * BT, M, t / MB};
+        // dense whole tiles: weight block fastest (CTA b keeps weight block b when the
+        // blocks match the grid, and the CTAs sweep the token blocks together, so the
+        // activations in use stay in L2); stream-K: token block fastest (a share then
+        // covers consecutive tiles of one weight block)
+        if (!grouped)
+            return SK ? Tile{0, (t % MB) * BT, M, t / MB} : Tile{0, (t / NB) * BT, M, t % NB};
         int lo = 0, hi = p.E - 1;  // last expert whose first tile is <= t
         while (lo < hi) {
             const int mid = (lo + hi + 1) >> 1;

@@ -23,8 +23,8 @@ from . import core
 
 __all__ = [
     "Module", "Linear", "QuantizedLinear", "FusedQuantizedLinear", "Embedding",
-    "QuantizedEmbedding", "SwitchLinear", "QuantizedSwitchLinear", "SwitchGLU", "quantize",
-    "silu",
+    "QuantizedEmbedding", "SwitchLinear", "QuantizedSwitchLinear", "SwitchGLU", "MoEBlock",
+    "route_topk", "quantize", "silu",
 ]
 
 
@@ -202,7 +202,9 @@ class QuantizedEmbedding(Module):
 
     def __call__(self, ids):
         flat = ids.reshape(-1)
-        rows = core.dequantize(self.weight[flat], self.scales[flat], self.biases[flat],
+        # (torch gathers no uint32 rows on CUDA: gather the packed words as int32)
+        wq = self.weight.view(torch.int32)[flat].view(torch.uint32)
+        rows = core.dequantize(wq, self.scales[flat], self.biases[flat],
                                self.group_size, self.bits, self.mode)
         return rows.reshape(*ids.shape, rows.shape[-1])
 
@@ -300,6 +302,46 @@ class SwitchGLU(Module):
         if do_sort:
             out = _scatter_unsort(out, inverse, indices.shape)
         return out.squeeze(-2)
+
+
+def route_topk(logits: torch.Tensor, top_k: int, norm_topk_prob: bool = True,
+               expert_bias: torch.Tensor | None = None):
+    """Top-k expert routing of an MoE layer (lfm2.py:366-373 of the reference):
+    softmax over the experts in float32, plus the optional per-expert bias, the
+    top_k experts per token (their order is not part of the contract: the
+    reference takes an argpartition), their gate values, renormalised to sum to
+    one when `norm_topk_prob` (with the reference's 1e-20 guard), cast back to
+    the logits' dtype. Returns (indices [.., top_k] int32, scores [.., top_k])."""
+    gates = torch.softmax(logits.float(), dim=-1)
+    if expert_bias is not None:
+        gates = gates + expert_bias.float()
+    scores, indices = torch.topk(gates, top_k, dim=-1)
+    if norm_topk_prob:
+        scores = scores / (scores.sum(dim=-1, keepdim=True) + 1e-20)
+    return indices.to(torch.int32), scores.to(logits.dtype)
+
+
+class MoEBlock(Module):
+    """Sparse MoE feed-forward (lfm2.py:345-375): a dense router, top-k routing,
+    the SwitchGLU expert bank (gather_qmm), outputs weighted by the gate scores
+    and summed over the k experts."""
+
+    def __init__(self, hidden: int, moe_inter: int, num_experts: int, top_k: int, *,
+                 norm_topk_prob: bool = True, use_expert_bias: bool = False, device="cuda",
+                 dtype=torch.bfloat16, generator=None):
+        self.top_k, self.norm_topk_prob = top_k, norm_topk_prob
+        self.gate = Linear(hidden, num_experts, bias=False, device=device, dtype=dtype,
+                           generator=generator)
+        self.switch_mlp = SwitchGLU(hidden, moe_inter, num_experts, device=device, dtype=dtype,
+                                    generator=generator)
+        if use_expert_bias:
+            self.expert_bias = torch.zeros(num_experts, device=device, dtype=torch.float32)
+
+    def __call__(self, x):
+        indices, scores = route_topk(self.gate(x), self.top_k, self.norm_topk_prob,
+                                     getattr(self, "expert_bias", None))
+        y = self.switch_mlp(x, indices)
+        return (y * scores.unsqueeze(-1)).sum(dim=-2)
 
 
 def quantize(model: Module, group_size: int = 64, bits: int = 4, mode: str = "affine",
