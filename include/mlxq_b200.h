@@ -159,6 +159,25 @@ int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const 
                     void* stream);
 
 /*
+ * quantized_matmul_swiglu: the gate and up projections of a SwiGLU MLP and the
+ * activation between them, silu(gate_proj(x)) * up_proj(x), in one decode launch.
+ * The reference computes it as two quantized_matmul calls, a silu and a multiply
+ * (qwen2.py:133-134, lfm2.py:212).
+ * w / scales / biases hold the gate and up matrices interleaved by 16-row tiles:
+ * tile j = gate rows 8j..8j+7 then up rows 8j..8j+7 (quantized rows copied as they
+ * are; mlx_server_runtime_b200.interleave_gate_up builds it). N = 2 * intermediate
+ * (a multiple of 16); out [M, N/2] = silu(g) * u with g, u each rounded to `dtype`
+ * first, as the two separate matmuls would be. Decode shapes only: M <= 8 and
+ * K/group_size a multiple of 8 (mlxq_swiglu_supported says so); workspace as
+ * mlxq_qmm_workspace_size(M, N, K, ...).
+ */
+int mlxq_swiglu_supported(int64_t M, int64_t N, int64_t K, int group_size, int bits, int dtype);
+int mlxq_quantized_matmul_swiglu(const void* x, const uint32_t* w, const void* scales,
+                                 const void* biases, void* out, int64_t M, int64_t N, int64_t K,
+                                 int group_size, int bits, int dtype, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/*
  * quantized_matmul_noalloc: the same operation as mlxq_quantized_matmul, for
  * callers that cannot allocate device memory -- a host that binds this C ABI
  * without a device allocator of its own, or a plugin inside a serving engine

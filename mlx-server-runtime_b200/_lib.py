@@ -34,6 +34,8 @@ EXPORTED = (
     "mlxq_get_launch_overlap",
     "mlxq_quantized_matmul_noalloc",
     "mlxq_device_error",
+    "mlxq_swiglu_supported",
+    "mlxq_quantized_matmul_swiglu",
 )
 
 _lock = threading.Lock()
@@ -83,6 +85,11 @@ def load(path: str | None = None):
         L.mlxq_quantized_matmul_noalloc.restype = i32
         L.mlxq_device_error.argtypes = [ctypes.POINTER(ctypes.c_int)]
         L.mlxq_device_error.restype = i32
+        L.mlxq_swiglu_supported.argtypes = [i64, i64, i64, i32, i32, i32]
+        L.mlxq_swiglu_supported.restype = i32
+        L.mlxq_quantized_matmul_swiglu.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i32, i32,
+                                                   i32, vp, sz, vp]
+        L.mlxq_quantized_matmul_swiglu.restype = i32
         v = L.mlxq_abi_version()
         if v != ABI_VERSION:
             raise LibraryError(f"{p} has ABI version {v}, expected {ABI_VERSION}; rebuild it")

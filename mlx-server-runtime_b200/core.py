@@ -29,7 +29,7 @@ from . import _lib
 _DT = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
 
 __all__ = ["quantize", "dequantize", "quantized_matmul", "gather_qmm", "concat_quantized",
-           "Workspace", "launch_overlap"]
+           "interleave_gate_up", "quantized_matmul_swiglu", "Workspace", "launch_overlap"]
 
 
 def _dtype_code(t: torch.Tensor, what: str, allowed=(torch.bfloat16, torch.float16)) -> int:
@@ -262,6 +262,74 @@ def concat_quantized(parts, group_size: int = 64, bits: int = 4):
     _check_qweights(w0, s0, b0, group_size, bits, s0.dtype)
     return (torch.cat([p[0] for p in parts], 0), torch.cat([p[1] for p in parts], 0),
             torch.cat([p[2] for p in parts], 0))
+
+
+def interleave_gate_up(gate, up, group_size: int = 64, bits: int = 4):
+    """The weight layout quantized_matmul_swiglu reads: the (w, scales, biases) of a
+    SwiGLU MLP's gate and up projections (same shape [I, ...], I a multiple of 8)
+    interleaved by 16-row tiles, tile j = gate rows 8j..8j+7 then up rows 8j..8j+7.
+    Rows are copied bit for bit (a load-time permutation, nothing is requantized)."""
+    (wg, sg, bg), (wu, su, bu) = gate, up
+    for a, c in ((wg, wu), (sg, su), (bg, bu)):
+        if a.shape != c.shape or a.dtype != c.dtype or a.ndim != 2:
+            raise ValueError("gate and up must be 2-D quantized matrices of the same shape")
+    _check_qweights(wg, sg, bg, group_size, bits, sg.dtype)
+    inter = wg.shape[0]
+    if inter % 8:
+        raise ValueError(f"gate/up rows ({inter}) must be a multiple of 8")
+
+    def mix(a, c):
+        return torch.stack([a.reshape(inter // 8, 8, -1), c.reshape(inter // 8, 8, -1)],
+                           dim=1).reshape(2 * inter, -1).contiguous()
+    if wg.dtype == torch.uint32:  # (torch has no uint32 stack on every device: move as int32)
+        w = mix(wg.view(torch.int32), wu.view(torch.int32)).view(torch.uint32)
+    else:
+        w = mix(wg, wu)
+    return w, mix(sg, su), mix(bg, bu)
+
+
+def quantized_matmul_swiglu(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
+                            biases: torch.Tensor, group_size: int = 64, bits: int = 4,
+                            mode: str = "affine") -> torch.Tensor:
+    """silu(x @ gate^T) * (x @ up^T) from interleave_gate_up's layout: [..., N/2].
+
+    Decode shapes (up to 8 rows, K/group_size a multiple of 8) run as one launch
+    with the activation in the matmul's epilogue; other shapes run
+    quantized_matmul and then the activation as torch element-wise ops. Either
+    way each projection is rounded to x's dtype before silu(g) * u is formed in
+    float32 and rounded once more.
+    """
+    _mode(mode)
+    dev = _cuda(x, w, scales, biases)
+    dt = _dtype_code(x, "x")
+    if w.ndim != 2:
+        raise ValueError(f"w must be 2-D [N, K*bits/32], got shape {tuple(w.shape)}")
+    K = _check_qweights(w, scales, biases, group_size, bits, x.dtype)
+    if x.shape[-1] != K:
+        raise ValueError(f"x has {x.shape[-1]} features but w expects K={K}")
+    N = w.shape[0]
+    if N % 16:
+        raise ValueError(f"w must hold gate/up 16-row tiles (N={N} is not a multiple of 16)")
+    lead = x.shape[:-1]
+    x2 = x.contiguous()
+    M = x2.numel() // K
+    L = _lib.load()
+    if M == 0 or not L.mlxq_swiglu_supported(M, N, K, group_size, bits, dt):
+        y = quantized_matmul(x, w, scales, biases, True, group_size, bits, mode)
+        y = y.reshape(*lead, N // 16, 2, 8).float()
+        g, u = y[..., 0, :], y[..., 1, :]
+        return (torch.nn.functional.silu(g) * u).to(x.dtype).reshape(*lead, N // 2)
+    out = torch.empty(*lead, N // 2, dtype=x.dtype, device=dev)
+    w, scales, biases = w.contiguous(), scales.contiguous(), biases.contiguous()
+    with torch.cuda.device(dev):
+        st = torch.cuda.current_stream(dev)
+        need = L.mlxq_qmm_workspace_size(M, N, K, group_size, bits, dt)
+        ws = Workspace.get(dev, st, need) if need else None
+        rc = L.mlxq_quantized_matmul_swiglu(_ptr(x2), _ptr(w), _ptr(scales), _ptr(biases),
+                                            _ptr(out), M, N, K, group_size, bits, dt, _ptr(ws),
+                                            0 if ws is None else ws.numel(), st.cuda_stream)
+    _lib.check(rc, "quantized_matmul_swiglu")
+    return out
 
 
 def _broadcast_shape(a, b):

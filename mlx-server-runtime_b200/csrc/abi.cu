@@ -290,6 +290,61 @@ int mlxq_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
     return MLXQ_OK;
 }
 
+int mlxq_swiglu_supported(int64_t M, int64_t N, int64_t K, int group_size, int bits, int dtype) {
+    if (check_bits_gs(bits, group_size, true) || check_k(K, group_size)) return 0;
+    if (M <= 0 || N <= 0 || N % 16 || M > kIntMax || N > kIntMax || K > kIntMax) return 0;
+    if (dtype != MLXQ_BF16 && dtype != MLXQ_F16) return 0;
+    DeviceInfo di;
+    if (device_info(&di, nullptr)) return 0;
+    mlxq::QtPlan tplan;
+    return mlxq::qmv_tma_plan(dtype, bits, group_size, static_cast<int>(M), static_cast<int>(N),
+                              static_cast<int>(K), di.num_sms, di.max_smem, di.sm_smem, &tplan)
+               ? 1 : 0;
+}
+
+int mlxq_quantized_matmul_swiglu(const void* x, const uint32_t* w, const void* scales,
+                                 const void* biases, void* out, int64_t M, int64_t N, int64_t K,
+                                 int group_size, int bits, int dtype, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+    int rc = check_bits_gs(bits, group_size, true);
+    if (rc) return rc;
+    if ((rc = check_k(K, group_size))) return rc;
+    if (M < 0 || N <= 0 || N % 16 || M > kIntMax || N > kIntMax || K > kIntMax)
+        return fail(MLXQ_ERR_SHAPE,
+                    "quantized_matmul_swiglu: bad shape M=%lld N=%lld K=%lld (N: gate + up rows, "
+                    "a multiple of 16)", (long long)M, (long long)N, (long long)K);
+    if (dtype != MLXQ_BF16 && dtype != MLXQ_F16)
+        return fail(MLXQ_ERR_DTYPE, "quantized_matmul_swiglu: dtype must be bfloat16 or float16");
+    if (!x || !w || !scales || !biases || !out)
+        return fail(MLXQ_ERR_NULL, "quantized_matmul_swiglu: NULL pointer");
+    if (!aligned16(x) || !aligned16(w) || !aligned16(scales) || !aligned16(biases) ||
+        !aligned16(out))
+        return fail(MLXQ_ERR_ALIGN, "quantized_matmul_swiglu: pointers must be 16-byte aligned");
+    if (M == 0) return MLXQ_OK;
+    DeviceInfo di;
+    if ((rc = device_info(&di, static_cast<cudaStream_t>(stream)))) return rc;
+    mlxq::QtPlan tplan;
+    if (!mlxq::qmv_tma_plan(dtype, bits, group_size, static_cast<int>(M), static_cast<int>(N),
+                            static_cast<int>(K), di.num_sms, di.max_smem, di.sm_smem, &tplan))
+        return fail(MLXQ_ERR_SHAPE,
+                    "quantized_matmul_swiglu: decode shapes only (M <= 8, K/group_size a "
+                    "multiple of 8); see mlxq_swiglu_supported");
+    if (tplan.ws_bytes > 0) {
+        if (!workspace || workspace_bytes < tplan.ws_bytes)
+            return fail(MLXQ_ERR_WORKSPACE,
+                        "quantized_matmul_swiglu: needs %zu workspace bytes, got %zu",
+                        tplan.ws_bytes, workspace ? workspace_bytes : (size_t)0);
+        if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+            return fail(MLXQ_ERR_ALIGN, "quantized_matmul_swiglu: workspace must be 256-byte aligned");
+    }
+    cudaError_t e = mlxq::qmv_tma_launch(
+        dtype, bits, group_size, tplan, x, w, scales, biases, nullptr, out, static_cast<int>(M),
+        static_cast<int>(N), static_cast<int>(K), workspace, mlxq::launch_overlap_enabled(),
+        static_cast<cudaStream_t>(stream), true);
+    if (e != cudaSuccess) return cuda_fail(e, "quantized_matmul_swiglu launch");
+    return MLXQ_OK;
+}
+
 size_t mlxq_gather_qmm_workspace_size(int64_t batch, int64_t M, int64_t N, int64_t K,
                                       int64_t num_experts, int group_size, int bits, int dtype,
                                       int sorted_indices) {

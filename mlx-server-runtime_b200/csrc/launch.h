@@ -75,7 +75,8 @@ cudaError_t qmv_launch(int dtype, int bits, int gs, const QmvPlan& plan, const Q
                        cudaStream_t st);
 
 // Plan of the TMA-fed decode kernel (qmv_tma.cu): M <= 8 tokens, K/group_size a
-// multiple of 8. Units of BR rows x 8 groups, split evenly over P CTAs.
+// multiple of 8. Units of BR rows x 8 groups, split evenly over P CTAs. With swiglu the
+// launch writes silu(gate) * up from a gate/up-interleaved w (N % 16 == 0, no bias).
 struct QtPlan {
     int BR;        // rows per unit (64 or 16)
     int RB;        // row blocks of BR rows
@@ -93,7 +94,7 @@ bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms,
 cudaError_t qmv_tma_launch(int dtype, int bits, int gs, const QtPlan& plan, const void* x,
                            const uint32_t* w, const void* s, const void* b, const void* bias,
                            void* out, int M, int N, int K, void* workspace, bool overlap,
-                           cudaStream_t st);
+                           cudaStream_t st, bool swiglu = false);
 cudaError_t qmv_tma_read_error(int* out_code);
 
 // One problem for the tcgen05 prefill kernel (qgemm_sm100.cu): dense, or grouped by

@@ -168,7 +168,18 @@ struct QtParams {
     int* err;           // device error flag
 };
 
-template <typename T, int BITS, int GS, int TM, int BR, bool HEADS>
+// SwiGLU epilogue (SWIGLU): w holds a gate/up pair per 16-row tile (rows 0-7 gate rows
+// 8j.., rows 8-15 the matching up rows), which are exactly the rows r and r + 8 one MMA
+// lane holds; the kernel writes silu(gate) * up, out[t, 8j + r], N / 2 columns, each
+// projection rounded to T first as two separate matmuls would be.
+template <typename T>
+__device__ __forceinline__ T swiglu_out(float g, float u) {
+    using ET = Elem<T>;
+    const float gr = ET::to_f(ET::from_f(g)), ur = ET::to_f(ET::from_f(u));
+    return ET::from_f(gr / (1.0f + expf(-gr)) * ur);
+}
+
+template <typename T, int BITS, int GS, int TM, int BR, bool HEADS, bool SWIGLU>
 __global__ void __launch_bounds__(qt::threads(HEADS), 1)
     qmv_tma_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ts,
                    const __grid_constant__ CUtensorMap tb, const QtParams p) {
@@ -462,13 +473,28 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
         const float* part = p.partial + static_cast<long long>(rb_) * p.maxc * M * BR;
         const int row0 = rb_ * BR;
         const int rows_here = min(BR, N - row0);
-        for (int idx = ctid; idx < M * rows_here; idx += CTHREADS) {
-            const int t = idx / rows_here, rw = idx % rows_here;
-            float v = 0.f;
-            for (int k = 0; k < nc; ++k) v += __ldcg(part + (k * M + t) * BR + rw);
-            T y = ET::from_f(v);
-            if (biasg) y = ET::from_f(ET::to_f(y) + ET::to_f(biasg[row0 + rw]));
-            og[static_cast<long long>(t) * N + row0 + rw] = y;
+        if constexpr (SWIGLU) {
+            // pairs (gate row 16i + j, up row 16i + j + 8) -> out column row0/2 + 8i + j
+            const int pairs = rows_here / 2;
+            for (int idx = ctid; idx < M * pairs; idx += CTHREADS) {
+                const int t = idx / pairs, pr = idx % pairs;
+                const int rw = 16 * (pr >> 3) + (pr & 7);
+                float g = 0.f, u = 0.f;
+                for (int k = 0; k < nc; ++k) {
+                    g += __ldcg(part + (k * M + t) * BR + rw);
+                    u += __ldcg(part + (k * M + t) * BR + rw + 8);
+                }
+                og[static_cast<long long>(t) * (N / 2) + row0 / 2 + pr] = swiglu_out<T>(g, u);
+            }
+        } else {
+            for (int idx = ctid; idx < M * rows_here; idx += CTHREADS) {
+                const int t = idx / rows_here, rw = idx % rows_here;
+                float v = 0.f;
+                for (int k = 0; k < nc; ++k) v += __ldcg(part + (k * M + t) * BR + rw);
+                T y = ET::from_f(v);
+                if (biasg) y = ET::from_f(ET::to_f(y) + ET::to_f(biasg[row0 + rw]));
+                og[static_cast<long long>(t) * N + row0 + rw] = y;
+            }
         }
         if (ctid == 0) p.counter[rb_] = 0u;
     };
@@ -600,16 +626,28 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
         if (st0 == 0 && st_end == S) {
             // the whole row block is this CTA's: write the outputs
             if (kq == 0 && !abort) {
-#pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    const int n = row0 + 16 * rt + r + 8 * hh;
+                if constexpr (SWIGLU) {
+                    // this lane holds gate row r and up row r + 8 of its tile
+                    const int n = (row0 + 16 * rt) / 2 + r;
 #pragma unroll
                     for (int q = 0; q < 2; ++q) {
                         const int t = 2 * c + q;
-                        if (t < M && n < N) {
-                            T y = ET::from_f(acc[2 * hh + q]);
-                            if (biasg) y = ET::from_f(ET::to_f(y) + ET::to_f(biasg[n]));
-                            og[static_cast<long long>(t) * N + n] = y;
+                        if (t < M && 2 * n < N)
+                            og[static_cast<long long>(t) * (N / 2) + n] =
+                                swiglu_out<T>(acc[q], acc[2 + q]);
+                    }
+                } else {
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        const int n = row0 + 16 * rt + r + 8 * hh;
+#pragma unroll
+                        for (int q = 0; q < 2; ++q) {
+                            const int t = 2 * c + q;
+                            if (t < M && n < N) {
+                                T y = ET::from_f(acc[2 * hh + q]);
+                                if (biasg) y = ET::from_f(ET::to_f(y) + ET::to_f(biasg[n]));
+                                og[static_cast<long long>(t) * N + n] = y;
+                            }
                         }
                     }
                 }

@@ -1,0 +1,5 @@
+#include "qmv_tma_inst.cuh"
+namespace mlxq {
+MLXQ_INSTANTIATE_QT(__nv_bfloat16, 64, false, true)
+MLXQ_INSTANTIATE_QT(__nv_bfloat16, 64, true, true)
+}

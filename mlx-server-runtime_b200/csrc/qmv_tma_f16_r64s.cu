@@ -1,0 +1,5 @@
+#include "qmv_tma_inst.cuh"
+namespace mlxq {
+MLXQ_INSTANTIATE_QT(__half, 64, false, true)
+MLXQ_INSTANTIATE_QT(__half, 64, true, true)
+}

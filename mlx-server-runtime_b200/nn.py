@@ -22,7 +22,7 @@ import torch
 from . import core
 
 __all__ = [
-    "Module", "Linear", "QuantizedLinear", "FusedQuantizedLinear", "Embedding",
+    "Module", "Linear", "QuantizedLinear", "FusedQuantizedLinear", "FusedGateUp", "Embedding",
     "QuantizedEmbedding", "SwitchLinear", "QuantizedSwitchLinear", "SwitchGLU", "MoEBlock",
     "route_topk", "quantize", "silu",
 ]
@@ -171,6 +171,29 @@ class FusedQuantizedLinear(Module):
                                   group_size=self.group_size, bits=self.bits, mode=self.mode,
                                   bias=getattr(self, "bias", None))
         return tuple(torch.split(y, self.splits, dim=-1))
+
+
+class FusedGateUp(Module):
+    """silu(gate_proj(x)) * up_proj(x) of a SwiGLU MLP (qwen2.py:133-134,
+    lfm2.py:212) from two bias-free QuantizedLinear layers, in one launch at decode:
+    their rows are interleaved once (core.interleave_gate_up) and the activation
+    runs in the matmul's epilogue (core.quantized_matmul_swiglu)."""
+
+    def __init__(self, gate: "QuantizedLinear", up: "QuantizedLinear"):
+        if not isinstance(gate, QuantizedLinear) or not isinstance(up, QuantizedLinear):
+            raise ValueError("FusedGateUp takes two QuantizedLinear layers")
+        if hasattr(gate, "bias") or hasattr(up, "bias"):
+            raise ValueError("FusedGateUp takes layers without bias")
+        if (gate.group_size, gate.bits, gate.mode) != (up.group_size, up.bits, up.mode):
+            raise ValueError("gate and up must share group_size, bits and mode")
+        self.group_size, self.bits, self.mode = gate.group_size, gate.bits, gate.mode
+        self.weight, self.scales, self.biases = core.interleave_gate_up(
+            (gate.weight, gate.scales, gate.biases), (up.weight, up.scales, up.biases),
+            gate.group_size, gate.bits)
+
+    def __call__(self, x):
+        return core.quantized_matmul_swiglu(x, self.weight, self.scales, self.biases,
+                                            self.group_size, self.bits, self.mode)
 
 
 class Embedding(Module):

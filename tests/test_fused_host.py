@@ -61,3 +61,32 @@ def test_fused_module_layout():
     g.bits = 8
     with pytest.raises(ValueError):
         mnn.FusedQuantizedLinear([a, g])
+
+
+def test_interleave_gate_up_layout():
+    g = _q(24, 256, seed=4)
+    u = _q(24, 256, seed=5)
+    w, s, b = mxq.interleave_gate_up(g, u, 64, 4)
+    assert w.shape == (48, 32) and s.shape == (48, 4)
+    for j in range(3):
+        for src, dst in ((g, slice(16 * j, 16 * j + 8)), (u, slice(16 * j + 8, 16 * j + 16))):
+            rows = slice(8 * j, 8 * j + 8)
+            assert torch.equal(w[dst].view(torch.int32), src[0][rows].view(torch.int32))
+            assert torch.equal(s[dst].view(torch.int16), src[1][rows].view(torch.int16))
+            assert torch.equal(b[dst].view(torch.int16), src[2][rows].view(torch.int16))
+    with pytest.raises(ValueError):
+        mxq.interleave_gate_up(_q(20, 256), _q(20, 256), 64, 4)   # rows not a multiple of 8
+    with pytest.raises(ValueError):
+        mxq.interleave_gate_up(_q(24, 256), _q(16, 256), 64, 4)
+
+
+def test_fused_gate_up_rejects_bias_and_mismatch():
+    a, b = _layer(16, 256, False, 1), _layer(16, 256, True, 2)
+    with pytest.raises(ValueError):
+        mnn.FusedGateUp(a, b)
+    c = _layer(16, 256, False, 3)
+    c.bits = 8
+    with pytest.raises(ValueError):
+        mnn.FusedGateUp(a, c)
+    f = mnn.FusedGateUp(a, _layer(16, 256, False, 4))
+    assert f.weight.shape == (32, 32)

@@ -61,3 +61,55 @@ def test_fused_module_qkv_with_and_without_bias():
         ref = layer(x)
         assert y.shape == ref.shape
         close(to_np(y.contiguous()), to_np(ref), "bfloat16")
+
+
+def _swiglu_ref(x, gate, up, dt, gs, bits):
+    from oracle import oracle_np as O
+    g = O.to_f32(coracle.quantized_matmul(x, *gate, dt, gs, bits), dt)
+    u = O.to_f32(coracle.quantized_matmul(x, *up, dt, gs, bits), dt)
+    return O.from_f32((g / (1.0 + np.exp(-g)) * u).astype(np.float32), dt)
+
+
+# (intermediate I, K): k/v-like (16-row CTAs), gate-like, down-like K (split row blocks)
+@pytest.mark.parametrize("I,K", [(256, 3584), (18944, 3584), (1792, 18944), (200, 1024)])
+@pytest.mark.parametrize("M", [1, 3, 8, 40])
+def test_swiglu_matches_oracle(I, K, M):
+    dt, gs, bits = "bfloat16", 64, 4
+    rng = np.random.default_rng(I + K + M)
+    gate = coracle.quantize(rand_weights(rng, (I, K), dt), dt, gs, bits)
+    up = coracle.quantize(rand_weights(rng, (I, K), dt), dt, gs, bits)
+    x = rand_x(rng, (M, K), dt)
+    ref = _swiglu_ref(x, gate, up, dt, gs, bits)
+    dev = lambda t: (to_dev(t[0]), to_dev(t[1], dt), to_dev(t[2], dt))
+    w, s, b = mxq.interleave_gate_up(dev(gate), dev(up), gs, bits)
+    y = mxq.quantized_matmul_swiglu(to_dev(x, dt), w, s, b, gs, bits)
+    torch.cuda.synchronize()
+    assert y.shape == (M, I)
+    close(to_np(y), ref, dt)
+
+
+@pytest.mark.parametrize("dt", ["bfloat16", "float16"])
+@pytest.mark.parametrize("bits,gs", [(4, 32), (4, 128), (8, 64)])
+def test_swiglu_types(dt, bits, gs):
+    rng = np.random.default_rng(bits + gs)
+    I, K, M = 512, 8 * gs * 4, 2
+    gate = coracle.quantize(rand_weights(rng, (I, K), dt), dt, gs, bits)
+    up = coracle.quantize(rand_weights(rng, (I, K), dt), dt, gs, bits)
+    x = rand_x(rng, (M, K), dt)
+    ref = _swiglu_ref(x, gate, up, dt, gs, bits)
+    dev = lambda t: (to_dev(t[0]), to_dev(t[1], dt), to_dev(t[2], dt))
+    w, s, b = mxq.interleave_gate_up(dev(gate), dev(up), gs, bits)
+    y = mxq.quantized_matmul_swiglu(to_dev(x, dt), w, s, b, gs, bits)
+    torch.cuda.synchronize()
+    close(to_np(y), ref, dt)
+
+
+def test_fused_gate_up_module_repeat():
+    torch.manual_seed(1)
+    gate, up = mnn.QuantizedLinear(1024, 768, bias=False), mnn.QuantizedLinear(1024, 768, bias=False)
+    f = mnn.FusedGateUp(gate, up)
+    x = torch.randn(4, 1024, device="cuda").to(torch.bfloat16)
+    ref = (torch.nn.functional.silu(gate(x).float()) * up(x).float()).to(torch.bfloat16)
+    outs = [f(x) for _ in range(3)]
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+    close(to_np(outs[0]), to_np(ref), "bfloat16")
