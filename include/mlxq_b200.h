@@ -159,6 +159,25 @@ int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const 
                     void* stream);
 
 /*
+ * quantized_matmul_argmax: greedy decoding's next token without the logits. The
+ * reference computes the vocabulary logits with the lm_head (or the tied
+ * embedding's as_linear) quantized_matmul, then takes their argmax per sequence
+ * (qwen2.py:225-227, executor.py:406-414). Here each logit is rounded to `dtype`
+ * (plus bias) exactly as mlxq_quantized_matmul would write it, and ids[t] (int32,
+ * t < M) receives the index of the largest, the first one on ties. Decode shapes
+ * only (M <= 8, K/group_size a multiple of 8). The workspace
+ * (mlxq_argmax_workspace_size bytes, at least 64 KiB, zero-filled once) is left
+ * zeroed again, like mlxq_quantized_matmul's; calls that overlap on the GPU must
+ * not share it.
+ */
+size_t mlxq_argmax_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, int bits,
+                                  int dtype);
+int mlxq_quantized_matmul_argmax(const void* x, const uint32_t* w, const void* scales,
+                                 const void* biases, const void* bias, int32_t* ids, int64_t M,
+                                 int64_t N, int64_t K, int group_size, int bits, int dtype,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * quantized_matmul_swiglu: the gate and up projections of a SwiGLU MLP and the
  * activation between them, silu(gate_proj(x)) * up_proj(x), in one decode launch.
  * The reference computes it as two quantized_matmul calls, a silu and a multiply

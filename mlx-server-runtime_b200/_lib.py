@@ -36,6 +36,8 @@ EXPORTED = (
     "mlxq_device_error",
     "mlxq_swiglu_supported",
     "mlxq_quantized_matmul_swiglu",
+    "mlxq_argmax_workspace_size",
+    "mlxq_quantized_matmul_argmax",
 )
 
 _lock = threading.Lock()
@@ -90,6 +92,11 @@ def load(path: str | None = None):
         L.mlxq_quantized_matmul_swiglu.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i32, i32,
                                                    i32, vp, sz, vp]
         L.mlxq_quantized_matmul_swiglu.restype = i32
+        L.mlxq_argmax_workspace_size.argtypes = [i64, i64, i64, i32, i32, i32]
+        L.mlxq_argmax_workspace_size.restype = sz
+        L.mlxq_quantized_matmul_argmax.argtypes = [vp, vp, vp, vp, vp, vp, i64, i64, i64, i32,
+                                                   i32, i32, vp, sz, vp]
+        L.mlxq_quantized_matmul_argmax.restype = i32
         v = L.mlxq_abi_version()
         if v != ABI_VERSION:
             raise LibraryError(f"{p} has ABI version {v}, expected {ABI_VERSION}; rebuild it")

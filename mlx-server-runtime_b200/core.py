@@ -29,7 +29,8 @@ from . import _lib
 _DT = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
 
 __all__ = ["quantize", "dequantize", "quantized_matmul", "gather_qmm", "concat_quantized",
-           "interleave_gate_up", "quantized_matmul_swiglu", "Workspace", "launch_overlap"]
+           "interleave_gate_up", "quantized_matmul_swiglu", "quantized_matmul_argmax",
+           "Workspace", "launch_overlap"]
 
 
 def _dtype_code(t: torch.Tensor, what: str, allowed=(torch.bfloat16, torch.float16)) -> int:
@@ -330,6 +331,49 @@ def quantized_matmul_swiglu(x: torch.Tensor, w: torch.Tensor, scales: torch.Tens
                                             0 if ws is None else ws.numel(), st.cuda_stream)
     _lib.check(rc, "quantized_matmul_swiglu")
     return out
+
+
+def quantized_matmul_argmax(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
+                            biases: torch.Tensor, group_size: int = 64, bits: int = 4,
+                            mode: str = "affine", bias: torch.Tensor | None = None
+                            ) -> torch.Tensor:
+    """Greedy next tokens: argmax over N of quantized_matmul(x, w, ...) (+ bias),
+    int32 [...], the first index on ties, without writing the logits.
+
+    Decode shapes (up to 8 rows, K/group_size a multiple of 8) run as one launch
+    with the argmax in the matmul's epilogue; other shapes compute the logits and
+    take torch.argmax. The logits compared are the ones quantized_matmul returns
+    (rounded to x's dtype), so both forms pick the same token.
+    """
+    _mode(mode)
+    dev = _cuda(x, w, scales, biases, bias)
+    dt = _dtype_code(x, "x")
+    if w.ndim != 2:
+        raise ValueError(f"w must be 2-D [N, K*bits/32], got shape {tuple(w.shape)}")
+    K = _check_qweights(w, scales, biases, group_size, bits, x.dtype)
+    if x.shape[-1] != K:
+        raise ValueError(f"x has {x.shape[-1]} features but w expects K={K}")
+    N = w.shape[0]
+    if bias is not None and (bias.shape != (N,) or bias.dtype != x.dtype):
+        raise ValueError(f"bias must be [{N}] of dtype {x.dtype}")
+    lead = x.shape[:-1]
+    x2 = x.contiguous()
+    M = x2.numel() // K
+    L = _lib.load()
+    need = L.mlxq_argmax_workspace_size(M, N, K, group_size, bits, dt) if M else 0
+    if need == 0:
+        y = quantized_matmul(x, w, scales, biases, True, group_size, bits, mode, bias=bias)
+        return y.argmax(dim=-1).to(torch.int32)
+    ids = torch.empty(*lead, dtype=torch.int32, device=dev)
+    w, scales, biases = w.contiguous(), scales.contiguous(), biases.contiguous()
+    with torch.cuda.device(dev):
+        st = torch.cuda.current_stream(dev)
+        ws = Workspace.get(dev, st, need)
+        rc = L.mlxq_quantized_matmul_argmax(_ptr(x2), _ptr(w), _ptr(scales), _ptr(biases),
+                                            _ptr(bias), _ptr(ids), M, N, K, group_size, bits, dt,
+                                            _ptr(ws), ws.numel(), st.cuda_stream)
+    _lib.check(rc, "quantized_matmul_argmax")
+    return ids
 
 
 def _broadcast_shape(a, b):

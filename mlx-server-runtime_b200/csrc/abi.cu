@@ -340,8 +340,61 @@ int mlxq_quantized_matmul_swiglu(const void* x, const uint32_t* w, const void* s
     cudaError_t e = mlxq::qmv_tma_launch(
         dtype, bits, group_size, tplan, x, w, scales, biases, nullptr, out, static_cast<int>(M),
         static_cast<int>(N), static_cast<int>(K), workspace, mlxq::launch_overlap_enabled(),
-        static_cast<cudaStream_t>(stream), true);
+        static_cast<cudaStream_t>(stream), 1);
     if (e != cudaSuccess) return cuda_fail(e, "quantized_matmul_swiglu launch");
+    return MLXQ_OK;
+}
+
+size_t mlxq_argmax_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, int bits,
+                                  int dtype) {
+    if (check_bits_gs(bits, group_size, true) || check_k(K, group_size)) return 0;
+    if (M <= 0 || N <= 0 || M > kIntMax || N > kIntMax || K > kIntMax) return 0;
+    DeviceInfo di;
+    if (device_info(&di, nullptr)) return 0;
+    mlxq::QtPlan tplan;
+    if (!mlxq::qmv_tma_plan(dtype, bits, group_size, static_cast<int>(M), static_cast<int>(N),
+                            static_cast<int>(K), di.num_sms, di.max_smem, di.sm_smem, &tplan))
+        return 0;
+    return tplan.ws_bytes > mlxq::kTicketBytes ? tplan.ws_bytes : mlxq::kTicketBytes;
+}
+
+int mlxq_quantized_matmul_argmax(const void* x, const uint32_t* w, const void* scales,
+                                 const void* biases, const void* bias, int32_t* ids, int64_t M,
+                                 int64_t N, int64_t K, int group_size, int bits, int dtype,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+    int rc = check_bits_gs(bits, group_size, true);
+    if (rc) return rc;
+    if ((rc = check_k(K, group_size))) return rc;
+    if (M < 0 || N <= 0 || M > kIntMax || N > kIntMax || K > kIntMax)
+        return fail(MLXQ_ERR_SHAPE, "quantized_matmul_argmax: bad shape M=%lld N=%lld K=%lld",
+                    (long long)M, (long long)N, (long long)K);
+    if (dtype != MLXQ_BF16 && dtype != MLXQ_F16)
+        return fail(MLXQ_ERR_DTYPE, "quantized_matmul_argmax: dtype must be bfloat16 or float16");
+    if (!x || !w || !scales || !biases || !ids)
+        return fail(MLXQ_ERR_NULL, "quantized_matmul_argmax: NULL pointer");
+    if (!aligned16(x) || !aligned16(w) || !aligned16(scales) || !aligned16(biases) ||
+        (bias && !aligned16(bias)))
+        return fail(MLXQ_ERR_ALIGN, "quantized_matmul_argmax: pointers must be 16-byte aligned");
+    if (M == 0) return MLXQ_OK;
+    DeviceInfo di;
+    if ((rc = device_info(&di, static_cast<cudaStream_t>(stream)))) return rc;
+    mlxq::QtPlan tplan;
+    if (!mlxq::qmv_tma_plan(dtype, bits, group_size, static_cast<int>(M), static_cast<int>(N),
+                            static_cast<int>(K), di.num_sms, di.max_smem, di.sm_smem, &tplan))
+        return fail(MLXQ_ERR_SHAPE,
+                    "quantized_matmul_argmax: decode shapes only (M <= 8, K/group_size a "
+                    "multiple of 8)");
+    const size_t need = tplan.ws_bytes > mlxq::kTicketBytes ? tplan.ws_bytes : mlxq::kTicketBytes;
+    if (!workspace || workspace_bytes < need)
+        return fail(MLXQ_ERR_WORKSPACE, "quantized_matmul_argmax: needs %zu workspace bytes, got %zu",
+                    need, workspace ? workspace_bytes : (size_t)0);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+        return fail(MLXQ_ERR_ALIGN, "quantized_matmul_argmax: workspace must be 256-byte aligned");
+    cudaError_t e = mlxq::qmv_tma_launch(
+        dtype, bits, group_size, tplan, x, w, scales, biases, bias, ids, static_cast<int>(M),
+        static_cast<int>(N), static_cast<int>(K), workspace, mlxq::launch_overlap_enabled(),
+        static_cast<cudaStream_t>(stream), 2);
+    if (e != cudaSuccess) return cuda_fail(e, "quantized_matmul_argmax launch");
     return MLXQ_OK;
 }
 

@@ -15,6 +15,9 @@ enum { kF32 = 0, kBF16 = 1, kF16 = 2 };
 // partial sums written by one call can never land where a later call, planned
 // with more row blocks, expects zeroed tickets.
 constexpr size_t kTicketBytes = 64 * 1024;
+// The last 256 bytes of the ticket region hold the fused greedy argmax's done counter
+// and per-token keys (zero between calls, like the tickets); tickets stay below it.
+constexpr size_t kArgmaxOffset = kTicketBytes - 256;
 
 cudaError_t launch_quantize(const void* w, int dtype, uint32_t* wq, void* s, void* b,
                             long long rows, long long K, int gs, int bits, cudaStream_t st);
@@ -75,8 +78,9 @@ cudaError_t qmv_launch(int dtype, int bits, int gs, const QmvPlan& plan, const Q
                        cudaStream_t st);
 
 // Plan of the TMA-fed decode kernel (qmv_tma.cu): M <= 8 tokens, K/group_size a
-// multiple of 8. Units of BR rows x 8 groups, split evenly over P CTAs. With swiglu the
-// launch writes silu(gate) * up from a gate/up-interleaved w (N % 16 == 0, no bias).
+// multiple of 8. Units of BR rows x 8 groups, split evenly over P CTAs. Epilogue `epi`:
+// 0 the outputs; 1 silu(gate) * up from a gate/up-interleaved w (N % 16 == 0, no bias);
+// 2 the greedy argmax over N per token into int32 out[M] (workspace required).
 struct QtPlan {
     int BR;        // rows per unit (64 or 16)
     int RB;        // row blocks of BR rows
@@ -94,7 +98,7 @@ bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms,
 cudaError_t qmv_tma_launch(int dtype, int bits, int gs, const QtPlan& plan, const void* x,
                            const uint32_t* w, const void* s, const void* b, const void* bias,
                            void* out, int M, int N, int K, void* workspace, bool overlap,
-                           cudaStream_t st, bool swiglu = false);
+                           cudaStream_t st, int epi = 0);
 cudaError_t qmv_tma_read_error(int* out_code);
 
 // One problem for the tcgen05 prefill kernel (qgemm_sm100.cu): dense, or grouped by

@@ -866,7 +866,7 @@ bool qgemm_plan(int M, int N, int K, int num_sms, QgemmPlan* plan) {
     const double fill = static_cast<double>(tiles) / static_cast<double>(waves * num_sms);
     const long long units = tiles * KB;
     if (num_sms > 0 && fill < kStreamKBelow && units >= num_sms && 3 * units >= KB * num_sms &&
-        tiles * 4 <= static_cast<long long>(kTicketBytes) &&
+        tiles * 4 <= static_cast<long long>(kArgmaxOffset) &&
         units * (num_sms + 1) < (1LL << 31)) {
         pl.stream_k = true;
         pl.ws_bytes = kTicketBytes + static_cast<size_t>(num_sms) * 2 * qg::BW *

@@ -59,7 +59,7 @@ bool qmv_plan(int dtype, int bits, int gs, int M, int N, int K, int mode, int z_
     pl.ws_bytes = 0;
     if (pl.splits > 1) {
         const size_t counters = static_cast<size_t>(pl.ztotal) * pl.rowblocks * 4;
-        if (counters > kTicketBytes) return false;
+        if (counters > kArgmaxOffset) return false;
         pl.ws_bytes = kTicketBytes +
                       static_cast<size_t>(pl.splits) * M * static_cast<size_t>(N) * 4;
     }

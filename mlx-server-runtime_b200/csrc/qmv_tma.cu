@@ -11,7 +11,7 @@ namespace mlxq {
 
 __device__ int g_qmv_tma_error;
 
-template <typename T, int BITS, int GS, int TM, int BR, bool HEADS, bool SW>
+template <typename T, int BITS, int GS, int TM, int BR, bool HEADS, int EPI>
 cudaError_t qt_launch_t(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tb,
                         const QtParams& p, int grid, size_t smem, bool overlap, cudaStream_t st);
 
@@ -99,7 +99,7 @@ bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms,
     QtPlan pl{};
     pl.BR = br;
     pl.RB = (N + br - 1) / br;
-    if (static_cast<size_t>(pl.RB) * 4 > kTicketBytes) return false;
+    if (static_cast<size_t>(pl.RB) * 4 > kArgmaxOffset) return false;
     pl.S = G / qt::SG;
     pl.U = static_cast<long long>(pl.RB) * pl.S;
     pl.P = static_cast<int>(std::min<long long>(pl.U, static_cast<long long>(num_sms) * kGridPerSm));
@@ -136,23 +136,24 @@ bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms,
     return true;
 }
 
-#define QT_CASE_TM(T, BITS, GS, BR, H, SW)                                                      \
+#define QT_CASE_TM(T, BITS, GS, BR, H, EPI)                                                      \
     switch (qt::token_slots(M)) {                                                                \
-        case 1: return qt_launch_t<T, BITS, GS, 1, BR, H, SW>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
-        case 2: return qt_launch_t<T, BITS, GS, 2, BR, H, SW>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
-        case 4: return qt_launch_t<T, BITS, GS, 4, BR, H, SW>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
-        default: return qt_launch_t<T, BITS, GS, 8, BR, H, SW>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
+        case 1: return qt_launch_t<T, BITS, GS, 1, BR, H, EPI>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
+        case 2: return qt_launch_t<T, BITS, GS, 2, BR, H, EPI>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
+        case 4: return qt_launch_t<T, BITS, GS, 4, BR, H, EPI>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
+        default: return qt_launch_t<T, BITS, GS, 8, BR, H, EPI>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
     }
-#define QT_CASE_SW(T, BITS, GS, SW)                                           \
-    if (plan.BR == 16) { QT_CASE_TM(T, BITS, GS, 16, false, SW) }             \
-    if (plan.heads) { QT_CASE_TM(T, BITS, GS, 64, true, SW) }                 \
-    QT_CASE_TM(T, BITS, GS, 64, false, SW)
+#define QT_CASE_SW(T, BITS, GS, EPI)                                           \
+    if (plan.BR == 16) { QT_CASE_TM(T, BITS, GS, 16, false, EPI) }             \
+    if (plan.heads) { QT_CASE_TM(T, BITS, GS, 64, true, EPI) }                 \
+    QT_CASE_TM(T, BITS, GS, 64, false, EPI)
 #define QT_CASE(T, BITS, GS)                                                  \
-    if (swiglu) { QT_CASE_SW(T, BITS, GS, true) }                             \
-    QT_CASE_SW(T, BITS, GS, false)
+    if (epi == 1) { QT_CASE_SW(T, BITS, GS, 1) }                              \
+    if (epi == 2) { QT_CASE_SW(T, BITS, GS, 2) }                              \
+    QT_CASE_SW(T, BITS, GS, 0)
 
 template <typename T>
-static cudaError_t qt_dispatch(int bits, int gs, int M, bool swiglu, const CUtensorMap& tw,
+static cudaError_t qt_dispatch(int bits, int gs, int M, int epi, const CUtensorMap& tw,
                                const CUtensorMap& ts, const CUtensorMap& tb, const QtParams& p,
                                const QtPlan& plan, bool overlap, cudaStream_t st) {
     if (bits == 4) {
@@ -183,7 +184,7 @@ static int* error_flag() {
 cudaError_t qmv_tma_launch(int dtype, int bits, int gs, const QtPlan& plan, const void* x,
                            const uint32_t* w, const void* s, const void* b, const void* bias,
                            void* out, int M, int N, int K, void* workspace, bool overlap,
-                           cudaStream_t st, bool swiglu) {
+                           cudaStream_t st, int epi) {
     const int G = K / gs;
     const unsigned long long kw = static_cast<unsigned long long>(K) * bits / 32;
     CUtensorMap tw, ts, tb;
@@ -205,11 +206,18 @@ cudaError_t qmv_tma_launch(int dtype, int bits, int gs, const QtPlan& plan, cons
         p.counter = static_cast<unsigned*>(workspace);
         p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kTicketBytes);
     }
-    if (swiglu && (N % 16 || bias)) return cudaErrorInvalidValue;
+    if (epi == 1 && (N % 16 || bias)) return cudaErrorInvalidValue;
+    if (epi == 2) {
+        // greedy argmax: per-token keys and a done counter at the end of the ticket region
+        if (!workspace) return cudaErrorInvalidValue;
+        p.am_done = reinterpret_cast<unsigned*>(static_cast<char*>(workspace) + kArgmaxOffset);
+        p.am_keys = reinterpret_cast<unsigned long long*>(static_cast<char*>(workspace) +
+                                                          kArgmaxOffset + 64);
+    }
     if (dtype == kBF16)
-        return qt_dispatch<__nv_bfloat16>(bits, gs, M, swiglu, tw, ts, tb, p, plan, overlap, st);
+        return qt_dispatch<__nv_bfloat16>(bits, gs, M, epi, tw, ts, tb, p, plan, overlap, st);
     if (dtype == kF16)
-        return qt_dispatch<__half>(bits, gs, M, swiglu, tw, ts, tb, p, plan, overlap, st);
+        return qt_dispatch<__half>(bits, gs, M, epi, tw, ts, tb, p, plan, overlap, st);
     return cudaErrorInvalidValue;
 }
 

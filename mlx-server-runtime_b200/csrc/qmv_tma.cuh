@@ -110,7 +110,7 @@ struct Geo {
 // Shared-memory layout (from a 1024-byte aligned base), in bytes; rt = row tiles
 // per unit (the cross-warp reduction holds (KSW - 1) * RT = 8 - rt warp tiles).
 struct Layout {
-    int ring, xf, rec, red, bars, flags, total;
+    int ring, xf, rec, red, bars, flags, best, total;
 };
 __host__ __device__ inline Layout layout(int stage_bytes, int stages, int G, int TM, int xg,
                                          int rt) {
@@ -122,7 +122,8 @@ __host__ __device__ inline Layout layout(int stage_bytes, int stages, int G, int
     L.bars = (L.red + (CWARPS - rt) * 4 * 32 * 4 + 7) & ~7;
     // full[stages], empty[stages], head_done, ticket_done
     L.flags = (L.bars + (2 * stages + 2) * 8 + 15) & ~15;  // abort, last, head_last
-    L.total = L.flags + 16;
+    L.best = L.flags + 16;                                  // argmax: best key per token
+    L.total = L.best + MAXM * 8;
     return L;
 }
 
@@ -166,12 +167,21 @@ struct QtParams {
     unsigned* counter;  // [RB], zero at entry and exit
     float* partial;     // [RB][maxc][M][64]
     int* err;           // device error flag
+    unsigned* am_done;            // argmax epilogue: CTAs done (zero at entry and exit)
+    unsigned long long* am_keys;  // argmax epilogue: best key per token (likewise)
 };
 
-// SwiGLU epilogue (SWIGLU): w holds a gate/up pair per 16-row tile (rows 0-7 gate rows
-// 8j.., rows 8-15 the matching up rows), which are exactly the rows r and r + 8 one MMA
-// lane holds; the kernel writes silu(gate) * up, out[t, 8j + r], N / 2 columns, each
-// projection rounded to T first as two separate matmuls would be.
+// Epilogues (EPI):
+// 0  the outputs out[t, n].
+// 1  SwiGLU: w holds a gate/up pair per 16-row tile (rows 0-7 gate rows 8j.., rows 8-15
+//    the matching up rows), which are exactly the rows r and r + 8 one MMA lane holds;
+//    the kernel writes silu(gate) * up, out[t, 8j + r], N / 2 columns, each projection
+//    rounded to T first as two separate matmuls would be.
+// 2  greedy argmax: no outputs; each output value (rounded to T, plus bias) becomes a
+//    key (order-preserving bits of the value, then the complement of n, so ties go to
+//    the first n); the CTA keeps its best key per token in shared memory, then one
+//    global atomicMax per token; the last CTA to finish (a done counter) writes the
+//    winning n per token to int32 out[t] and re-arms the keys and the counter.
 template <typename T>
 __device__ __forceinline__ T swiglu_out(float g, float u) {
     using ET = Elem<T>;
@@ -179,7 +189,13 @@ __device__ __forceinline__ T swiglu_out(float g, float u) {
     return ET::from_f(gr / (1.0f + expf(-gr)) * ur);
 }
 
-template <typename T, int BITS, int GS, int TM, int BR, bool HEADS, bool SWIGLU>
+__device__ __forceinline__ unsigned long long argmax_key(float v, int n) {
+    uint32_t u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return (static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(n));
+}
+
+template <typename T, int BITS, int GS, int TM, int BR, bool HEADS, int EPI>
 __global__ void __launch_bounds__(qt::threads(HEADS), 1)
     qmv_tma_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ts,
                    const __grid_constant__ CUtensorMap tb, const QtParams p) {
@@ -210,6 +226,7 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
     volatile int* s_abort = reinterpret_cast<volatile int*>(base + L.flags);
     volatile int* s_last = s_abort + 1;
     volatile int* s_head_last = s_abort + 2;
+    unsigned long long* s_best = reinterpret_cast<unsigned long long*>(base + L.best);
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const long long U = p.U;
@@ -235,6 +252,7 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
         *s_abort = 0;
         *s_last = 0;
         *s_head_last = 0;
+        for (int t = 0; t < MAXM; ++t) s_best[t] = 0ull;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     __syncthreads();
@@ -473,7 +491,16 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
         const float* part = p.partial + static_cast<long long>(rb_) * p.maxc * M * BR;
         const int row0 = rb_ * BR;
         const int rows_here = min(BR, N - row0);
-        if constexpr (SWIGLU) {
+        if constexpr (EPI == 2) {
+            for (int idx = ctid; idx < M * rows_here; idx += CTHREADS) {
+                const int t = idx / rows_here, rw = idx % rows_here;
+                float v = 0.f;
+                for (int k = 0; k < nc; ++k) v += __ldcg(part + (k * M + t) * BR + rw);
+                T y = ET::from_f(v);
+                if (biasg) y = ET::from_f(ET::to_f(y) + ET::to_f(biasg[row0 + rw]));
+                atomicMax(s_best + t, argmax_key(ET::to_f(y), row0 + rw));
+            }
+        } else if constexpr (EPI == 1) {
             // pairs (gate row 16i + j, up row 16i + j + 8) -> out column row0/2 + 8i + j
             const int pairs = rows_here / 2;
             for (int idx = ctid; idx < M * pairs; idx += CTHREADS) {
@@ -626,7 +653,21 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
         if (st0 == 0 && st_end == S) {
             // the whole row block is this CTA's: write the outputs
             if (kq == 0 && !abort) {
-                if constexpr (SWIGLU) {
+                if constexpr (EPI == 2) {
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        const int n = row0 + 16 * rt + r + 8 * hh;
+#pragma unroll
+                        for (int q = 0; q < 2; ++q) {
+                            const int t = 2 * c + q;
+                            if (t < M && n < N) {
+                                T y = ET::from_f(acc[2 * hh + q]);
+                                if (biasg) y = ET::from_f(ET::to_f(y) + ET::to_f(biasg[n]));
+                                atomicMax(s_best + t, argmax_key(ET::to_f(y), n));
+                            }
+                        }
+                    }
+                } else if constexpr (EPI == 1) {
                     // this lane holds gate row r and up row r + 8 of its tile
                     const int n = (row0 + 16 * rt) / 2 + r;
 #pragma unroll
@@ -699,6 +740,25 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
             } else if (*s_head_last) {
                 reduce_row_block(head_rb);
             }
+        }
+    }
+    if constexpr (EPI == 2) {
+        // this CTA's best key per token -> the global keys; the last CTA to get here
+        // (acq_rel done counter, as for the row-block tickets) turns them into token
+        // ids and re-arms keys and counter for the next call
+        named_bar_sync(1, CTHREADS);
+        if (ctid < M && s_best[ctid] != 0ull) atomicMax(p.am_keys + ctid, s_best[ctid]);
+        named_bar_sync(1, CTHREADS);
+        if (ctid == 0)
+            *s_last = atom_add_acq_rel_gpu(p.am_done, 1u) == static_cast<unsigned>(P - 1);
+        named_bar_sync(1, CTHREADS);
+        if (*s_last) {
+            if (ctid < M) {
+                const unsigned long long k = atomicExch(p.am_keys + ctid, 0ull);
+                static_cast<int*>(p.out)[ctid] =
+                    static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull));
+            }
+            if (ctid == 0) *p.am_done = 0u;
         }
     }
 }

@@ -1,0 +1,5 @@
+#include "qmv_tma_inst.cuh"
+namespace mlxq {
+// greedy argmax epilogue
+MLXQ_INSTANTIATE_QT(__nv_bfloat16, 16, false, 2)
+}

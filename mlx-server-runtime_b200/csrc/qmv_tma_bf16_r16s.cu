@@ -1,4 +1,5 @@
 #include "qmv_tma_inst.cuh"
 namespace mlxq {
-MLXQ_INSTANTIATE_QT(__nv_bfloat16, 16, false, true)
+// SwiGLU epilogue
+MLXQ_INSTANTIATE_QT(__nv_bfloat16, 16, false, 1)
 }

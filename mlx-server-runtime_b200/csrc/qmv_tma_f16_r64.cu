@@ -1,4 +1,4 @@
 #include "qmv_tma_inst.cuh"
 namespace mlxq {
-MLXQ_INSTANTIATE_QT(__half, 64, false, false)
+MLXQ_INSTANTIATE_QT(__half, 64, false, 0)
 }

@@ -1,5 +1,6 @@
 #include "qmv_tma_inst.cuh"
 namespace mlxq {
-MLXQ_INSTANTIATE_QT(__half, 64, false, true)
-MLXQ_INSTANTIATE_QT(__half, 64, true, true)
+// SwiGLU epilogue
+MLXQ_INSTANTIATE_QT(__half, 64, false, 1)
+MLXQ_INSTANTIATE_QT(__half, 64, true, 1)
 }

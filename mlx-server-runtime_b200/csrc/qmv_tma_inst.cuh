@@ -6,10 +6,10 @@
 
 namespace mlxq {
 
-template <typename T, int BITS, int GS, int TM, int BR, bool HEADS, bool SW>
+template <typename T, int BITS, int GS, int TM, int BR, bool HEADS, int EPI>
 cudaError_t qt_launch_t(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tb,
                         const QtParams& p, int grid, size_t smem, bool overlap, cudaStream_t st) {
-    auto kern = qmv_tma_kernel<T, BITS, GS, TM, BR, HEADS, SW>;
+    auto kern = qmv_tma_kernel<T, BITS, GS, TM, BR, HEADS, EPI>;
     static int configured[64] = {0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -34,23 +34,23 @@ cudaError_t qt_launch_t(const CUtensorMap& tw, const CUtensorMap& ts, const CUte
     return cudaLaunchKernelEx(&cfg, kern, tw, ts, tb, p);
 }
 
-#define MLXQ_QT_INST0(T, BITS, GS, TM, BR, H, SW)                                               \
-    template cudaError_t qt_launch_t<T, BITS, GS, TM, BR, H, SW>(                                \
+#define MLXQ_QT_INST0(T, BITS, GS, TM, BR, H, EPI)                                               \
+    template cudaError_t qt_launch_t<T, BITS, GS, TM, BR, H, EPI>(                                \
         const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const QtParams&, int, size_t, \
         bool, cudaStream_t);
-#define MLXQ_QT_INST1(T, BITS, GS, BR, H, SW) \
-    MLXQ_QT_INST0(T, BITS, GS, 1, BR, H, SW)  \
-    MLXQ_QT_INST0(T, BITS, GS, 2, BR, H, SW)  \
-    MLXQ_QT_INST0(T, BITS, GS, 4, BR, H, SW)  \
-    MLXQ_QT_INST0(T, BITS, GS, 8, BR, H, SW)
+#define MLXQ_QT_INST1(T, BITS, GS, BR, H, EPI) \
+    MLXQ_QT_INST0(T, BITS, GS, 1, BR, H, EPI)  \
+    MLXQ_QT_INST0(T, BITS, GS, 2, BR, H, EPI)  \
+    MLXQ_QT_INST0(T, BITS, GS, 4, BR, H, EPI)  \
+    MLXQ_QT_INST0(T, BITS, GS, 8, BR, H, EPI)
 
 // Every (bits, group size) the plan accepts, for activation type T, BR-row units,
 // ticket warp or not, and plain or SwiGLU epilogue.
-#define MLXQ_INSTANTIATE_QT(T, BR, H, SW)  \
-    MLXQ_QT_INST1(T, 4, 32, BR, H, SW)     \
-    MLXQ_QT_INST1(T, 4, 64, BR, H, SW)     \
-    MLXQ_QT_INST1(T, 4, 128, BR, H, SW)    \
-    MLXQ_QT_INST1(T, 8, 32, BR, H, SW)     \
-    MLXQ_QT_INST1(T, 8, 64, BR, H, SW)
+#define MLXQ_INSTANTIATE_QT(T, BR, H, EPI)  \
+    MLXQ_QT_INST1(T, 4, 32, BR, H, EPI)     \
+    MLXQ_QT_INST1(T, 4, 64, BR, H, EPI)     \
+    MLXQ_QT_INST1(T, 4, 128, BR, H, EPI)    \
+    MLXQ_QT_INST1(T, 8, 32, BR, H, EPI)     \
+    MLXQ_QT_INST1(T, 8, 64, BR, H, EPI)
 
 }  // namespace mlxq

@@ -126,6 +126,13 @@ class QuantizedLinear(Module):
                                      group_size=self.group_size, bits=self.bits, mode=self.mode,
                                      bias=getattr(self, "bias", None))
 
+    def greedy_tokens(self, x):
+        """argmax over this layer's outputs (an lm_head's greedy next token), int32,
+        without writing the logits at decode (core.quantized_matmul_argmax)."""
+        return core.quantized_matmul_argmax(x, self.weight, self.scales, self.biases,
+                                            self.group_size, self.bits, self.mode,
+                                            bias=getattr(self, "bias", None))
+
 
 class FusedQuantizedLinear(Module):
     """QuantizedLinear layers that read the same input, computed in one launch.
@@ -234,6 +241,11 @@ class QuantizedEmbedding(Module):
     def as_linear(self, x):
         return core.quantized_matmul(x, self.weight, self.scales, self.biases, True,
                                      self.group_size, self.bits, self.mode)
+
+    def greedy_tokens(self, x):
+        """argmax of as_linear(x) per row (tied-head greedy decoding), int32."""
+        return core.quantized_matmul_argmax(x, self.weight, self.scales, self.biases,
+                                            self.group_size, self.bits, self.mode)
 
 
 class SwitchLinear(Module):
