@@ -232,6 +232,7 @@ int mlxq_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
         // workspace; without one (or too small) the kernel runs whole tiles instead.
         mlxq::QgemmPlan gp;
         mlxq::qgemm_plan(q.M, q.N, q.K, di.num_sms, &gp);
+        q.narrow = gp.narrow ? 1 : 0;
         if (gp.stream_k && workspace && workspace_bytes >= gp.ws_bytes &&
             !(reinterpret_cast<uintptr_t>(workspace) & 255u)) {
             q.sk = 1;

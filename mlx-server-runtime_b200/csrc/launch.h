@@ -120,12 +120,14 @@ struct QgemmParams {
     int sk;            // stream-K (dense only): CTAs take equal shares of tiles x K blocks
     unsigned* counter; // stream-K tickets, one per tile, zero at entry and exit
     float* partial;    // stream-K fp32 partial tiles, two slots per CTA
+    int narrow;        // dense whole tiles of 128 tokens instead of 192 (more tiles)
 };
 
 // Plan of the prefill kernel for a dense problem: data-parallel whole tiles, or
 // stream-K when whole tiles would leave a large part of the last wave idle.
 struct QgemmPlan {
     bool stream_k;
+    bool narrow;      // whole tiles of 128 tokens: more tiles for a shape that has few
     size_t ws_bytes;  // workspace (tickets + partial tiles) for stream-K, else 0
 };
 bool qgemm_plan(int M, int N, int K, int num_sms, QgemmPlan* plan);

@@ -790,10 +790,11 @@ static cudaError_t qgemm_launch_bt(const QgemmParams& p, cudaStream_t st) {
     return cudaGetLastError();
 }
 
-// Experts' row segments are short (a few hundred rows): 128-token tiles waste less.
+// Experts' row segments are short (a few hundred rows): 128-token tiles waste less; a
+// dense shape with few tiles (see qgemm_plan) also gets more of them at 128 tokens.
 template <typename T, int BITS, int GS>
 static cudaError_t qgemm_launch_t(const QgemmParams& p, cudaStream_t st) {
-    if (p.E > 0) return qgemm_launch_bt<T, BITS, GS, qg::BT_GROUPED, false>(p, st);
+    if (p.E > 0 || p.narrow) return qgemm_launch_bt<T, BITS, GS, qg::BT_GROUPED, false>(p, st);
     if (p.sk) return qgemm_launch_bt<T, BITS, GS, qg::BT_DENSE, true>(p, st);
     return qgemm_launch_bt<T, BITS, GS, qg::BT_DENSE, false>(p, st);
 }
@@ -871,6 +872,14 @@ bool qgemm_plan(int M, int N, int K, int num_sms, QgemmPlan* plan) {
         pl.stream_k = true;
         pl.ws_bytes = kTicketBytes + static_cast<size_t>(num_sms) * 2 * qg::BW *
                                          qg::BT_DENSE * sizeof(float);
+    } else if (fill < kStreamKBelow) {
+        // too few tiles and too short a K for stream-K (k/v at a few thousand tokens):
+        // 128-token tiles give the SMs more of them (a tile's pipeline, not its width,
+        // sets its time)
+        const long long tiles128 = static_cast<long long>((M + qg::BT_GROUPED - 1) /
+                                                          qg::BT_GROUPED) *
+                                   ((N + qg::BW - 1) / qg::BW);
+        pl.narrow = tiles128 > tiles && tiles < num_sms;
     }
     *plan = pl;
     return true;
