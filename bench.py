@@ -199,7 +199,8 @@ def run_reference(args):
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(step_bytes / (value * 1e9) * 1e3, 3),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "higher_is_better": True, "scaling": "strong" if args.gpus > 1 else "weak",
+        "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded numpy, W~N(0,0.02) bf16 -> 4-bit g64, x~N(0,1))",
         "config": {"workload": "qwen2.5-7b decode-token projections, M=1, 4-bit g64 "
                                "(CPU sample: one layer per step)", "global_batch": 1,
