@@ -18,8 +18,8 @@ With --gpus N (torchrun), every projection is N-sharded by output rows; each
 rank streams its shard and the step ends with one NCCL all-gather of all
 outputs; value = all ranks' algorithmic bytes / max-over-ranks step time.
 
---impl reference runs the CPU restatement of MLX's algorithm (the oracle, all
-host threads) on a bounded sample of the same workload (one decoder layer).
+--impl reference runs the CPU restatement of MLX's algorithm (the oracle, every
+host core) on the same decode step (rank 0 only under torchrun).
 """
 from __future__ import annotations
 
@@ -131,37 +131,80 @@ def dist_env():
     return world, rank, local
 
 
-class CpuLayer:
-    """One Qwen2.5-7B decoder layer's quantized projections in host memory, for
-    the C oracle (CPU restatement of MLX's algorithm)."""
+def host_cores() -> int:
+    """Host threads this process may run on (its CPU affinity)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover - non-Linux
+        return os.cpu_count() or 1
 
-    def __init__(self, threads: int | None = None):
+
+class CpuStep:
+    """The decode step's quantized projections in host memory, for the C oracle
+    (CPU restatement of MLX's algorithm), pinned to every host core.
+
+    One Qwen2.5-7B layer's 7 projections are quantized from N(0, 0.02) bf16
+    weights; `layers` distinct copies of that layer's packed weights (separate
+    buffers, so every layer streams its own memory as on the GPU) plus, with
+    `lm_head`, a 152064 x 3584 head made of copies of quantized rows."""
+
+    _base = None  # the one quantized layer, built once per process
+
+    @classmethod
+    def base_layer(cls):
+        if cls._base is None:
+            import numpy as np
+            import torch
+
+            from oracle import coracle
+
+            gen = torch.Generator().manual_seed(0)
+            layer = []
+            for name, N, K in PROJ:
+                # torch's CPU RNG and bf16 rounding (round to nearest even) are fast
+                w = (torch.randn(N, K, generator=gen) * 0.02).to(torch.bfloat16)
+                w = w.view(torch.int16).numpy().view(np.uint16)
+                wq, s, b = coracle.quantize(w, "bfloat16", GS, BITS)
+                x = torch.randn(1, K, generator=gen).to(torch.bfloat16)
+                layer.append((x.view(torch.int16).numpy().view(np.uint16), wq, s, b))
+            cls._base = layer
+        return cls._base
+
+    def __init__(self, layers: int = 1, lm_head: bool = False):
         import numpy as np
 
-        from oracle import coracle, oracle_np
+        from oracle import coracle
 
         coracle.build()
-        if threads:
-            coracle.set_num_threads(threads)
+        # torchrun sets OMP_NUM_THREADS=1 for its workers; the baseline uses every
+        # core it may run on, whatever the launcher set
+        coracle.set_num_threads(host_cores())
         self.coracle = coracle
-        rng = np.random.default_rng(0)
-        self.layer = []
-        for name, N, K in PROJ:
-            w = oracle_np.from_f32(rng.standard_normal((N, K), dtype=np.float32) * 0.02,
-                                   "bfloat16")
-            wq, s, b = coracle.quantize(w, "bfloat16", GS, BITS)
-            x = oracle_np.from_f32(rng.standard_normal((1, K), dtype=np.float32), "bfloat16")
-            self.layer.append((x, wq, s, b))
-        self.bytes = sum(qmm_bytes(1, N, K) for _, N, K in PROJ)
+        layer = self.base_layer()
+        self.ops = []
+        for i in range(layers):
+            self.ops += [(x, wq if i == 0 else wq.copy(), s if i == 0 else s.copy(),
+                          b if i == 0 else b.copy()) for x, wq, s, b in layer]
+        if lm_head:
+            gate = layer[4]  # 18944 rows; 8 copies + 512 rows = 152064
+            reps = VOCAB // INTER + 1
+            wq = np.concatenate([gate[1]] * reps)[:VOCAB].copy()
+            s = np.concatenate([gate[2]] * reps)[:VOCAB].copy()
+            b = np.concatenate([gate[3]] * reps)[:VOCAB].copy()
+            self.ops.append((gate[0], wq, s, b))
+        self.bytes = sum(qmm_bytes(1, wq.shape[0], x.shape[1]) for x, wq, _, _ in self.ops)
         self.threads = coracle.num_threads()
 
+    def step(self):
+        for x, wq, s, b in self.ops:
+            self.coracle.quantized_matmul(x, wq, s, b, "bfloat16", GS, BITS)
+
     def run(self, seconds: float):
-        """Whole-layer passes until `seconds` elapse; returns (GB/s, passes, seconds)."""
+        """Whole passes until `seconds` elapse; returns (GB/s, passes, seconds)."""
         t0 = time.perf_counter()
         passes = 0
         while True:
-            for x, wq, s, b in self.layer:
-                self.coracle.quantized_matmul(x, wq, s, b, "bfloat16", GS, BITS)
+            self.step()
             passes += 1
             if time.perf_counter() - t0 > seconds:
                 break
@@ -169,52 +212,262 @@ class CpuLayer:
         return self.bytes * passes / dt / 1e9, passes, dt
 
 
-def cpu_baseline(seconds: float = 12.0, threads: int | None = None):
+def cpu_baseline(seconds: float = 12.0):
     """Time the C oracle on one decoder layer's projections at M=1 (bounded sample)."""
-    lay = CpuLayer(threads)
+    lay = CpuStep(layers=1)
     lay.run(0.0)  # warm-up pass
     gbs, passes, dt = lay.run(seconds)
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": lay.threads, "kind": "port",
             "sample": f"{passes} pass(es) over one Qwen2.5-7B layer's 7 projections at M=1 "
-                      f"({lay.bytes / 1e6:.1f} MB each), C oracle -O3 OpenMP, "
-                      f"{dt:.1f} s of CPU work",
+                      f"({lay.bytes / 1e6:.1f} MB each), C oracle -O3 OpenMP on every host "
+                      f"core, {dt:.1f} s of CPU work",
             "seconds": round(dt, 2)}
 
 
 def run_reference(args):
+    """The reference's CPU implementation of the path (its algorithm restated in C:
+    MLX itself has no wheel here) on the same decode step as the B200 arm: 28 layers
+    x 7 projections + lm_head at M=1, 4-bit g64, every host core, rank 0 only. A step
+    is the whole decode step when K + W of them fit in about two minutes, else the
+    first L layers of it (said in `sample`)."""
     world, rank, _ = dist_env()
     if rank != 0:
         return
-    import numpy as np  # noqa: F401
-
-    lay = CpuLayer()
-    nthreads = lay.threads
-    per_step = min(10.0, max(0.5, 90.0 / max(1, args.steps + args.warmup)))
-    vals = []
+    probe = CpuStep(layers=1)
+    probe.step()
+    t0 = time.perf_counter()
+    probe.step()
+    layer_s = time.perf_counter() - t0
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    full_s = layer_s * (LAYERS + VOCAB * HIDDEN / sum(N * K for _, N, K in PROJ))
+    if full_s <= budget:
+        step = CpuStep(layers=LAYERS, lm_head=True)
+        what = "the whole decode step (28 layers x 7 projections + lm_head, 3.98 GB)"
+        same = True
+    else:
+        L = max(1, min(LAYERS, int(budget / layer_s)))
+        step = CpuStep(layers=L)
+        what = f"the first {L} of the step's 28 layers (7 projections each) per step"
+        same = False
+    del probe
+    times = []
     for i in range(args.warmup + args.steps):
-        gbs, _, _ = lay.run(per_step)
+        t0 = time.perf_counter()
+        step.step()
+        dt = time.perf_counter() - t0
         if i >= args.warmup:
-            vals.append(gbs)
-    value = round(statistics.median(vals), 3)
-    step_bytes = sum(qmm_bytes(1, N, K) for _, N, K in shapes())
+            times.append(dt)
+    ms = 1e3 * sum(times) / len(times)
+    value = round(step.bytes / (ms * 1e-3) / 1e9, 3)
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(step_bytes / (value * 1e9) * 1e3, 3),
-        "higher_is_better": True, "scaling": "strong" if args.gpus > 1 else "weak",
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded numpy, W~N(0,0.02) bf16 -> 4-bit g64, x~N(0,1))",
-        "config": {"workload": "qwen2.5-7b decode-token projections, M=1, 4-bit g64 "
-                               "(CPU sample: one layer per step)", "global_batch": 1,
-                   "parallelism": "cpu"},
+        "data": "synthetic (seeded torch CPU RNG: W~N(0,0.02) bf16 -> 4-bit g64 by the C oracle, x~N(0,1) bf16)",
+        "config": {"workload": "qwen2.5-7b decode-token quantized projections at M=1: "
+                               "28 layers x q/k/v/o/gate/up/down + lm_head, 4-bit g64",
+                   "global_batch": 1, "parallelism": "cpu", "step_bytes": step.bytes,
+                   "same_config": same},
         "impl": "reference",
-        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": nthreads, "kind": "port",
-                         "sample": "one Qwen2.5-7B layer's 7 projections at M=1 per step "
-                                   "(C restatement of MLX's CPU algorithm; MLX itself is not "
-                                   "installable here)"},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": step.threads, "kind": "port",
+                         "sample": what + "; C restatement of MLX's CPU algorithm (MLX itself "
+                                          "has no wheel here), OpenMP on every host core"},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def graph_ms(torch, calls, reps, stream, warm=2):
+    """Milliseconds per replay of a CUDA graph of `calls` (zero-argument callables
+    issuing public-API calls), captured on `stream` after eager warm-up there (which
+    also allocates the per-stream workspaces); CUDA events on that stream."""
+    with torch.cuda.stream(stream):
+        for _ in range(warm):
+            for c in calls:
+                c()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for c in calls:
+            c()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    del g
+    return ms
+
+
+SWEEP_SHAPES = [("q_o", HIDDEN, HIDDEN), ("k_v", KV, HIDDEN), ("gate_up", INTER, HIDDEN),
+                ("down", HIDDEN, INTER)]
+
+
+def decode_sweep(torch, mxq, dev, stream, peak_gbs):
+    """Config 2 (and config 1 = 4-bit gate_up at M=1): every shape x M x bits, each
+    timed as a graph of launches over enough weight copies to exceed L2 twice."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2)
+    out = {"unit": "GB/s", "peak": peak_gbs, "l2": "rotating weight copies totalling >= 256 MB"}
+    for bits in (4, 8):
+        for name, N, K in SWEEP_SHAPES:
+            wbytes = N * K * bits // 8 + 4 * N * K // GS
+            copies = max(2, min(256, -(-256_000_000 // wbytes)))
+            w = (torch.randn(N, K, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+            w0 = mxq.quantize(w, GS, bits)
+            del w
+            ws = [w0] + [tuple(t.clone() for t in w0) for _ in range(copies - 1)]
+            row = {}
+            for M in (1, 2, 4, 8, 16, 32):
+                x = torch.randn(M, K, device=dev, generator=gen).to(torch.bfloat16)
+                calls = [(lambda wt=wt: mxq.quantized_matmul(x, *wt, group_size=GS, bits=bits))
+                         for wt in ws]
+                ms = graph_ms(torch, calls, max(2, 1200 // copies), stream)
+                us = ms * 1e3 / copies
+                gbs = qmm_bytes(M, N, K, bits) / (us * 1e-6) / 1e9
+                row[str(M)] = {"us": round(us, 2), "GB/s": round(gbs, 1),
+                               "frac": round(gbs / peak_gbs, 4)}
+            out.setdefault(f"w{bits}", {})[name] = row
+            del ws, w0
+            torch.cuda.empty_cache()
+    return out
+
+
+def prefill_sweep(torch, mxq, dev, stream, peak_tf):
+    """Config 3: every 7B shape at M in {512, 2048, 8192}, 4-bit g64, TFLOP/s."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3)
+    out = {"unit": "TFLOP/s", "peak": peak_tf, "peak_source": "measured bf16 burst",
+           "shapes": {}}
+    best = None
+    for name, N, K in SWEEP_SHAPES:
+        w = (torch.randn(N, K, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+        w0 = mxq.quantize(w, GS, BITS)
+        del w
+        ws = [w0, tuple(t.clone() for t in w0)]
+        row = {}
+        for M in (512, 2048, 8192):
+            x = torch.randn(M, K, device=dev, generator=gen).to(torch.bfloat16)
+            calls = [(lambda wt=wt: mxq.quantized_matmul(x, *wt, group_size=GS, bits=BITS))
+                     for wt in ws]
+            ms = graph_ms(torch, calls, 4 if M == 8192 else 10, stream) / len(ws)
+            tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+            row[str(M)] = {"us": round(ms * 1e3, 1), "TFLOP/s": round(tf, 1),
+                           "frac": round(tf / peak_tf, 4)}
+            if name == "gate_up" and M == 2048:
+                best = {"bound": "tensor", "kernel": "qgemm_kernel", "case": "gate_up M=2048",
+                        "achieved": round(tf, 1), "peak": peak_tf, "unit": "TFLOP/s",
+                        "frac": round(tf / peak_tf, 4)}
+            del x
+        out["shapes"][name] = row
+        del ws, w0
+        torch.cuda.empty_cache()
+    out["roofline"] = best
+    return out
+
+
+MOE_E, MOE_TOPK, MOE_HID, MOE_INTER = 128, 8, 2048, 768
+
+
+def moe_weights(torch, mxq, dev, seed=11, experts=MOE_E):
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    ws = {}
+    for name, (n, k) in (("gate", (MOE_INTER, MOE_HID)), ("up", (MOE_INTER, MOE_HID)),
+                         ("down", (MOE_HID, MOE_INTER))):
+        w = (torch.randn(experts, n, k, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+        ws[name] = mxq.quantize(w, GS, BITS)
+        del w
+    return ws
+
+
+def switch_glu(mxq, ws):
+    from mlx_server_runtime_b200 import nn
+    sw = nn.SwitchGLU.__new__(nn.SwitchGLU)
+    for name, attr in (("gate", "gate_proj"), ("up", "up_proj"), ("down", "down_proj")):
+        q = nn.QuantizedSwitchLinear.__new__(nn.QuantizedSwitchLinear)
+        q.group_size, q.bits, q.mode = GS, BITS, "affine"
+        q.weight, q.scales, q.biases = ws[name]
+        setattr(sw, attr, q)
+    return sw
+
+
+def moe_sweep(torch, mxq, dev, stream, peak_gbs, peak_tf):
+    """Config 5: the Qwen3-30B-A3B-shaped SwitchGLU block (128 experts, top-8 of a
+    softmax over N(0,1) router logits, 2048 -> 768 -> 2048, 4-bit g64) as the model
+    graphs call it, at T in {1, 64, 4096} tokens."""
+    from mlx_server_runtime_b200 import nn
+    ws = moe_weights(torch, mxq, dev)
+    sw = switch_glu(mxq, ws)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(12)
+    per_expert = sum(n * k * BITS // 8 + 4 * n * k // GS
+                     for n, k in ((MOE_INTER, MOE_HID), (MOE_INTER, MOE_HID), (MOE_HID, MOE_INTER)))
+    out = {"what": "SwitchGLU block: sort by expert (T >= 8), up, gate, silu*up, down, unsort",
+           "peak_gbs": peak_gbs, "peak_tflops": peak_tf, "T": {}}
+    for T in (1, 64, 4096):
+        x = torch.randn(T, MOE_HID, device=dev, generator=gen).to(torch.bfloat16)
+        logits = torch.randn(T, MOE_E, device=dev, generator=gen)
+        idx, _ = nn.route_topk(logits, MOE_TOPK)
+        used = int(torch.unique(idx).numel())
+        ms = graph_ms(torch, [lambda: sw(x, idx)], 20 if T < 4096 else 10, stream)
+        rows = T * MOE_TOPK
+        byts = used * per_expert + 2 * rows * (MOE_HID + 2 * MOE_INTER) * 2
+        flops = 2.0 * rows * 3 * MOE_INTER * MOE_HID
+        gbs = byts / (ms * 1e-3) / 1e9
+        tf = flops / (ms * 1e-3) / 1e12
+        e = {"us": round(ms * 1e3, 1), "experts_touched": used, "bytes": byts,
+             "GB/s": round(gbs, 1), "TFLOP/s": round(tf, 2)}
+        e["roofline"] = ({"bound": "hbm", "frac": round(gbs / peak_gbs, 4)} if T <= 64
+                         else {"bound": "tensor", "frac": round(tf / peak_tf, 4)})
+        out["T"][str(T)] = e
+    del sw, ws
+    torch.cuda.empty_cache()
+    return out
+
+
+def expert_parallel_bench(torch, mxq, dist, dev, world, rank, stream):
+    """Config 5 expert-parallel over the ranks: each rank routes its own T tokens,
+    owns 128 / N experts, and exchanges rows with NCCL all-to-alls
+    (distributed.ExpertParallelSwitchGLU). Max-over-ranks time per call."""
+    from mlx_server_runtime_b200 import distributed, nn
+    e_local = MOE_E // world
+    ws = moe_weights(torch, mxq, dev, seed=100 + rank, experts=e_local)
+    ep = distributed.ExpertParallelSwitchGLU(ws["gate"], ws["up"], ws["down"],
+                                             num_experts=MOE_E, group_size=GS, bits=BITS)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(200 + rank)
+    res = {}
+    for T in (64, 4096):
+        x = torch.randn(T, MOE_HID, device=dev, generator=gen).to(torch.bfloat16)
+        idx, _ = nn.route_topk(torch.randn(T, MOE_E, device=dev, generator=gen), MOE_TOPK)
+        for _ in range(3):
+            ep(x, idx)
+        dist.barrier()
+        torch.cuda.synchronize()
+        reps = 10
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            ep(x, idx)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([e0.elapsed_time(e1) / reps], dtype=torch.float64, device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        ms = float(ms.item())
+        res[str(T)] = {"ms": round(ms, 3), "tokens_per_s": round(world * T / (ms * 1e-3), 1)}
+    del ep, ws
+    torch.cuda.empty_cache()
+    return {"what": "SwitchGLU with 128 experts split over the ranks, T tokens per rank, "
+                    "NCCL all-to-all dispatch and combine (host-synchronised split sizes)",
+            "T_per_rank": res}
 
 
 def run(args):
@@ -297,10 +550,14 @@ def run(args):
                 [weights[i] for i in g], GS, BITS)
             fused_ops.append((xs[g[0]], wt))
     fused_bytes = sum(qmm_bytes(1, wt[0].shape[0], x.shape[-1]) for x, wt in fused_ops)
+    fused_outs = [None] * len(fused_ops)
+    fused_flat = torch.empty(sum(wt[0].shape[0] for _, wt in fused_ops), dtype=torch.bfloat16,
+                             device=dev)
 
     def step_fused_eager():
-        for x, wt in fused_ops:
-            mxq.quantized_matmul(x, *wt, group_size=GS, bits=BITS)
+        for i, (x, wt) in enumerate(fused_ops):
+            fused_outs[i] = mxq.quantized_matmul(x, *wt, group_size=GS, bits=BITS)
+        torch.cat([o.reshape(-1) for o in fused_outs], out=fused_flat)
 
     for _ in range(2):
         step_fused_eager()
@@ -313,14 +570,20 @@ def run(args):
             step_fused_eager()
     torch.cuda.synchronize()
 
-    gathered = None
+    gathered = fused_gathered = None
     if world > 1:
         gathered = torch.empty(world * out_flat.numel(), dtype=torch.bfloat16, device=dev)
+        fused_gathered = torch.empty(world * fused_flat.numel(), dtype=torch.bfloat16, device=dev)
 
     def step():
         graph.replay()
         if world > 1:
             dist.all_gather_into_tensor(gathered, out_flat)
+
+    def step_fused():
+        graph_fused.replay()
+        if world > 1:
+            dist.all_gather_into_tensor(fused_gathered, fused_flat)
 
     step_bytes = sum(qmm_bytes(1, N, K) for _, N, K in shp if N)
     total_bytes = step_bytes
@@ -334,45 +597,45 @@ def run(args):
             dist.barrier()
         torch.cuda.synchronize()
 
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(fn, steps):
+        """ms per call of fn: barrier + synchronize on both sides, CUDA events on
+        the current stream, max over ranks."""
+        cur = torch.cuda.current_stream(dev)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cur)
+        for _ in range(steps):
+            fn()
+        e1.record(cur)
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1) / steps)
+
     for _ in range(max(3, args.warmup)):
         step()
     barrier()
-    cur = torch.cuda.current_stream(dev)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index) as clk:
-        barrier()
-        ev0.record(cur)
-        for _ in range(args.steps):
-            step()
-        ev1.record(cur)
-        barrier()
-    ms = ev0.elapsed_time(ev1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms = timed(step, args.steps)
     value = total_bytes / (ms * 1e-3) / 1e9
+    # the matmuls alone (the step without its all-gather), for N > 1
+    ms_kernels = timed(graph.replay, args.steps) if world > 1 else ms
 
-    # ---- fused projections (device-resident, like value) --------------------------
+    # ---- fused projections (device-resident, like value; all-gather included) -----
     for _ in range(3):
-        graph_fused.replay()
-    barrier()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(cur)
-    for _ in range(args.steps):
-        graph_fused.replay()
-    f1.record(cur)
-    barrier()
-    ms_fused = f0.elapsed_time(f1) / args.steps
+        step_fused()
+    ms_fused = timed(step_fused, args.steps)
+    ms_fused_kernels = timed(graph_fused.replay, args.steps) if world > 1 else ms_fused
+    fused_total = float(fused_bytes)
     if world > 1:
-        t = torch.tensor([ms_fused, float(fused_bytes)], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_fused = float(t[0].item())
         tb = torch.tensor([float(fused_bytes)], dtype=torch.float64, device=dev)
         dist.all_reduce(tb)
         fused_total = float(tb.item())
-    else:
-        fused_total = float(fused_bytes)
     del graph_fused
 
     # ---- end to end: pinned H2D of inputs, replay, D2H of outputs ---------------
@@ -390,19 +653,7 @@ def run(args):
 
     for _ in range(3):
         step_e2e()
-    barrier()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record(cur)
-    for _ in range(args.steps):
-        step_e2e()
-    t1.record(cur)
-    barrier()
-    ms_e2e = t0.elapsed_time(t1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms_e2e], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_e2e = float(t.item())
+    ms_e2e = timed(step_e2e, args.steps)
     e2e = total_bytes / (ms_e2e * 1e-3) / 1e9
 
     peaks = {}
@@ -412,6 +663,7 @@ def run(args):
     except Exception:
         pass
     peak = float(peaks.get("hbm_gbs", 6650.0))
+    peak_tf = float(peaks.get("bf16_tflops", 1590.0))
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
     traffic = None
     try:
@@ -421,6 +673,24 @@ def run(args):
     except Exception:
         pass
 
+    del graph
+    torch.cuda.empty_cache()
+    extras = {}
+    if not args.no_extras:
+        if world == 1:
+            sweep = decode_sweep(torch, mxq, dev, stream, peak)
+            extras["decode_sweep"] = sweep
+            c1 = sweep["w4"]["gate_up"]["1"]
+            extras["config1"] = {"what": "one quantized_matmul x[1,3584] @ W[18944,3584]^T, "
+                                         "4-bit g64 (graph replay, weights rotated past L2)",
+                                 "us": c1["us"], "GB/s": c1["GB/s"], "frac": c1["frac"],
+                                 "frac_of_8TBs_nominal": round(c1["GB/s"] / 8000.0, 4)}
+            extras["prefill"] = prefill_sweep(torch, mxq, dev, stream, peak_tf)
+            extras["moe"] = moe_sweep(torch, mxq, dev, stream, peak, peak_tf)
+        else:
+            extras["expert_parallel"] = expert_parallel_bench(torch, mxq, dist, dev, world,
+                                                              rank, stream)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         try:
@@ -429,7 +699,6 @@ def run(args):
             cpu = {"value": None, "error": str(e)[:200]}
 
     if world > 1:
-        graph.reset() if hasattr(graph, "reset") else None
         dist.barrier()
     if rank == 0:
         line = {
@@ -449,7 +718,8 @@ def run(args):
                        else None,
                        "qmm_only_tok_per_s": round(1000.0 / ms, 1)},
             "gpu_launches": launches_per_step * args.steps,
-            "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak * world,
+            "roofline": {"bound": "hbm", "kernel": "qmv_tma_kernel (decode step)",
+                         "achieved": round(value, 1), "peak": peak * world,
                          "unit": "GB/s", "frac": round(value / (peak * world), 4),
                          "peak_source": peak_src + (f" (per GPU x {world})" if world > 1 else ""),
                          "frac_of_8TBs_nominal": round(value / (8000.0 * world), 4),
@@ -464,10 +734,19 @@ def run(args):
                 "launches_per_step": len(fused_ops),
                 "qmm_only_tok_per_s": round(1000.0 / ms_fused, 1),
                 "what": "same projections with q/k/v and gate/up stacked along N "
-                        "(concat_quantized): one launch each, same weight bytes"},
+                        "(concat_quantized): one launch each, same weight bytes"
+                        + ("; all-gather of all outputs included" if world > 1 else "")},
         }
+        if world > 1:
+            line["kernel_only"] = {
+                "what": "the same steps without the all-gather (matmul graph replay only)",
+                "ms_per_step": round(ms_kernels, 4),
+                "value": round(total_bytes / (ms_kernels * 1e-3) / 1e9, 1),
+                "allgather_ms": round(ms - ms_kernels, 4),
+                "fused_ms_per_step": round(ms_fused_kernels, 4),
+                "fused_value": round(fused_total / (ms_fused_kernels * 1e-3) / 1e9, 1)}
+        line.update(extras)
         print(json.dumps(line), flush=True)
-    del graph
     if world > 1:
         dist.destroy_process_group()
 
@@ -538,7 +817,6 @@ def run_case(args):
 
 
 MOE_CASES = {"moe_gate": (768, 2048), "moe_down": (2048, 768)}  # (N, K), 128 experts
-MOE_E, MOE_TOPK = 128, 8
 
 
 def run_moe_case(args):
@@ -599,6 +877,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the decode sweep, prefill, MoE and expert-parallel objects")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -85,8 +85,20 @@ int mlxq_get_launch_overlap(void);
  * that wait on hardware barriers give up after a bounded number of polls
  * instead of hanging; they then record a nonzero code here, skip their output
  * and exit. Synchronous (reads device memory). No counterpart in the reference.
+ * A kernel that gave up may have left tickets of its workspace nonzero: after a
+ * nonzero code, zero-fill every workspace passed to the matmuls again before
+ * reusing it (the Python layer's device_error() does this for its workspaces).
  */
 int mlxq_device_error(int* code);
+
+/*
+ * Failure-path check: enqueues one bounded mbarrier wait that nothing completes
+ * (`polls` in [1, 2^22] polls), which gives up and records the timeout code (2) in
+ * the device error word, as a kernel whose barrier never completed would. The
+ * context stays usable. Lets a caller test its handling of mlxq_device_error
+ * without any device fault. No counterpart in the reference.
+ */
+int mlxq_check_bounded_wait(uint32_t polls, void* stream);
 
 /*
  * quantize: replaces mx.quantize(w, group_size, bits, mode="affine")

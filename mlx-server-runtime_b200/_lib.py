@@ -38,6 +38,7 @@ EXPORTED = (
     "mlxq_quantized_matmul_swiglu",
     "mlxq_argmax_workspace_size",
     "mlxq_quantized_matmul_argmax",
+    "mlxq_check_bounded_wait",
 )
 
 _lock = threading.Lock()
@@ -97,6 +98,8 @@ def load(path: str | None = None):
         L.mlxq_quantized_matmul_argmax.argtypes = [vp, vp, vp, vp, vp, vp, i64, i64, i64, i32,
                                                    i32, i32, vp, sz, vp]
         L.mlxq_quantized_matmul_argmax.restype = i32
+        L.mlxq_check_bounded_wait.argtypes = [ctypes.c_uint32, vp]
+        L.mlxq_check_bounded_wait.restype = i32
         v = L.mlxq_abi_version()
         if v != ABI_VERSION:
             raise LibraryError(f"{p} has ABI version {v}, expected {ABI_VERSION}; rebuild it")
@@ -106,9 +109,16 @@ def load(path: str | None = None):
 
 
 def device_error() -> int:
-    """Read and clear the current device's kernel error code (0 = none)."""
+    """Read and clear the current device's kernel error code (0 = none).
+
+    A kernel that gave up on a bounded wait may have left workspace tickets
+    nonzero, so after a nonzero code every cached workspace is zero-filled again
+    (core.Workspace.reset) before later calls reuse it."""
     code = ctypes.c_int(0)
     check(load().mlxq_device_error(ctypes.byref(code)), "device_error")
+    if code.value:
+        from .core import Workspace
+        Workspace.reset()
     return code.value
 
 

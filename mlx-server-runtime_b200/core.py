@@ -95,6 +95,16 @@ class Workspace:
         with cls._lock:
             cls._bufs.clear()
 
+    @classmethod
+    def reset(cls) -> None:
+        """Zero-fill every cached buffer on its own stream (after a kernel gave
+        up on a bounded wait and may have left tickets nonzero)."""
+        with cls._lock:
+            for (dev, stream_ptr, _kind), buf in cls._bufs.items():
+                st = torch.cuda.ExternalStream(stream_ptr, device=torch.device("cuda", dev))
+                with torch.cuda.stream(st):
+                    buf.zero_()
+
 
 class launch_overlap:
     """Context manager (or plain call) enabling launch overlap for quantized_matmul.

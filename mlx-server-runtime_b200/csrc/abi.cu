@@ -4,6 +4,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 #include "../../include/mlxq_b200.h"
@@ -36,9 +37,11 @@ struct DeviceInfo {
     int sm_smem = 0;   // shared memory per SM
 };
 
-// Properties of the calling thread's current device (cached per device).
+// Properties of the calling thread's current device (cached per device: filled once
+// under the setup mutex, published by a release store of `ready`).
 int device_info(DeviceInfo* out, cudaStream_t stream) {
     static DeviceInfo cache[64];
+    static std::atomic<int> ready[64];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -60,7 +63,12 @@ int device_info(DeviceInfo* out, cudaStream_t stream) {
     (void)stream;
 #endif
     if (dev < 0 || dev >= 64) return fail(MLXQ_ERR_CUDA, "device ordinal %d out of range", dev);
-    if (cache[dev].num_sms == 0) {
+    if (!ready[dev].load(std::memory_order_acquire)) {
+        std::lock_guard<std::mutex> lock(mlxq::setup_mutex());
+        if (ready[dev].load(std::memory_order_relaxed)) {
+            *out = cache[dev];
+            return MLXQ_OK;
+        }
         int sms = 0, smem = 0;
         e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SMs)");
@@ -72,6 +80,7 @@ int device_info(DeviceInfo* out, cudaStream_t stream) {
         cache[dev].max_smem = smem - 1024;  // room for the kernels' static shared memory
         cache[dev].sm_smem = sm_smem;
         cache[dev].num_sms = sms;
+        ready[dev].store(1, std::memory_order_release);
     }
     *out = cache[dev];
     return MLXQ_OK;
@@ -111,6 +120,11 @@ size_t dense_plan(int64_t M, int64_t N, int64_t K, int group_size, int bits, int
 namespace mlxq {
 bool launch_overlap_enabled() { return g_overlap.load(std::memory_order_relaxed) != 0; }
 
+std::mutex& setup_mutex() {
+    static std::mutex mu;
+    return mu;
+}
+
 // Records the message mlxq_last_error() returns; for entry points defined in
 // other translation units.
 int set_last_error(int code, const char* msg) {
@@ -136,6 +150,14 @@ int mlxq_device_error(int* code) {
     if (e == cudaSuccess) e = mlxq::qmv_tma_read_error(&b);
     if (e != cudaSuccess) return cuda_fail(e, "device_error");
     *code = a ? a : b;
+    return MLXQ_OK;
+}
+
+int mlxq_check_bounded_wait(uint32_t polls, void* stream) {
+    if (polls == 0 || polls > (1u << 22))
+        return fail(MLXQ_ERR_SHAPE, "check_bounded_wait: polls=%u must be in [1, 2^22]", polls);
+    cudaError_t e = mlxq::launch_bounded_wait_check(polls, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "check_bounded_wait launch");
     return MLXQ_OK;
 }
 

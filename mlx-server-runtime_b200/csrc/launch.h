@@ -5,7 +5,33 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+
 namespace mlxq {
+
+// Serializes the one-time per-device setup calls of every launcher (abi.cu).
+std::mutex& setup_mutex();
+
+// Per-device record of a value set up once (a kernel's dynamic shared-memory
+// limit, an SM count): zero until set, only ever raised, published with release
+// order so a thread that reads it also sees what was done before.
+struct PerDevice {
+    std::atomic<int> v[64];
+};
+
+// Raises `kern`'s dynamic shared-memory limit on the current device `dev` to at
+// least `smem` (never lowers it); host threads racing on a first launch serialize.
+template <typename K>
+cudaError_t ensure_smem_attr(K kern, PerDevice& cache, int dev, int smem) {
+    if (cache.v[dev].load(std::memory_order_acquire) >= smem) return cudaSuccess;
+    std::lock_guard<std::mutex> lock(setup_mutex());
+    if (cache.v[dev].load(std::memory_order_relaxed) >= smem) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    cache.v[dev].store(smem, std::memory_order_release);
+    return cudaSuccess;
+}
 
 enum { kF32 = 0, kBF16 = 1, kF16 = 2 };
 
@@ -100,6 +126,8 @@ cudaError_t qmv_tma_launch(int dtype, int bits, int gs, const QtPlan& plan, cons
                            void* out, int M, int N, int K, void* workspace, bool overlap,
                            cudaStream_t st, int epi = 0);
 cudaError_t qmv_tma_read_error(int* out_code);
+// A single bounded wait that runs out (mlxq_check_bounded_wait).
+cudaError_t launch_bounded_wait_check(uint32_t polls, cudaStream_t st);
 
 // One problem for the tcgen05 prefill kernel (qgemm_sm100.cu): dense, or grouped by
 // expert (sorted gather_qmm) when E > 0: rows [seg[e]*rpe, seg[e+1]*rpe) of x and out

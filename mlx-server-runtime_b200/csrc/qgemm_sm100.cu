@@ -759,19 +759,16 @@ static cudaError_t qgemm_launch_bt(const QgemmParams& p, cudaStream_t st) {
     auto kern = qgemm_kernel<T, BITS, GS, BT, SK>;
     constexpr int smem = qg::smem_bytes<BITS, BT>();
     static_assert(smem <= 232448, "at most 227 KB of dynamic shared memory per CTA");
-    static int configured[64] = {0};
-    static int num_sms[64] = {0};
+    static PerDevice configured;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!configured[dev]) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        e = cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return e;
-        configured[dev] = 1;
-    }
+    e = ensure_smem_attr(kern, configured, dev, smem);
+    if (e != cudaSuccess) return e;
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
     CUtensorMap tx, tw;
     const unsigned long long kw = static_cast<unsigned long long>(p.K) * BITS / 32;
     if (!qg_map(&tx, p.x, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, p.K, p.M, qg::BK, BT,
@@ -784,8 +781,7 @@ static cudaError_t qgemm_launch_bt(const QgemmParams& p, cudaStream_t st) {
     // is at most ceil(M / BT) + E
     const long long mblocks = (p.M + BT - 1) / BT + (p.E > 0 ? p.E : 0);
     const long long tiles = mblocks * ((p.N + qg::BW - 1) / qg::BW);
-    const int grid = SK ? num_sms[dev]
-                        : static_cast<int>(tiles < num_sms[dev] ? tiles : num_sms[dev]);
+    const int grid = SK ? sms : static_cast<int>(tiles < sms ? tiles : sms);
     kern<<<grid, qg::THREADS, smem, st>>>(tx, tw, p);
     return cudaGetLastError();
 }

@@ -2,7 +2,9 @@
 // device memory (see include/mlxq_b200.h). The K-split scratch of the decode
 // kernel lives in a fixed array in this library's device image instead of a
 // caller workspace.
+#include <atomic>
 #include <cstdio>
+#include <mutex>
 
 #include "../../include/mlxq_b200.h"
 #include "launch.h"
@@ -15,9 +17,16 @@ constexpr size_t kScratchBytes = MLXQ_NOALLOC_SCRATCH_BYTES;
 static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
-void* g_scratch_ptr[kMaxDevices] = {};  // device address of g_scratch, per device
-int g_num_sms[kMaxDevices] = {};
-int g_max_smem[kMaxDevices] = {};
+// Per-device launch limits and the device address of g_scratch. A device's entry
+// is filled once under g_setup_mu; g_scratch_ptr is stored last with release
+// order, so a thread that loads a non-null pointer (acquire) also sees the limits.
+struct DeviceSetup {
+    int num_sms = 0;
+    int max_smem = 0;
+};
+DeviceSetup g_setup[kMaxDevices];
+std::atomic<void*> g_scratch_ptr[kMaxDevices];
+std::mutex g_setup_mu;
 
 int fail(int code, const char* fmt, long long a = 0, long long b = 0) {
     char buf[256];
@@ -34,9 +43,20 @@ int cuda_fail(cudaError_t e, const char* what) {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Once per device, with that device current: the device address of the scratch
-// array (the host-side symbol is only a stand-in) and the launch limits.
-int setup_device(int dev) {
-    if (g_scratch_ptr[dev] != nullptr) return MLXQ_OK;
+// array (the host-side symbol is only a stand-in) and the launch limits. Host
+// threads making a device's first call at the same time serialize on the mutex.
+int setup_device(int dev, void** scratch) {
+    void* ready = g_scratch_ptr[dev].load(std::memory_order_acquire);
+    if (ready != nullptr) {
+        *scratch = ready;
+        return MLXQ_OK;
+    }
+    std::lock_guard<std::mutex> lock(g_setup_mu);
+    ready = g_scratch_ptr[dev].load(std::memory_order_acquire);
+    if (ready != nullptr) {
+        *scratch = ready;
+        return MLXQ_OK;
+    }
     int sms = 0, smem = 0;
     cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SMs)");
@@ -45,9 +65,10 @@ int setup_device(int dev) {
     void* ptr = nullptr;
     e = cudaGetSymbolAddress(&ptr, g_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(scratch)");
-    g_num_sms[dev] = sms;
-    g_max_smem[dev] = smem - 1024;
-    g_scratch_ptr[dev] = ptr;
+    g_setup[dev].num_sms = sms;
+    g_setup[dev].max_smem = smem - 1024;
+    g_scratch_ptr[dev].store(ptr, std::memory_order_release);
+    *scratch = ptr;
     return MLXQ_OK;
 }
 
@@ -80,18 +101,27 @@ extern "C" int mlxq_quantized_matmul_noalloc(const void* x, const uint32_t* w, c
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
     if (dev < 0 || dev >= kMaxDevices) return fail(MLXQ_ERR_CUDA, "device %lld out of range", dev);
-    int rc = setup_device(dev);
+    void* scratch = nullptr;
+    int rc = setup_device(dev, &scratch);
     if (rc) return rc;
 
     mlxq::QmvPlan plan;
     if (!mlxq::qmv_plan(dtype, bits, group_size, static_cast<int>(M), static_cast<int>(N),
-                        static_cast<int>(K), 0, 0, g_num_sms[dev], g_max_smem[dev], &plan))
+                        static_cast<int>(K), 0, 0, g_setup[dev].num_sms, g_setup[dev].max_smem,
+                        &plan))
         return fail(MLXQ_ERR_SHAPE, "quantized_matmul_noalloc: no launch plan fits shared memory");
-    if (plan.ws_bytes > kScratchBytes)
+    // This entry point's scratch layout: the tickets (one per row block and token
+    // tile), rounded up to 256 bytes, then the fp32 partial sums of every K split.
+    const size_t counters = static_cast<size_t>(plan.ztotal) * plan.rowblocks * 4;
+    const size_t need = plan.splits > 1
+                            ? (counters + 255) / 256 * 256 +
+                                  static_cast<size_t>(plan.splits) * M * static_cast<size_t>(N) * 4
+                            : 0;
+    if (need > kScratchBytes)
         return fail(MLXQ_ERR_WORKSPACE,
                     "quantized_matmul_noalloc: this shape needs %lld bytes of scratch but the "
                     "built-in scratch holds %lld; use mlxq_quantized_matmul with a workspace",
-                    static_cast<long long>(plan.ws_bytes), static_cast<long long>(kScratchBytes));
+                    static_cast<long long>(need), static_cast<long long>(kScratchBytes));
 
     mlxq::QmvParams p{};
     p.x = x; p.w = w; p.s = scales; p.b = biases; p.bias = bias; p.out = out;
@@ -100,10 +130,9 @@ extern "C" int mlxq_quantized_matmul_noalloc(const void* x, const uint32_t* w, c
     p.batch = 0; p.num_experts = 1; p.x_batches = 1; p.w_estride = 0; p.sb_estride = 0;
     p.splits = plan.splits; p.gps = plan.gps; p.win = plan.win; p.ztotal = plan.ztotal;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (plan.ws_bytes > 0) {
+    if (need > 0) {
         // The tickets must start at zero: the array keeps whatever the last call left.
-        const size_t counters = static_cast<size_t>(plan.ztotal) * plan.rowblocks * 4;
-        char* base = static_cast<char*>(g_scratch_ptr[dev]);
+        char* base = static_cast<char*>(scratch);
         e = cudaMemsetAsync(base, 0, counters, st);
         if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(scratch tickets)");
         p.counter = reinterpret_cast<unsigned*>(base);

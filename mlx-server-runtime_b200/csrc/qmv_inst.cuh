@@ -11,17 +11,13 @@ template <typename T, int BITS, int GS, int NT, bool SBV, bool ODD>
 cudaError_t qmv_launch_t(const QmvPlan& plan, const QmvParams& p, cudaStream_t st) {
     auto kern = qmv_kernel<T, BITS, GS, NT, SBV, ODD>;
     constexpr QmvGeom geo = qmv_geom(BITS, GS, NT, SBV, qmv_two_sums<T, BITS>());
-    static int configured[64] = {0};
+    static PerDevice configured;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (configured[dev] < static_cast<int>(plan.smem)) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(plan.smem));
-        if (e != cudaSuccess) return e;
-        configured[dev] = static_cast<int>(plan.smem);
-    }
+    e = ensure_smem_attr(kern, configured, dev, static_cast<int>(plan.smem));
+    if (e != cudaSuccess) return e;
     dim3 grid(plan.rowblocks, plan.splits, plan.gridz);
     if (!plan.overlap) {
         kern<<<grid, geo.nwarp * 32, plan.smem, st>>>(p);

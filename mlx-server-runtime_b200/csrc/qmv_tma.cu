@@ -169,16 +169,18 @@ static cudaError_t qt_dispatch(int bits, int gs, int M, int epi, const CUtensorM
 
 // Device address of g_qmv_tma_error, looked up once per device (kernels in other
 // translation units reach the flag through this pointer).
-static int* error_flag() {
-    static int* addr[64] = {nullptr};
+int* qmv_tma_error_flag() {
+    static std::atomic<int*> addr[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-    if (!addr[dev]) {
-        void* a = nullptr;
-        if (cudaGetSymbolAddress(&a, g_qmv_tma_error) != cudaSuccess) return nullptr;
-        addr[dev] = static_cast<int*>(a);
+    int* a = addr[dev].load(std::memory_order_acquire);
+    if (!a) {
+        void* sym = nullptr;
+        if (cudaGetSymbolAddress(&sym, g_qmv_tma_error) != cudaSuccess) return nullptr;
+        a = static_cast<int*>(sym);
+        addr[dev].store(a, std::memory_order_release);  // the same value from every thread
     }
-    return addr[dev];
+    return a;
 }
 
 cudaError_t qmv_tma_launch(int dtype, int bits, int gs, const QtPlan& plan, const void* x,
@@ -197,7 +199,7 @@ cudaError_t qmv_tma_launch(int dtype, int bits, int gs, const QtPlan& plan, cons
                   CU_TENSOR_MAP_SWIZZLE_NONE))
         return cudaErrorInvalidValue;
     QtParams p{};
-    p.err = error_flag();
+    p.err = qmv_tma_error_flag();
     if (!p.err) return cudaErrorInvalidSymbol;
     p.x = x; p.bias = bias; p.out = out;
     p.M = M; p.N = N; p.K = K; p.G = G;
@@ -219,6 +221,27 @@ cudaError_t qmv_tma_launch(int dtype, int bits, int gs, const QtPlan& plan, cons
     if (dtype == kF16)
         return qt_dispatch<__half>(bits, gs, M, epi, tw, ts, tb, p, plan, overlap, st);
     return cudaErrorInvalidValue;
+}
+
+// One bounded mbarrier wait that nothing completes: thread 0 initialises a barrier
+// that expects one arrival, never arrives, and polls it `polls` times with the same
+// bounded wait the decode kernels use; when the wait gives up it records
+// kErrTimeout in the error word, exactly as a kernel whose copies never landed
+// would. No copy or tensor-core operation is in flight, so nothing is left pending.
+__global__ void bounded_wait_check_kernel(int* err, uint32_t polls) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x != 0) return;
+    const uint32_t b = smem_u32(&bar);
+    mbar_init(b, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    if (!mbar_wait_bounded(b, 0, polls)) atomicCAS(err, 0, qt::kErrTimeout);
+}
+
+cudaError_t launch_bounded_wait_check(uint32_t polls, cudaStream_t st) {
+    int* err = qmv_tma_error_flag();
+    if (!err) return cudaErrorInvalidSymbol;
+    bounded_wait_check_kernel<<<1, 32, 0, st>>>(err, polls);
+    return cudaGetLastError();
 }
 
 cudaError_t qmv_tma_read_error(int* code) {

@@ -10,17 +10,13 @@ template <typename T, int BITS, int GS, int TM, int BR, bool HEADS, int EPI>
 cudaError_t qt_launch_t(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tb,
                         const QtParams& p, int grid, size_t smem, bool overlap, cudaStream_t st) {
     auto kern = qmv_tma_kernel<T, BITS, GS, TM, BR, HEADS, EPI>;
-    static int configured[64] = {0};
+    static PerDevice configured;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (configured[dev] < static_cast<int>(smem)) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(smem));
-        if (e != cudaSuccess) return e;
-        configured[dev] = static_cast<int>(smem);
-    }
+    e = ensure_smem_attr(kern, configured, dev, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;

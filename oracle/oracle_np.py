@@ -28,12 +28,20 @@ def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
 
 
 def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
-    """Round-to-nearest-even float32 -> bfloat16 bit pattern."""
-    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    """Round-to-nearest-even float32 -> bfloat16 bit pattern (NaNs stay quiet NaNs).
+
+    In uint32: the rounding add cannot wrap for a non-NaN pattern (the largest,
+    -inf = 0xFF800000, plus 0x8000 stays below 2^32); NaN lanes are replaced."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    r = (u >> 16) & 1
+    r += 0x7FFF
+    r += u
+    r >>= 16
+    out = r.astype(np.uint16)
     nan = (u & 0x7FFFFFFF) > 0x7F800000
-    r = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
-    r = np.where(nan, (u >> 16) | 0x40, r)
-    return r.astype(np.uint16)
+    if nan.any():
+        out[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    return out
 
 
 def to_f32(a: np.ndarray, dtype: str) -> np.ndarray:

@@ -1,8 +1,14 @@
-"""GPU test of mlxq_quantized_matmul_noalloc, the entry point for callers that
-cannot allocate device memory (a host binding the C ABI without an allocator of
-its own, or a plugin whose engine owns all device memory). It runs the decode
-kernel's K-split path with the library's built-in 2 MiB scratch instead of a
-caller workspace; its results must match mlxq_quantized_matmul's.
+"""GPU tests of mlxq_quantized_matmul_noalloc, the entry point for callers that
+cannot allocate device memory: a host that binds the C ABI without a device
+allocator of its own, or a plugin inside a serving engine whose memory manager
+owns all device memory (and where a cudaMalloc in the middle of a decode step
+could synchronize the device). It runs the decode kernel's K-split path with the
+library's built-in 2 MiB scratch instead of a caller workspace.
+
+Each case calls the entry point twice in a row (the scratch keeps the last
+call's contents, so the second call checks that the tickets are cleared) and
+checks both results against the C oracle and against mlxq_quantized_matmul,
+within the path's tolerance max|d| <= 2e-2 * max|ref|.
 
 This file is collected last on purpose, so a stop-at-first-failure run has
 already run every other test before it."""
@@ -14,54 +20,67 @@ import torch
 
 import mlx_server_runtime_b200 as mxq
 from mlx_server_runtime_b200 import _lib
+from oracle import coracle
 
 from gpu_util import close, rand_weights, rand_x, to_dev, to_np
 
 pytestmark = pytest.mark.gpu
 
+_CODE = {"bfloat16": _lib.BF16, "float16": _lib.F16}
 
-def _noalloc(x, wq, s, b, bias=None, group_size=64, bits=4):
+
+def _noalloc(x, wq, s, b, bias, group_size, bits, dt):
     M, K = x.shape
     N = wq.shape[0]
     out = torch.empty(M, N, dtype=x.dtype, device=x.device)
     rc = _lib.load().mlxq_quantized_matmul_noalloc(
         x.data_ptr(), wq.data_ptr(), s.data_ptr(), b.data_ptr(),
         None if bias is None else bias.data_ptr(), out.data_ptr(), M, N, K, group_size, bits,
-        _lib.BF16, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        _CODE[dt], ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     return rc, out
 
 
-def _problem(seed, M, N, K, bits=4):
-    rng = np.random.default_rng(seed)
-    w = to_dev(rand_weights(rng, (N, K), "bfloat16"), "bfloat16")
-    wq, s, b = mxq.quantize(w, 64, bits)
-    x = to_dev(rand_x(rng, (M, K), "bfloat16"), "bfloat16")
-    return x, wq, s, b
+# (M, N, K, bits, group_size, dtype, bias): every shape splits K over CTAs (few
+# 128-row blocks or a long K), so every call uses the built-in scratch.
+CASES = [
+    (4, 512, 3584, 4, 64, "bfloat16", False),
+    (1, 3584, 18944, 8, 64, "bfloat16", True),
+    (2, 640, 2048, 4, 32, "float16", True),
+    (3, 512, 4096, 4, 128, "float16", False),
+    (8, 256, 8192, 8, 128, "bfloat16", True),
+    (17, 384, 3072, 8, 32, "float16", True),
+]
 
 
-def test_noalloc_matches_workspace_entry_point_twice():
-    # The no-alloc entry point runs the skinny kernel, whose plan splits K when the
-    # rows are few (N=512) or K is long (the down projection): it then needs its
-    # scratch (partial sums + tickets) for every call.
-    for call, (M, N, K, bits) in enumerate([(4, 512, 3584, 4), (4, 512, 3584, 4),
-                                            (1, 3584, 18944, 8)]):
-        x, wq, s, b = _problem(100 + call, M, N, K, bits)
-        ref = mxq.quantized_matmul(x, wq, s, b, group_size=64, bits=bits)
-        rc, got = _noalloc(x, wq, s, b, bits=bits)
+@pytest.mark.parametrize("M,N,K,bits,gs,dt,with_bias", CASES)
+def test_noalloc_matches_oracle_and_workspace_entry_point(M, N, K, bits, gs, dt, with_bias):
+    rng = np.random.default_rng(M * 1000 + N + K + bits + gs)
+    w = rand_weights(rng, (N, K), dt)
+    wq, s, b = coracle.quantize(w, dt, gs, bits)
+    x = rand_x(rng, (M, K), dt)
+    bias = rand_x(rng, (N,), dt) if with_bias else None
+    ref = coracle.quantized_matmul(x, wq, s, b, dt, gs, bits, bias=bias)
+    xd, wd, sd, bd = to_dev(x, dt), to_dev(wq), to_dev(s, dt), to_dev(b, dt)
+    biasd = to_dev(bias, dt) if with_bias else None
+    with_ws = to_np(mxq.quantized_matmul(xd, wd, sd, bd, group_size=gs, bits=bits, bias=biasd))
+    close(with_ws, ref, dt)
+    for _ in range(2):
+        rc, got = _noalloc(xd, wd, sd, bd, biasd, gs, bits, dt)
         assert rc == 0, _lib.last_error()
         torch.cuda.synchronize()
-        close(to_np(got), to_np(ref), "bfloat16")
-        rc2, again = _noalloc(x, wq, s, b, bits=bits)
-        assert rc2 == 0, _lib.last_error()
-        torch.cuda.synchronize()
-        close(to_np(again), to_np(ref), "bfloat16")
+        got = to_np(got)
+        close(got, ref, dt)
+        close(got, with_ws, dt)
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch():
-    # 32 tokens against a 3584x3584 projection split five ways needs ~2.3 MB > 2 MiB.
-    x, wq, s, b = _problem(7, 32, 3584, 3584)
-    need = _lib.load().mlxq_qmm_workspace_size(32, 3584, 3584, 64, 4, _lib.BF16)
-    assert need > 2 * 1024 * 1024
-    rc, _ = _noalloc(x, wq, s, b)
+    # 32 tokens against a 3584x3584 projection split five ways needs ~2.3 MB of
+    # partial sums, more than the 2 MiB the library holds.
+    rng = np.random.default_rng(7)
+    w = rand_weights(rng, (3584, 3584), "bfloat16")
+    wq, s, b = coracle.quantize(w, "bfloat16", 64, 4)
+    x = rand_x(rng, (32, 3584), "bfloat16")
+    rc, _ = _noalloc(to_dev(x, "bfloat16"), to_dev(wq), to_dev(s, "bfloat16"),
+                     to_dev(b, "bfloat16"), None, 64, 4, "bfloat16")
     assert rc == _lib.ERR_WORKSPACE
     assert "scratch" in _lib.last_error()
