@@ -433,6 +433,87 @@ def moe_sweep(torch, mxq, dev, stream, peak_gbs, peak_tf):
     return out
 
 
+def decoder_e2e(torch, mxq, dev, peak_gbs, batch=8, prompt=512, new_tokens=128):
+    """Config 4: the Qwen2.5-7B-architecture decoder (28 layers, hidden 3584, 28/4
+    heads of 128, SwiGLU 18944, vocab 152064, RoPE theta 1e6, RMSNorm eps 1e-6), random
+    init, every linear layer and the embedding quantized 4-bit g64, bf16 paged KV cache
+    of 16-token pages. 8 prompts of 512 uniform-random ids: one prefill, then greedy
+    decoding of 128 tokens per sequence (the first from the prefill, the second from
+    the decode graph's warm-up step, the other 126 from graph replays, timed)."""
+    from mlx_server_runtime_b200 import qwen2
+    from mlx_server_runtime_b200.attention import PagedKVCache
+    cfg = qwen2.Qwen2Config()
+    with mxq.launch_overlap(True):
+        model = qwen2.Qwen2ForCausalLM(cfg, device=dev, seed=0)
+        max_len = prompt + new_tokens
+        pages = batch * (-(-max_len // 16))
+        cache = PagedKVCache(cfg.num_hidden_layers, cfg.num_key_value_heads, cfg.head_dim,
+                             num_pages=pages, device=dev)
+        gen = torch.Generator().manual_seed(0)
+        prompts = torch.randint(0, cfg.vocab_size, (batch * prompt,), generator=gen,
+                                dtype=torch.int32).pin_memory()
+        lengths = [prompt] * batch
+        dec = qwen2.GreedyDecoder(model, cache, batch, max_len)
+        dec.prefill(prompts, lengths)       # warm-up (kernel attributes, workspaces)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        dec.prefill(prompts.to(dev, non_blocking=True), lengths)
+        e1.record()
+        torch.cuda.synchronize()
+        ttft_ms = e0.elapsed_time(e1)
+        dec.capture()
+        steps = new_tokens - 2
+        for _ in range(3):                  # warm replays (generate past the timed ones)
+            dec.replay()
+        torch.cuda.synchronize()
+        # device-resident: 126 decode steps back to back (positions rewound first)
+        dec.positions.sub_(3)
+        dec.kv_lens.sub_(3)
+        slots = cache.slots(dec.block_table, [[prompt + 1]] * batch)
+        dec.slots.copy_(slots)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(steps):
+            dec.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        step_ms = e0.elapsed_time(e1) / steps
+        # end to end through the public API: prompts from pinned host memory, prefill,
+        # every step's 8 token ids read back to the host (as a server streams them)
+        tokens_host = torch.empty(new_tokens, batch, dtype=torch.int32).pin_memory()
+        t0 = time.perf_counter()
+        first = dec.prefill(prompts.to(dev, non_blocking=True), lengths)
+        tokens_host[0].copy_(first)
+        for i in range(1, new_tokens):
+            dec.replay()
+            tokens_host[i].copy_(dec.ids, non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+        e2e_s = time.perf_counter() - t0
+        distinct = int(torch.unique(tokens_host).numel())
+        dec.close()
+    w_bytes = sum(qmm_bytes(batch, N, K) for _, N, K in shapes())  # projections + lm_head
+    del model, cache, dec
+    torch.cuda.empty_cache()
+    return {
+        "what": "Qwen2.5-7B-architecture decoder, random init, 4-bit g64 linears and "
+                "embedding, bf16 paged KV (16-token pages): 8 prompts x 512 random ids, "
+                "greedy 128 tokens each",
+        "e2e_decode_tok_s": round(batch * steps / (step_ms * steps * 1e-3), 1),
+        "decode_ms_per_step": round(step_ms, 4),
+        "decode_weight_GB/s": round(w_bytes / (step_ms * 1e-3) / 1e9, 1),
+        "decode_frac_of_hbm": round(w_bytes / (step_ms * 1e-3) / 1e9 / peak_gbs, 4),
+        "ttft_ms": round(ttft_ms, 2),
+        "prefill_tok_s": round(batch * prompt / (ttft_ms * 1e-3), 1),
+        "e2e_wall": {"seconds": round(e2e_s, 4),
+                     "tok_s": round(batch * new_tokens / e2e_s, 1),
+                     "what": "wall clock: prompts H2D from pinned memory, prefill, 127 graph "
+                             "replays each followed by a D2H read of the step's 8 token ids"},
+        "distinct_tokens": distinct,
+        "launches_per_decode_step": 4 + 8 * LAYERS,
+    }
+
+
 def expert_parallel_bench(torch, mxq, dist, dev, world, rank, stream):
     """Config 5 expert-parallel over the ranks: each rank routes its own T tokens,
     owns 128 / N experts, and exchanges rows with NCCL all-to-alls
@@ -687,6 +768,7 @@ def run(args):
                                  "frac_of_8TBs_nominal": round(c1["GB/s"] / 8000.0, 4)}
             extras["prefill"] = prefill_sweep(torch, mxq, dev, stream, peak_tf)
             extras["moe"] = moe_sweep(torch, mxq, dev, stream, peak, peak_tf)
+            extras["decoder"] = decoder_e2e(torch, mxq, dev, peak)
         else:
             extras["expert_parallel"] = expert_parallel_bench(torch, mxq, dist, dev, world,
                                                               rank, stream)
@@ -863,6 +945,32 @@ def run_moe_case(args):
                       "TFLOP/s": round(flops / (us * 1e-6) / 1e12, 2)}), flush=True)
 
 
+def run_only(args):
+    """One extra measurement by itself (for sweeps and profiling)."""
+    import torch
+    mxq = load_package()
+    mxq.load_library()
+    dev = torch.device("cuda", 0)
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    peak, peak_tf = float(peaks.get("hbm_gbs", 6650.0)), float(peaks.get("bf16_tflops", 1590.0))
+    stream = torch.cuda.Stream(device=dev)
+    with mxq.launch_overlap(not args.no_overlap):
+        if args.only == "decoder":
+            res = decoder_e2e(torch, mxq, dev, peak)
+        elif args.only == "prefill":
+            res = prefill_sweep(torch, mxq, dev, stream, peak_tf)
+        elif args.only == "moe":
+            res = moe_sweep(torch, mxq, dev, stream, peak, peak_tf)
+        else:
+            res = decode_sweep(torch, mxq, dev, stream, peak)
+    print(json.dumps({args.only: res}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", choices=sorted(CASES) + sorted(MOE_CASES), default=None,
@@ -877,11 +985,15 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--only", choices=["decoder", "prefill", "moe", "sweep"], default=None,
+                    help="run one of the extra measurements alone and print it")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the decode sweep, prefill, MoE and expert-parallel objects")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.only:
+        run_only(args)
     elif args.case in MOE_CASES:
         run_moe_case(args)
     elif args.case:

@@ -238,6 +238,100 @@ size_t mlxq_gather_qmm_workspace_size(int64_t batch, int64_t M, int64_t N, int64
                                       int64_t num_experts, int group_size, int bits, int dtype,
                                       int sorted_indices);
 
+
+/* ---------------------------------------------------------------------------------
+ * Decoder-layer operators around the projections (the row after the matmul on
+ * either side of it in every layer of the reference's Qwen2-style graphs). The
+ * same conventions hold; with launch overlap on they take part in it like the
+ * matmuls (they wait for the previous kernel before reading its outputs).
+ * dtype: MLXQ_BF16 or MLXQ_F16 for every activation, weight and cache buffer.
+ */
+
+/*
+ * RMSNorm: replaces nn.RMSNorm (models/qwen2.py:144-147,161-165, mx.fast.rms_norm).
+ * h = x, or with `residual` h = round(x + residual) (written to residual_out when
+ * not NULL: the decoder block's `hidden = x + attn_out`, qwen2.py:161-165);
+ * out = round(round(h * rsqrt(mean(h^2) + eps)) * weight) per row of `dim` (a
+ * multiple of 8, at most 8192).
+ */
+int mlxq_rms_norm(const void* x, const void* residual, const void* weight, void* out,
+                  void* residual_out, int64_t rows, int64_t dim, float eps, int dtype,
+                  void* stream);
+
+/*
+ * RoPE and the paged KV append: replaces the two mx.fast.rope calls of
+ * Qwen2Attention (qwen2.py:91-105, traditional=False) and the cache staging of
+ * PagedBatchReservation.stage_layer (cache.py:485-520). qkv [tokens, ld] holds each
+ * token's q (n_q_heads * head_dim), k and v (n_kv_heads * head_dim each), as the
+ * fused q/k/v projection writes them. Writes the rotated queries to q_out
+ * [tokens, n_q_heads, head_dim]; the rotated keys and the values to row slots[t]
+ * of k_cache / v_cache, pools of [pages * page_size, n_kv_heads, head_dim] (the
+ * reference's [pages, page_size, kv_heads, head_dim] layout); a negative slot
+ * skips the append. Angle of pair i at position p: p * rope_base^(-2i/head_dim).
+ */
+int mlxq_rope_kv_append(const void* qkv, int64_t ld, void* q_out, void* k_cache, void* v_cache,
+                        const int32_t* positions, const int32_t* slots, int64_t tokens,
+                        int n_q_heads, int n_kv_heads, int head_dim, float rope_base, int dtype,
+                        void* stream);
+
+/*
+ * Paged attention: replaces PagedLayerAttentionContext.append_and_attend's SDPA
+ * over the sequence's pages (attention.py:215-298, mask from _dense_causal_mask,
+ * attention.py:404-427): softmax(q k^T * scale + causal mask) v per query head,
+ * the kv head being q_head / (n_q_heads / n_kv_heads). block_table [batch,
+ * max_blocks] holds each sequence's page ids; kv_lens[b] = keys cached for
+ * sequence b, the new ones included. head_dim 64 or 128, page_size 8, 16 or 32.
+ *
+ * decode: one query per sequence, q [batch, n_q_heads, head_dim] at position
+ * kv_lens[b] - 1, attending every cached key; max_kv_len bounds kv_lens and sizes
+ * the launch. The workspace (mlxq_paged_attention_workspace_size bytes, 256-byte
+ * aligned, zero-filled once; the kernel leaves it zeroed) holds the partial results
+ * of sequences longer than 128 keys; calls that overlap on the GPU must not share it.
+ */
+size_t mlxq_paged_attention_workspace_size(int64_t batch, int n_kv_heads, int64_t max_kv_len,
+                                           int head_dim);
+int mlxq_paged_attention_decode(const void* q, const void* k_cache, const void* v_cache,
+                                const int32_t* block_table, int64_t max_blocks,
+                                const int32_t* kv_lens, int64_t max_kv_len, void* out,
+                                int64_t batch, int n_q_heads, int n_kv_heads, int head_dim,
+                                int page_size, float scale, int dtype, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
+/*
+ * prefill: the new tokens of every sequence, q [total, n_q_heads, head_dim] with
+ * sequence b's queries at rows [cu_q[b], cu_q[b+1]) (cu_q [batch + 1], at most
+ * max_q_len per sequence); query i of sequence b sits at position
+ * kv_lens[b] - (cu_q[b+1] - cu_q[b]) + i and attends the keys at or before it
+ * (chunked prefill over an existing cache included). out like q.
+ */
+int mlxq_paged_attention_prefill(const void* q, const int32_t* cu_q, int64_t max_q_len,
+                                 const void* k_cache, const void* v_cache,
+                                 const int32_t* block_table, int64_t max_blocks,
+                                 const int32_t* kv_lens, void* out, int64_t batch, int n_q_heads,
+                                 int n_kv_heads, int head_dim, int page_size, float scale,
+                                 int dtype, void* stream);
+
+/*
+ * Quantized embedding lookup: replaces QuantizedEmbedding.__call__ (embed_tokens,
+ * qwen2.py:185, once nn.quantize has converted the table): out [n, dim] row i =
+ * dequantize(row ids[i] of wq / scales / biases), bit-identical to mlxq_dequantize
+ * of that row; ids outside [0, vocab) give zero rows.
+ */
+int mlxq_quantized_embedding(const int32_t* ids, int64_t n, const uint32_t* wq,
+                             const void* scales, const void* biases, void* out, int64_t vocab,
+                             int64_t dim, int group_size, int bits, int dtype, void* stream);
+
+/*
+ * Decode-loop bookkeeping on the device, so a captured decode step replays with no
+ * host work: for each sequence, positions[b] += 1, kv_lens[b] = positions[b] + 1,
+ * slots[b] = that position's cache row from block_table (-1 past its end). The
+ * reference's executor gathers the cache lengths on the host before every step
+ * (executor.py:272-293).
+ */
+int mlxq_decode_advance(int32_t* positions, int32_t* kv_lens, int32_t* slots,
+                        const int32_t* block_table, int64_t max_blocks, int64_t batch,
+                        int page_size, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -39,6 +39,13 @@ EXPORTED = (
     "mlxq_argmax_workspace_size",
     "mlxq_quantized_matmul_argmax",
     "mlxq_check_bounded_wait",
+    "mlxq_rms_norm",
+    "mlxq_rope_kv_append",
+    "mlxq_paged_attention_workspace_size",
+    "mlxq_paged_attention_decode",
+    "mlxq_paged_attention_prefill",
+    "mlxq_quantized_embedding",
+    "mlxq_decode_advance",
 )
 
 _lock = threading.Lock()
@@ -100,6 +107,25 @@ def load(path: str | None = None):
         L.mlxq_quantized_matmul_argmax.restype = i32
         L.mlxq_check_bounded_wait.argtypes = [ctypes.c_uint32, vp]
         L.mlxq_check_bounded_wait.restype = i32
+        f32 = ctypes.c_float
+        L.mlxq_rms_norm.argtypes = [vp, vp, vp, vp, vp, i64, i64, f32, i32, vp]
+        L.mlxq_rms_norm.restype = i32
+        L.mlxq_rope_kv_append.argtypes = [vp, i64, vp, vp, vp, vp, vp, i64, i32, i32, i32, f32,
+                                          i32, vp]
+        L.mlxq_rope_kv_append.restype = i32
+        L.mlxq_paged_attention_workspace_size.argtypes = [i64, i32, i64, i32]
+        L.mlxq_paged_attention_workspace_size.restype = sz
+        L.mlxq_paged_attention_decode.argtypes = [vp, vp, vp, vp, i64, vp, i64, vp, i64, i32, i32,
+                                                  i32, i32, f32, i32, vp, sz, vp]
+        L.mlxq_paged_attention_decode.restype = i32
+        L.mlxq_paged_attention_prefill.argtypes = [vp, vp, i64, vp, vp, vp, i64, vp, vp, i64, i32,
+                                                   i32, i32, i32, f32, i32, vp]
+        L.mlxq_paged_attention_prefill.restype = i32
+        L.mlxq_quantized_embedding.argtypes = [vp, i64, vp, vp, vp, vp, i64, i64, i32, i32, i32,
+                                               vp]
+        L.mlxq_quantized_embedding.restype = i32
+        L.mlxq_decode_advance.argtypes = [vp, vp, vp, vp, i64, i64, i32, vp]
+        L.mlxq_decode_advance.restype = i32
         v = L.mlxq_abi_version()
         if v != ABI_VERSION:
             raise LibraryError(f"{p} has ABI version {v}, expected {ABI_VERSION}; rebuild it")

@@ -345,15 +345,16 @@ def quantized_matmul_swiglu(x: torch.Tensor, w: torch.Tensor, scales: torch.Tens
 
 def quantized_matmul_argmax(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
                             biases: torch.Tensor, group_size: int = 64, bits: int = 4,
-                            mode: str = "affine", bias: torch.Tensor | None = None
-                            ) -> torch.Tensor:
+                            mode: str = "affine", bias: torch.Tensor | None = None,
+                            out: torch.Tensor | None = None) -> torch.Tensor:
     """Greedy next tokens: argmax over N of quantized_matmul(x, w, ...) (+ bias),
     int32 [...], the first index on ties, without writing the logits.
 
     Decode shapes (up to 8 rows, K/group_size a multiple of 8) run as one launch
     with the argmax in the matmul's epilogue; other shapes compute the logits and
     take torch.argmax. The logits compared are the ones quantized_matmul returns
-    (rounded to x's dtype), so both forms pick the same token.
+    (rounded to x's dtype), so both forms pick the same token. `out` (int32, the
+    leading shape of x) receives the ids when given.
     """
     _mode(mode)
     dev = _cuda(x, w, scales, biases, bias)
@@ -370,11 +371,18 @@ def quantized_matmul_argmax(x: torch.Tensor, w: torch.Tensor, scales: torch.Tens
     x2 = x.contiguous()
     M = x2.numel() // K
     L = _lib.load()
+    if out is not None and (out.dtype != torch.int32 or out.shape != lead or
+                            not out.is_contiguous()):
+        raise ValueError(f"out must be a contiguous int32 tensor of shape {tuple(lead)}")
     need = L.mlxq_argmax_workspace_size(M, N, K, group_size, bits, dt) if M else 0
     if need == 0:
         y = quantized_matmul(x, w, scales, biases, True, group_size, bits, mode, bias=bias)
-        return y.argmax(dim=-1).to(torch.int32)
-    ids = torch.empty(*lead, dtype=torch.int32, device=dev)
+        ids = y.argmax(dim=-1).to(torch.int32)
+        if out is not None:
+            out.copy_(ids)
+            return out
+        return ids
+    ids = out if out is not None else torch.empty(*lead, dtype=torch.int32, device=dev)
     w, scales, biases = w.contiguous(), scales.contiguous(), biases.contiguous()
     with torch.cuda.device(dev):
         st = torch.cuda.current_stream(dev)

@@ -1,0 +1,749 @@
+// The decoder-layer operators around the quantized projections (sm_100a):
+// RMSNorm with a fused residual add, RoPE with the paged KV-cache append,
+// attention over the paged cache (decode and prefill forms), the quantized
+// embedding lookup, and the position advance of a decode loop.
+//
+// Reference (huydt84/mlx-server-runtime, python/mlx_worker/native_mlx/):
+//   RMSNorm           models/qwen2.py:144-147,161-165 (nn.RMSNorm, eps 1e-6)
+//   RoPE              models/qwen2.py:91-105 (mx.fast.rope, traditional=False, base 1e6)
+//   KV append         cache.py:485-520 (PagedBatchReservation.stage_layer: new keys and
+//                     values written to their slots of the [pages, page_size, kv_heads,
+//                     head_dim] pools)
+//   attention         attention.py:215-298 (append_and_attend: SDPA over the sequence's
+//                     pages with a causal mask offset by the cached length)
+//   embedding         models/qwen2.py:185 (embed_tokens(inputs), a QuantizedEmbedding
+//                     once nn.quantize has run)
+//
+// Every kernel here takes part in launch overlap the way the matmuls do: it lets
+// the next kernel on the stream start at once (griddepcontrol.launch_dependents)
+// and waits for the previous one (griddepcontrol.wait) before it reads anything
+// that kernel may have written. Launched without the overlap attribute, both
+// instructions are no-ops.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "decoder_ops.h"
+#include "sm100.cuh"
+
+namespace mlxq {
+
+namespace {
+
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t u) {
+    return make_float2(Elem<T>::lo(u), Elem<T>::hi(u));
+}
+
+template <typename T>
+__device__ __forceinline__ uint16_t bits16(T v) {
+    return *reinterpret_cast<const uint16_t*>(&v);
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    return static_cast<uint32_t>(bits16(Elem<T>::from_f(a))) |
+           (static_cast<uint32_t>(bits16(Elem<T>::from_f(b))) << 16);
+}
+
+template <typename T>
+__device__ __forceinline__ float round_t(float v) {
+    return Elem<T>::to_f(Elem<T>::from_f(v));
+}
+
+cudaError_t launch_ex(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                      bool overlap, void** args) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = overlap ? attr : nullptr;
+    cfg.numAttrs = overlap ? 1 : 0;
+    return cudaLaunchKernelExC(&cfg, func, args);
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------
+// RMSNorm: h = x (+ delta, rounded to T, written to sum_out); y = rms_norm(h) * w.
+// One CTA per row; thread i owns elements [8i, 8i + 8). The normalized value is
+// rounded to T before the weight product, which is rounded again (one rounding
+// per operation in the activation type).
+template <typename T>
+__global__ void rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ delta,
+                                const T* __restrict__ w, T* __restrict__ y,
+                                T* __restrict__ sum_out, int D, float eps) {
+    __shared__ float red[32];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int row = blockIdx.x;
+    const int i = threadIdx.x;
+    const bool on = 8 * i < D;
+    float h[8];
+    float ss = 0.f;
+    if (on) {
+        const uint4 xv = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * D + 8 * i);
+        const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+        if (delta) {
+            const uint4 dv =
+                *reinterpret_cast<const uint4*>(delta + static_cast<size_t>(row) * D + 8 * i);
+            const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 a = unpack2<T>(xw[k]), b = unpack2<T>(dw[k]);
+                h[2 * k] = round_t<T>(a.x + b.x);
+                h[2 * k + 1] = round_t<T>(a.y + b.y);
+            }
+            if (sum_out) {
+                uint4 o;
+                o.x = pack2<T>(h[0], h[1]);
+                o.y = pack2<T>(h[2], h[3]);
+                o.z = pack2<T>(h[4], h[5]);
+                o.w = pack2<T>(h[6], h[7]);
+                *reinterpret_cast<uint4*>(sum_out + static_cast<size_t>(row) * D + 8 * i) = o;
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 a = unpack2<T>(xw[k]);
+                h[2 * k] = a.x;
+                h[2 * k + 1] = a.y;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ss = fmaf(h[k], h[k], ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const int warps = (blockDim.x + 31) >> 5;
+    if ((i & 31) == 0) red[i >> 5] = ss;
+    __syncthreads();
+    if (i < 32) {
+        float v = i < warps ? red[i] : 0.f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (i == 0) red[0] = v;
+    }
+    __syncthreads();
+    const float r = rsqrtf(red[0] / static_cast<float>(D) + eps);
+    if (on) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(w + 8 * i);
+        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 g = unpack2<T>(ww[k]);
+            o[k] = pack2<T>(round_t<T>(h[2 * k] * r) * g.x, round_t<T>(h[2 * k + 1] * r) * g.y);
+        }
+        *reinterpret_cast<uint4*>(y + static_cast<size_t>(row) * D + 8 * i) =
+            make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+cudaError_t launch_rms_norm(int dtype, const void* x, const void* delta, const void* w, void* y,
+                            void* sum_out, int rows, int D, float eps, bool overlap,
+                            cudaStream_t st) {
+    const int threads = ((D / 8) + 31) / 32 * 32;
+    void* args[] = {&x, &delta, &w, &y, &sum_out, &D, &eps};
+    const void* f = dtype == kBF16
+                        ? reinterpret_cast<const void*>(&rms_norm_kernel<__nv_bfloat16>)
+                        : reinterpret_cast<const void*>(&rms_norm_kernel<__half>);
+    return launch_ex(f, dim3(rows), dim3(threads), 0, st, overlap, args);
+}
+
+// ------------------------------------------------------------------------------------
+// RoPE (half-rotation form, traditional=False) of the queries and keys of one token
+// per CTA, queries to q_out [T, Hq, hd], keys and values to their cache slot
+// (slot = page * page_size + offset; a negative slot skips the append).
+//   freq_i = base^(-2i/hd), angle = position * freq_i, for i < hd/2:
+//   (a, b) = (x_i, x_{i+hd/2}) -> (a cos - b sin, a sin + b cos), rounded to T.
+template <typename T>
+__global__ void rope_append_kernel(const T* __restrict__ qkv, int ld, T* __restrict__ q_out,
+                                   T* __restrict__ k_cache, T* __restrict__ v_cache,
+                                   const int32_t* __restrict__ positions,
+                                   const int32_t* __restrict__ slots, int Hq, int Hkv, int hd,
+                                   float log2_base) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int t = blockIdx.x;
+    const T* src = qkv + static_cast<size_t>(t) * ld;
+    const float pos = static_cast<float>(positions[t]);
+    const int slot = slots[t];
+    const int half = hd / 2;
+    const int pairs = (Hq + Hkv) * half;
+    for (int p = threadIdx.x; p < pairs; p += blockDim.x) {
+        const int h = p / half, i = p % half;
+        const float freq = exp2f(-(2.0f * static_cast<float>(i) / static_cast<float>(hd)) *
+                                 log2_base);
+        float sn, cs;
+        sincosf(pos * freq, &sn, &cs);
+        const float a = Elem<T>::to_f(src[h * hd + i]);
+        const float b = Elem<T>::to_f(src[h * hd + i + half]);
+        const T ra = Elem<T>::from_f(a * cs - b * sn);
+        const T rb = Elem<T>::from_f(a * sn + b * cs);
+        if (h < Hq) {
+            T* dq = q_out + (static_cast<size_t>(t) * Hq + h) * hd;
+            dq[i] = ra;
+            dq[i + half] = rb;
+        } else if (slot >= 0) {
+            T* dk = k_cache + (static_cast<size_t>(slot) * Hkv + (h - Hq)) * hd;
+            dk[i] = ra;
+            dk[i + half] = rb;
+        }
+    }
+    if (slot >= 0) {
+        const int vchunks = Hkv * hd / 8;
+        const uint4* vs = reinterpret_cast<const uint4*>(src + (Hq + Hkv) * hd);
+        uint4* vd = reinterpret_cast<uint4*>(v_cache + static_cast<size_t>(slot) * Hkv * hd);
+        for (int c = threadIdx.x; c < vchunks; c += blockDim.x) vd[c] = vs[c];
+    }
+}
+
+cudaError_t launch_rope_append(int dtype, const void* qkv, int ld, void* q_out, void* k_cache,
+                               void* v_cache, const int32_t* positions, const int32_t* slots,
+                               int tokens, int Hq, int Hkv, int hd, float log2_base, bool overlap,
+                               cudaStream_t st) {
+    void* args[] = {&qkv, &ld, &q_out, &k_cache, &v_cache, &positions, &slots,
+                    &Hq, &Hkv, &hd, &log2_base};
+    const void* f = dtype == kBF16
+                        ? reinterpret_cast<const void*>(&rope_append_kernel<__nv_bfloat16>)
+                        : reinterpret_cast<const void*>(&rope_append_kernel<__half>);
+    return launch_ex(f, dim3(tokens), dim3(256), 0, st, overlap, args);
+}
+
+// ------------------------------------------------------------------------------------
+// Decode attention: one query token per sequence. CTA (split s, kv head g, sequence
+// b) takes keys [s*SK, min((s+1)*SK, L_b)) of the sequence's L_b cached keys and the
+// G = Hq/Hkv query heads that share kv head g:
+//   scores  thread j = key j: G dot products of its key row with the prescaled queries
+//   softmax per head over the split's keys (max, exp2, sum)
+//   values  thread d = dimension d: sum over keys of p * v
+// A sequence with one split writes its outputs; otherwise each split stores its
+// (max, sum, unnormalised output) and the last split to finish (acquire-release
+// ticket per (b, g), zero between calls) merges them in split order.
+namespace attn {
+constexpr int SK = 128;       // keys per split (one per thread)
+constexpr int THREADS = 128;
+constexpr int MAXG = 8;       // query heads per kv head
+}  // namespace attn
+
+template <typename T, int HD>
+__global__ void __launch_bounds__(attn::THREADS)
+    attn_decode_kernel(const T* __restrict__ q, const T* __restrict__ k_cache,
+                       const T* __restrict__ v_cache, const int32_t* __restrict__ block_table,
+                       int max_blocks, const int32_t* __restrict__ kv_lens, T* __restrict__ out,
+                       int Hq, int Hkv, int page, float scale_log2, float* __restrict__ ws_o,
+                       float2* __restrict__ ws_ml, unsigned* __restrict__ tickets,
+                       int max_splits, int max_kv) {
+    using namespace attn;
+    static_assert(HD == 64 || HD == 128, "head_dim");
+    __shared__ __align__(16) float qs[MAXG][HD];
+    __shared__ float ps[MAXG][SK];
+    __shared__ float mls[2][MAXG];
+    __shared__ int s_last;
+    pdl_launch_dependents();
+    pdl_wait();
+    const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+    const int G = Hq / Hkv;
+    const int L = min(kv_lens[b], max_kv);  // max_kv <= the block table's reach
+    const int nsplit = (L + SK - 1) / SK;
+    if (split >= nsplit) return;
+    const int k0 = split * SK;
+    const int n = min(SK, L - k0);
+    const int tid = threadIdx.x;
+
+    for (int e = tid; e < G * HD; e += THREADS) {
+        const int h = e / HD, d = e % HD;
+        qs[h][d] = Elem<T>::to_f(q[(static_cast<size_t>(b) * Hq + g * G + h) * HD + d]) *
+                   scale_log2;
+    }
+    __syncthreads();
+    const int32_t* bt = block_table + static_cast<size_t>(b) * max_blocks;
+    // scores: thread tid takes key k0 + tid
+    if (tid < n) {
+        const int key = k0 + tid;
+        const size_t row = static_cast<size_t>(bt[key / page]) * page + key % page;
+        const uint4* kr = reinterpret_cast<const uint4*>(k_cache + (row * Hkv + g) * HD);
+        float acc[MAXG];
+#pragma unroll
+        for (int h = 0; h < MAXG; ++h) acc[h] = 0.f;
+#pragma unroll 4
+        for (int c = 0; c < HD / 8; ++c) {
+            const uint4 kv = kr[c];
+            const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
+            float kf[8];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 f = unpack2<T>(kw[j]);
+                kf[2 * j] = f.x;
+                kf[2 * j + 1] = f.y;
+            }
+#pragma unroll
+            for (int h = 0; h < MAXG; ++h) {
+                if (h < G) {
+                    const float4 qa = *reinterpret_cast<const float4*>(&qs[h][8 * c]);
+                    const float4 qb = *reinterpret_cast<const float4*>(&qs[h][8 * c + 4]);
+                    acc[h] = fmaf(qa.x, kf[0], acc[h]);
+                    acc[h] = fmaf(qa.y, kf[1], acc[h]);
+                    acc[h] = fmaf(qa.z, kf[2], acc[h]);
+                    acc[h] = fmaf(qa.w, kf[3], acc[h]);
+                    acc[h] = fmaf(qb.x, kf[4], acc[h]);
+                    acc[h] = fmaf(qb.y, kf[5], acc[h]);
+                    acc[h] = fmaf(qb.z, kf[6], acc[h]);
+                    acc[h] = fmaf(qb.w, kf[7], acc[h]);
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < MAXG; ++h)
+            if (h < G) ps[h][tid] = acc[h];
+    }
+    __syncthreads();
+    // softmax over this split's keys, one warp per head (in base 2: scores carry log2 e)
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int h = warp; h < G; h += THREADS / 32) {
+        float m = -INFINITY;
+        for (int j = lane; j < n; j += 32) m = fmaxf(m, ps[h][j]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float l = 0.f;
+        for (int j = lane; j < n; j += 32) {
+            const float p = exp2f(ps[h][j] - m);
+            ps[h][j] = p;
+            l += p;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) {
+            mls[0][h] = m;
+            mls[1][h] = l;
+        }
+    }
+    __syncthreads();
+    // values: thread d takes dimension d (two key halves for 64-dim heads)
+    constexpr int KP = THREADS / HD;  // key phases
+    const int d = tid % HD, ph = tid / HD;
+    float o[MAXG];
+#pragma unroll
+    for (int h = 0; h < MAXG; ++h) o[h] = 0.f;
+    for (int j = ph; j < n; j += KP) {
+        const int key = k0 + j;
+        const size_t row = static_cast<size_t>(bt[key / page]) * page + key % page;
+        const float v = Elem<T>::to_f(v_cache[(row * Hkv + g) * HD + d]);
+#pragma unroll
+        for (int h = 0; h < MAXG; ++h)
+            if (h < G) o[h] = fmaf(ps[h][j], v, o[h]);
+    }
+    if (KP > 1) {
+        __syncthreads();  // ps is reused as the exchange buffer of the two halves
+        float* xch = &ps[0][0];
+        if (ph == 1)
+            for (int h = 0; h < G; ++h) xch[h * HD + d] = o[h];
+        __syncthreads();
+        if (ph == 0)
+            for (int h = 0; h < G; ++h) o[h] += xch[h * HD + d];
+    }
+    if (nsplit == 1) {
+        if (ph == 0)
+            for (int h = 0; h < G; ++h)
+                out[(static_cast<size_t>(b) * Hq + g * G + h) * HD + d] =
+                    Elem<T>::from_f(o[h] / mls[1][h]);
+        return;
+    }
+    // this split's partials: [b][g][split][h][HD] and (m, l) per head
+    const size_t base = (static_cast<size_t>(b) * Hkv + g) * max_splits;
+    if (ph == 0)
+        for (int h = 0; h < G; ++h) ws_o[((base + split) * MAXG + h) * HD + d] = o[h];
+    if (tid < G) ws_ml[(base + split) * MAXG + tid] = make_float2(mls[0][tid], mls[1][tid]);
+    // The barrier orders every thread's partials before thread 0's acq_rel ticket,
+    // whose release publishes them GPU-wide and whose acquire (with the second
+    // barrier) makes the other splits' partials visible to this CTA.
+    __syncthreads();
+    if (tid == 0)
+        s_last = atom_add_acq_rel_gpu(tickets + b * Hkv + g, 1u) ==
+                 static_cast<unsigned>(nsplit - 1);
+    __syncthreads();
+    if (!s_last) return;
+    if (ph == 0) {
+        for (int h = 0; h < G; ++h) {
+            float M = -INFINITY;
+            for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(&ws_ml[(base + s) * MAXG + h]).x);
+            float num = 0.f, den = 0.f;
+            for (int s = 0; s < nsplit; ++s) {
+                const float2 ml = __ldcg(&ws_ml[(base + s) * MAXG + h]);
+                const float c = exp2f(ml.x - M);
+                num = fmaf(c, __ldcg(&ws_o[((base + s) * MAXG + h) * HD + d]), num);
+                den = fmaf(c, ml.y, den);
+            }
+            out[(static_cast<size_t>(b) * Hq + g * G + h) * HD + d] = Elem<T>::from_f(num / den);
+        }
+    }
+    if (tid == 0) tickets[b * Hkv + g] = 0u;
+}
+
+// ------------------------------------------------------------------------------------
+// Prefill attention (flash-attention form on mma.sync m16n8k16, fp32 accumulation):
+// CTA (query tile of 64 tokens, query head h, sequence b), 4 warps of 16 query rows.
+// Query i of sequence b sits at position L_b - Lq_b + i and attends keys at positions
+// <= its own (keys < L_b). Key and value tiles of 64 keys come from the pages through
+// a two-stage cp.async ring, XOR-swizzled by 16-byte chunk so ldmatrix reads are
+// conflict free; probabilities stay in registers as the A operand of P V.
+namespace pf {
+constexpr int QT = 64;   // queries per CTA
+constexpr int KT = 64;   // keys per tile
+constexpr int THREADS = 128;
+}  // namespace pf
+
+template <int HD>
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+    return static_cast<uint32_t>(row * (HD * 2) + ((chunk ^ (row & 7)) << 4));
+}
+
+template <typename T, int HD>
+__global__ void __launch_bounds__(pf::THREADS)
+    attn_prefill_kernel(const T* __restrict__ q, const int32_t* __restrict__ cu_q,
+                        const T* __restrict__ k_cache, const T* __restrict__ v_cache,
+                        const int32_t* __restrict__ block_table, int max_blocks,
+                        const int32_t* __restrict__ kv_lens, T* __restrict__ out, int Hq,
+                        int Hkv, int page, float scale_log2) {
+    using namespace pf;
+    static_assert(HD == 64 || HD == 128, "head_dim");
+    constexpr int CH = HD / 8;  // 16-byte chunks per row
+    extern __shared__ __align__(128) uint8_t pf_smem[];
+    uint8_t* qsm = pf_smem;                      // [QT][HD]
+    uint8_t* ksm = qsm + QT * HD * 2;            // [2][KT][HD]
+    uint8_t* vsm = ksm + 2 * KT * HD * 2;        // [2][KT][HD]
+    pdl_launch_dependents();
+    pdl_wait();
+    const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int q0 = cu_q[b], Lq = cu_q[b + 1] - q0;
+    if (qt * QT >= Lq) return;
+    const int L = min(kv_lens[b], max_blocks * page);
+    const int g = h / (Hq / Hkv);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int pos0 = L - Lq;  // position of query 0
+    const int qlo = qt * QT, qhi = min(Lq, qlo + QT);
+    const int kend = min(L, pos0 + qhi);  // keys [0, kend) are visible to some row
+    const int ntiles = (kend + KT - 1) / KT;
+    const int32_t* bt = block_table + static_cast<size_t>(b) * max_blocks;
+
+    // queries (rows past Lq are zero)
+    for (int c = tid; c < QT * CH; c += THREADS) {
+        const int r = c / CH, ch = c % CH;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (qlo + r < Lq)
+            v = *reinterpret_cast<const uint4*>(
+                q + (static_cast<size_t>(q0 + qlo + r) * Hq + h) * HD + ch * 8);
+        *reinterpret_cast<uint4*>(qsm + swz<HD>(r, ch)) = v;
+    }
+    auto load_tile = [&](int tile, int stage) {
+        uint8_t* kd = ksm + stage * KT * HD * 2;
+        uint8_t* vd = vsm + stage * KT * HD * 2;
+        for (int c = tid; c < KT * CH; c += THREADS) {
+            const int r = c / CH, ch = c % CH;
+            const int key = tile * KT + r;
+            const bool ok = key < kend;
+            const int kk = ok ? key : 0;
+            const size_t row = static_cast<size_t>(bt[kk / page]) * page + kk % page;
+            const size_t off = (row * Hkv + g) * HD + ch * 8;
+            cp_async16(kd + swz<HD>(r, ch), k_cache + off, ok ? 16 : 0);
+            cp_async16(vd + swz<HD>(r, ch), v_cache + off, ok ? 16 : 0);
+        }
+        cp_async_commit();
+    };
+    if (ntiles > 0) load_tile(0, 0);
+    __syncthreads();
+
+    // this warp's 16 query rows as A fragments (k = head dims)
+    uint32_t qa[HD / 16][4];
+    {
+        const uint32_t qb = smem_u32(qsm);
+        const int r = warp * 16 + (lane & 15);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+            const int ch = 2 * kk + (lane >> 4);
+            ldmatrix_x4(qb + swz<HD>(r, ch), qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
+        }
+    }
+    float o[HD / 8][4];
+#pragma unroll
+    for (int j = 0; j < HD / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+    // positions of the two rows this lane holds (rows r and r + 8 of the warp's tile)
+    const int qpos[2] = {pos0 + qlo + warp * 16 + (lane >> 2),
+                         pos0 + qlo + warp * 16 + (lane >> 2) + 8};
+
+    for (int tile = 0; tile < ntiles; ++tile) {
+        const int stage = tile & 1;
+        if (tile + 1 < ntiles) {
+            load_tile(tile + 1, stage ^ 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const uint32_t kb = smem_u32(ksm + stage * KT * HD * 2);
+        const uint32_t vb = smem_u32(vsm + stage * KT * HD * 2);
+        // S = Q K^T for 64 keys: 8 n-tiles of 8 keys
+        float s[KT / 8][4];
+#pragma unroll
+        for (int nt = 0; nt < KT / 8; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+#pragma unroll
+            for (int np = 0; np < KT / 16; ++np) {
+                // keys 16np..16np+15, dims 16kk..16kk+15: x4 gives two n-tiles' B
+                const int r = np * 16 + (lane & 7) + ((lane >> 4) << 3);
+                const int ch = 2 * kk + ((lane >> 3) & 1);
+                uint32_t b0, b1, b2, b3;
+                ldmatrix_x4(kb + swz<HD>(r, ch), b0, b1, b2, b3);
+                mma16816<T>(s[2 * np], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b0, b1);
+                mma16816<T>(s[2 * np + 1], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b2, b3);
+            }
+        }
+        // mask, scale (base 2), online softmax
+        float mnew[2] = {mrow[0], mrow[1]};
+#pragma unroll
+        for (int nt = 0; nt < KT / 8; ++nt) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int key = tile * KT + nt * 8 + 2 * (lane & 3) + (e & 1);
+                const int rr = e >> 1;
+                const bool ok = key < kend && key <= qpos[rr];
+                s[nt][e] = ok ? s[nt][e] * scale_log2 : -INFINITY;
+                mnew[rr] = fmaxf(mnew[rr], s[nt][e]);
+            }
+        }
+        float corr[2];
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+            mnew[rr] = fmaxf(mnew[rr], __shfl_xor_sync(0xffffffffu, mnew[rr], 1));
+            mnew[rr] = fmaxf(mnew[rr], __shfl_xor_sync(0xffffffffu, mnew[rr], 2));
+            const float mref = mnew[rr] == -INFINITY ? 0.f : mnew[rr];
+            corr[rr] = exp2f(mrow[rr] - mref);
+            mrow[rr] = mnew[rr];
+            lrow[rr] *= corr[rr];
+        }
+        uint32_t pa[KT / 16][4];
+#pragma unroll
+        for (int nt = 0; nt < KT / 8; ++nt) {
+            float p[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int rr = e >> 1;
+                const float mref = mrow[rr] == -INFINITY ? 0.f : mrow[rr];
+                p[e] = exp2f(s[nt][e] - mref);
+                lrow[rr] += p[e];
+            }
+            // C fragment of n-tile nt = half of the A fragment of k-step nt/2
+            pa[nt >> 1][(nt & 1) * 2 + 0] = pack2<T>(p[0], p[1]);
+            pa[nt >> 1][(nt & 1) * 2 + 1] = pack2<T>(p[2], p[3]);
+        }
+#pragma unroll
+        for (int j = 0; j < HD / 8; ++j) {
+            o[j][0] *= corr[0];
+            o[j][1] *= corr[0];
+            o[j][2] *= corr[1];
+            o[j][3] *= corr[1];
+        }
+        // O += P V: k = keys, n = head dims; V rows are [key][dim], read transposed
+#pragma unroll
+        for (int kk = 0; kk < KT / 16; ++kk) {
+#pragma unroll
+            for (int dp = 0; dp < HD / 16; ++dp) {
+                const int r = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+                const int ch = 2 * dp + (lane >> 4);
+                uint32_t b0, b1, b2, b3;
+                ldmatrix_x4_trans(vb + swz<HD>(r, ch), b0, b1, b2, b3);
+                mma16816<T>(o[2 * dp], pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3], b0, b1);
+                mma16816<T>(o[2 * dp + 1], pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3], b2, b3);
+            }
+        }
+        __syncthreads();  // the stage is refilled next iteration
+    }
+    // normalise and store rows r, r + 8
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+        float l = lrow[rr];
+        l += __shfl_xor_sync(0xffffffffu, l, 1);
+        l += __shfl_xor_sync(0xffffffffu, l, 2);
+        const int qi = qlo + warp * 16 + (lane >> 2) + 8 * rr;
+        if (qi >= Lq) continue;
+        const float inv = l > 0.f ? 1.0f / l : 0.f;
+        T* dst = out + (static_cast<size_t>(q0 + qi) * Hq + h) * HD;
+#pragma unroll
+        for (int j = 0; j < HD / 8; ++j) {
+            const int d = j * 8 + 2 * (lane & 3);
+            *reinterpret_cast<uint32_t*>(dst + d) =
+                pack2<T>(o[j][2 * rr] * inv, o[j][2 * rr + 1] * inv);
+        }
+    }
+}
+
+size_t attn_decode_workspace(int B, int Hkv, int max_kv_len, int head_dim) {
+    const int splits = (max_kv_len + attn::SK - 1) / attn::SK;
+    if (splits <= 1) return 0;
+    const size_t tickets = (static_cast<size_t>(B) * Hkv * 4 + 255) / 256 * 256;
+    const size_t parts = static_cast<size_t>(B) * Hkv * splits * attn::MAXG;
+    return tickets + parts * head_dim * 4 + parts * 8;
+}
+
+cudaError_t launch_attn_decode(int dtype, const void* q, const void* k_cache, const void* v_cache,
+                               const int32_t* block_table, int max_blocks, const int32_t* kv_lens,
+                               int max_kv_len, void* out, int B, int Hq, int Hkv, int hd, int page,
+                               float scale, void* workspace, bool overlap, cudaStream_t st) {
+    const int splits = (max_kv_len + attn::SK - 1) / attn::SK;
+    float scale_log2 = scale * 1.4426950408889634f;
+    unsigned* tickets = nullptr;
+    float* ws_o = nullptr;
+    float2* ws_ml = nullptr;
+    if (splits > 1) {
+        char* base = static_cast<char*>(workspace);
+        const size_t tb = (static_cast<size_t>(B) * Hkv * 4 + 255) / 256 * 256;
+        const size_t parts = static_cast<size_t>(B) * Hkv * splits * attn::MAXG;
+        tickets = reinterpret_cast<unsigned*>(base);
+        ws_o = reinterpret_cast<float*>(base + tb);
+        ws_ml = reinterpret_cast<float2*>(base + tb + parts * hd * 4);
+    }
+    int max_splits = splits;
+    void* args[] = {&q, &k_cache, &v_cache, &block_table, &max_blocks, &kv_lens, &out,
+                    &Hq, &Hkv, &page, &scale_log2, &ws_o, &ws_ml, &tickets, &max_splits,
+                    &max_kv_len};
+    const void* f = nullptr;
+    if (dtype == kBF16)
+        f = hd == 128 ? reinterpret_cast<const void*>(&attn_decode_kernel<__nv_bfloat16, 128>)
+                      : reinterpret_cast<const void*>(&attn_decode_kernel<__nv_bfloat16, 64>);
+    else
+        f = hd == 128 ? reinterpret_cast<const void*>(&attn_decode_kernel<__half, 128>)
+                      : reinterpret_cast<const void*>(&attn_decode_kernel<__half, 64>);
+    return launch_ex(f, dim3(splits, Hkv, B), dim3(attn::THREADS), 0, st, overlap, args);
+}
+
+size_t attn_prefill_smem(int hd) { return static_cast<size_t>(pf::QT + 4 * pf::KT) * hd * 2; }
+
+cudaError_t launch_attn_prefill(int dtype, const void* q, const int32_t* cu_q, int max_q_len,
+                                const void* k_cache, const void* v_cache,
+                                const int32_t* block_table, int max_blocks,
+                                const int32_t* kv_lens, void* out, int B, int Hq, int Hkv, int hd,
+                                int page, float scale, bool overlap, cudaStream_t st) {
+    float scale_log2 = scale * 1.4426950408889634f;
+    const size_t smem = attn_prefill_smem(hd);
+    const void* f = nullptr;
+    if (dtype == kBF16)
+        f = hd == 128 ? reinterpret_cast<const void*>(&attn_prefill_kernel<__nv_bfloat16, 128>)
+                      : reinterpret_cast<const void*>(&attn_prefill_kernel<__nv_bfloat16, 64>);
+    else
+        f = hd == 128 ? reinterpret_cast<const void*>(&attn_prefill_kernel<__half, 128>)
+                      : reinterpret_cast<const void*>(&attn_prefill_kernel<__half, 64>);
+    static PerDevice configured[4];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    const int which = (dtype == kBF16 ? 0 : 2) + (hd == 128 ? 0 : 1);
+    e = ensure_smem_attr(f, configured[which], dev, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    void* args[] = {&q, &cu_q, &k_cache, &v_cache, &block_table, &max_blocks, &kv_lens, &out,
+                    &Hq, &Hkv, &page, &scale_log2};
+    const int qtiles = (max_q_len + pf::QT - 1) / pf::QT;
+    return launch_ex(f, dim3(qtiles, Hq, B), dim3(pf::THREADS), smem, st, overlap, args);
+}
+
+// ------------------------------------------------------------------------------------
+// Quantized embedding lookup: out[i] = dequantize(row ids[i]) with MLX's rounding,
+// round(round(scale * q) + bias) in T (bit-identical to mlxq_dequantize of that row).
+// One CTA per id, one thread per packed word; ids outside [0, vocab) give zeros.
+template <typename T, int BITS>
+__global__ void embed_kernel(const int32_t* __restrict__ ids, const uint32_t* __restrict__ wq,
+                             const T* __restrict__ scales, const T* __restrict__ biases,
+                             T* __restrict__ out, int vocab, int K, int gs) {
+    constexpr int EPW = 32 / BITS;
+    pdl_launch_dependents();
+    pdl_wait();
+    const int i = blockIdx.x;
+    const int id = ids[i];
+    const int words = K / EPW;
+    T* dst = out + static_cast<size_t>(i) * K;
+    for (int wi = threadIdx.x; wi < words; wi += blockDim.x) {
+        uint32_t packed[EPW / 2];
+        if (id >= 0 && id < vocab) {
+            const uint32_t wv = wq[static_cast<size_t>(id) * words + wi];
+            const int g = wi * EPW / gs;
+            const float s = Elem<T>::to_f(scales[static_cast<size_t>(id) * (K / gs) + g]);
+            const float b = Elem<T>::to_f(biases[static_cast<size_t>(id) * (K / gs) + g]);
+#pragma unroll
+            for (int e = 0; e < EPW; e += 2) {
+                const float q0 = static_cast<float>((wv >> (BITS * e)) & ((1u << BITS) - 1u));
+                const float q1 = static_cast<float>((wv >> (BITS * (e + 1))) & ((1u << BITS) - 1u));
+                packed[e / 2] = pack2<T>(round_t<T>(s * q0) + b, round_t<T>(s * q1) + b);
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < EPW / 2; ++e) packed[e] = 0u;
+        }
+        if constexpr (EPW == 8) {
+            *reinterpret_cast<uint4*>(dst + wi * EPW) =
+                make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        } else {
+            *reinterpret_cast<uint2*>(dst + wi * EPW) = make_uint2(packed[0], packed[1]);
+        }
+    }
+}
+
+cudaError_t launch_embed(int dtype, int bits, const int32_t* ids, int n, const uint32_t* wq,
+                         const void* scales, const void* biases, void* out, int vocab, int K,
+                         int gs, bool overlap, cudaStream_t st) {
+    void* args[] = {&ids, &wq, &scales, &biases, &out, &vocab, &K, &gs};
+    const void* f = nullptr;
+    if (dtype == kBF16)
+        f = bits == 4 ? reinterpret_cast<const void*>(&embed_kernel<__nv_bfloat16, 4>)
+                      : reinterpret_cast<const void*>(&embed_kernel<__nv_bfloat16, 8>);
+    else
+        f = bits == 4 ? reinterpret_cast<const void*>(&embed_kernel<__half, 4>)
+                      : reinterpret_cast<const void*>(&embed_kernel<__half, 8>);
+    const int words = K * bits / 32;
+    const int threads = words >= 256 ? 256 : (words + 31) / 32 * 32;
+    return launch_ex(f, dim3(n), dim3(threads), 0, st, overlap, args);
+}
+
+// ------------------------------------------------------------------------------------
+// One decode step further for every sequence: the next token sits at position
+// p + 1, the cache then holds p + 2 keys, and its slot is that position's place in
+// the sequence's pages (-1 past the block table).
+__global__ void decode_advance_kernel(int32_t* __restrict__ positions,
+                                      int32_t* __restrict__ kv_lens, int32_t* __restrict__ slots,
+                                      const int32_t* __restrict__ block_table, int max_blocks,
+                                      int B, int page) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    const int p = positions[b] + 1;
+    positions[b] = p;
+    kv_lens[b] = p + 1;
+    const int blk = p / page;
+    slots[b] = blk < max_blocks
+                   ? block_table[static_cast<size_t>(b) * max_blocks + blk] * page + p % page
+                   : -1;
+}
+
+cudaError_t launch_decode_advance(int32_t* positions, int32_t* kv_lens, int32_t* slots,
+                                  const int32_t* block_table, int max_blocks, int B, int page,
+                                  bool overlap, cudaStream_t st) {
+    void* args[] = {&positions, &kv_lens, &slots, &block_table, &max_blocks, &B, &page};
+    return launch_ex(reinterpret_cast<const void*>(&decode_advance_kernel), dim3((B + 127) / 128),
+                     dim3(128), 0, st, overlap, args);
+}
+
+}  // namespace mlxq
