@@ -58,8 +58,15 @@ __device__ __forceinline__ float round_t(float v) {
     return Elem<T>::to_f(Elem<T>::from_f(v));
 }
 
-cudaError_t launch_ex(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                      bool overlap, void** args) {
+// Launch with the overlap attribute when asked; the kernel's carveout is set to the
+// whole shared-memory capacity once per device (see ensure_smem_attr).
+cudaError_t launch_ex(const void* func, PerDevice& cache, dim3 grid, dim3 block, size_t smem,
+                      cudaStream_t st, bool overlap, void** args) {
+    int dev = 0;
+    cudaError_t e = current_device(&dev);
+    if (e != cudaSuccess) return e;
+    e = ensure_smem_attr(func, cache, dev, smem > 0 ? static_cast<int>(smem) : 1);
+    if (e != cudaSuccess) return e;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -86,10 +93,14 @@ __global__ void rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ d
                                 T* __restrict__ sum_out, int D, float eps) {
     __shared__ float red[32];
     pdl_launch_dependents();
-    pdl_wait();
     const int row = blockIdx.x;
     const int i = threadIdx.x;
     const bool on = 8 * i < D;
+    // the weight is a parameter (not written by the kernels before this one): load
+    // it before waiting for them
+    uint4 wv = make_uint4(0u, 0u, 0u, 0u);
+    if (on) wv = *reinterpret_cast<const uint4*>(w + 8 * i);
+    pdl_wait();
     float h[8];
     float ss = 0.f;
     if (on) {
@@ -138,7 +149,6 @@ __global__ void rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ d
     __syncthreads();
     const float r = rsqrtf(red[0] / static_cast<float>(D) + eps);
     if (on) {
-        const uint4 wv = *reinterpret_cast<const uint4*>(w + 8 * i);
         const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
         uint32_t o[4];
 #pragma unroll
@@ -156,18 +166,24 @@ cudaError_t launch_rms_norm(int dtype, const void* x, const void* delta, const v
                             cudaStream_t st) {
     const int threads = ((D / 8) + 31) / 32 * 32;
     void* args[] = {&x, &delta, &w, &y, &sum_out, &D, &eps};
-    const void* f = dtype == kBF16
-                        ? reinterpret_cast<const void*>(&rms_norm_kernel<__nv_bfloat16>)
-                        : reinterpret_cast<const void*>(&rms_norm_kernel<__half>);
-    return launch_ex(f, dim3(rows), dim3(threads), 0, st, overlap, args);
+    static PerDevice cfg[2];
+    const bool bf = dtype == kBF16;
+    const void* f = bf ? reinterpret_cast<const void*>(&rms_norm_kernel<__nv_bfloat16>)
+                       : reinterpret_cast<const void*>(&rms_norm_kernel<__half>);
+    return launch_ex(f, cfg[bf ? 0 : 1], dim3(rows), dim3(threads), 0, st, overlap, args);
 }
 
 // ------------------------------------------------------------------------------------
-// RoPE (half-rotation form, traditional=False) of the queries and keys of one token
-// per CTA, queries to q_out [T, Hq, hd], keys and values to their cache slot
-// (slot = page * page_size + offset; a negative slot skips the append).
+// RoPE (half-rotation form, traditional=False) and the paged KV append. CTA (token t,
+// head block y) rotates ROPE_HEADS heads, one (i, i + hd/2) pair per thread, so
+// every thread has one load of each operand in flight; queries go to q_out
+// [T, Hq, hd], keys and values to their cache slot (slot = page * page_size +
+// offset; a negative slot skips the append). The values are copied by the CTAs
+// of the token's first head block.
 //   freq_i = base^(-2i/hd), angle = position * freq_i, for i < hd/2:
 //   (a, b) = (x_i, x_{i+hd/2}) -> (a cos - b sin, a sin + b cos), rounded to T.
+constexpr int ROPE_HEADS = 4;
+
 template <typename T>
 __global__ void rope_append_kernel(const T* __restrict__ qkv, int ld, T* __restrict__ q_out,
                                    T* __restrict__ k_cache, T* __restrict__ v_cache,
@@ -175,21 +191,22 @@ __global__ void rope_append_kernel(const T* __restrict__ qkv, int ld, T* __restr
                                    const int32_t* __restrict__ slots, int Hq, int Hkv, int hd,
                                    float log2_base) {
     pdl_launch_dependents();
+    const int half = hd / 2;
+    const int i = threadIdx.x % half;
+    const int h = blockIdx.y * ROPE_HEADS + threadIdx.x / half;
+    // the frequency depends on nothing the previous kernel writes
+    const float freq =
+        exp2f(-(2.0f * static_cast<float>(i) / static_cast<float>(hd)) * log2_base);
     pdl_wait();
     const int t = blockIdx.x;
     const T* src = qkv + static_cast<size_t>(t) * ld;
-    const float pos = static_cast<float>(positions[t]);
     const int slot = slots[t];
-    const int half = hd / 2;
-    const int pairs = (Hq + Hkv) * half;
-    for (int p = threadIdx.x; p < pairs; p += blockDim.x) {
-        const int h = p / half, i = p % half;
-        const float freq = exp2f(-(2.0f * static_cast<float>(i) / static_cast<float>(hd)) *
-                                 log2_base);
-        float sn, cs;
-        sincosf(pos * freq, &sn, &cs);
+    if (h < Hq + Hkv) {
+        const float pos = static_cast<float>(positions[t]);
         const float a = Elem<T>::to_f(src[h * hd + i]);
         const float b = Elem<T>::to_f(src[h * hd + i + half]);
+        float sn, cs;
+        sincosf(pos * freq, &sn, &cs);
         const T ra = Elem<T>::from_f(a * cs - b * sn);
         const T rb = Elem<T>::from_f(a * sn + b * cs);
         if (h < Hq) {
@@ -202,7 +219,7 @@ __global__ void rope_append_kernel(const T* __restrict__ qkv, int ld, T* __restr
             dk[i + half] = rb;
         }
     }
-    if (slot >= 0) {
+    if (blockIdx.y == 0 && slot >= 0) {
         const int vchunks = Hkv * hd / 8;
         const uint4* vs = reinterpret_cast<const uint4*>(src + (Hq + Hkv) * hd);
         uint4* vd = reinterpret_cast<uint4*>(v_cache + static_cast<size_t>(slot) * Hkv * hd);
@@ -216,27 +233,42 @@ cudaError_t launch_rope_append(int dtype, const void* qkv, int ld, void* q_out, 
                                cudaStream_t st) {
     void* args[] = {&qkv, &ld, &q_out, &k_cache, &v_cache, &positions, &slots,
                     &Hq, &Hkv, &hd, &log2_base};
-    const void* f = dtype == kBF16
-                        ? reinterpret_cast<const void*>(&rope_append_kernel<__nv_bfloat16>)
-                        : reinterpret_cast<const void*>(&rope_append_kernel<__half>);
-    return launch_ex(f, dim3(tokens), dim3(256), 0, st, overlap, args);
+    static PerDevice cfg[2];
+    const bool bf = dtype == kBF16;
+    const void* f = bf ? reinterpret_cast<const void*>(&rope_append_kernel<__nv_bfloat16>)
+                       : reinterpret_cast<const void*>(&rope_append_kernel<__half>);
+    const int blocks_y = (Hq + Hkv + ROPE_HEADS - 1) / ROPE_HEADS;
+    return launch_ex(f, cfg[bf ? 0 : 1], dim3(tokens, blocks_y), dim3(ROPE_HEADS * hd / 2), 0, st,
+                     overlap, args);
 }
 
 // ------------------------------------------------------------------------------------
 // Decode attention: one query token per sequence. CTA (split s, kv head g, sequence
 // b) takes keys [s*SK, min((s+1)*SK, L_b)) of the sequence's L_b cached keys and the
 // G = Hq/Hkv query heads that share kv head g:
-//   scores  thread j = key j: G dot products of its key row with the prescaled queries
+//   load    the split's key and value rows, gathered from the pages with cp.async
+//           into shared memory (16-byte chunks XOR-swizzled by row, so reading one
+//           chunk of consecutive rows is conflict free); every load is in flight at
+//           once, values land while the scores are computed
+//   scores  thread (key j, head half): dot products of key j with its heads'
+//           prescaled queries
 //   softmax per head over the split's keys (max, exp2, sum)
-//   values  thread d = dimension d: sum over keys of p * v
+//   values  thread (dimension pair, key range): sum over its keys of p * v, the key
+//           ranges then added in a fixed order
 // A sequence with one split writes its outputs; otherwise each split stores its
 // (max, sum, unnormalised output) and the last split to finish (acquire-release
 // ticket per (b, g), zero between calls) merges them in split order.
 namespace attn {
-constexpr int SK = 128;       // keys per split (one per thread)
+constexpr int SK = 64;        // keys per split
 constexpr int THREADS = 128;
 constexpr int MAXG = 8;       // query heads per kv head
 }  // namespace attn
+
+template <int HD>
+__device__ __forceinline__ uint32_t kv_swz(int row, int chunk) {
+    constexpr int CH = HD / 8;
+    return static_cast<uint32_t>(row * (HD * 2) + ((chunk ^ (row & (CH - 1))) << 4));
+}
 
 template <typename T, int HD>
 __global__ void __launch_bounds__(attn::THREADS)
@@ -248,8 +280,17 @@ __global__ void __launch_bounds__(attn::THREADS)
                        int max_splits, int max_kv) {
     using namespace attn;
     static_assert(HD == 64 || HD == 128, "head_dim");
+    constexpr int CH = HD / 8;             // 16-byte chunks per row
+    constexpr int DP = HD / 2;             // dimension pairs
+    constexpr int KPH = THREADS / DP;      // key ranges of the value pass (2 or 4)
+    constexpr int KPR = SK / KPH;          // keys per range
+    constexpr int HH = THREADS / SK;       // head halves of the score pass (2)
+    constexpr int HPT = MAXG / HH;         // heads per score thread (4)
+    __shared__ __align__(16) uint8_t ks[SK * HD * 2];
+    __shared__ __align__(16) uint8_t vs[SK * HD * 2];
     __shared__ __align__(16) float qs[MAXG][HD];
-    __shared__ float ps[MAXG][SK];
+    __shared__ __align__(16) float ps[MAXG][SK];
+    __shared__ __align__(16) float xch[(KPH - 1) * MAXG * HD];
     __shared__ float mls[2][MAXG];
     __shared__ int s_last;
     pdl_launch_dependents();
@@ -262,55 +303,74 @@ __global__ void __launch_bounds__(attn::THREADS)
     const int k0 = split * SK;
     const int n = min(SK, L - k0);
     const int tid = threadIdx.x;
+    const int32_t* bt = block_table + static_cast<size_t>(b) * max_blocks;
 
+    // keys, then values: rows past n are zero-filled (their source stays in bounds)
+    for (int pass = 0; pass < 2; ++pass) {
+        const T* src = pass == 0 ? k_cache : v_cache;
+        uint8_t* dst = pass == 0 ? ks : vs;
+        for (int c = tid; c < SK * CH; c += THREADS) {
+            const int r = c / CH, ch = c % CH;
+            const bool ok = r < n;
+            const int key = ok ? k0 + r : k0;
+            const size_t row = static_cast<size_t>(bt[key / page]) * page + key % page;
+            cp_async16(dst + kv_swz<HD>(r, ch), src + (row * Hkv + g) * HD + ch * 8, ok ? 16 : 0);
+        }
+        cp_async_commit();
+    }
     for (int e = tid; e < G * HD; e += THREADS) {
         const int h = e / HD, d = e % HD;
         qs[h][d] = Elem<T>::to_f(q[(static_cast<size_t>(b) * Hq + g * G + h) * HD + d]) *
                    scale_log2;
     }
+    cp_async_wait<1>();
     __syncthreads();
-    const int32_t* bt = block_table + static_cast<size_t>(b) * max_blocks;
-    // scores: thread tid takes key k0 + tid
-    if (tid < n) {
-        const int key = k0 + tid;
-        const size_t row = static_cast<size_t>(bt[key / page]) * page + key % page;
-        const uint4* kr = reinterpret_cast<const uint4*>(k_cache + (row * Hkv + g) * HD);
-        float acc[MAXG];
+
+    // scores: thread (key j, heads HPT*hh ..)
+    {
+        const int j = tid % SK, hh = tid / SK;
+        float acc[HPT];
 #pragma unroll
-        for (int h = 0; h < MAXG; ++h) acc[h] = 0.f;
+        for (int k = 0; k < HPT; ++k) acc[k] = 0.f;
+        const uint32_t kb = smem_u32(ks);
 #pragma unroll 4
-        for (int c = 0; c < HD / 8; ++c) {
-            const uint4 kv = kr[c];
-            const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
+        for (int c = 0; c < CH; ++c) {
+            uint32_t w0, w1, w2, w3;
+            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                         : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
+                         : "r"(kb + kv_swz<HD>(j, c)));
+            const uint32_t kw[4] = {w0, w1, w2, w3};
             float kf[8];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float2 f = unpack2<T>(kw[j]);
-                kf[2 * j] = f.x;
-                kf[2 * j + 1] = f.y;
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = unpack2<T>(kw[e]);
+                kf[2 * e] = f.x;
+                kf[2 * e + 1] = f.y;
             }
 #pragma unroll
-            for (int h = 0; h < MAXG; ++h) {
+            for (int k = 0; k < HPT; ++k) {
+                const int h = hh * HPT + k;
                 if (h < G) {
                     const float4 qa = *reinterpret_cast<const float4*>(&qs[h][8 * c]);
                     const float4 qb = *reinterpret_cast<const float4*>(&qs[h][8 * c + 4]);
-                    acc[h] = fmaf(qa.x, kf[0], acc[h]);
-                    acc[h] = fmaf(qa.y, kf[1], acc[h]);
-                    acc[h] = fmaf(qa.z, kf[2], acc[h]);
-                    acc[h] = fmaf(qa.w, kf[3], acc[h]);
-                    acc[h] = fmaf(qb.x, kf[4], acc[h]);
-                    acc[h] = fmaf(qb.y, kf[5], acc[h]);
-                    acc[h] = fmaf(qb.z, kf[6], acc[h]);
-                    acc[h] = fmaf(qb.w, kf[7], acc[h]);
+                    acc[k] = fmaf(qa.x, kf[0], acc[k]);
+                    acc[k] = fmaf(qa.y, kf[1], acc[k]);
+                    acc[k] = fmaf(qa.z, kf[2], acc[k]);
+                    acc[k] = fmaf(qa.w, kf[3], acc[k]);
+                    acc[k] = fmaf(qb.x, kf[4], acc[k]);
+                    acc[k] = fmaf(qb.y, kf[5], acc[k]);
+                    acc[k] = fmaf(qb.z, kf[6], acc[k]);
+                    acc[k] = fmaf(qb.w, kf[7], acc[k]);
                 }
             }
         }
 #pragma unroll
-        for (int h = 0; h < MAXG; ++h)
-            if (h < G) ps[h][tid] = acc[h];
+        for (int k = 0; k < HPT; ++k)
+            if (hh * HPT + k < G) ps[hh * HPT + k][j] = acc[k];
     }
     __syncthreads();
-    // softmax over this split's keys, one warp per head (in base 2: scores carry log2 e)
+    // softmax over this split's keys, one warp per head (base 2: scores carry log2 e);
+    // probabilities of keys past n are zero
     const int warp = tid >> 5, lane = tid & 31;
     for (int h = warp; h < G; h += THREADS / 32) {
         float m = -INFINITY;
@@ -318,8 +378,8 @@ __global__ void __launch_bounds__(attn::THREADS)
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         float l = 0.f;
-        for (int j = lane; j < n; j += 32) {
-            const float p = exp2f(ps[h][j] - m);
+        for (int j = lane; j < SK; j += 32) {
+            const float p = j < n ? exp2f(ps[h][j] - m) : 0.f;
             ps[h][j] = p;
             l += p;
         }
@@ -330,64 +390,94 @@ __global__ void __launch_bounds__(attn::THREADS)
             mls[1][h] = l;
         }
     }
+    cp_async_wait<0>();
     __syncthreads();
-    // values: thread d takes dimension d (two key halves for 64-dim heads)
-    constexpr int KP = THREADS / HD;  // key phases
-    const int d = tid % HD, ph = tid / HD;
-    float o[MAXG];
+    // values: thread (dimension pair dp, key range kr)
+    const int dp = tid % DP, kr = tid / DP;
+    float o[MAXG][2];
 #pragma unroll
-    for (int h = 0; h < MAXG; ++h) o[h] = 0.f;
-    for (int j = ph; j < n; j += KP) {
-        const int key = k0 + j;
-        const size_t row = static_cast<size_t>(bt[key / page]) * page + key % page;
-        const float v = Elem<T>::to_f(v_cache[(row * Hkv + g) * HD + d]);
+    for (int h = 0; h < MAXG; ++h) o[h][0] = o[h][1] = 0.f;
+    {
+        const uint32_t vb = smem_u32(vs);
 #pragma unroll
-        for (int h = 0; h < MAXG; ++h)
-            if (h < G) o[h] = fmaf(ps[h][j], v, o[h]);
+        for (int j4 = 0; j4 < KPR; j4 += 4) {
+            float2 v[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int j = kr * KPR + j4 + e;
+                uint32_t u;
+                asm volatile("ld.shared.u32 %0, [%1];\n"
+                             : "=r"(u)
+                             : "r"(vb + kv_swz<HD>(j, dp >> 2) + (dp & 3) * 4));
+                v[e] = unpack2<T>(u);
+            }
+#pragma unroll
+            for (int h = 0; h < MAXG; ++h) {
+                if (h < G) {
+                    const float4 p4 = *reinterpret_cast<const float4*>(&ps[h][kr * KPR + j4]);
+                    o[h][0] = fmaf(p4.x, v[0].x, o[h][0]);
+                    o[h][1] = fmaf(p4.x, v[0].y, o[h][1]);
+                    o[h][0] = fmaf(p4.y, v[1].x, o[h][0]);
+                    o[h][1] = fmaf(p4.y, v[1].y, o[h][1]);
+                    o[h][0] = fmaf(p4.z, v[2].x, o[h][0]);
+                    o[h][1] = fmaf(p4.z, v[2].y, o[h][1]);
+                    o[h][0] = fmaf(p4.w, v[3].x, o[h][0]);
+                    o[h][1] = fmaf(p4.w, v[3].y, o[h][1]);
+                }
+            }
+        }
     }
-    if (KP > 1) {
-        __syncthreads();  // ps is reused as the exchange buffer of the two halves
-        float* xch = &ps[0][0];
-        if (ph == 1)
-            for (int h = 0; h < G; ++h) xch[h * HD + d] = o[h];
-        __syncthreads();
-        if (ph == 0)
-            for (int h = 0; h < G; ++h) o[h] += xch[h * HD + d];
-    }
+    // key ranges 1.. hand their sums to range 0, which adds them in range order
+    if (kr > 0)
+        for (int h = 0; h < G; ++h)
+            *reinterpret_cast<float2*>(&xch[((kr - 1) * MAXG + h) * HD + 2 * dp]) =
+                make_float2(o[h][0], o[h][1]);
+    __syncthreads();
+    if (kr > 0) return;
+    for (int r = 1; r < KPH; ++r)
+        for (int h = 0; h < G; ++h) {
+            const float2 x = *reinterpret_cast<const float2*>(&xch[((r - 1) * MAXG + h) * HD + 2 * dp]);
+            o[h][0] += x.x;
+            o[h][1] += x.y;
+        }
     if (nsplit == 1) {
-        if (ph == 0)
-            for (int h = 0; h < G; ++h)
-                out[(static_cast<size_t>(b) * Hq + g * G + h) * HD + d] =
-                    Elem<T>::from_f(o[h] / mls[1][h]);
+        for (int h = 0; h < G; ++h) {
+            const float inv = 1.0f / mls[1][h];
+            *reinterpret_cast<uint32_t*>(out + (static_cast<size_t>(b) * Hq + g * G + h) * HD +
+                                         2 * dp) = pack2<T>(o[h][0] * inv, o[h][1] * inv);
+        }
         return;
     }
     // this split's partials: [b][g][split][h][HD] and (m, l) per head
     const size_t base = (static_cast<size_t>(b) * Hkv + g) * max_splits;
-    if (ph == 0)
-        for (int h = 0; h < G; ++h) ws_o[((base + split) * MAXG + h) * HD + d] = o[h];
+    for (int h = 0; h < G; ++h)
+        *reinterpret_cast<float2*>(&ws_o[((base + split) * MAXG + h) * HD + 2 * dp]) =
+            make_float2(o[h][0], o[h][1]);
     if (tid < G) ws_ml[(base + split) * MAXG + tid] = make_float2(mls[0][tid], mls[1][tid]);
-    // The barrier orders every thread's partials before thread 0's acq_rel ticket,
-    // whose release publishes them GPU-wide and whose acquire (with the second
-    // barrier) makes the other splits' partials visible to this CTA.
-    __syncthreads();
+    // A barrier of the range-0 threads orders their partials before thread 0's acq_rel
+    // ticket, whose release publishes them GPU-wide and whose acquire (with the second
+    // barrier) makes the other splits' partials visible to these threads.
+    named_bar_sync(1, DP);
     if (tid == 0)
         s_last = atom_add_acq_rel_gpu(tickets + b * Hkv + g, 1u) ==
                  static_cast<unsigned>(nsplit - 1);
-    __syncthreads();
+    named_bar_sync(1, DP);
     if (!s_last) return;
-    if (ph == 0) {
-        for (int h = 0; h < G; ++h) {
-            float M = -INFINITY;
-            for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(&ws_ml[(base + s) * MAXG + h]).x);
-            float num = 0.f, den = 0.f;
-            for (int s = 0; s < nsplit; ++s) {
-                const float2 ml = __ldcg(&ws_ml[(base + s) * MAXG + h]);
-                const float c = exp2f(ml.x - M);
-                num = fmaf(c, __ldcg(&ws_o[((base + s) * MAXG + h) * HD + d]), num);
-                den = fmaf(c, ml.y, den);
-            }
-            out[(static_cast<size_t>(b) * Hq + g * G + h) * HD + d] = Elem<T>::from_f(num / den);
+    for (int h = 0; h < G; ++h) {
+        float M = -INFINITY;
+        for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(&ws_ml[(base + sp) * MAXG + h]).x);
+        float n0 = 0.f, n1 = 0.f, den = 0.f;
+        for (int sp = 0; sp < nsplit; ++sp) {
+            const float2 ml = __ldcg(&ws_ml[(base + sp) * MAXG + h]);
+            const float c = exp2f(ml.x - M);
+            const float2 v = __ldcg(reinterpret_cast<const float2*>(
+                &ws_o[((base + sp) * MAXG + h) * HD + 2 * dp]));
+            n0 = fmaf(c, v.x, n0);
+            n1 = fmaf(c, v.y, n1);
+            den = fmaf(c, ml.y, den);
         }
+        *reinterpret_cast<uint32_t*>(out + (static_cast<size_t>(b) * Hq + g * G + h) * HD +
+                                     2 * dp) = pack2<T>(n0 / den, n1 / den);
     }
     if (tid == 0) tickets[b * Hkv + g] = 0u;
 }
@@ -627,7 +717,10 @@ cudaError_t launch_attn_decode(int dtype, const void* q, const void* k_cache, co
     else
         f = hd == 128 ? reinterpret_cast<const void*>(&attn_decode_kernel<__half, 128>)
                       : reinterpret_cast<const void*>(&attn_decode_kernel<__half, 64>);
-    return launch_ex(f, dim3(splits, Hkv, B), dim3(attn::THREADS), 0, st, overlap, args);
+    static PerDevice cfg[4];
+    const int which = (dtype == kBF16 ? 0 : 2) + (hd == 128 ? 0 : 1);
+    return launch_ex(f, cfg[which], dim3(splits, Hkv, B), dim3(attn::THREADS), 0, st, overlap,
+                     args);
 }
 
 size_t attn_prefill_smem(int hd) { return static_cast<size_t>(pf::QT + 4 * pf::KT) * hd * 2; }
@@ -646,18 +739,13 @@ cudaError_t launch_attn_prefill(int dtype, const void* q, const int32_t* cu_q, i
     else
         f = hd == 128 ? reinterpret_cast<const void*>(&attn_prefill_kernel<__half, 128>)
                       : reinterpret_cast<const void*>(&attn_prefill_kernel<__half, 64>);
-    static PerDevice configured[4];
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    static PerDevice cfg[4];
     const int which = (dtype == kBF16 ? 0 : 2) + (hd == 128 ? 0 : 1);
-    e = ensure_smem_attr(f, configured[which], dev, static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
     void* args[] = {&q, &cu_q, &k_cache, &v_cache, &block_table, &max_blocks, &kv_lens, &out,
                     &Hq, &Hkv, &page, &scale_log2};
     const int qtiles = (max_q_len + pf::QT - 1) / pf::QT;
-    return launch_ex(f, dim3(qtiles, Hq, B), dim3(pf::THREADS), smem, st, overlap, args);
+    return launch_ex(f, cfg[which], dim3(qtiles, Hq, B), dim3(pf::THREADS), smem, st, overlap,
+                     args);
 }
 
 // ------------------------------------------------------------------------------------
@@ -714,7 +802,9 @@ cudaError_t launch_embed(int dtype, int bits, const int32_t* ids, int n, const u
                       : reinterpret_cast<const void*>(&embed_kernel<__half, 8>);
     const int words = K * bits / 32;
     const int threads = words >= 256 ? 256 : (words + 31) / 32 * 32;
-    return launch_ex(f, dim3(n), dim3(threads), 0, st, overlap, args);
+    static PerDevice cfg[4];
+    const int which = (dtype == kBF16 ? 0 : 2) + (bits == 4 ? 0 : 1);
+    return launch_ex(f, cfg[which], dim3(n), dim3(threads), 0, st, overlap, args);
 }
 
 // ------------------------------------------------------------------------------------
@@ -742,7 +832,8 @@ cudaError_t launch_decode_advance(int32_t* positions, int32_t* kv_lens, int32_t*
                                   const int32_t* block_table, int max_blocks, int B, int page,
                                   bool overlap, cudaStream_t st) {
     void* args[] = {&positions, &kv_lens, &slots, &block_table, &max_blocks, &B, &page};
-    return launch_ex(reinterpret_cast<const void*>(&decode_advance_kernel), dim3((B + 127) / 128),
+    static PerDevice cfg;
+    return launch_ex(reinterpret_cast<const void*>(&decode_advance_kernel), cfg, dim3((B + 127) / 128),
                      dim3(128), 0, st, overlap, args);
 }
 

@@ -22,15 +22,40 @@ struct PerDevice {
 
 // Raises `kern`'s dynamic shared-memory limit on the current device `dev` to at
 // least `smem` (never lowers it); host threads racing on a first launch serialize.
+// The kernel's preferred carveout is set to the whole shared-memory capacity at the
+// same time. The SM's L1/shared split otherwise follows each kernel's own size
+// (e.g. 132 KB for one 104 KB CTA), and an SM configured for one split has to drain
+// before it takes a CTA that needs another: back-to-back kernels with different
+// needs could then never share an SM, and launch overlap would not overlap.
 template <typename K>
 cudaError_t ensure_smem_attr(K kern, PerDevice& cache, int dev, int smem) {
     if (cache.v[dev].load(std::memory_order_acquire) >= smem) return cudaSuccess;
     std::lock_guard<std::mutex> lock(setup_mutex());
-    if (cache.v[dev].load(std::memory_order_relaxed) >= smem) return cudaSuccess;
+    const int have = cache.v[dev].load(std::memory_order_relaxed);
+    if (have >= smem) return cudaSuccess;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
+    if (have == 0) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 cudaSharedmemCarveoutMaxShared);
+        if (e != cudaSuccess) return e;
+    }
     cache.v[dev].store(smem, std::memory_order_release);
     return cudaSuccess;
+}
+
+// The carveout part of ensure_smem_attr alone, for kernels with no dynamic shared
+// memory above the default limit.
+template <typename K>
+cudaError_t ensure_carveout(K kern, PerDevice& cache, int dev) {
+    return ensure_smem_attr(kern, cache, dev, 1);
+}
+
+// The calling thread's current device, checked against the per-device tables.
+inline cudaError_t current_device(int* dev) {
+    cudaError_t e = cudaGetDevice(dev);
+    if (e != cudaSuccess) return e;
+    return (*dev < 0 || *dev >= 64) ? cudaErrorInvalidDevice : cudaSuccess;
 }
 
 enum { kF32 = 0, kBF16 = 1, kF16 = 2 };

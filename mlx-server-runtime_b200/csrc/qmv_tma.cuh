@@ -334,11 +334,35 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
     const int rt = warp % RT, kq = warp / RT;
     const int r = lane >> 2, c = lane & 3;
     const int ctid = threadIdx.x;  // 0 .. CTHREADS-1
+    // The K groups this CTA's units use: stages u % S of its share, at most two
+    // ranges [ga0, ga1) and [gb0, gb1) of groups (whole stages of 8 groups).
+    int ga0 = 0, ga1 = G, gb0 = 0, gb1 = 0;
+    if (u_hi - u_lo < S) {
+        const int s0 = static_cast<int>(u_lo % S);
+        const int s1 = s0 + static_cast<int>(u_hi - u_lo);
+        ga0 = s0 * SG;
+        ga1 = min(s1, S) * SG;
+        gb1 = s1 > S ? (s1 - S) * SG : 0;
+    }
+    const int na = ga1 - ga0;
+    // x may still be being written by the kernel before this one, so it is read only
+    // after griddepcontrol.wait; an L2 prefetch of its lines is safe before (L2 is
+    // where global memory is coherent: the writes land in the lines prefetched), and
+    // the reads after the wait then find them there instead of in HBM.
+    {
+        const char* xb = static_cast<const char*>(p.x);
+        const int items = (na + gb1 - gb0) * M;
+        for (int i = ctid; i < items; i += CTHREADS) {
+            const int t = i % M, j = i / M;
+            const int g = j < na ? ga0 + j : gb0 + (j - na);
+            const char* a = xb + (static_cast<long long>(t) * p.K + g * GS) * sizeof(T);
+            asm volatile("prefetch.global.L2 [%0];\n" ::"l"(a));
+        }
+    }
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
 
-    // x[M, K] -> f16 B fragments and records, for the groups this CTA's units use:
-    // stages u % S of its share, at most two ranges [ga0, ga1) and [gb0, gb1) of
-    // groups. Item i = ((j * TM + t) * 4 + c), j the group's position in those ranges:
+    // x[M, K] -> f16 B fragments and records, for the groups this CTA's units use
+    // ([ga0, ga1) and [gb0, gb1) above). Item i = ((j * TM + t) * 4 + c), j the group's position in those ranges:
     // lane c of token slot t holds words c, c+4, ... of the group (the words ldmatrix
     // gives that lane). The ranges are whole stages (8 groups), so the item count is
     // a multiple of 32: every warp runs whole iterations and the 4 lanes of an item
@@ -347,15 +371,6 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
         const T* xg = static_cast<const T*>(p.x);
         constexpr int XW = BITS == 4 ? 8 : 4;  // activations per packed word
         constexpr int PB = (CPG * XW / 2 <= 8) ? 4 : 2;  // items with loads in flight together
-        int ga0 = 0, ga1 = G, gb0 = 0, gb1 = 0;
-        if (u_hi - u_lo < S) {
-            const int s0 = static_cast<int>(u_lo % S);
-            const int s1 = s0 + static_cast<int>(u_hi - u_lo);
-            ga0 = s0 * SG;
-            ga1 = min(s1, S) * SG;
-            gb1 = s1 > S ? (s1 - S) * SG : 0;
-        }
-        const int na = ga1 - ga0;
         const int total = (na + gb1 - gb0) * TM * 4;
         for (int i0 = ctid; i0 < total; i0 += PB * CTHREADS) {
           uint32_t raw[PB][CPG][XW / 2];

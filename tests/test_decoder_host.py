@@ -34,7 +34,7 @@ def test_rejections_before_any_launch():
                                  1e6, _lib.BF16, None) == _lib.ERR_SHAPE  # ld too small
     assert L.mlxq_quantized_embedding(FAKE, 3, FAKE, FAKE, FAKE, FAKE, 10, 100, 64, 4,
                                       _lib.BF16, None) == _lib.ERR_SHAPE  # dim % group
-    assert L.mlxq_paged_attention_workspace_size(8, 4, 128, 128) == 0     # one split
+    assert L.mlxq_paged_attention_workspace_size(8, 4, 64, 128) == 0      # one split of 64 keys
     assert L.mlxq_paged_attention_workspace_size(8, 4, 640, 128) > 0
     assert _lib.last_error()
 
