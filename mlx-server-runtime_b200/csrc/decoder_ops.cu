@@ -304,24 +304,39 @@ __global__ void __launch_bounds__(attn::THREADS)
     const int n = min(SK, L - k0);
     const int tid = threadIdx.x;
     const int32_t* bt = block_table + static_cast<size_t>(b) * max_blocks;
-
+    // the split's page ids and the queries, each in one round of loads
+    __shared__ int pid[SK / 8 + 2];
+    const int p0 = k0 / page;
+    const int np = (k0 + n - 1) / page - p0 + 1;
+    if (tid < np) pid[tid] = bt[p0 + tid];
+    {
+        const uint4* qsrc = reinterpret_cast<const uint4*>(q + (static_cast<size_t>(b) * Hq + g * G) * HD);
+        for (int c = tid; c < G * HD / 8; c += THREADS) {
+            const uint4 v = qsrc[c];
+            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+            const int h = (8 * c) / HD, d = (8 * c) % HD;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = unpack2<T>(w4[e]);
+                qs[h][d + 2 * e] = f.x * scale_log2;
+                qs[h][d + 2 * e + 1] = f.y * scale_log2;
+            }
+        }
+    }
+    __syncthreads();
     // keys, then values: rows past n are zero-filled (their source stays in bounds)
     for (int pass = 0; pass < 2; ++pass) {
         const T* src = pass == 0 ? k_cache : v_cache;
         uint8_t* dst = pass == 0 ? ks : vs;
+#pragma unroll 4
         for (int c = tid; c < SK * CH; c += THREADS) {
             const int r = c / CH, ch = c % CH;
             const bool ok = r < n;
             const int key = ok ? k0 + r : k0;
-            const size_t row = static_cast<size_t>(bt[key / page]) * page + key % page;
+            const size_t row = static_cast<size_t>(pid[key / page - p0]) * page + key % page;
             cp_async16(dst + kv_swz<HD>(r, ch), src + (row * Hkv + g) * HD + ch * 8, ok ? 16 : 0);
         }
         cp_async_commit();
-    }
-    for (int e = tid; e < G * HD; e += THREADS) {
-        const int h = e / HD, d = e % HD;
-        qs[h][d] = Elem<T>::to_f(q[(static_cast<size_t>(b) * Hq + g * G + h) * HD + d]) *
-                   scale_log2;
     }
     cp_async_wait<1>();
     __syncthreads();

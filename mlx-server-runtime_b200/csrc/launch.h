@@ -138,6 +138,7 @@ struct QtPlan {
     int S;         // units per row block
     long long U;   // units
     int P;         // CTAs
+    int GL;        // most K groups one CTA stages activations for
     int stages;    // ring depth
     int maxc;      // most CTAs sharing one row block
     bool heads;    // a ticket warp takes the head row blocks' tickets (64-row units)

@@ -82,7 +82,8 @@ bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms,
     if (G % qt::SG) return false;  // scale/bias rows must be whole 16-byte TMA boxes
     if (!encode_fn()) return false;
     // the driver reserves 1 KB of shared memory per CTA
-    max_smem = std::min(max_smem, sm_smem / kCtasPerSm - 1024);
+    const int full_smem = max_smem;
+    const int half_smem = std::min(max_smem, sm_smem / kCtasPerSm - 1024);
     const int TM = qt::token_slots(M);
     // Unit rows: a matrix with short rows (at most kWholeRowBlockStages stages) whose
     // 16-row blocks all fit on the SMs at kCtasPerSm CTAs per SM takes one CTA per
@@ -94,8 +95,6 @@ bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms,
                  ? 16 : 64;
     const int rt = br / 16;
     const int stage = qt::stage_stride(bits, gs, br);
-    const int fixed = qt::layout(stage, 0, G, TM, gs * 2, rt).total + 1024;  // + alignment slack
-    if (fixed + 2 * stage > max_smem) return false;
     QtPlan pl{};
     pl.BR = br;
     pl.RB = (N + br - 1) / br;
@@ -110,10 +109,21 @@ bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms,
                 : (pl.RB <= num_sms && pl.S <= kWholeRowBlockStages))
         pl.P = pl.RB;
     const long long per_cta = (pl.U + pl.P - 1) / pl.P;
-    int stages = std::min((max_smem - fixed) / stage, qt::MAX_STAGES);
+    // activation fragments are staged for the K groups of a CTA's own units only
+    pl.GL = static_cast<int>(std::min<long long>(G, per_cta * qt::SG));
+    const int fixed = qt::layout(stage, 0, pl.GL, TM, gs * 2, rt).total + 1024;  // + alignment
+    // Half an SM's shared memory lets the next matmul's CTAs co-reside where their warps
+    // fit; a plan whose staged activations leave that too shallow a ring (many tokens,
+    // long shares) takes the whole SM instead.
+    int cap = half_smem;
+    const int want = static_cast<int>(std::min<long long>(4, std::max<long long>(2, per_cta)));
+    if ((cap - fixed) / stage < want) cap = full_smem;
+    if (fixed + 2 * stage > cap) return false;
+    int stages = std::min((cap - fixed) / stage, qt::MAX_STAGES);
     stages = static_cast<int>(std::min<long long>(stages, std::max<long long>(2, per_cta)));
     pl.stages = std::max(2, stages);
-    pl.smem = static_cast<size_t>(qt::layout(stage, pl.stages, G, TM, gs * 2, rt).total) + 1024;
+    pl.smem = static_cast<size_t>(qt::layout(stage, pl.stages, pl.GL, TM, gs * 2, rt).total) +
+              1024;
     int maxc = 1;
     for (int rb = 0; rb < pl.RB; ++rb) {
         const long long ub = static_cast<long long>(rb) * pl.S;
@@ -202,7 +212,7 @@ cudaError_t qmv_tma_launch(int dtype, int bits, int gs, const QtPlan& plan, cons
     p.err = qmv_tma_error_flag();
     if (!p.err) return cudaErrorInvalidSymbol;
     p.x = x; p.bias = bias; p.out = out;
-    p.M = M; p.N = N; p.K = K; p.G = G;
+    p.M = M; p.N = N; p.K = K; p.G = G; p.GL = plan.GL;
     p.S = plan.S; p.RB = plan.RB; p.U = plan.U; p.stages = plan.stages; p.maxc = plan.maxc;
     if (plan.ws_bytes) {
         p.counter = static_cast<unsigned*>(workspace);

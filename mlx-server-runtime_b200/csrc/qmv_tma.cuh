@@ -159,6 +159,7 @@ struct QtParams {
     const void* bias;
     void* out;
     int M, N, K, G;
+    int GL;         // most K groups one CTA's units use (activation fragments staged)
     int S;          // stages (units) per row block = G / 8
     int RB;         // row blocks
     long long U;    // units
@@ -214,7 +215,7 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
     // array by pointer arithmetic so every access stays a shared-memory access
     uint8_t* base = qt_smem_raw + ((1024u - (smem_u32(qt_smem_raw) & 1023u)) & 1023u);
     const int M = p.M, N = p.N, G = p.G, S = p.S, stages = p.stages;
-    const Layout L = layout(STAGE, stages, G, TM, XG, RT);
+    const Layout L = layout(STAGE, stages, p.GL, TM, XG, RT);
     uint8_t* ring = base + L.ring;
     uint8_t* xf = base + L.xf;
     float4* rec = reinterpret_cast<float4*>(base + L.rec);
@@ -398,7 +399,6 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
             const int i = i0 + b * CTHREADS;
             if (i >= total) break;  // warp-uniform: total and CTHREADS are multiples of 32
             const int cc = i & 3, t = (i >> 2) % TM, j = (i >> 2) / TM;
-            const int g = j < na ? ga0 + j : gb0 + (j - na);
             float v[CPG][XW];
             float m = 0.f;
 #pragma unroll
@@ -445,7 +445,9 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
                 s_even += __shfl_xor_sync(0xffffffffu, s_even, o);
                 s_odd += __shfl_xor_sync(0xffffffffu, s_odd, o);
             }
-            uint4* dst = reinterpret_cast<uint4*>(xf + static_cast<size_t>(g) * TM * XG);
+            // fragments and records are stored by the group's position j in the CTA's
+            // ranges (at most p.GL of them), not by its index in K
+            uint4* dst = reinterpret_cast<uint4*>(xf + static_cast<size_t>(j) * TM * XG);
 #pragma unroll
             for (int f = 0; f < FR / 4; ++f)
                 dst[(f * TM + t) * 4 + cc] =
@@ -455,7 +457,7 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
                 // MMA slot); 8-bit: every activation meets both nibble operands.
                 const float toff = (BITS == 4) ? OFF::kOffE * s_even + OFF::kOffO * s_odd
                                                : OFF::kOff * (s_even + s_odd);
-                rec[g * TM + t] = make_float4(s_all, toff, pow2i(-e), 0.f);
+                rec[j * TM + t] = make_float4(s_all, toff, pow2i(-e), 0.f);
             }
           }
         }
@@ -550,8 +552,11 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
         const int st0 = static_cast<int>(u % S);
         const int st_end = static_cast<int>(st0 + (u_hi - u) < S ? st0 + (u_hi - u) : S);
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        const uint8_t* xs = xl + static_cast<size_t>(st0) * SG * TM * XG;
-        const float4* rs = rl + st0 * SG * TM;
+        // local position of stage st0 in the staged ranges: range a holds stages
+        // ga0/SG.., range b (a share that wraps into the next row block) stages 0..
+        const int lst = st0 >= ga0 / SG ? st0 - ga0 / SG : na / SG + st0;
+        const uint8_t* xs = xl + static_cast<size_t>(lst) * SG * TM * XG;
+        const float4* rs = rl + lst * SG * TM;
 
         for (int st = st0; st < st_end; ++st, ++it) {
             if (!*s_abort) {
