@@ -322,6 +322,20 @@ int mlxq_quantized_embedding(const int32_t* ids, int64_t n, const uint32_t* wq,
                              int64_t dim, int group_size, int bits, int dtype, void* stream);
 
 /*
+ * MoE routing: replaces the router of Lfm2MoE.__call__ (lfm2.py:366-375):
+ * gates = softmax(logits as float32) (+ expert_bias [num_experts] float32 when not
+ * NULL), the top_k experts per token and their gates, renormalised to sum to one
+ * (with the reference's + 1e-20) when norm_topk_prob, written as indices [tokens,
+ * top_k] int32 and scores [tokens, top_k] of scores_dtype. The reference takes an
+ * argpartition, whose order within the k is unspecified; here experts come in
+ * descending gate order, the lower index first on ties. num_experts <= 1024,
+ * top_k <= 32. Logits of any float dtype.
+ */
+int mlxq_moe_route(const void* logits, int logits_dtype, const float* expert_bias,
+                   int32_t* indices, void* scores, int scores_dtype, int64_t tokens,
+                   int num_experts, int top_k, int norm_topk_prob, void* stream);
+
+/*
  * Decode-loop bookkeeping on the device, so a captured decode step replays with no
  * host work: for each sequence, positions[b] += 1, kv_lens[b] = positions[b] + 1,
  * slots[b] = that position's cache row from block_table (-1 past its end). The

@@ -46,6 +46,7 @@ EXPORTED = (
     "mlxq_paged_attention_prefill",
     "mlxq_quantized_embedding",
     "mlxq_decode_advance",
+    "mlxq_moe_route",
 )
 
 _lock = threading.Lock()
@@ -126,6 +127,8 @@ def load(path: str | None = None):
         L.mlxq_quantized_embedding.restype = i32
         L.mlxq_decode_advance.argtypes = [vp, vp, vp, vp, i64, i64, i32, vp]
         L.mlxq_decode_advance.restype = i32
+        L.mlxq_moe_route.argtypes = [vp, i32, vp, vp, vp, i32, i64, i32, i32, i32, vp]
+        L.mlxq_moe_route.restype = i32
         v = L.mlxq_abi_version()
         if v != ABI_VERSION:
             raise LibraryError(f"{p} has ABI version {v}, expected {ABI_VERSION}; rebuild it")

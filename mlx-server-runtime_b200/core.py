@@ -29,6 +29,7 @@ from . import _lib
 _DT = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
 
 __all__ = ["quantize", "dequantize", "quantized_matmul", "gather_qmm", "concat_quantized",
+           "moe_route",
            "interleave_gate_up", "quantized_matmul_swiglu", "quantized_matmul_argmax",
            "Workspace", "launch_overlap"]
 
@@ -480,3 +481,34 @@ def gather_qmm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
                                0 if ws is None else ws.numel(), st.cuda_stream)
     _lib.check(rc, "gather_qmm")
     return out
+
+
+def moe_route(logits: torch.Tensor, top_k: int, norm_topk_prob: bool = True,
+              expert_bias: torch.Tensor | None = None):
+    """Top-k expert routing of an MoE layer on the device (the router of
+    Lfm2MoE.__call__, lfm2.py:366-375): softmax of the logits in float32 (+ the
+    optional float32 per-expert bias), the top_k experts per token and their gates,
+    renormalised to sum to one (with the reference's 1e-20 guard) when
+    norm_topk_prob, in the logits' dtype. Experts come in descending gate order (the
+    reference's argpartition leaves the order unspecified). Returns (indices int32
+    [..., top_k], scores [..., top_k])."""
+    dev = _cuda(logits, expert_bias)
+    dt = _dtype_code(logits, "logits", (torch.float32, torch.bfloat16, torch.float16))
+    E = logits.shape[-1]
+    if not 1 <= top_k <= min(32, E) or E > 1024:
+        raise ValueError(f"top_k={top_k} must be in [1, min(32, {E})] and experts <= 1024")
+    if expert_bias is not None:
+        if expert_bias.shape != (E,):
+            raise ValueError(f"expert_bias must be [{E}]")
+        expert_bias = expert_bias.float().contiguous()
+    lead = logits.shape[:-1]
+    x = logits.contiguous()
+    T = x.numel() // E
+    idx = torch.empty(*lead, top_k, dtype=torch.int32, device=dev)
+    sc = torch.empty(*lead, top_k, dtype=logits.dtype, device=dev)
+    with torch.cuda.device(dev):
+        st = torch.cuda.current_stream(dev)
+        rc = _lib.load().mlxq_moe_route(_ptr(x), dt, _ptr(expert_bias), _ptr(idx), _ptr(sc), dt,
+                                        T, E, top_k, int(bool(norm_topk_prob)), st.cuda_stream)
+    _lib.check(rc, "moe_route")
+    return idx, sc

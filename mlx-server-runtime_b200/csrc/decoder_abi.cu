@@ -176,6 +176,26 @@ int mlxq_quantized_embedding(const int32_t* ids, int64_t n, const uint32_t* wq,
     return e == cudaSuccess ? MLXQ_OK : cuda_fail(e, "quantized_embedding launch");
 }
 
+int mlxq_moe_route(const void* logits, int logits_dtype, const float* expert_bias,
+                   int32_t* indices, void* scores, int scores_dtype, int64_t tokens,
+                   int num_experts, int top_k, int norm_topk_prob, void* stream) {
+    auto ok_dt = [](int d) { return d == MLXQ_F32 || d == MLXQ_BF16 || d == MLXQ_F16; };
+    if (!ok_dt(logits_dtype) || !ok_dt(scores_dtype))
+        return fail(MLXQ_ERR_DTYPE, "moe_route: dtypes must be float32, bfloat16 or float16");
+    if (tokens < 0 || tokens > kIntMax / 32 || num_experts < 1 || num_experts > 1024 ||
+        top_k < 1 || top_k > 32 || top_k > num_experts)
+        return fail(MLXQ_ERR_SHAPE, "moe_route: need 1 <= top_k <= min(32, num_experts), "
+                                    "num_experts <= 1024");
+    if (!logits || !indices || !scores) return fail(MLXQ_ERR_NULL, "moe_route: NULL pointer");
+    if (tokens == 0) return MLXQ_OK;
+    cudaError_t e = mlxq::launch_moe_route(logits_dtype, logits, expert_bias, indices,
+                                           scores_dtype, scores, static_cast<int>(tokens),
+                                           num_experts, top_k, norm_topk_prob ? 1 : 0,
+                                           mlxq::launch_overlap_enabled(),
+                                           static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MLXQ_OK : cuda_fail(e, "moe_route launch");
+}
+
 int mlxq_decode_advance(int32_t* positions, int32_t* kv_lens, int32_t* slots,
                         const int32_t* block_table, int64_t max_blocks, int64_t batch,
                         int page_size, void* stream) {

@@ -443,20 +443,29 @@ __global__ void __launch_bounds__(attn::THREADS)
         }
     }
     // key ranges 1.. hand their sums to range 0, which adds them in range order
-    if (kr > 0)
-        for (int h = 0; h < G; ++h)
-            *reinterpret_cast<float2*>(&xch[((kr - 1) * MAXG + h) * HD + 2 * dp]) =
+    // (every loop over heads has compile-time bounds, so o stays in registers)
+    if (kr > 0) {
+#pragma unroll
+        for (int h = 0; h < MAXG; ++h)
+            if (h < G)
+                *reinterpret_cast<float2*>(&xch[((kr - 1) * MAXG + h) * HD + 2 * dp]) =
                 make_float2(o[h][0], o[h][1]);
+    }
     __syncthreads();
     if (kr > 0) return;
+#pragma unroll
     for (int r = 1; r < KPH; ++r)
-        for (int h = 0; h < G; ++h) {
+#pragma unroll
+        for (int h = 0; h < MAXG; ++h) {
+            if (h >= G) continue;
             const float2 x = *reinterpret_cast<const float2*>(&xch[((r - 1) * MAXG + h) * HD + 2 * dp]);
             o[h][0] += x.x;
             o[h][1] += x.y;
         }
     if (nsplit == 1) {
-        for (int h = 0; h < G; ++h) {
+#pragma unroll
+        for (int h = 0; h < MAXG; ++h) {
+            if (h >= G) continue;
             const float inv = 1.0f / mls[1][h];
             *reinterpret_cast<uint32_t*>(out + (static_cast<size_t>(b) * Hq + g * G + h) * HD +
                                          2 * dp) = pack2<T>(o[h][0] * inv, o[h][1] * inv);
@@ -465,8 +474,10 @@ __global__ void __launch_bounds__(attn::THREADS)
     }
     // this split's partials: [b][g][split][h][HD] and (m, l) per head
     const size_t base = (static_cast<size_t>(b) * Hkv + g) * max_splits;
-    for (int h = 0; h < G; ++h)
-        *reinterpret_cast<float2*>(&ws_o[((base + split) * MAXG + h) * HD + 2 * dp]) =
+#pragma unroll
+    for (int h = 0; h < MAXG; ++h)
+        if (h < G)
+            *reinterpret_cast<float2*>(&ws_o[((base + split) * MAXG + h) * HD + 2 * dp]) =
             make_float2(o[h][0], o[h][1]);
     if (tid < G) ws_ml[(base + split) * MAXG + tid] = make_float2(mls[0][tid], mls[1][tid]);
     // A barrier of the range-0 threads orders their partials before thread 0's acq_rel
@@ -820,6 +831,114 @@ cudaError_t launch_embed(int dtype, int bits, const int32_t* ids, int n, const u
     static PerDevice cfg[4];
     const int which = (dtype == kBF16 ? 0 : 2) + (bits == 4 ? 0 : 1);
     return launch_ex(f, cfg[which], dim3(n), dim3(threads), 0, st, overlap, args);
+}
+
+// ------------------------------------------------------------------------------------
+// MoE routing (lfm2.py:366-375): per token, gates = softmax(logits in float32)
+// (+ expert_bias), the top_k experts by gate (their order is not part of the
+// reference's contract, which takes an argpartition; here: descending gate, the
+// lower index first on ties), their gates, renormalised to sum to one with the
+// reference's 1e-20 guard when norm_topk, rounded to the scores' dtype. One warp per
+// token; lane l holds experts l, l + 32, ...
+template <typename TL, typename TS>
+__global__ void moe_route_kernel(const TL* __restrict__ logits, const float* __restrict__ bias,
+                                 int32_t* __restrict__ indices, TS* __restrict__ scores, int T,
+                                 int E, int K, int norm) {
+    constexpr int MAXE = 1024 / 32;
+    pdl_launch_dependents();
+    pdl_wait();
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= T) return;
+    const TL* row = logits + static_cast<size_t>(warp) * E;
+    float v[MAXE];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < MAXE; ++i) {
+        const int e = lane + 32 * i;
+        v[i] = e < E ? static_cast<float>(Elem<TL>::to_f(row[e])) : -INFINITY;
+        m = fmaxf(m, v[i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXE; ++i) {
+        v[i] = lane + 32 * i < E ? expf(v[i] - m) : 0.f;
+        sum += v[i];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float inv = 1.0f / sum;
+#pragma unroll
+    for (int i = 0; i < MAXE; ++i) {
+        const int e = lane + 32 * i;
+        v[i] = e < E ? v[i] * inv + (bias ? bias[e] : 0.f) : -INFINITY;
+    }
+    float picked = 0.f;   // lane k (< K) keeps the k-th pick
+    int picked_idx = 0;
+    float total = 0.f;
+    for (int k = 0; k < K; ++k) {
+        float best = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < MAXE; ++i) {
+            const int e = lane + 32 * i;
+            if (v[i] > best || (v[i] == best && e < bi)) {
+                best = v[i];
+                bi = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ob > best || (ob == best && oi < bi)) {
+                best = ob;
+                bi = oi;
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < MAXE; ++i)
+            if (lane + 32 * i == bi) v[i] = -INFINITY;
+        if (lane == k) {
+            picked = best;
+            picked_idx = bi;
+        }
+        total += best;
+    }
+    if (lane < K) {
+        const float sc = norm ? picked / (total + 1e-20f) : picked;
+        indices[static_cast<size_t>(warp) * K + lane] = picked_idx;
+        scores[static_cast<size_t>(warp) * K + lane] = Elem<TS>::from_f(sc);
+    }
+}
+
+cudaError_t launch_moe_route(int logits_dtype, const void* logits, const float* bias,
+                             int32_t* indices, int scores_dtype, void* scores, int T, int E, int K,
+                             int norm, bool overlap, cudaStream_t st) {
+    void* args[] = {&logits, &bias, &indices, &scores, &T, &E, &K, &norm};
+    static PerDevice cfg[9];
+    const void* f = nullptr;
+    int which = 0;
+#define MLXQ_ROUTE_CASE(LD, LT, SD, STY, W)                                             \
+    if (logits_dtype == LD && scores_dtype == SD) {                                    \
+        f = reinterpret_cast<const void*>(&moe_route_kernel<LT, STY>);                 \
+        which = W;                                                                      \
+    }
+    MLXQ_ROUTE_CASE(kF32, float, kBF16, __nv_bfloat16, 0)
+    MLXQ_ROUTE_CASE(kF32, float, kF16, __half, 1)
+    MLXQ_ROUTE_CASE(kF32, float, kF32, float, 2)
+    MLXQ_ROUTE_CASE(kBF16, __nv_bfloat16, kBF16, __nv_bfloat16, 3)
+    MLXQ_ROUTE_CASE(kBF16, __nv_bfloat16, kF16, __half, 4)
+    MLXQ_ROUTE_CASE(kBF16, __nv_bfloat16, kF32, float, 5)
+    MLXQ_ROUTE_CASE(kF16, __half, kBF16, __nv_bfloat16, 6)
+    MLXQ_ROUTE_CASE(kF16, __half, kF16, __half, 7)
+    MLXQ_ROUTE_CASE(kF16, __half, kF32, float, 8)
+#undef MLXQ_ROUTE_CASE
+    if (!f) return cudaErrorInvalidValue;
+    const int warps_per_cta = 4;
+    return launch_ex(f, cfg[which], dim3((T + warps_per_cta - 1) / warps_per_cta),
+                     dim3(32 * warps_per_cta), 0, st, overlap, args);
 }
 
 // ------------------------------------------------------------------------------------

@@ -32,6 +32,9 @@ cudaError_t launch_attn_prefill(int dtype, const void* q, const int32_t* cu_q, i
 cudaError_t launch_embed(int dtype, int bits, const int32_t* ids, int n, const uint32_t* wq,
                          const void* scales, const void* biases, void* out, int vocab, int K,
                          int gs, bool overlap, cudaStream_t st);
+cudaError_t launch_moe_route(int logits_dtype, const void* logits, const float* bias,
+                             int32_t* indices, int scores_dtype, void* scores, int T, int E, int K,
+                             int norm, bool overlap, cudaStream_t st);
 cudaError_t launch_decode_advance(int32_t* positions, int32_t* kv_lens, int32_t* slots,
                                   const int32_t* block_table, int max_blocks, int B, int page,
                                   bool overlap, cudaStream_t st);

@@ -341,19 +341,14 @@ class SwitchGLU(Module):
 
 def route_topk(logits: torch.Tensor, top_k: int, norm_topk_prob: bool = True,
                expert_bias: torch.Tensor | None = None):
-    """Top-k expert routing of an MoE layer (lfm2.py:366-373 of the reference):
-    softmax over the experts in float32, plus the optional per-expert bias, the
-    top_k experts per token (their order is not part of the contract: the
-    reference takes an argpartition), their gate values, renormalised to sum to
-    one when `norm_topk_prob` (with the reference's 1e-20 guard), cast back to
-    the logits' dtype. Returns (indices [.., top_k] int32, scores [.., top_k])."""
-    gates = torch.softmax(logits.float(), dim=-1)
-    if expert_bias is not None:
-        gates = gates + expert_bias.float()
-    scores, indices = torch.topk(gates, top_k, dim=-1)
-    if norm_topk_prob:
-        scores = scores / (scores.sum(dim=-1, keepdim=True) + 1e-20)
-    return indices.to(torch.int32), scores.to(logits.dtype)
+    """Top-k expert routing of an MoE layer (lfm2.py:366-373 of the reference), one
+    device kernel (core.moe_route): softmax over the experts in float32, plus the
+    optional per-expert bias, the top_k experts per token (their order is not part of
+    the contract: the reference takes an argpartition), their gate values,
+    renormalised to sum to one when `norm_topk_prob` (with the reference's 1e-20
+    guard), cast back to the logits' dtype. Returns (indices [.., top_k] int32,
+    scores [.., top_k])."""
+    return core.moe_route(logits, top_k, norm_topk_prob, expert_bias)
 
 
 class MoEBlock(Module):

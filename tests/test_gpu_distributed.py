@@ -1,6 +1,7 @@
 """Two-GPU NCCL tests of the sharded forms with the CUDA operators as the
 per-rank compute: N-sharded QuantizedLinear + all-gather, and the
-expert-parallel SwitchGLU. Checked against the oracle within the matmul
+expert-parallel SwitchGLU (NCCL all-to-all dispatch and combine). Both are
+checked against the CPU oracle (numpy and C restatements) within the matmul
 tolerance. Skipped with fewer than two GPUs."""
 import os
 import socket
@@ -36,7 +37,7 @@ def _worker(rank, world, port, q):
         from mlx_server_runtime_b200.distributed import (ExpertParallelSwitchGLU,
                                                          ShardedQuantizedLinear)
         from gpu_util import close, rand_weights, rand_x, to_dev, to_np
-        from oracle import oracle_np
+        from oracle import coracle, oracle_np
 
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
@@ -73,18 +74,20 @@ def _worker(rank, world, port, q):
         moe = ExpertParallelSwitchGLU(*local, num_experts=E, group_size=64, bits=4)
         got = moe(to_dev(x_np, "bfloat16", dev), torch.from_numpy(idx_np).to(dev))
         torch.cuda.synchronize()
-        # reference: the same expert chain on this rank's GPU without any exchange
-        x_d = to_dev(x_np, "bfloat16", dev)
-        ref = torch.empty(T, k, D, dtype=torch.bfloat16, device=dev)
-        for t in range(T):
-            for j in range(k):
-                e = int(idx_np[t, j])
-                g = mxq.quantized_matmul(x_d[t:t + 1], *(a[e] for a in full[0]), group_size=64)
-                u = mxq.quantized_matmul(x_d[t:t + 1], *(a[e] for a in full[1]), group_size=64)
-                h = torch.nn.functional.silu(g) * u
-                ref[t, j] = mxq.quantized_matmul(h, *(a[e] for a in full[2]), group_size=64)[0]
-        torch.cuda.synchronize()
-        close(to_np(got), to_np(ref), "bfloat16")
+        # reference: the C oracle over the same full expert weights, per (token, expert)
+        # row: silu(gate) rounded, times up rounded, then down (lfm2.py:193-218)
+        host = [tuple(to_np(a) for a in t) for t in full]
+        flat = idx_np.reshape(-1)
+        lhs = np.repeat(np.arange(T, dtype=np.int32), k)
+        xs = x_np.reshape(T, 1, D)
+        g = oracle_np.to_f32(coracle.gather_qmm(xs, *host[0], flat, "bfloat16", 64, 4, lhs=lhs),
+                             "bfloat16")
+        u = oracle_np.to_f32(coracle.gather_qmm(xs, *host[1], flat, "bfloat16", 64, 4, lhs=lhs),
+                             "bfloat16")
+        act = oracle_np.round_to(g / (1.0 + np.exp(-g)), "bfloat16")
+        h = oracle_np.from_f32(act * u, "bfloat16")
+        ref = coracle.gather_qmm(h, *host[2], flat, "bfloat16", 64, 4).reshape(T, k, D)
+        close(to_np(got), ref, "bfloat16")
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, True, ""))

@@ -109,19 +109,8 @@ def test_assign_rejects_mismatch_and_strays(tmp_path):
         loader.assign_weights(m, missing)
 
 
-def test_route_topk_matches_softmax_topk_renorm():
-    rng = np.random.default_rng(3)
-    logits = rng.standard_normal((16, 128)).astype(np.float32)
-    bias = rng.standard_normal(128).astype(np.float32) * 0.01
-    for norm in (True, False):
-        idx, sc = nn.route_topk(torch.from_numpy(logits), 8, norm, torch.from_numpy(bias))
-        e = np.exp(logits - logits.max(-1, keepdims=True))
-        p = e / e.sum(-1, keepdims=True) + bias
-        top = np.argsort(-p, axis=-1)[:, :8]
-        for r in range(16):
-            assert set(idx[r].tolist()) == set(top[r].tolist())
-            ref = p[r, idx[r].numpy()]
-            if norm:
-                ref = ref / (ref.sum() + 1e-20)
-            np.testing.assert_allclose(sc[r].numpy(), ref, rtol=1e-5, atol=1e-7)
-    assert idx.dtype == torch.int32
+def test_route_topk_runs_on_the_device_only():
+    """The router is a device kernel (core.moe_route; its parity test is
+    tests/test_gpu_router.py): host tensors are refused, as every operator here does."""
+    with pytest.raises(ValueError, match="CUDA"):
+        nn.route_topk(torch.zeros(4, 16), 2)
