@@ -177,7 +177,7 @@ int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const 
  * (qwen2.py:225-227, executor.py:406-414). Here each logit is rounded to `dtype`
  * (plus bias) exactly as mlxq_quantized_matmul would write it, and ids[t] (int32,
  * t < M) receives the index of the largest, the first one on ties. Decode shapes
- * only (M <= 8, K/group_size a multiple of 8). The workspace
+ * only (M <= 16, K/group_size a multiple of 8). The workspace
  * (mlxq_argmax_workspace_size bytes, at least 64 KiB, zero-filled once) is left
  * zeroed again, like mlxq_quantized_matmul's; calls that overlap on the GPU must
  * not share it.
@@ -198,7 +198,7 @@ int mlxq_quantized_matmul_argmax(const void* x, const uint32_t* w, const void* s
  * tile j = gate rows 8j..8j+7 then up rows 8j..8j+7 (quantized rows copied as they
  * are; mlx_server_runtime_b200.interleave_gate_up builds it). N = 2 * intermediate
  * (a multiple of 16); out [M, N/2] = silu(g) * u with g, u each rounded to `dtype`
- * first, as the two separate matmuls would be. Decode shapes only: M <= 8 and
+ * first, as the two separate matmuls would be. Decode shapes only: M <= 16 and
  * K/group_size a multiple of 8 (mlxq_swiglu_supported says so); workspace as
  * mlxq_qmm_workspace_size(M, N, K, ...).
  */

@@ -305,7 +305,7 @@ def quantized_matmul_swiglu(x: torch.Tensor, w: torch.Tensor, scales: torch.Tens
                             mode: str = "affine") -> torch.Tensor:
     """silu(x @ gate^T) * (x @ up^T) from interleave_gate_up's layout: [..., N/2].
 
-    Decode shapes (up to 8 rows, K/group_size a multiple of 8) run as one launch
+    Decode shapes (up to 16 rows, K/group_size a multiple of 8) run as one launch
     with the activation in the matmul's epilogue; other shapes run
     quantized_matmul and then the activation as torch element-wise ops. Either
     way each projection is rounded to x's dtype before silu(g) * u is formed in
@@ -351,7 +351,7 @@ def quantized_matmul_argmax(x: torch.Tensor, w: torch.Tensor, scales: torch.Tens
     """Greedy next tokens: argmax over N of quantized_matmul(x, w, ...) (+ bias),
     int32 [...], the first index on ties, without writing the logits.
 
-    Decode shapes (up to 8 rows, K/group_size a multiple of 8) run as one launch
+    Decode shapes (up to 16 rows, K/group_size a multiple of 8) run as one launch
     with the argmax in the matmul's epilogue; other shapes compute the logits and
     take torch.argmax. The logits compared are the ones quantized_matmul returns
     (rounded to x's dtype), so both forms pick the same token. `out` (int32, the

@@ -269,7 +269,7 @@ int mlxq_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
     mlxq::QtPlan tplan;
     if (mlxq::qmv_tma_plan(dtype, bits, group_size, static_cast<int>(M), static_cast<int>(N),
                            static_cast<int>(K), di.num_sms, di.max_smem, di.sm_smem, &tplan)) {
-        // decode, M <= 8: TMA-fed stream-K kernel
+        // decode, M <= 16: TMA-fed stream-K kernel
         if (tplan.ws_bytes > 0) {
             if (!workspace || workspace_bytes < tplan.ws_bytes)
                 return fail(MLXQ_ERR_WORKSPACE,
@@ -350,7 +350,7 @@ int mlxq_quantized_matmul_swiglu(const void* x, const uint32_t* w, const void* s
     if (!mlxq::qmv_tma_plan(dtype, bits, group_size, static_cast<int>(M), static_cast<int>(N),
                             static_cast<int>(K), di.num_sms, di.max_smem, di.sm_smem, &tplan))
         return fail(MLXQ_ERR_SHAPE,
-                    "quantized_matmul_swiglu: decode shapes only (M <= 8, K/group_size a "
+                    "quantized_matmul_swiglu: decode shapes only (M <= 16, K/group_size a "
                     "multiple of 8); see mlxq_swiglu_supported");
     if (tplan.ws_bytes > 0) {
         if (!workspace || workspace_bytes < tplan.ws_bytes)
@@ -405,7 +405,7 @@ int mlxq_quantized_matmul_argmax(const void* x, const uint32_t* w, const void* s
     if (!mlxq::qmv_tma_plan(dtype, bits, group_size, static_cast<int>(M), static_cast<int>(N),
                             static_cast<int>(K), di.num_sms, di.max_smem, di.sm_smem, &tplan))
         return fail(MLXQ_ERR_SHAPE,
-                    "quantized_matmul_argmax: decode shapes only (M <= 8, K/group_size a "
+                    "quantized_matmul_argmax: decode shapes only (M <= 16, K/group_size a "
                     "multiple of 8)");
     const size_t need = tplan.ws_bytes > mlxq::kTicketBytes ? tplan.ws_bytes : mlxq::kTicketBytes;
     if (!workspace || workspace_bytes < need)

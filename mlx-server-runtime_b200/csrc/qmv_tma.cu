@@ -151,7 +151,8 @@ bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms,
         case 1: return qt_launch_t<T, BITS, GS, 1, BR, H, EPI>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
         case 2: return qt_launch_t<T, BITS, GS, 2, BR, H, EPI>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
         case 4: return qt_launch_t<T, BITS, GS, 4, BR, H, EPI>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
-        default: return qt_launch_t<T, BITS, GS, 8, BR, H, EPI>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
+        case 8: return qt_launch_t<T, BITS, GS, 8, BR, H, EPI>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
+        default: return qt_launch_t<T, BITS, GS, 16, BR, H, EPI>(tw, ts, tb, p, plan.P, plan.smem, overlap, st); \
     }
 #define QT_CASE_SW(T, BITS, GS, EPI)                                           \
     if (plan.BR == 16) { QT_CASE_TM(T, BITS, GS, 16, false, EPI) }             \

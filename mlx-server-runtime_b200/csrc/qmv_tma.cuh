@@ -36,9 +36,9 @@
 //     f16, so bf16 activations use the cheaper f16 extraction too. A record
 //     {sum x, sum offset * x 2^e, 2^-e} per slice turns the MMA result D into
 //       acc += (scale * 2^-e) * (D - sum offset * x 2^e) + bias * sum x.
-//     The token count is a compile-time slot count TM in {1, 2, 4, 8} (M rounded
-//     up; absent tokens are zero), so every shared-memory address in the main
-//     loop is a per-lane base plus a constant.
+//     The token count is a compile-time slot count TM in {1, 2, 4, 8, 16} (M
+//     rounded up; absent tokens are zero; 16 slots are two MMA n-tiles of 8), so
+//     every shared-memory address in the main loop is a per-lane base plus a constant.
 // Every wait is bounded: a timeout records an error in *p.err, sets a CTA-wide
 // abort flag that turns the remaining waits and all global writes off, and
 // lets every warp run to the end (so the named barriers still meet).
@@ -69,7 +69,7 @@ struct Rows {
     static constexpr int KSW = CWARPS / RT;
     static constexpr int GPW = SG / KSW;
 };
-constexpr int MAXM = 8;                  // tokens per launch
+constexpr int MAXM = 16;                 // tokens per launch
 constexpr int MAX_STAGES = 16;
 constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr int kErrTimeout = 2;
@@ -78,9 +78,11 @@ constexpr uint32_t kTicketParkNs = 1000;
 constexpr uint32_t kTicketParkLimit = 1u << 20;
 
 // Token slots a kernel instance is compiled for; M is rounded up to one of them.
+// An MMA covers 8 token slots: 16 slots take two MMA n-tiles per weight fragment.
 __host__ __device__ constexpr int token_slots(int M) {
-    return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8;
+    return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : M <= 8 ? 8 : 16;
 }
+__host__ __device__ constexpr int n_tiles(int TM) { return TM > 8 ? TM / 8 : 1; }
 
 // Bytes one stage's TMA copies deliver (packed codes, scales, biases) and the
 // stage's stride in the ring (rounded up to the 1024-byte period of the 128-byte
@@ -119,7 +121,7 @@ __host__ __device__ inline Layout layout(int stage_bytes, int stages, int G, int
     L.xf = stages * stage_bytes;               // [G][FR/4][TM][4 lanes] x 16 B
     L.rec = L.xf + G * TM * xg;                // [G][TM] float4 records
     L.red = L.rec + G * TM * 16;               // cross-warp reduction
-    L.bars = (L.red + (CWARPS - rt) * 4 * 32 * 4 + 7) & ~7;
+    L.bars = (L.red + (CWARPS - rt) * n_tiles(TM) * 4 * 32 * 4 + 7) & ~7;
     // full[stages], empty[stages], head_done, ticket_done
     L.flags = (L.bars + (2 * stages + 2) * 8 + 15) & ~15;  // abort, last, head_last
     L.best = L.flags + 16;                                  // argmax: best key per token
@@ -209,6 +211,8 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
     constexpr int STAGE = GEO::STAGE, W_BYTES = GEO::W_BYTES, SB_BYTES = GEO::SB_BYTES;
     constexpr int RT = Rows<BR>::RT, KSW = Rows<BR>::KSW, GPW = Rows<BR>::GPW;
     constexpr bool ODD = TM > 1;
+    constexpr int NT = n_tiles(TM);           // MMA n-tiles of 8 token slots
+    constexpr int TS = TM < 8 ? TM : 8;       // token slots of one n-tile
 
     extern __shared__ __align__(16) uint8_t qt_smem_raw[];
     // 1024-byte aligned base (128-byte swizzled TMA boxes), derived from the shared
@@ -495,10 +499,11 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
     const int sb_sh = GPW == 1 ? 16 * (kq & 1) : 0;
     //   the B fragments of token slot r (lanes past the last slot repeat a slot:
     //   their MMA columns are never read),
-    const int tr = r & (TM - 1);
+    //   (n-tile nt's slots are 8 nt.. : its fragments sit 8 * 64 bytes further)
+    const int tr = r & (TS - 1);
     const uint8_t* xl = xf + (tr * 4 + c) * 16 + GPW * kq * TM * XG;
     //   and the records of tokens 2c, 2c+1 (wrapped into the slots likewise).
-    const float4* rl = rec + ((2 * c) & (TM - 1)) + GPW * kq * TM;
+    const float4* rl = rec + ((2 * c) & (TS - 1)) + GPW * kq * TM;
 
     // Last contributor to row block rb_: adds the contributors' fp32 partials in CTA
     // order, writes the outputs and re-arms the ticket.
@@ -551,7 +556,9 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
         const int rb = static_cast<int>(u / S);
         const int st0 = static_cast<int>(u % S);
         const int st_end = static_cast<int>(st0 + (u_hi - u) < S ? st0 + (u_hi - u) : S);
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        float acc[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
         // local position of stage st0 in the staged ranges: range a holds stages
         // ga0/SG.., range b (a share that wraps into the next row block) stages 0..
         const int lst = st0 >= ga0 / SG ? st0 - ga0 / SG : na / SG + st0;
@@ -602,10 +609,13 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
                     EH::template extract<BITS>(wa[w], ta[w], magic_a, magic_b);
                     EH::template extract<BITS>(wb[w], tb[w], magic_a, magic_b);
                 }
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
                 uint32_t X[FR];
 #pragma unroll
                 for (int f = 0; f < FR / 4; ++f) {
-                    const uint4 v = *reinterpret_cast<const uint4*>(xs + h * TM * XG + f * TM * 64);
+                    const uint4 v = *reinterpret_cast<const uint4*>(xs + h * TM * XG + f * TM * 64 +
+                                                                    nt * 8 * 64);
                     X[4 * f + 0] = v.x; X[4 * f + 1] = v.y;
                     X[4 * f + 2] = v.z; X[4 * f + 3] = v.w;
                 }
@@ -632,14 +642,15 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
                                          X[2 * w + 1]);
                     }
                 }
-                // fold this group into tokens 2c, 2c+1 of rows r, r+8
-                const float4 q0 = rs[h * TM];
-                acc[0] = fmaf(s0 * q0.z, d[0] - q0.y, fmaf(b0, q0.x, acc[0]));
-                acc[2] = fmaf(s1 * q0.z, d[2] - q0.y, fmaf(b1, q0.x, acc[2]));
+                // fold this group into tokens 8 nt + 2c, 8 nt + 2c + 1 of rows r, r+8
+                const float4 q0 = rs[h * TM + 8 * nt];
+                acc[nt][0] = fmaf(s0 * q0.z, d[0] - q0.y, fmaf(b0, q0.x, acc[nt][0]));
+                acc[nt][2] = fmaf(s1 * q0.z, d[2] - q0.y, fmaf(b1, q0.x, acc[nt][2]));
                 if constexpr (ODD) {
-                    const float4 q1 = rs[h * TM + 1];
-                    acc[1] = fmaf(s0 * q1.z, d[1] - q1.y, fmaf(b0, q1.x, acc[1]));
-                    acc[3] = fmaf(s1 * q1.z, d[3] - q1.y, fmaf(b1, q1.x, acc[3]));
+                    const float4 q1 = rs[h * TM + 8 * nt + 1];
+                    acc[nt][1] = fmaf(s0 * q1.z, d[1] - q1.y, fmaf(b0, q1.x, acc[nt][1]));
+                    acc[nt][3] = fmaf(s1 * q1.z, d[3] - q1.y, fmaf(b1, q1.x, acc[nt][3]));
+                }
                 }
             }
             __syncwarp();
@@ -655,17 +666,21 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
         // ---- combine the four group-interleaved warps of each row tile (fixed order)
         named_bar_sync(1, CTHREADS);
         if (kq > 0) {
-            float* dst = red + ((kq - 1) * RT + rt) * 4 * 32 + lane;
+            float* dst = red + ((kq - 1) * RT + rt) * NT * 4 * 32 + lane;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) dst[e * 32] = acc[e];
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) dst[(nt * 4 + e) * 32] = acc[nt][e];
         }
         named_bar_sync(1, CTHREADS);
         if (kq == 0) {
 #pragma unroll
             for (int h = 1; h < KSW; ++h) {
-                const float* src = red + ((h - 1) * RT + rt) * 4 * 32 + lane;
+                const float* src = red + ((h - 1) * RT + rt) * NT * 4 * 32 + lane;
 #pragma unroll
-                for (int e = 0; e < 4; ++e) acc[e] += src[e * 32];
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) acc[nt][e] += src[(nt * 4 + e) * 32];
             }
         }
         const bool abort = *s_abort != 0;
@@ -673,15 +688,17 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
         if (st0 == 0 && st_end == S) {
             // the whole row block is this CTA's: write the outputs
             if (kq == 0 && !abort) {
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) {
                 if constexpr (EPI == 2) {
 #pragma unroll
                     for (int hh = 0; hh < 2; ++hh) {
                         const int n = row0 + 16 * rt + r + 8 * hh;
 #pragma unroll
                         for (int q = 0; q < 2; ++q) {
-                            const int t = 2 * c + q;
+                            const int t = 8 * nt + 2 * c + q;
                             if (t < M && n < N) {
-                                T y = ET::from_f(acc[2 * hh + q]);
+                                T y = ET::from_f(acc[nt][2 * hh + q]);
                                 if (biasg) y = ET::from_f(ET::to_f(y) + ET::to_f(biasg[n]));
                                 atomicMax(s_best + t, argmax_key(ET::to_f(y), n));
                             }
@@ -692,10 +709,10 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
                     const int n = (row0 + 16 * rt) / 2 + r;
 #pragma unroll
                     for (int q = 0; q < 2; ++q) {
-                        const int t = 2 * c + q;
+                        const int t = 8 * nt + 2 * c + q;
                         if (t < M && 2 * n < N)
                             og[static_cast<long long>(t) * (N / 2) + n] =
-                                swiglu_out<T>(acc[q], acc[2 + q]);
+                                swiglu_out<T>(acc[nt][q], acc[nt][2 + q]);
                     }
                 } else {
 #pragma unroll
@@ -703,15 +720,16 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
                         const int n = row0 + 16 * rt + r + 8 * hh;
 #pragma unroll
                         for (int q = 0; q < 2; ++q) {
-                            const int t = 2 * c + q;
+                            const int t = 8 * nt + 2 * c + q;
                             if (t < M && n < N) {
-                                T y = ET::from_f(acc[2 * hh + q]);
+                                T y = ET::from_f(acc[nt][2 * hh + q]);
                                 if (biasg) y = ET::from_f(ET::to_f(y) + ET::to_f(biasg[n]));
                                 og[static_cast<long long>(t) * N + n] = y;
                             }
                         }
                     }
                 }
+              }
             }
         } else {
             // part of a row block: fp32 partial, then the last contributor reduces
@@ -720,12 +738,15 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
             float* part = p.partial + static_cast<long long>(rb) * p.maxc * M * BR;
             if (kq == 0 && !abort) {
 #pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
                 for (int hh = 0; hh < 2; ++hh) {
                     const int rw = 16 * rt + r + 8 * hh;
 #pragma unroll
                     for (int q = 0; q < 2; ++q) {
-                        const int t = 2 * c + q;
-                        if (t < M && row0 + rw < N) part[(ci * M + t) * BR + rw] = acc[2 * hh + q];
+                        const int t = 8 * nt + 2 * c + q;
+                        if (t < M && row0 + rw < N)
+                            part[(ci * M + t) * BR + rw] = acc[nt][2 * hh + q];
                     }
                 }
             }

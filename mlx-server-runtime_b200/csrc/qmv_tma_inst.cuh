@@ -38,7 +38,8 @@ cudaError_t qt_launch_t(const CUtensorMap& tw, const CUtensorMap& ts, const CUte
     MLXQ_QT_INST0(T, BITS, GS, 1, BR, H, EPI)  \
     MLXQ_QT_INST0(T, BITS, GS, 2, BR, H, EPI)  \
     MLXQ_QT_INST0(T, BITS, GS, 4, BR, H, EPI)  \
-    MLXQ_QT_INST0(T, BITS, GS, 8, BR, H, EPI)
+    MLXQ_QT_INST0(T, BITS, GS, 8, BR, H, EPI)  \
+    MLXQ_QT_INST0(T, BITS, GS, 16, BR, H, EPI)
 
 // Every (bits, group size) the plan accepts, for activation type T, BR-row units,
 // ticket warp or not, and plain or SwiGLU epilogue.

@@ -22,7 +22,8 @@ def _weights(rng, N, K, dt="bfloat16", gs=64, bits=4):
 
 
 @pytest.mark.parametrize("N,K,M", [(152064, 3584, 1), (152064, 3584, 8), (9473, 3584, 3),
-                                   (512, 3584, 2), (3584, 18944, 1), (1000, 1536, 5)])
+                                   (512, 3584, 2), (3584, 18944, 1), (1000, 1536, 5),
+                                   (152064, 3584, 16), (9473, 3584, 11)])
 def test_argmax_equals_argmax_of_logits(N, K, M):
     rng = np.random.default_rng(N + K + M)
     wq, s, b = _weights(rng, N, K)

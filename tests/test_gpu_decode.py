@@ -30,14 +30,14 @@ def _case(dt, bits, gs, M, N, K, seed, bias=False, calls=1):
     return [to_np(y) for y in outs]
 
 
-@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 6, 7, 8])
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 6, 7, 8, 9, 12, 16])
 def test_decode_token_counts(M):
     _case("bfloat16", 4, 64, M, 3584, 3584, seed=100 + M)
 
 
 @pytest.mark.parametrize("dt", ["bfloat16", "float16"])
 @pytest.mark.parametrize("bits,gs", [(4, 32), (4, 64), (4, 128), (8, 32), (8, 64)])
-@pytest.mark.parametrize("M", [1, 3, 8])
+@pytest.mark.parametrize("M", [1, 3, 8, 13, 16])
 def test_decode_types_and_groups(dt, bits, gs, M):
     _case(dt, bits, gs, M, 1000, 8 * gs * 3, seed=bits * 1000 + gs + M)
 

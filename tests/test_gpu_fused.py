@@ -72,7 +72,7 @@ def _swiglu_ref(x, gate, up, dt, gs, bits):
 
 # (intermediate I, K): k/v-like (16-row CTAs), gate-like, down-like K (split row blocks)
 @pytest.mark.parametrize("I,K", [(256, 3584), (18944, 3584), (1792, 18944), (200, 1024)])
-@pytest.mark.parametrize("M", [1, 3, 8, 40])
+@pytest.mark.parametrize("M", [1, 3, 8, 11, 16, 40])
 def test_swiglu_matches_oracle(I, K, M):
     dt, gs, bits = "bfloat16", 64, 4
     rng = np.random.default_rng(I + K + M)
