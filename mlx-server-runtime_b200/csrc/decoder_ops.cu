@@ -244,24 +244,27 @@ cudaError_t launch_rope_append(int dtype, const void* qkv, int ld, void* q_out, 
 
 // ------------------------------------------------------------------------------------
 // Decode attention: one query token per sequence. CTA (split s, kv head g, sequence
-// b) takes keys [s*SK, min((s+1)*SK, L_b)) of the sequence's L_b cached keys and the
-// G = Hq/Hkv query heads that share kv head g:
-//   load    the split's key and value rows, gathered from the pages with cp.async
+// b) takes a contiguous range of the sequence's L_b cached keys (tps tiles of SK keys;
+// at most 64 splits per sequence) and the G = Hq/Hkv query heads that share kv head g.
+// Per tile of SK keys:
+//   load    the tile's key and value rows, gathered from the pages with cp.async
 //           into shared memory (16-byte chunks XOR-swizzled by row, so reading one
-//           chunk of consecutive rows is conflict free); every load is in flight at
-//           once, values land while the scores are computed
+//           chunk of consecutive rows is conflict free); values land while the
+//           scores are computed
 //   scores  thread (key j, head half): dot products of key j with its heads'
 //           prescaled queries
-//   softmax per head over the split's keys (max, exp2, sum)
-//   values  thread (dimension pair, key range): sum over its keys of p * v, the key
-//           ranges then added in a fixed order
-// A sequence with one split writes its outputs; otherwise each split stores its
-// (max, sum, unnormalised output) and the last split to finish (acquire-release
-// ticket per (b, g), zero between calls) merges them in split order.
+//   softmax per head, online across the tiles (running max and sum, exp2)
+//   values  thread (dimension pair, key range): its keys' p * v added to its running
+//           output, rescaled when the running max moves
+// The key ranges are then added in a fixed order. A sequence with one split writes
+// its outputs; otherwise each split stores its (max, sum, unnormalised output) and
+// the last split to finish (acquire-release ticket per (b, g), zero between calls)
+// merges them in split order.
 namespace attn {
-constexpr int SK = 64;        // keys per split
+constexpr int SK = 64;        // keys per tile
 constexpr int THREADS = 128;
 constexpr int MAXG = 8;       // query heads per kv head
+constexpr int MAXSPLIT = 64;  // splits per sequence
 }  // namespace attn
 
 template <int HD>
@@ -277,7 +280,7 @@ __global__ void __launch_bounds__(attn::THREADS)
                        int max_blocks, const int32_t* __restrict__ kv_lens, T* __restrict__ out,
                        int Hq, int Hkv, int page, float scale_log2, float* __restrict__ ws_o,
                        float2* __restrict__ ws_ml, unsigned* __restrict__ tickets,
-                       int max_splits, int max_kv) {
+                       int max_splits, int max_kv, int tps) {
     using namespace attn;
     static_assert(HD == 64 || HD == 128, "head_dim");
     constexpr int CH = HD / 8;             // 16-byte chunks per row
@@ -291,26 +294,27 @@ __global__ void __launch_bounds__(attn::THREADS)
     __shared__ __align__(16) float qs[MAXG][HD];
     __shared__ __align__(16) float ps[MAXG][SK];
     __shared__ __align__(16) float xch[(KPH - 1) * MAXG * HD];
-    __shared__ float mls[2][MAXG];
+    __shared__ float mrun[MAXG], lrun[MAXG], corr[MAXG];
+    __shared__ float mw[MAXG][MAXSPLIT], lw[MAXG][MAXSPLIT];
+    __shared__ int pid[SK / 8 + 2];
     __shared__ int s_last;
     pdl_launch_dependents();
     pdl_wait();
     const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int G = Hq / Hkv;
     const int L = min(kv_lens[b], max_kv);  // max_kv <= the block table's reach
-    const int nsplit = (L + SK - 1) / SK;
+    const int skeys = tps * SK;             // keys per split
+    const int nsplit = (L + skeys - 1) / skeys;
     if (split >= nsplit) return;
-    const int k0 = split * SK;
-    const int n = min(SK, L - k0);
+    const int ks0 = split * skeys, ke = min(L, ks0 + skeys);
+    const int ntile = (ke - ks0 + SK - 1) / SK;
     const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
     const int32_t* bt = block_table + static_cast<size_t>(b) * max_blocks;
-    // the split's page ids and the queries, each in one round of loads
-    __shared__ int pid[SK / 8 + 2];
-    const int p0 = k0 / page;
-    const int np = (k0 + n - 1) / page - p0 + 1;
-    if (tid < np) pid[tid] = bt[p0 + tid];
-    {
-        const uint4* qsrc = reinterpret_cast<const uint4*>(q + (static_cast<size_t>(b) * Hq + g * G) * HD);
+
+    {  // the queries, prescaled, in one round of loads
+        const uint4* qsrc =
+            reinterpret_cast<const uint4*>(q + (static_cast<size_t>(b) * Hq + g * G) * HD);
         for (int c = tid; c < G * HD / 8; c += THREADS) {
             const uint4 v = qsrc[c];
             const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
@@ -322,125 +326,145 @@ __global__ void __launch_bounds__(attn::THREADS)
                 qs[h][d + 2 * e + 1] = f.y * scale_log2;
             }
         }
-    }
-    __syncthreads();
-    // keys, then values: rows past n are zero-filled (their source stays in bounds)
-    for (int pass = 0; pass < 2; ++pass) {
-        const T* src = pass == 0 ? k_cache : v_cache;
-        uint8_t* dst = pass == 0 ? ks : vs;
-#pragma unroll 4
-        for (int c = tid; c < SK * CH; c += THREADS) {
-            const int r = c / CH, ch = c % CH;
-            const bool ok = r < n;
-            const int key = ok ? k0 + r : k0;
-            const size_t row = static_cast<size_t>(pid[key / page - p0]) * page + key % page;
-            cp_async16(dst + kv_swz<HD>(r, ch), src + (row * Hkv + g) * HD + ch * 8, ok ? 16 : 0);
-        }
-        cp_async_commit();
-    }
-    cp_async_wait<1>();
-    __syncthreads();
-
-    // scores: thread (key j, heads HPT*hh ..)
-    {
-        const int j = tid % SK, hh = tid / SK;
-        float acc[HPT];
-#pragma unroll
-        for (int k = 0; k < HPT; ++k) acc[k] = 0.f;
-        const uint32_t kb = smem_u32(ks);
-#pragma unroll 4
-        for (int c = 0; c < CH; ++c) {
-            uint32_t w0, w1, w2, w3;
-            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
-                         : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
-                         : "r"(kb + kv_swz<HD>(j, c)));
-            const uint32_t kw[4] = {w0, w1, w2, w3};
-            float kf[8];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float2 f = unpack2<T>(kw[e]);
-                kf[2 * e] = f.x;
-                kf[2 * e + 1] = f.y;
-            }
-#pragma unroll
-            for (int k = 0; k < HPT; ++k) {
-                const int h = hh * HPT + k;
-                if (h < G) {
-                    const float4 qa = *reinterpret_cast<const float4*>(&qs[h][8 * c]);
-                    const float4 qb = *reinterpret_cast<const float4*>(&qs[h][8 * c + 4]);
-                    acc[k] = fmaf(qa.x, kf[0], acc[k]);
-                    acc[k] = fmaf(qa.y, kf[1], acc[k]);
-                    acc[k] = fmaf(qa.z, kf[2], acc[k]);
-                    acc[k] = fmaf(qa.w, kf[3], acc[k]);
-                    acc[k] = fmaf(qb.x, kf[4], acc[k]);
-                    acc[k] = fmaf(qb.y, kf[5], acc[k]);
-                    acc[k] = fmaf(qb.z, kf[6], acc[k]);
-                    acc[k] = fmaf(qb.w, kf[7], acc[k]);
-                }
-            }
-        }
-#pragma unroll
-        for (int k = 0; k < HPT; ++k)
-            if (hh * HPT + k < G) ps[hh * HPT + k][j] = acc[k];
-    }
-    __syncthreads();
-    // softmax over this split's keys, one warp per head (base 2: scores carry log2 e);
-    // probabilities of keys past n are zero
-    const int warp = tid >> 5, lane = tid & 31;
-    for (int h = warp; h < G; h += THREADS / 32) {
-        float m = -INFINITY;
-        for (int j = lane; j < n; j += 32) m = fmaxf(m, ps[h][j]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float l = 0.f;
-        for (int j = lane; j < SK; j += 32) {
-            const float p = j < n ? exp2f(ps[h][j] - m) : 0.f;
-            ps[h][j] = p;
-            l += p;
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-        if (lane == 0) {
-            mls[0][h] = m;
-            mls[1][h] = l;
+        if (tid < MAXG) {
+            mrun[tid] = -INFINITY;
+            lrun[tid] = 0.f;
         }
     }
-    cp_async_wait<0>();
-    __syncthreads();
-    // values: thread (dimension pair dp, key range kr)
     const int dp = tid % DP, kr = tid / DP;
     float o[MAXG][2];
 #pragma unroll
     for (int h = 0; h < MAXG; ++h) o[h][0] = o[h][1] = 0.f;
-    {
-        const uint32_t vb = smem_u32(vs);
-#pragma unroll
-        for (int j4 = 0; j4 < KPR; j4 += 4) {
-            float2 v[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int j = kr * KPR + j4 + e;
-                uint32_t u;
-                asm volatile("ld.shared.u32 %0, [%1];\n"
-                             : "=r"(u)
-                             : "r"(vb + kv_swz<HD>(j, dp >> 2) + (dp & 3) * 4));
-                v[e] = unpack2<T>(u);
+
+    for (int tile = 0; tile < ntile; ++tile) {
+        const int k0 = ks0 + tile * SK;
+        const int n = min(SK, ke - k0);
+        const int p0 = k0 / page;
+        const int np = (k0 + n - 1) / page - p0 + 1;
+        if (tid < np) pid[tid] = bt[p0 + tid];
+        __syncthreads();
+        // keys, then values: rows past n are zero-filled (their source stays in bounds)
+        for (int pass = 0; pass < 2; ++pass) {
+            const T* src = pass == 0 ? k_cache : v_cache;
+            uint8_t* dst = pass == 0 ? ks : vs;
+#pragma unroll 4
+            for (int c = tid; c < SK * CH; c += THREADS) {
+                const int r = c / CH, ch = c % CH;
+                const bool ok = r < n;
+                const int key = ok ? k0 + r : k0;
+                const size_t row = static_cast<size_t>(pid[key / page - p0]) * page + key % page;
+                cp_async16(dst + kv_swz<HD>(r, ch), src + (row * Hkv + g) * HD + ch * 8,
+                           ok ? 16 : 0);
             }
+            cp_async_commit();
+        }
+        cp_async_wait<1>();
+        __syncthreads();
+        {  // scores: thread (key j, heads HPT*hh ..)
+            const int j = tid % SK, hh = tid / SK;
+            float acc[HPT];
+#pragma unroll
+            for (int k = 0; k < HPT; ++k) acc[k] = 0.f;
+            const uint32_t kb = smem_u32(ks);
+#pragma unroll 4
+            for (int c = 0; c < CH; ++c) {
+                uint32_t w0, w1, w2, w3;
+                asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                             : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
+                             : "r"(kb + kv_swz<HD>(j, c)));
+                const uint32_t kw[4] = {w0, w1, w2, w3};
+                float kf[8];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = unpack2<T>(kw[e]);
+                    kf[2 * e] = f.x;
+                    kf[2 * e + 1] = f.y;
+                }
+#pragma unroll
+                for (int k = 0; k < HPT; ++k) {
+                    const int h = hh * HPT + k;
+                    if (h < G) {
+                        const float4 qa = *reinterpret_cast<const float4*>(&qs[h][8 * c]);
+                        const float4 qb = *reinterpret_cast<const float4*>(&qs[h][8 * c + 4]);
+                        acc[k] = fmaf(qa.x, kf[0], acc[k]);
+                        acc[k] = fmaf(qa.y, kf[1], acc[k]);
+                        acc[k] = fmaf(qa.z, kf[2], acc[k]);
+                        acc[k] = fmaf(qa.w, kf[3], acc[k]);
+                        acc[k] = fmaf(qb.x, kf[4], acc[k]);
+                        acc[k] = fmaf(qb.y, kf[5], acc[k]);
+                        acc[k] = fmaf(qb.z, kf[6], acc[k]);
+                        acc[k] = fmaf(qb.w, kf[7], acc[k]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < HPT; ++k)
+                if (hh * HPT + k < G) ps[hh * HPT + k][j] = acc[k];
+        }
+        __syncthreads();
+        // online softmax, one warp per head (base 2: scores carry log2 e); keys past n
+        // get probability zero
+        for (int h = warp; h < G; h += THREADS / 32) {
+            float m = mrun[h];
+            for (int j = lane; j < n; j += 32) m = fmaxf(m, ps[h][j]);
+#pragma unroll
+            for (int o2 = 16; o2 > 0; o2 >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o2));
+            float l = 0.f;
+            for (int j = lane; j < SK; j += 32) {
+                const float pj = j < n ? exp2f(ps[h][j] - m) : 0.f;
+                ps[h][j] = pj;
+                l += pj;
+            }
+#pragma unroll
+            for (int o2 = 16; o2 > 0; o2 >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o2);
+            if (lane == 0) {
+                const float c = exp2f(mrun[h] - m);  // 0 on the first tile (mrun = -inf)
+                corr[h] = c;
+                lrun[h] = lrun[h] * c + l;
+                mrun[h] = m;
+            }
+        }
+        cp_async_wait<0>();
+        __syncthreads();
+        {  // values
+            const uint32_t vb = smem_u32(vs);
 #pragma unroll
             for (int h = 0; h < MAXG; ++h) {
                 if (h < G) {
-                    const float4 p4 = *reinterpret_cast<const float4*>(&ps[h][kr * KPR + j4]);
-                    o[h][0] = fmaf(p4.x, v[0].x, o[h][0]);
-                    o[h][1] = fmaf(p4.x, v[0].y, o[h][1]);
-                    o[h][0] = fmaf(p4.y, v[1].x, o[h][0]);
-                    o[h][1] = fmaf(p4.y, v[1].y, o[h][1]);
-                    o[h][0] = fmaf(p4.z, v[2].x, o[h][0]);
-                    o[h][1] = fmaf(p4.z, v[2].y, o[h][1]);
-                    o[h][0] = fmaf(p4.w, v[3].x, o[h][0]);
-                    o[h][1] = fmaf(p4.w, v[3].y, o[h][1]);
+                    const float c = corr[h];
+                    o[h][0] *= c;
+                    o[h][1] *= c;
+                }
+            }
+#pragma unroll
+            for (int j4 = 0; j4 < KPR; j4 += 4) {
+                float2 v[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int j = kr * KPR + j4 + e;
+                    uint32_t u;
+                    asm volatile("ld.shared.u32 %0, [%1];\n"
+                                 : "=r"(u)
+                                 : "r"(vb + kv_swz<HD>(j, dp >> 2) + (dp & 3) * 4));
+                    v[e] = unpack2<T>(u);
+                }
+#pragma unroll
+                for (int h = 0; h < MAXG; ++h) {
+                    if (h < G) {
+                        const float4 p4 = *reinterpret_cast<const float4*>(&ps[h][kr * KPR + j4]);
+                        o[h][0] = fmaf(p4.x, v[0].x, o[h][0]);
+                        o[h][1] = fmaf(p4.x, v[0].y, o[h][1]);
+                        o[h][0] = fmaf(p4.y, v[1].x, o[h][0]);
+                        o[h][1] = fmaf(p4.y, v[1].y, o[h][1]);
+                        o[h][0] = fmaf(p4.z, v[2].x, o[h][0]);
+                        o[h][1] = fmaf(p4.z, v[2].y, o[h][1]);
+                        o[h][0] = fmaf(p4.w, v[3].x, o[h][0]);
+                        o[h][1] = fmaf(p4.w, v[3].y, o[h][1]);
+                    }
                 }
             }
         }
+        __syncthreads();  // the tile's buffers are refilled next iteration
     }
     // key ranges 1.. hand their sums to range 0, which adds them in range order
     // (every loop over heads has compile-time bounds, so o stays in registers)
@@ -449,7 +473,7 @@ __global__ void __launch_bounds__(attn::THREADS)
         for (int h = 0; h < MAXG; ++h)
             if (h < G)
                 *reinterpret_cast<float2*>(&xch[((kr - 1) * MAXG + h) * HD + 2 * dp]) =
-                make_float2(o[h][0], o[h][1]);
+                    make_float2(o[h][0], o[h][1]);
     }
     __syncthreads();
     if (kr > 0) return;
@@ -458,7 +482,8 @@ __global__ void __launch_bounds__(attn::THREADS)
 #pragma unroll
         for (int h = 0; h < MAXG; ++h) {
             if (h >= G) continue;
-            const float2 x = *reinterpret_cast<const float2*>(&xch[((r - 1) * MAXG + h) * HD + 2 * dp]);
+            const float2 x =
+                *reinterpret_cast<const float2*>(&xch[((r - 1) * MAXG + h) * HD + 2 * dp]);
             o[h][0] += x.x;
             o[h][1] += x.y;
         }
@@ -466,7 +491,7 @@ __global__ void __launch_bounds__(attn::THREADS)
 #pragma unroll
         for (int h = 0; h < MAXG; ++h) {
             if (h >= G) continue;
-            const float inv = 1.0f / mls[1][h];
+            const float inv = 1.0f / lrun[h];
             *reinterpret_cast<uint32_t*>(out + (static_cast<size_t>(b) * Hq + g * G + h) * HD +
                                          2 * dp) = pack2<T>(o[h][0] * inv, o[h][1] * inv);
         }
@@ -478,8 +503,8 @@ __global__ void __launch_bounds__(attn::THREADS)
     for (int h = 0; h < MAXG; ++h)
         if (h < G)
             *reinterpret_cast<float2*>(&ws_o[((base + split) * MAXG + h) * HD + 2 * dp]) =
-            make_float2(o[h][0], o[h][1]);
-    if (tid < G) ws_ml[(base + split) * MAXG + tid] = make_float2(mls[0][tid], mls[1][tid]);
+                make_float2(o[h][0], o[h][1]);
+    if (tid < G) ws_ml[(base + split) * MAXG + tid] = make_float2(mrun[tid], lrun[tid]);
     // A barrier of the range-0 threads orders their partials before thread 0's acq_rel
     // ticket, whose release publishes them GPU-wide and whose acquire (with the second
     // barrier) makes the other splits' partials visible to these threads.
@@ -489,21 +514,43 @@ __global__ void __launch_bounds__(attn::THREADS)
                  static_cast<unsigned>(nsplit - 1);
     named_bar_sync(1, DP);
     if (!s_last) return;
-    for (int h = 0; h < G; ++h) {
+    // The last split merges all of them: every split's (max, sum) per head is read into
+    // shared memory at once, turned into the splits' weights exp2(m_s - M), then each
+    // thread reads its dimension pair of every split's outputs, loads in flight together.
+    for (int e = tid; e < G * nsplit; e += DP) {
+        const int h = e / nsplit, sp = e % nsplit;
+        const float2 ml = __ldcg(&ws_ml[(base + sp) * MAXG + h]);
+        mw[h][sp] = ml.x;
+        lw[h][sp] = ml.y;
+    }
+    named_bar_sync(1, DP);
+    for (int h = tid; h < G; h += DP) {
         float M = -INFINITY;
-        for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(&ws_ml[(base + sp) * MAXG + h]).x);
-        float n0 = 0.f, n1 = 0.f, den = 0.f;
+        for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, mw[h][sp]);
+        float den = 0.f;
         for (int sp = 0; sp < nsplit; ++sp) {
-            const float2 ml = __ldcg(&ws_ml[(base + sp) * MAXG + h]);
-            const float c = exp2f(ml.x - M);
+            const float c = exp2f(mw[h][sp] - M);
+            mw[h][sp] = c;
+            den = fmaf(c, lw[h][sp], den);
+        }
+        lrun[h] = 1.0f / den;
+    }
+    named_bar_sync(1, DP);
+#pragma unroll
+    for (int h = 0; h < MAXG; ++h) {
+        if (h >= G) continue;
+        float n0 = 0.f, n1 = 0.f;
+#pragma unroll 4
+        for (int sp = 0; sp < nsplit; ++sp) {
             const float2 v = __ldcg(reinterpret_cast<const float2*>(
                 &ws_o[((base + sp) * MAXG + h) * HD + 2 * dp]));
+            const float c = mw[h][sp];
             n0 = fmaf(c, v.x, n0);
             n1 = fmaf(c, v.y, n1);
-            den = fmaf(c, ml.y, den);
         }
+        const float inv = lrun[h];
         *reinterpret_cast<uint32_t*>(out + (static_cast<size_t>(b) * Hq + g * G + h) * HD +
-                                     2 * dp) = pack2<T>(n0 / den, n1 / den);
+                                     2 * dp) = pack2<T>(n0 * inv, n1 * inv);
     }
     if (tid == 0) tickets[b * Hkv + g] = 0u;
 }
@@ -707,8 +754,18 @@ __global__ void __launch_bounds__(pf::THREADS)
     }
 }
 
+// Tiles of SK keys per split: one until a sequence would need more than MAXSPLIT splits.
+static int attn_tiles_per_split(int max_kv_len) {
+    const int tiles = (max_kv_len + attn::SK - 1) / attn::SK;
+    return (tiles + attn::MAXSPLIT - 1) / attn::MAXSPLIT;
+}
+static int attn_splits(int max_kv_len) {
+    const int keys = attn_tiles_per_split(max_kv_len) * attn::SK;
+    return (max_kv_len + keys - 1) / keys;
+}
+
 size_t attn_decode_workspace(int B, int Hkv, int max_kv_len, int head_dim) {
-    const int splits = (max_kv_len + attn::SK - 1) / attn::SK;
+    const int splits = attn_splits(max_kv_len);
     if (splits <= 1) return 0;
     const size_t tickets = (static_cast<size_t>(B) * Hkv * 4 + 255) / 256 * 256;
     const size_t parts = static_cast<size_t>(B) * Hkv * splits * attn::MAXG;
@@ -719,7 +776,8 @@ cudaError_t launch_attn_decode(int dtype, const void* q, const void* k_cache, co
                                const int32_t* block_table, int max_blocks, const int32_t* kv_lens,
                                int max_kv_len, void* out, int B, int Hq, int Hkv, int hd, int page,
                                float scale, void* workspace, bool overlap, cudaStream_t st) {
-    const int splits = (max_kv_len + attn::SK - 1) / attn::SK;
+    const int splits = attn_splits(max_kv_len);
+    int tps = attn_tiles_per_split(max_kv_len);
     float scale_log2 = scale * 1.4426950408889634f;
     unsigned* tickets = nullptr;
     float* ws_o = nullptr;
@@ -735,7 +793,7 @@ cudaError_t launch_attn_decode(int dtype, const void* q, const void* k_cache, co
     int max_splits = splits;
     void* args[] = {&q, &k_cache, &v_cache, &block_table, &max_blocks, &kv_lens, &out,
                     &Hq, &Hkv, &page, &scale_log2, &ws_o, &ws_ml, &tickets, &max_splits,
-                    &max_kv_len};
+                    &max_kv_len, &tps};
     const void* f = nullptr;
     if (dtype == kBF16)
         f = hd == 128 ? reinterpret_cast<const void*>(&attn_decode_kernel<__nv_bfloat16, 128>)

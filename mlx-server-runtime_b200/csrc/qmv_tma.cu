@@ -93,6 +93,10 @@ bool qmv_tma_plan(int dtype, int bits, int gs, int M, int N, int K, int num_sms,
     if (!br)
         br = ((N + 15) / 16 <= kCtasPerSm * num_sms && G / qt::SG <= kWholeRowBlockStages)
                  ? 16 : 64;
+    // 16 token slots stage twice the activations of 8: a 16-row plan (one CTA per row
+    // block) then fits one CTA per SM, so it is taken only when its row blocks fit on
+    // the SMs at that (else the cp.async kernel is faster for these shapes).
+    if (TM > 8 && br == 16 && (N + 15) / 16 > num_sms) return false;
     const int rt = br / 16;
     const int stage = qt::stage_stride(bits, gs, br);
     QtPlan pl{};

@@ -78,11 +78,14 @@ def _paged_problem(rng, B, hkv, hd, kv_lens, page=16, dt="bfloat16"):
     return bt, kpool, vpool
 
 
-@pytest.mark.parametrize("hq,hkv,hd", [(28, 4, 128), (8, 2, 64), (4, 4, 128)])
-def test_paged_attention_decode(hq, hkv, hd):
+@pytest.mark.parametrize("hq,hkv,hd,long", [(28, 4, 128, False), (8, 2, 64, False),
+                                            (4, 4, 128, False), (28, 4, 128, True)])
+def test_paged_attention_decode(hq, hkv, hd, long):
     dt = "bfloat16"
-    rng = np.random.default_rng(hq * hd)
+    rng = np.random.default_rng(hq * hd + long)
     kv_lens = np.array([1, 17, 128, 129, 300, 640, 511, 64], np.int32)
+    if long:  # more than 64 tiles of 64 keys: several tiles per split
+        kv_lens = np.array([5000, 4097, 1, 300], np.int32)
     B = len(kv_lens)
     bt, kpool, vpool = _paged_problem(rng, B, hkv, hd, kv_lens)
     q = rand_x(rng, (B, hq, hd), dt)
