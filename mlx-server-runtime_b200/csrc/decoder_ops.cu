@@ -243,34 +243,30 @@ cudaError_t launch_rope_append(int dtype, const void* qkv, int ld, void* q_out, 
 }
 
 // ------------------------------------------------------------------------------------
-// Decode attention: one query token per sequence. CTA (split s, kv head g, sequence
-// b) takes a contiguous range of the sequence's L_b cached keys (tps tiles of SK keys;
-// at most 64 splits per sequence) and the G = Hq/Hkv query heads that share kv head g.
-// Per tile of SK keys:
-//   load    the tile's key and value rows, gathered from the pages with cp.async
-//           into shared memory (16-byte chunks XOR-swizzled by row, so reading one
-//           chunk of consecutive rows is conflict free); values land while the
-//           scores are computed
-//   scores  thread (key j, head half): dot products of key j with its heads'
-//           prescaled queries
-//   softmax per head, online across the tiles (running max and sum, exp2)
-//   values  thread (dimension pair, key range): its keys' p * v added to its running
-//           output, rescaled when the running max moves
-// The key ranges are then added in a fixed order. A sequence with one split writes
-// its outputs; otherwise each split stores its (max, sum, unnormalised output) and
-// the last split to finish (acquire-release ticket per (b, g), zero between calls)
-// merges them in split order.
+// Decode attention on the tensor cores: one query token per sequence. CTA (split s,
+// kv head g, sequence b) takes a contiguous range of the sequence's L_b cached keys
+// (tps tiles of 64 keys; at most 64 splits per sequence) and the G = Hq/Hkv <= 8 query
+// heads sharing kv head g, which are the rows of the m16n8k16 MMAs (rows G..15 zero).
+// Per tile, the key and value rows are gathered from the pages with cp.async into
+// shared memory (16-byte chunks XOR-swizzled by row: ldmatrix reads are conflict
+// free); warp w owns keys 16w..16w+15 of every tile:
+//   S = Q K^T      2 n-tiles of 8 keys x 8 k-steps of 16 dimensions (fp32)
+//   softmax        online per row over the warp's keys (running max, sum; exp2)
+//   O += P V       P stays in registers as the A operand, V read transposed
+// The 4 warps' (max, sum, O) are merged in shared memory. A sequence with one split
+// writes its outputs; otherwise each split stores its (max, sum, unnormalised output)
+// and the last split to finish (acquire-release ticket per (b, g), zero between
+// calls) merges them in split order.
 namespace attn {
 constexpr int SK = 64;        // keys per tile
-constexpr int THREADS = 128;
+constexpr int THREADS = 128;  // 4 warps x 16 keys
 constexpr int MAXG = 8;       // query heads per kv head
 constexpr int MAXSPLIT = 64;  // splits per sequence
 }  // namespace attn
 
 template <int HD>
 __device__ __forceinline__ uint32_t kv_swz(int row, int chunk) {
-    constexpr int CH = HD / 8;
-    return static_cast<uint32_t>(row * (HD * 2) + ((chunk ^ (row & (CH - 1))) << 4));
+    return static_cast<uint32_t>(row * (HD * 2) + ((chunk ^ (row & 7)) << 4));
 }
 
 template <typename T, int HD>
@@ -283,21 +279,17 @@ __global__ void __launch_bounds__(attn::THREADS)
                        int max_splits, int max_kv, int tps) {
     using namespace attn;
     static_assert(HD == 64 || HD == 128, "head_dim");
-    constexpr int CH = HD / 8;             // 16-byte chunks per row
-    constexpr int DP = HD / 2;             // dimension pairs
-    constexpr int KPH = THREADS / DP;      // key ranges of the value pass (2 or 4)
-    constexpr int KPR = SK / KPH;          // keys per range
-    constexpr int HH = THREADS / SK;       // head halves of the score pass (2)
-    constexpr int HPT = MAXG / HH;         // heads per score thread (4)
-    __shared__ __align__(16) uint8_t ks[SK * HD * 2];
-    __shared__ __align__(16) uint8_t vs[SK * HD * 2];
-    __shared__ __align__(16) float qs[MAXG][HD];
-    __shared__ __align__(16) float ps[MAXG][SK];
-    __shared__ __align__(16) float xch[(KPH - 1) * MAXG * HD];
-    __shared__ float mrun[MAXG], lrun[MAXG], corr[MAXG];
+    constexpr int CH = HD / 8;            // 16-byte chunks per row
+    constexpr int NW = THREADS / 32;      // warps
+    constexpr int DPT = HD / 16;          // dimensions per thread in the merges (8 or 4)
+    __shared__ __align__(128) uint8_t qsm[16 * HD * 2];
+    __shared__ __align__(128) uint8_t kv[2 * SK * HD * 2];  // keys, values; then warp O
+    __shared__ float wm[NW][MAXG], wl[NW][MAXG];
     __shared__ float mw[MAXG][MAXSPLIT], lw[MAXG][MAXSPLIT];
+    __shared__ float cinv[MAXG];
     __shared__ int pid[SK / 8 + 2];
     __shared__ int s_last;
+    static_assert(NW * MAXG * HD * 4 <= 2 * SK * HD * 2, "warp outputs fit the tile buffer");
     pdl_launch_dependents();
     pdl_wait();
     const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
@@ -308,249 +300,212 @@ __global__ void __launch_bounds__(attn::THREADS)
     if (split >= nsplit) return;
     const int ks0 = split * skeys, ke = min(L, ks0 + skeys);
     const int ntile = (ke - ks0 + SK - 1) / SK;
-    const int tid = threadIdx.x;
-    const int warp = tid >> 5, lane = tid & 31;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int32_t* bt = block_table + static_cast<size_t>(b) * max_blocks;
+    uint8_t* ksm = kv;
+    uint8_t* vsm = kv + SK * HD * 2;
 
-    {  // the queries, prescaled, in one round of loads
-        const uint4* qsrc =
-            reinterpret_cast<const uint4*>(q + (static_cast<size_t>(b) * Hq + g * G) * HD);
-        for (int c = tid; c < G * HD / 8; c += THREADS) {
-            const uint4 v = qsrc[c];
-            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-            const int h = (8 * c) / HD, d = (8 * c) % HD;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float2 f = unpack2<T>(w4[e]);
-                qs[h][d + 2 * e] = f.x * scale_log2;
-                qs[h][d + 2 * e + 1] = f.y * scale_log2;
-            }
-        }
-        if (tid < MAXG) {
-            mrun[tid] = -INFINITY;
-            lrun[tid] = 0.f;
-        }
+    // queries: rows = the group's heads, rows G..15 zero
+    for (int c = tid; c < 16 * CH; c += THREADS) {
+        const int r = c / CH, ch = c % CH;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (r < G)
+            v = *reinterpret_cast<const uint4*>(
+                q + (static_cast<size_t>(b) * Hq + g * G + r) * HD + ch * 8);
+        *reinterpret_cast<uint4*>(qsm + kv_swz<HD>(r, ch)) = v;
     }
-    const int dp = tid % DP, kr = tid / DP;
-    float o[MAXG][2];
+    __syncthreads();
+    uint32_t qa[HD / 16][4];
+    {
+        const uint32_t qb = smem_u32(qsm);
+        const int r = lane & 15;
 #pragma unroll
-    for (int h = 0; h < MAXG; ++h) o[h][0] = o[h][1] = 0.f;
+        for (int kk = 0; kk < HD / 16; ++kk)
+            ldmatrix_x4(qb + kv_swz<HD>(r, 2 * kk + (lane >> 4)), qa[kk][0], qa[kk][1],
+                        qa[kk][2], qa[kk][3]);
+    }
+    float o[HD / 8][4];
+#pragma unroll
+    for (int j = 0; j < HD / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float mrow = -INFINITY, lrow = 0.f;  // row lane/4 (a head); rows 8.. are padding
 
     for (int tile = 0; tile < ntile; ++tile) {
         const int k0 = ks0 + tile * SK;
         const int n = min(SK, ke - k0);
         const int p0 = k0 / page;
         const int np = (k0 + n - 1) / page - p0 + 1;
+        if (tile > 0) __syncthreads();  // the previous tile's buffers are free
         if (tid < np) pid[tid] = bt[p0 + tid];
         __syncthreads();
-        // keys, then values: rows past n are zero-filled (their source stays in bounds)
-        for (int pass = 0; pass < 2; ++pass) {
-            const T* src = pass == 0 ? k_cache : v_cache;
-            uint8_t* dst = pass == 0 ? ks : vs;
 #pragma unroll 4
-            for (int c = tid; c < SK * CH; c += THREADS) {
-                const int r = c / CH, ch = c % CH;
-                const bool ok = r < n;
-                const int key = ok ? k0 + r : k0;
-                const size_t row = static_cast<size_t>(pid[key / page - p0]) * page + key % page;
-                cp_async16(dst + kv_swz<HD>(r, ch), src + (row * Hkv + g) * HD + ch * 8,
-                           ok ? 16 : 0);
-            }
-            cp_async_commit();
+        for (int c = tid; c < SK * CH; c += THREADS) {
+            const int r = c / CH, ch = c % CH;
+            const bool ok = r < n;
+            const int key = ok ? k0 + r : k0;
+            const size_t row = static_cast<size_t>(pid[key / page - p0]) * page + key % page;
+            const size_t off = (row * Hkv + g) * HD + ch * 8;
+            cp_async16(ksm + kv_swz<HD>(r, ch), k_cache + off, ok ? 16 : 0);
+            cp_async16(vsm + kv_swz<HD>(r, ch), v_cache + off, ok ? 16 : 0);
         }
-        cp_async_wait<1>();
-        __syncthreads();
-        {  // scores: thread (key j, heads HPT*hh ..)
-            const int j = tid % SK, hh = tid / SK;
-            float acc[HPT];
-#pragma unroll
-            for (int k = 0; k < HPT; ++k) acc[k] = 0.f;
-            const uint32_t kb = smem_u32(ks);
-#pragma unroll 4
-            for (int c = 0; c < CH; ++c) {
-                uint32_t w0, w1, w2, w3;
-                asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
-                             : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
-                             : "r"(kb + kv_swz<HD>(j, c)));
-                const uint32_t kw[4] = {w0, w1, w2, w3};
-                float kf[8];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 f = unpack2<T>(kw[e]);
-                    kf[2 * e] = f.x;
-                    kf[2 * e + 1] = f.y;
-                }
-#pragma unroll
-                for (int k = 0; k < HPT; ++k) {
-                    const int h = hh * HPT + k;
-                    if (h < G) {
-                        const float4 qa = *reinterpret_cast<const float4*>(&qs[h][8 * c]);
-                        const float4 qb = *reinterpret_cast<const float4*>(&qs[h][8 * c + 4]);
-                        acc[k] = fmaf(qa.x, kf[0], acc[k]);
-                        acc[k] = fmaf(qa.y, kf[1], acc[k]);
-                        acc[k] = fmaf(qa.z, kf[2], acc[k]);
-                        acc[k] = fmaf(qa.w, kf[3], acc[k]);
-                        acc[k] = fmaf(qb.x, kf[4], acc[k]);
-                        acc[k] = fmaf(qb.y, kf[5], acc[k]);
-                        acc[k] = fmaf(qb.z, kf[6], acc[k]);
-                        acc[k] = fmaf(qb.w, kf[7], acc[k]);
-                    }
-                }
-            }
-#pragma unroll
-            for (int k = 0; k < HPT; ++k)
-                if (hh * HPT + k < G) ps[hh * HPT + k][j] = acc[k];
-        }
-        __syncthreads();
-        // online softmax, one warp per head (base 2: scores carry log2 e); keys past n
-        // get probability zero
-        for (int h = warp; h < G; h += THREADS / 32) {
-            float m = mrun[h];
-            for (int j = lane; j < n; j += 32) m = fmaxf(m, ps[h][j]);
-#pragma unroll
-            for (int o2 = 16; o2 > 0; o2 >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o2));
-            float l = 0.f;
-            for (int j = lane; j < SK; j += 32) {
-                const float pj = j < n ? exp2f(ps[h][j] - m) : 0.f;
-                ps[h][j] = pj;
-                l += pj;
-            }
-#pragma unroll
-            for (int o2 = 16; o2 > 0; o2 >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o2);
-            if (lane == 0) {
-                const float c = exp2f(mrun[h] - m);  // 0 on the first tile (mrun = -inf)
-                corr[h] = c;
-                lrun[h] = lrun[h] * c + l;
-                mrun[h] = m;
-            }
-        }
+        cp_async_commit();
         cp_async_wait<0>();
         __syncthreads();
-        {  // values
-            const uint32_t vb = smem_u32(vs);
+        // S = Q K^T over this warp's 16 keys
+        float sc[2][4];
 #pragma unroll
-            for (int h = 0; h < MAXG; ++h) {
-                if (h < G) {
-                    const float c = corr[h];
-                    o[h][0] *= c;
-                    o[h][1] *= c;
-                }
-            }
+        for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+        const uint32_t kb = smem_u32(ksm), vb = smem_u32(vsm);
 #pragma unroll
-            for (int j4 = 0; j4 < KPR; j4 += 4) {
-                float2 v[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int j = kr * KPR + j4 + e;
-                    uint32_t u;
-                    asm volatile("ld.shared.u32 %0, [%1];\n"
-                                 : "=r"(u)
-                                 : "r"(vb + kv_swz<HD>(j, dp >> 2) + (dp & 3) * 4));
-                    v[e] = unpack2<T>(u);
-                }
-#pragma unroll
-                for (int h = 0; h < MAXG; ++h) {
-                    if (h < G) {
-                        const float4 p4 = *reinterpret_cast<const float4*>(&ps[h][kr * KPR + j4]);
-                        o[h][0] = fmaf(p4.x, v[0].x, o[h][0]);
-                        o[h][1] = fmaf(p4.x, v[0].y, o[h][1]);
-                        o[h][0] = fmaf(p4.y, v[1].x, o[h][0]);
-                        o[h][1] = fmaf(p4.y, v[1].y, o[h][1]);
-                        o[h][0] = fmaf(p4.z, v[2].x, o[h][0]);
-                        o[h][1] = fmaf(p4.z, v[2].y, o[h][1]);
-                        o[h][0] = fmaf(p4.w, v[3].x, o[h][0]);
-                        o[h][1] = fmaf(p4.w, v[3].y, o[h][1]);
-                    }
-                }
-            }
+        for (int kk = 0; kk < HD / 16; ++kk) {
+            const int r = warp * 16 + (lane & 7) + ((lane >> 4) << 3);
+            uint32_t b0, b1, b2, b3;
+            ldmatrix_x4(kb + kv_swz<HD>(r, 2 * kk + ((lane >> 3) & 1)), b0, b1, b2, b3);
+            mma16816<T>(sc[0], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b0, b1);
+            mma16816<T>(sc[1], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b2, b3);
         }
-        __syncthreads();  // the tile's buffers are refilled next iteration
-    }
-    // key ranges 1.. hand their sums to range 0, which adds them in range order
-    // (every loop over heads has compile-time bounds, so o stays in registers)
-    if (kr > 0) {
+        // mask the tile's tail, scale (base 2), online softmax of row lane/4
+        float mnew = mrow;
 #pragma unroll
-        for (int h = 0; h < MAXG; ++h)
-            if (h < G)
-                *reinterpret_cast<float2*>(&xch[((kr - 1) * MAXG + h) * HD + 2 * dp]) =
-                    make_float2(o[h][0], o[h][1]);
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int key = warp * 16 + nt * 8 + 2 * (lane & 3) + e;
+                sc[nt][e] = key < n ? sc[nt][e] * scale_log2 : -INFINITY;
+                mnew = fmaxf(mnew, sc[nt][e]);
+            }
+        mnew = fmaxf(mnew, __shfl_xor_sync(0xffffffffu, mnew, 1));
+        mnew = fmaxf(mnew, __shfl_xor_sync(0xffffffffu, mnew, 2));
+        const float mref = mnew == -INFINITY ? 0.f : mnew;
+        const float corr = exp2f(mrow - mref);
+        mrow = mnew;
+        lrow *= corr;
+        uint32_t pa[4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+            const float p0v = exp2f(sc[nt][0] - mref), p1v = exp2f(sc[nt][1] - mref);
+            lrow += p0v + p1v;
+            pa[2 * nt] = pack2<T>(p0v, p1v);
+            pa[2 * nt + 1] = 0u;  // rows 8..15 (padding) carry nothing
+        }
+#pragma unroll
+        for (int j = 0; j < HD / 8; ++j) {
+            o[j][0] *= corr;
+            o[j][1] *= corr;
+        }
+        // O += P V over this warp's 16 keys
+#pragma unroll
+        for (int dpp = 0; dpp < HD / 16; ++dpp) {
+            const int r = warp * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+            uint32_t b0, b1, b2, b3;
+            ldmatrix_x4_trans(vb + kv_swz<HD>(r, 2 * dpp + (lane >> 4)), b0, b1, b2, b3);
+            mma16816<T>(o[2 * dpp], pa[0], pa[1], pa[2], pa[3], b0, b1);
+            mma16816<T>(o[2 * dpp + 1], pa[0], pa[1], pa[2], pa[3], b2, b3);
+        }
+    }
+    // merge the warps: row sums, then (max, sum, O) of rows < G through shared memory
+    lrow += __shfl_xor_sync(0xffffffffu, lrow, 1);
+    lrow += __shfl_xor_sync(0xffffffffu, lrow, 2);
+    const int hr = lane >> 2;  // this lane's head row
+    if ((lane & 3) == 0 && hr < MAXG) {
+        wm[warp][hr] = mrow;
+        wl[warp][hr] = lrow;
+    }
+    __syncthreads();  // (the tile buffers are free from here: they hold the warps' O)
+    float* wo = reinterpret_cast<float*>(kv);  // [NW][MAXG][HD]
+    if (hr < G) {
+#pragma unroll
+        for (int j = 0; j < HD / 8; ++j)
+            *reinterpret_cast<float2*>(&wo[(warp * MAXG + hr) * HD + 8 * j + 2 * (lane & 3)]) =
+                make_float2(o[j][0], o[j][1]);
     }
     __syncthreads();
-    if (kr > 0) return;
+    // thread (head h, dimensions DPT*dd ..): the CTA's result for its slice
+    const int h = tid / (HD / DPT), dd = tid % (HD / DPT);
+    float res[DPT];
+    float Mc = -INFINITY, Lc = 0.f;
+    if (h < G) {
 #pragma unroll
-    for (int r = 1; r < KPH; ++r)
+        for (int w = 0; w < NW; ++w) Mc = fmaxf(Mc, wm[w][h]);
 #pragma unroll
-        for (int h = 0; h < MAXG; ++h) {
-            if (h >= G) continue;
-            const float2 x =
-                *reinterpret_cast<const float2*>(&xch[((r - 1) * MAXG + h) * HD + 2 * dp]);
-            o[h][0] += x.x;
-            o[h][1] += x.y;
+        for (int e = 0; e < DPT; ++e) res[e] = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            const float c = wm[w][h] == -INFINITY ? 0.f : exp2f(wm[w][h] - Mc);
+            Lc = fmaf(c, wl[w][h], Lc);
+#pragma unroll
+            for (int e = 0; e < DPT; ++e) res[e] = fmaf(c, wo[(w * MAXG + h) * HD + DPT * dd + e], res[e]);
         }
+    }
     if (nsplit == 1) {
+        if (h < G) {
+            const float inv = 1.0f / Lc;
+            T* dst = out + (static_cast<size_t>(b) * Hq + g * G + h) * HD + DPT * dd;
 #pragma unroll
-        for (int h = 0; h < MAXG; ++h) {
-            if (h >= G) continue;
-            const float inv = 1.0f / lrun[h];
-            *reinterpret_cast<uint32_t*>(out + (static_cast<size_t>(b) * Hq + g * G + h) * HD +
-                                         2 * dp) = pack2<T>(o[h][0] * inv, o[h][1] * inv);
+            for (int e = 0; e < DPT; e += 2)
+                *reinterpret_cast<uint32_t*>(dst + e) = pack2<T>(res[e] * inv, res[e + 1] * inv);
         }
         return;
     }
     // this split's partials: [b][g][split][h][HD] and (m, l) per head
     const size_t base = (static_cast<size_t>(b) * Hkv + g) * max_splits;
+    if (h < G) {
 #pragma unroll
-    for (int h = 0; h < MAXG; ++h)
-        if (h < G)
-            *reinterpret_cast<float2*>(&ws_o[((base + split) * MAXG + h) * HD + 2 * dp]) =
-                make_float2(o[h][0], o[h][1]);
-    if (tid < G) ws_ml[(base + split) * MAXG + tid] = make_float2(mrun[tid], lrun[tid]);
-    // A barrier of the range-0 threads orders their partials before thread 0's acq_rel
-    // ticket, whose release publishes them GPU-wide and whose acquire (with the second
-    // barrier) makes the other splits' partials visible to these threads.
-    named_bar_sync(1, DP);
+        for (int e = 0; e < DPT; ++e) ws_o[((base + split) * MAXG + h) * HD + DPT * dd + e] = res[e];
+        if (dd == 0) ws_ml[(base + split) * MAXG + h] = make_float2(Mc, Lc);
+    }
+    // The barrier orders every thread's partials before thread 0's acq_rel ticket,
+    // whose release publishes them GPU-wide and whose acquire (with the second barrier)
+    // makes the other splits' partials visible to this CTA.
+    __syncthreads();
     if (tid == 0)
         s_last = atom_add_acq_rel_gpu(tickets + b * Hkv + g, 1u) ==
                  static_cast<unsigned>(nsplit - 1);
-    named_bar_sync(1, DP);
+    __syncthreads();
     if (!s_last) return;
-    // The last split merges all of them: every split's (max, sum) per head is read into
-    // shared memory at once, turned into the splits' weights exp2(m_s - M), then each
-    // thread reads its dimension pair of every split's outputs, loads in flight together.
-    for (int e = tid; e < G * nsplit; e += DP) {
-        const int h = e / nsplit, sp = e % nsplit;
-        const float2 ml = __ldcg(&ws_ml[(base + sp) * MAXG + h]);
-        mw[h][sp] = ml.x;
-        lw[h][sp] = ml.y;
+    // The last split merges them: every split's (max, sum) per head into shared memory
+    // at once, turned into weights exp2(m_s - M); then each thread reads its slice of
+    // every split's outputs with the loads in flight together.
+    for (int e = tid; e < G * nsplit; e += THREADS) {
+        const int hh = e / nsplit, sp = e % nsplit;
+        const float2 ml = __ldcg(&ws_ml[(base + sp) * MAXG + hh]);
+        mw[hh][sp] = ml.x;
+        lw[hh][sp] = ml.y;
     }
-    named_bar_sync(1, DP);
-    for (int h = tid; h < G; h += DP) {
+    __syncthreads();
+    for (int hh = tid; hh < G; hh += THREADS) {
         float M = -INFINITY;
-        for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, mw[h][sp]);
+        for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, mw[hh][sp]);
         float den = 0.f;
         for (int sp = 0; sp < nsplit; ++sp) {
-            const float c = exp2f(mw[h][sp] - M);
-            mw[h][sp] = c;
-            den = fmaf(c, lw[h][sp], den);
+            const float c = exp2f(mw[hh][sp] - M);
+            mw[hh][sp] = c;
+            den = fmaf(c, lw[hh][sp], den);
         }
-        lrun[h] = 1.0f / den;
+        cinv[hh] = 1.0f / den;
     }
-    named_bar_sync(1, DP);
+    __syncthreads();
+    if (h < G) {
+        float acc[DPT];
 #pragma unroll
-    for (int h = 0; h < MAXG; ++h) {
-        if (h >= G) continue;
-        float n0 = 0.f, n1 = 0.f;
+        for (int e = 0; e < DPT; ++e) acc[e] = 0.f;
 #pragma unroll 4
         for (int sp = 0; sp < nsplit; ++sp) {
-            const float2 v = __ldcg(reinterpret_cast<const float2*>(
-                &ws_o[((base + sp) * MAXG + h) * HD + 2 * dp]));
             const float c = mw[h][sp];
-            n0 = fmaf(c, v.x, n0);
-            n1 = fmaf(c, v.y, n1);
+            const float* src = &ws_o[((base + sp) * MAXG + h) * HD + DPT * dd];
+#pragma unroll
+            for (int e = 0; e < DPT; e += 4) {
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(src + e));
+                acc[e] = fmaf(c, v.x, acc[e]);
+                acc[e + 1] = fmaf(c, v.y, acc[e + 1]);
+                acc[e + 2] = fmaf(c, v.z, acc[e + 2]);
+                acc[e + 3] = fmaf(c, v.w, acc[e + 3]);
+            }
         }
-        const float inv = lrun[h];
-        *reinterpret_cast<uint32_t*>(out + (static_cast<size_t>(b) * Hq + g * G + h) * HD +
-                                     2 * dp) = pack2<T>(n0 * inv, n1 * inv);
+        const float inv = cinv[h];
+        T* dst = out + (static_cast<size_t>(b) * Hq + g * G + h) * HD + DPT * dd;
+#pragma unroll
+        for (int e = 0; e < DPT; e += 2)
+            *reinterpret_cast<uint32_t*>(dst + e) = pack2<T>(acc[e] * inv, acc[e + 1] * inv);
     }
     if (tid == 0) tickets[b * Hkv + g] = 0u;
 }
