@@ -14,16 +14,15 @@
 // deterministic. When every row block fits on the SMs, each CTA takes one whole
 // row block instead and no ticket is needed.
 //
-// Per CTA: 8 warps, which fit twice on an SM next to the CTAs of the kernel before
-// or after (launch overlap then streams the next matmul's weights while this one
-// finishes).
-//   * Loads (thread 0): for every unit, 2-D TMA loads of the packed weights
-//     [BR rows x 128 B] per box (128-byte swizzle) plus one box each of scales and
-//     biases [BR rows x 8 groups], into a ring of `stages` slots with full/empty
-//     mbarriers. The first `stages` units are requested at kernel start, before the
-//     wait for the previous kernel; afterwards thread 0 refills the slot of the unit
-//     before the one its warp just finished, once every warp has released it. The
-//     ring holds most of the CTA's share, so nearly all of it is requested early.
+// Per CTA: one producer warp and 8 consumer warps (plus, in kernels built with
+// HEADS, a ticket warp: a share that starts inside a row block stores that head
+// row block's partials and goes on at once, while the ticket warp takes its
+// ticket; whether the CTA came last to it is read when the share is done).
+//   * Producer (one thread): for every unit, 2-D TMA loads of the packed
+//     weights [BR rows x 128 B] per box (128-byte swizzle) plus one box each of
+//     scales and biases [BR rows x 8 groups], into a ring of `stages` slots with
+//     full/empty mbarriers. The ring holds most of the CTA's share, so nearly
+//     all of it is requested from HBM at kernel start.
 //   * Consumers: warp (rt, kq) owns row tile rt (16 rows) and GPW groups, GPW*kq..,
 //     of every stage (64-row units: 4 row tiles x 2 warps of 4 groups; 16-row
 //     units: 1 row tile x 8 warps of 1 group). ldmatrix reads the swizzled tiles
@@ -40,9 +39,6 @@
 //     The token count is a compile-time slot count TM in {1, 2, 4, 8, 16} (M
 //     rounded up; absent tokens are zero; 16 slots are two MMA n-tiles of 8), so
 //     every shared-memory address in the main loop is a per-lane base plus a constant.
-// A share that starts inside a row block (its head row block, shared with the
-// previous CTA) stores that row block's partials and goes on; its ticket is taken
-// once the share is done, so no warp waits for the atomic mid-share.
 // Every wait is bounded: a timeout records an error in *p.err, sets a CTA-wide
 // abort flag that turns the remaining waits and all global writes off, and
 // lets every warp run to the end (so the named barriers still meet).
@@ -60,7 +56,8 @@ namespace qt {
 constexpr int SG = 8;                    // quantization groups per unit (stage)
 constexpr int CWARPS = 8;                // consumer warps
 constexpr int CTHREADS = CWARPS * 32;
-__host__ __device__ constexpr int threads(bool) { return CTHREADS; }
+// + producer warp (+ ticket warp in the kernels that hand off head tickets)
+__host__ __device__ constexpr int threads(bool heads) { return CTHREADS + (heads ? 64 : 32); }
 // Split of the 8 consumer warps over a unit of BR weight rows (64 or 16): RT
 // row tiles of 16 rows times KSW warps along K, each warp taking GPW of the
 // stage's 8 groups. Shorter units put more CTAs on a matrix with few rows and
@@ -76,6 +73,9 @@ constexpr int MAXM = 16;                 // tokens per launch
 constexpr int MAX_STAGES = 16;
 constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr int kErrTimeout = 2;
+// The ticket warp parks (suspend-time hint) while the consumers finish a head row block.
+constexpr uint32_t kTicketParkNs = 1000;
+constexpr uint32_t kTicketParkLimit = 1u << 20;
 
 // Token slots a kernel instance is compiled for; M is rounded up to one of them.
 // An MMA covers 8 token slots: 16 slots take two MMA n-tiles per weight fragment.
@@ -122,8 +122,8 @@ __host__ __device__ inline Layout layout(int stage_bytes, int stages, int G, int
     L.rec = L.xf + G * TM * xg;                // [G][TM] float4 records
     L.red = L.rec + G * TM * 16;               // cross-warp reduction
     L.bars = (L.red + (CWARPS - rt) * n_tiles(TM) * 4 * 32 * 4 + 7) & ~7;
-    // full[stages], empty[stages]
-    L.flags = (L.bars + 2 * stages * 8 + 15) & ~15;  // abort, last, head_last
+    // full[stages], empty[stages], head_done, ticket_done
+    L.flags = (L.bars + (2 * stages + 2) * 8 + 15) & ~15;  // abort, last, head_last
     L.best = L.flags + 16;                                  // argmax: best key per token
     L.total = L.best + MAXM * 8;
     return L;
@@ -226,6 +226,8 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
     float* red = reinterpret_cast<float*>(base + L.red);
     uint64_t* full = reinterpret_cast<uint64_t*>(base + L.bars);
     uint64_t* empty = full + stages;
+    uint64_t* head_done = empty + stages;
+    uint64_t* ticket_done = head_done + 1;
     volatile int* s_abort = reinterpret_cast<volatile int*>(base + L.flags);
     volatile int* s_last = s_abort + 1;
     volatile int* s_head_last = s_abort + 2;
@@ -235,10 +237,10 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
     const long long U = p.U;
     const int P = gridDim.x;
     const long long u_lo = U * blockIdx.x / P, u_hi = U * (blockIdx.x + 1) / P;
-    const int nu = static_cast<int>(u_hi - u_lo);  // units of this CTA's share
     // A share that starts inside a row block and runs past its end has a head row
-    // block shared with the previous CTA(s): its partials are stored when it is done
-    // and its ticket is taken after the rest of the share.
+    // block shared with the previous CTA(s). Its ticket is taken by the ticket warp
+    // while the consumers go on with the rest of the share; whether this CTA came
+    // last to it (and so reduces it) is looked at once the share is done.
     const int head_rb = static_cast<int>(u_lo / S);
     const bool has_head =
         HEADS && (u_lo % S) != 0 && u_hi > static_cast<long long>(head_rb + 1) * S;
@@ -247,6 +249,10 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
         for (int s = 0; s < stages; ++s) {
             mbar_init(smem_u32(full + s), 1);
             mbar_init(smem_u32(empty + s), CWARPS);
+        }
+        if constexpr (HEADS) {
+            mbar_init(smem_u32(head_done), CWARPS);
+            mbar_init(smem_u32(ticket_done), 1);
         }
         *s_abort = 0;
         *s_last = 0;
@@ -260,28 +266,73 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
     // every global write come after it.
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 
-    // unit j of the share (0-based) into ring slot j % stages (thread 0 only)
-    auto issue = [&](int j) {
-        const long long u = u_lo + j;
-        const int rb = static_cast<int>(u / S), st = static_cast<int>(u % S);
-        const int slot = j % stages;
-        const uint32_t dst = smem_u32(ring + slot * STAGE);
-        const uint32_t bar = smem_u32(full + slot);
-        mbar_arrive_expect_tx(bar, GEO::STAGE_TX);
+    if (warp == CWARPS) {
+        // ------------------------------ producer ------------------------------------
+        if (lane == 0) {
+            tma_prefetch_map(&tw);
+            tma_prefetch_map(&ts);
+            tma_prefetch_map(&tb);
+            uint32_t it = 0;
+            int slot = 0;
+            uint32_t phase = 0;  // parity of the empty-barrier phase to wait for
+            int rb = static_cast<int>(u_lo / S), st = static_cast<int>(u_lo % S);
+            for (long long u = u_lo; u < u_hi; ++u, ++it) {
+                if (it >= static_cast<uint32_t>(stages)) {
+                    if (*s_abort) break;
+                    if (!mbar_wait_bounded(smem_u32(empty + slot), phase, kSpinLimit)) {
+                        atomicCAS(p.err, 0, kErrTimeout);
+                        *s_abort = 1;
+                        break;
+                    }
+                }
+                const uint32_t dst = smem_u32(ring + slot * STAGE);
+                const uint32_t bar = smem_u32(full + slot);
+                mbar_arrive_expect_tx(bar, GEO::STAGE_TX);
 #pragma unroll
-        for (int b = 0; b < GEO::BOXES; ++b)
-            tma_load_2d(dst + b * (BR * 128), &tw, bar, (st * SG * WPG) + b * 32, rb * BR);
-        tma_load_2d(dst + W_BYTES, &ts, bar, st * SG, rb * BR);
-        tma_load_2d(dst + W_BYTES + SB_BYTES, &tb, bar, st * SG, rb * BR);
-    };
-    int issued = 0;  // units requested so far (thread 0's count)
-    if (threadIdx.x == 0) {
-        tma_prefetch_map(&tw);
-        tma_prefetch_map(&ts);
-        tma_prefetch_map(&tb);
-        const int first = nu < stages ? nu : stages;
-        for (int j = 0; j < first; ++j) issue(j);
-        issued = first;
+                for (int b = 0; b < GEO::BOXES; ++b)
+                    tma_load_2d(dst + b * (BR * 128), &tw, bar, (st * SG * WPG) + b * 32, rb * BR);
+                tma_load_2d(dst + W_BYTES, &ts, bar, st * SG, rb * BR);
+                tma_load_2d(dst + W_BYTES + SB_BYTES, &tb, bar, st * SG, rb * BR);
+                if (++slot == stages) {
+                    slot = 0;
+                    if (it >= static_cast<uint32_t>(stages)) phase ^= 1u;  // not after the first pass
+                }
+                if (++st == S) {
+                    st = 0;
+                    ++rb;
+                }
+            }
+            if (*s_abort) {
+                // let the copies already issued land before the CTA can exit
+                const uint32_t n = it < static_cast<uint32_t>(stages) ? it : stages;
+                for (uint32_t j = it - n; j < it; ++j)
+                    mbar_wait_bounded(smem_u32(full + j % stages), (j / stages) & 1, kSpinLimit);
+            }
+        }
+        return;
+    }
+    if (HEADS && warp == CWARPS + 1) {
+        // ---------------------------- ticket warp ------------------------------------
+        // Takes the head row block's ticket once every consumer warp has stored its
+        // partials (head_done), so the consumers never wait for the atomic's round trip.
+        if (lane == 0 && has_head) {
+            asm volatile("griddepcontrol.wait;\n" ::: "memory");
+            int last = 0;
+            if (!mbar_wait_park(smem_u32(head_done), 0, kTicketParkLimit, kTicketParkNs)) {
+                atomicCAS(p.err, 0, kErrTimeout);
+                *s_abort = 1;
+            } else if (!*s_abort) {
+                const long long ub = static_cast<long long>(head_rb) * S;
+                const int nc = owner(ub + S - 1, U, P) - owner(ub, U, P) + 1;
+                // acq_rel: releases the partials the consumers stored (observed through
+                // head_done) and acquires the other contributors' for the reduction
+                last = atom_add_acq_rel_gpu(p.counter + head_rb, 1u) ==
+                       static_cast<unsigned>(nc - 1);
+            }
+            *s_head_last = last;
+            mbar_arrive(smem_u32(ticket_done));
+        }
+        return;
     }
 
     // -------------------------------- consumers ------------------------------------
@@ -604,19 +655,6 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(empty + slot));
-            // thread 0 refills the slot of the unit before this one (a stage of slack:
-            // the other warps have usually released it by now)
-            if (ctid == 0 && it >= 1 && issued < nu && !*s_abort) {
-                const uint32_t jr = it - 1;
-                if (mbar_wait_bounded(smem_u32(empty + jr % stages), (jr / stages) & 1u,
-                                      kSpinLimit)) {
-                    issue(issued);
-                    ++issued;
-                } else {
-                    atomicCAS(p.err, 0, kErrTimeout);
-                    *s_abort = 1;
-                }
-            }
             xs += SG * TM * XG;
             rs += SG * TM;
             if (++slot == stages) {
@@ -713,7 +751,10 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
                 }
             }
             if (HEADS && has_head && u == u_lo) {
-                // head row block, more units follow: its ticket is taken at the end
+                // head row block, more units follow: hand the ticket to the ticket warp
+                // (mbarrier arrive: release of this warp's partials at CTA scope)
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(head_done));
             } else {
                 // The barrier orders every thread's partial before thread 0's acq_rel
                 // ticket; its release makes them visible GPU-wide (cumulatively) and its
@@ -732,25 +773,15 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
     }
     if constexpr (HEADS) {
         if (has_head) {
-            // the head row block's ticket, now that the rest of the share is done: the
-            // barrier orders the partials stored long ago (and everything since) before
-            // thread 0's acq_rel ticket, as for the other row blocks
-            named_bar_sync(1, CTHREADS);
-            if (ctid == 0) {
-                const long long ub = static_cast<long long>(head_rb) * S;
-                const int nc = owner(ub + S - 1, U, P) - owner(ub, U, P) + 1;
-                *s_head_last = (!*s_abort && atom_add_acq_rel_gpu(p.counter + head_rb, 1u) ==
-                                                 static_cast<unsigned>(nc - 1));
+            // the head row block's ticket (taken by the ticket warp)
+            const uint32_t tb_bar = smem_u32(ticket_done);
+            if (!mbar_try_wait(tb_bar, 0) && !wait_slow(tb_bar, 0)) {
+                atomicCAS(p.err, 0, kErrTimeout);
+                *s_abort = 1;
+            } else if (*s_head_last) {
+                reduce_row_block(head_rb);
             }
-            named_bar_sync(1, CTHREADS);
-            if (*s_head_last) reduce_row_block(head_rb);
         }
-    }
-    if (ctid == 0 && *s_abort) {
-        // let the copies already requested land before the CTA can exit
-        const int n = issued < stages ? issued : stages;
-        for (int j = issued - n; j < issued; ++j)
-            mbar_wait_bounded(smem_u32(full + j % stages), (j / stages) & 1, kSpinLimit);
     }
     if constexpr (EPI == 2) {
         // this CTA's best key per token -> the global keys; the last CTA to get here
