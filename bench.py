@@ -433,16 +433,19 @@ def moe_sweep(torch, mxq, dev, stream, peak_gbs, peak_tf):
     return out
 
 
-def decoder_e2e(torch, mxq, dev, peak_gbs, batch=8, prompt=512, new_tokens=128):
+def decoder_e2e(torch, mxq, dev, peak_gbs, batch=8, prompt=512, new_tokens=128,
+                nvtx_step=False, layers=LAYERS):
     """Config 4: the Qwen2.5-7B-architecture decoder (28 layers, hidden 3584, 28/4
     heads of 128, SwiGLU 18944, vocab 152064, RoPE theta 1e6, RMSNorm eps 1e-6), random
     init, every linear layer and the embedding quantized 4-bit g64, bf16 paged KV cache
     of 16-token pages. 8 prompts of 512 uniform-random ids: one prefill, then greedy
     decoding of 128 tokens per sequence (the first from the prefill, the second from
     the decode graph's warm-up step, the other 126 from graph replays, timed)."""
+    import dataclasses
+
     from mlx_server_runtime_b200 import qwen2
     from mlx_server_runtime_b200.attention import PagedKVCache
-    cfg = qwen2.Qwen2Config()
+    cfg = dataclasses.replace(qwen2.Qwen2Config(), num_hidden_layers=layers)
     with mxq.launch_overlap(True):
         model = qwen2.Qwen2ForCausalLM(cfg, device=dev, seed=0)
         max_len = prompt + new_tokens
@@ -479,6 +482,11 @@ def decoder_e2e(torch, mxq, dev, peak_gbs, batch=8, prompt=512, new_tokens=128):
         e1.record()
         torch.cuda.synchronize()
         step_ms = e0.elapsed_time(e1) / steps
+        if nvtx_step:  # one more (untimed) decode step, marked for a profiler's range filter
+            torch.cuda.nvtx.range_push("step")
+            dec.replay()
+            torch.cuda.nvtx.range_pop()
+            torch.cuda.synchronize()
         # end to end through the public API: prompts from pinned host memory, prefill,
         # every step's 8 token ids read back to the host (as a server streams them)
         tokens_host = torch.empty(new_tokens, batch, dtype=torch.int32).pin_memory()
@@ -492,7 +500,8 @@ def decoder_e2e(torch, mxq, dev, peak_gbs, batch=8, prompt=512, new_tokens=128):
         e2e_s = time.perf_counter() - t0
         distinct = int(torch.unique(tokens_host).numel())
         dec.close()
-    w_bytes = sum(qmm_bytes(batch, N, K) for _, N, K in shapes())  # projections + lm_head
+    w_bytes = (sum(qmm_bytes(batch, N, K) for _, N, K in PROJ) * layers +
+               qmm_bytes(batch, VOCAB, HIDDEN))  # projections + lm_head
     del model, cache, dec
     torch.cuda.empty_cache()
     return {
@@ -510,7 +519,8 @@ def decoder_e2e(torch, mxq, dev, peak_gbs, batch=8, prompt=512, new_tokens=128):
                      "what": "wall clock: prompts H2D from pinned memory, prefill, 127 graph "
                              "replays each followed by a D2H read of the step's 8 token ids"},
         "distinct_tokens": distinct,
-        "launches_per_decode_step": 4 + 8 * LAYERS,
+        "launches_per_decode_step": 4 + 8 * layers,
+        "layers": layers,
     }
 
 
@@ -701,6 +711,11 @@ def run(args):
     for _ in range(max(3, args.warmup)):
         step()
     barrier()
+    if args.nvtx_step:  # one more (untimed) step, marked for a profiler's range filter
+        torch.cuda.nvtx.range_push("step")
+        step()
+        torch.cuda.nvtx.range_pop()
+        barrier()
     with ClockSampler(dev.index) as clk:
         ms = timed(step, args.steps)
     value = total_bytes / (ms * 1e-3) / 1e9
@@ -837,6 +852,38 @@ CASES = {"q": (HIDDEN, HIDDEN), "kv": (KV, HIDDEN), "gate": (INTER, HIDDEN),
          "down": (HIDDEN, INTER), "lm_head": (VOCAB, HIDDEN)}
 
 
+def run_quantize_case(args):
+    """quantize and dequantize of the gate/up matrix (18944 x 3584 bf16, 4-bit g64),
+    a few times each: GB/s of each over its algorithmic bytes."""
+    import torch
+
+    mxq = load_package()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    N, K = INTER, HIDDEN
+    w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    for _ in range(max(3, args.warmup)):
+        wq, s, b = mxq.quantize(w, GS, BITS)
+        mxq.dequantize(wq, s, b, GS, BITS)
+    torch.cuda.synchronize()
+    res = {}
+    for name, fn, byts in (
+            ("quantize", lambda: mxq.quantize(w, GS, BITS),
+             2 * N * K + N * K * BITS // 8 + 4 * N * K // GS),
+            ("dequantize", lambda: mxq.dequantize(wq, s, b, GS, BITS),
+             N * K * BITS // 8 + 4 * N * K // GS + 2 * N * K)):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / args.steps
+        res[name] = {"us": round(us, 2), "bytes": byts, "GB/s": round(byts / (us * 1e-6) / 1e9, 1)}
+    print(json.dumps({"case": "quantize", "N": N, "K": K, **res}), flush=True)
+
+
 def run_case(args):
     """A few launches of one projection (small, for ncu captures and sweeps):
     rotates over enough weight copies that their total exceeds L2."""
@@ -961,7 +1008,8 @@ def run_only(args):
     stream = torch.cuda.Stream(device=dev)
     with mxq.launch_overlap(not args.no_overlap):
         if args.only == "decoder":
-            res = decoder_e2e(torch, mxq, dev, peak)
+            res = decoder_e2e(torch, mxq, dev, peak, nvtx_step=args.nvtx_step,
+                              layers=args.layers)
         elif args.only == "prefill":
             res = prefill_sweep(torch, mxq, dev, stream, peak_tf)
         elif args.only == "moe":
@@ -973,7 +1021,8 @@ def run_only(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", choices=sorted(CASES) + sorted(MOE_CASES), default=None,
+    ap.add_argument("--case", choices=sorted(CASES) + sorted(MOE_CASES) + ["quantize"],
+                    default=None,
                     help="time one projection only (eager launches, for profiling)")
     ap.add_argument("--m", type=int, default=1, help="tokens for --case")
     ap.add_argument("--eager", action="store_true", help="--case: plain launches, no graph")
@@ -985,6 +1034,12 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="--only decoder: decoder layers (28 = Qwen2.5-7B; fewer for small "
+                         "profiler captures)")
+    ap.add_argument("--nvtx-step", action="store_true",
+                    help="run one extra untimed step inside an NVTX range named 'step' "
+                         "(for ncu --nvtx --nvtx-include step/)")
     ap.add_argument("--only", choices=["decoder", "prefill", "moe", "sweep"], default=None,
                     help="run one of the extra measurements alone and print it")
     ap.add_argument("--no-extras", action="store_true",
@@ -994,6 +1049,8 @@ def main():
         run_reference(args)
     elif args.only:
         run_only(args)
+    elif args.case == "quantize":
+        run_quantize_case(args)
     elif args.case in MOE_CASES:
         run_moe_case(args)
     elif args.case:
