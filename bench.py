@@ -399,10 +399,11 @@ def switch_glu(mxq, ws):
     return sw
 
 
-def moe_sweep(torch, mxq, dev, stream, peak_gbs, peak_tf):
+def moe_sweep(torch, mxq, dev, stream, peak_gbs, peak_tf, nvtx_step=False):
     """Config 5: the Qwen3-30B-A3B-shaped SwitchGLU block (128 experts, top-8 of a
     softmax over N(0,1) router logits, 2048 -> 768 -> 2048, 4-bit g64) as the model
-    graphs call it, at T in {1, 64, 4096} tokens."""
+    graphs call it, at T in {1, 64, 4096} tokens. nvtx_step: one more (untimed) call
+    per T inside an NVTX range "moe<T>", for a profiler's range filter."""
     from mlx_server_runtime_b200 import nn
     ws = moe_weights(torch, mxq, dev)
     sw = switch_glu(mxq, ws)
@@ -418,6 +419,12 @@ def moe_sweep(torch, mxq, dev, stream, peak_gbs, peak_tf):
         idx, _ = nn.route_topk(logits, MOE_TOPK)
         used = int(torch.unique(idx).numel())
         ms = graph_ms(torch, [lambda: sw(x, idx)], 20 if T < 4096 else 10, stream)
+        if nvtx_step:
+            torch.cuda.synchronize()
+            torch.cuda.nvtx.range_push(f"moe{T}")
+            sw(x, idx)
+            torch.cuda.nvtx.range_pop()
+            torch.cuda.synchronize()
         rows = T * MOE_TOPK
         byts = used * per_expert + 2 * rows * (MOE_HID + 2 * MOE_INTER) * 2
         flops = 2.0 * rows * 3 * MOE_INTER * MOE_HID
@@ -1013,7 +1020,7 @@ def run_only(args):
         elif args.only == "prefill":
             res = prefill_sweep(torch, mxq, dev, stream, peak_tf)
         elif args.only == "moe":
-            res = moe_sweep(torch, mxq, dev, stream, peak, peak_tf)
+            res = moe_sweep(torch, mxq, dev, stream, peak, peak_tf, nvtx_step=args.nvtx_step)
         else:
             res = decode_sweep(torch, mxq, dev, stream, peak)
     print(json.dumps({args.only: res}), flush=True)
