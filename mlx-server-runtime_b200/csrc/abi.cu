@@ -4,6 +4,8 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <string>
 
@@ -430,6 +432,16 @@ size_t mlxq_gather_qmm_workspace_size(int64_t batch, int64_t M, int64_t N, int64
     return (2 * (static_cast<size_t>(num_experts) + 1) * 4 + 255) / 256 * 256;
 }
 
+// MLXQ_GATHER_KERNEL=cpasync (read once per process) sends decode-sized gather_qmm
+// calls to the cp.async kernel instead of the TMA-fed grouped one.
+static bool gather_cpasync_forced() {
+    static const bool v = [] {
+        const char* e = std::getenv("MLXQ_GATHER_KERNEL");
+        return e && std::strcmp(e, "cpasync") == 0;
+    }();
+    return v;
+}
+
 int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const void* biases,
                     const int32_t* lhs_indices, int64_t lhs_div, const int32_t* rhs_indices,
                     void* out, int64_t batch, int64_t M, int64_t N, int64_t K,
@@ -490,6 +502,25 @@ int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const 
         e = mlxq::qgemm_launch(dtype, bits, group_size, q, st);
         if (e != cudaSuccess) return cuda_fail(e, "gather_qmm (grouped) launch");
         return MLXQ_OK;
+    }
+    // Otherwise the TMA-fed grouped decode kernel: sorted rows of an expert taken
+    // together, else one entry at a time (the cp.async kernel below when its plan does
+    // not fit, or when MLXQ_GATHER_KERNEL=cpasync asks for it, for comparisons).
+    if (!gather_cpasync_forced()) {
+        const bool rows_sorted = mode == 2 && !lhs_indices && lhs_div == 1 && x_batches == batch;
+        mlxq::QgdPlan gp;
+        if (mlxq::qmv_grouped_plan(bits, group_size, batch, static_cast<int>(M),
+                                   static_cast<int>(N), static_cast<int>(K),
+                                   static_cast<int>(num_experts), rows_sorted, di.num_sms,
+                                   di.max_smem, di.sm_smem, &gp)) {
+            cudaError_t e = mlxq::qmv_grouped_launch(
+                dtype, bits, group_size, gp, x, w, scales, biases, out, rhs_indices, lhs_indices,
+                static_cast<int>(lhs_div < 1 ? 1 : lhs_div), static_cast<int>(batch),
+                static_cast<int>(x_batches), static_cast<int>(M), static_cast<int>(N),
+                static_cast<int>(K), static_cast<int>(num_experts), false, st);
+            if (e != cudaSuccess) return cuda_fail(e, "gather_qmm (grouped decode) launch");
+            return MLXQ_OK;
+        }
     }
     mlxq::QmvPlan plan;
     const int zhint = (mode == 2) ? static_cast<int>(batch * M / num_experts) : static_cast<int>(batch);

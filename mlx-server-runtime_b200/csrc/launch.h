@@ -152,6 +152,29 @@ cudaError_t qmv_tma_launch(int dtype, int bits, int gs, const QtPlan& plan, cons
                            void* out, int M, int N, int K, void* workspace, bool overlap,
                            cudaStream_t st, int epi = 0);
 cudaError_t qmv_tma_read_error(int* out_code);
+
+// One problem for the TMA-fed grouped decode kernel (qmv_grouped.cu): gather_qmm
+// entries b (expert rhs[b], x entry lhs[b] or b / lhs_div, M rows each) against
+// experts' weights stacked [E, N, ...]. sorted: rhs is non-decreasing and entry b's
+// x rows are entry b's (no lhs, x_batches == batch), so an expert's rows are taken
+// together, TM at a time.
+struct QgdPlan {
+    int TM;        // token slots of a chunk
+    int BR;        // weight rows per item
+    int S;         // 8-group stages per item
+    int RB;        // row blocks of N
+    int P;         // CTAs
+    int stages;    // ring depth
+    bool sorted;
+    size_t smem;
+};
+bool qmv_grouped_plan(int bits, int gs, long long batch, int M, int N, int K, int E, bool sorted,
+                      int num_sms, int max_smem, int sm_smem, QgdPlan* plan);
+cudaError_t qmv_grouped_launch(int dtype, int bits, int gs, const QgdPlan& plan, const void* x,
+                               const uint32_t* w, const void* s, const void* b, void* out,
+                               const int32_t* rhs, const int32_t* lhs, int lhs_div, int batch,
+                               int x_batches, int M, int N, int K, int E, bool overlap,
+                               cudaStream_t st);
 // A single bounded wait that runs out (mlxq_check_bounded_wait).
 cudaError_t launch_bounded_wait_check(uint32_t polls, cudaStream_t st);
 

@@ -49,6 +49,13 @@ bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esiz
 
 }  // namespace
 
+bool qt_make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esize,
+                 unsigned long long cols, unsigned long long rows, unsigned box_cols,
+                 unsigned box_rows, CUtensorMapSwizzle swz) {
+    return make_map(m, base, dt, esize, cols, rows, box_cols, box_rows, swz);
+}
+bool qt_maps_available() { return encode_fn() != nullptr; }
+
 // CTAs of this kernel meant to fit on one SM together: with 2, the shared memory
 // of a CTA is capped at half the SM's, so under launch overlap the next matmul's
 // CTAs can start streaming their weights while this one finishes.

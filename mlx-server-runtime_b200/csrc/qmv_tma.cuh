@@ -156,6 +156,16 @@ static __device__ __noinline__ bool wait_slow(uint32_t bar, uint32_t parity) {
 }
 }  // namespace qt
 
+// 2-D tiled tensor map over a row-major [rows, cols] array of `esize`-byte elements
+// with box [box_rows, box_cols] (qmv_tma.cu); false when the driver's encoder is
+// missing or rejects the map.
+bool qt_make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esize,
+                 unsigned long long cols, unsigned long long rows, unsigned box_cols,
+                 unsigned box_rows, CUtensorMapSwizzle swz);
+bool qt_maps_available();
+// Device address of the decode kernels' error word (qmv_tma.cu).
+int* qmv_tma_error_flag();
+
 struct QtParams {
     const void* x;
     const void* bias;
@@ -197,6 +207,284 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int n) {
     u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
     return (static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(n));
 }
+
+// x -> f16 MMA B fragments and per-slice records in shared memory, for nj group
+// positions j (a multiple of 8) and TM token slots. xrow(t) is token slot t's row of x
+// (nullptr: an absent slot, staged as zeros), grp(j) the K group staged at position j
+// (-1: padding past K, zeros). Item i = ((j * TM + t) * 4 + c): lane c of token slot t
+// holds words c, c+4, ... of the group (the words ldmatrix gives that lane). The item
+// count is a multiple of 32, so every warp runs whole iterations and the 4 lanes of an
+// item share a warp. Fragments and records are stored by position j.
+template <typename T, int BITS, int GS, int TM, typename XRow, typename Grp>
+__device__ __forceinline__ void qt_stage_activations(uint8_t* xf, float4* rec, int nj, XRow xrow,
+                                                     Grp grp, int ctid) {
+    using namespace qt;
+    using ET = Elem<T>;
+    using EH = Elem<__half>;
+    using OFF = typename EH::template Off<BITS>;
+    using GEO = Geo<BITS, GS, 16>;
+    constexpr int CPG = GEO::CPG, FR = GEO::FR, XG = GEO::XG;
+    constexpr int XW = BITS == 4 ? 8 : 4;  // activations per packed word
+    constexpr int PB = (CPG * XW / 2 <= 8) ? 4 : 2;  // items with loads in flight together
+    const int total = nj * TM * 4;
+    for (int i0 = ctid; i0 < total; i0 += PB * CTHREADS) {
+      uint32_t raw[PB][CPG][XW / 2];
+#pragma unroll
+      for (int b = 0; b < PB; ++b) {
+        const int i = i0 + b * CTHREADS;
+        const int cc = i & 3, t = (i >> 2) % TM, j = (i >> 2) / TM;
+        const T* row = i < total ? xrow(t) : nullptr;
+        const int g = i < total ? grp(j) : -1;
+#pragma unroll
+        for (int w = 0; w < CPG; ++w) {
+            const int off = g * GS + (4 * w + cc) * XW;
+            if constexpr (BITS == 4) {
+                uint4 q = make_uint4(0u, 0u, 0u, 0u);
+                if (row && g >= 0) q = *reinterpret_cast<const uint4*>(row + off);
+                raw[b][w][0] = q.x; raw[b][w][1] = q.y; raw[b][w][2] = q.z; raw[b][w][3] = q.w;
+            } else {
+                uint2 q = make_uint2(0u, 0u);
+                if (row && g >= 0) q = *reinterpret_cast<const uint2*>(row + off);
+                raw[b][w][0] = q.x; raw[b][w][1] = q.y;
+            }
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < PB; ++b) {
+        const int i = i0 + b * CTHREADS;
+        if (i >= total) break;  // warp-uniform: total and CTHREADS are multiples of 32
+        const int cc = i & 3, t = (i >> 2) % TM, j = (i >> 2) / TM;
+        float v[CPG][XW];
+        float m = 0.f;
+#pragma unroll
+        for (int w = 0; w < CPG; ++w) {
+#pragma unroll
+            for (int k = 0; k < XW / 2; ++k) {
+                v[w][2 * k] = ET::lo(raw[b][w][k]);
+                v[w][2 * k + 1] = ET::hi(raw[b][w][k]);
+                m = fmaxf(m, fmaxf(fabsf(v[w][2 * k]), fabsf(v[w][2 * k + 1])));
+            }
+        }
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        // fmaxf drops NaN, and an infinite maximum keeps e = 0: NaN and inf
+        // activations reach D unchanged and propagate to the output.
+        const int e = slice_exponent(m);
+        const float sc = pow2i(e);
+        uint32_t fr[FR];
+        float s_all = 0.f, s_even = 0.f, s_odd = 0.f;
+#pragma unroll
+        for (int w = 0; w < CPG; ++w) {
+            float y[XW];
+#pragma unroll
+            for (int k = 0; k < XW; ++k) {
+                y[k] = v[w][k] * sc;
+                s_all += v[w][k];
+                if (k & 1) s_odd += y[k]; else s_even += y[k];
+            }
+            if constexpr (BITS == 4) {
+                // operands pair nibbles (0,4) (1,5) (2,6) (3,7) of the word
+                fr[4 * w + 0] = pack_half2(y[0], y[4]);
+                fr[4 * w + 1] = pack_half2(y[1], y[5]);
+                fr[4 * w + 2] = pack_half2(y[2], y[6]);
+                fr[4 * w + 3] = pack_half2(y[3], y[7]);
+            } else {
+                // operands pair bytes (0,2) and (1,3) of the word
+                fr[2 * w + 0] = pack_half2(y[0], y[2]);
+                fr[2 * w + 1] = pack_half2(y[1], y[3]);
+            }
+        }
+#pragma unroll
+        for (int o = 1; o <= 2; o <<= 1) {
+            s_all += __shfl_xor_sync(0xffffffffu, s_all, o);
+            s_even += __shfl_xor_sync(0xffffffffu, s_even, o);
+            s_odd += __shfl_xor_sync(0xffffffffu, s_odd, o);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(xf + static_cast<size_t>(j) * TM * XG);
+#pragma unroll
+        for (int f = 0; f < FR / 4; ++f)
+            dst[(f * TM + t) * 4 + cc] =
+                make_uint4(fr[4 * f], fr[4 * f + 1], fr[4 * f + 2], fr[4 * f + 3]);
+        if (cc == 0) {
+            // 4-bit: even code positions carry offset kOffE, odd ones kOffO (per
+            // MMA slot); 8-bit: every activation meets both nibble operands.
+            const float toff = (BITS == 4) ? OFF::kOffE * s_even + OFF::kOffO * s_odd
+                                           : OFF::kOff * (s_even + s_odd);
+            rec[j * TM + t] = make_float4(s_all, toff, pow2i(-e), 0.f);
+        }
+      }
+    }
+}
+
+// One consumer warp's view of the ring: warp (rt, kq) owns row tile rt (16 rows) and
+// groups GPW*kq.. of every stage. The constructor fixes the per-lane offsets; stage()
+// folds one stage's groups into acc (token slots 8 nt + 2c, 8 nt + 2c + 1 of rows r and
+// r + 8 of the row tile), reading the staged activations of the stage's first group at
+// xs / rs (as returned by x_at / rec_at for the stage's position in the staged groups).
+template <typename T, int BITS, int GS, int TM, int BR>
+struct QtConsumer {
+    using ET = Elem<T>;
+    using EH = Elem<__half>;
+    using GEO = qt::Geo<BITS, GS, BR>;
+    static constexpr int WPG = GEO::WPG, CPG = GEO::CPG, FR = GEO::FR, XG = GEO::XG;
+    static constexpr int W_BYTES = GEO::W_BYTES, SB_BYTES = GEO::SB_BYTES;
+    static constexpr int RT = qt::Rows<BR>::RT, KSW = qt::Rows<BR>::KSW, GPW = qt::Rows<BR>::GPW;
+    static constexpr bool ODD = TM > 1;
+    static constexpr int NT = qt::n_tiles(TM);  // MMA n-tiles of 8 token slots
+    static constexpr int TS = TM < 8 ? TM : 8;  // token slots of one n-tile
+    static constexpr int NLD = CPG > 1 ? CPG / 2 : 1;
+    static constexpr int SBW = GPW >= 2 ? GPW / 2 : 1;
+
+    int rt, kq, r, c;
+    uint32_t lmo[GPW][NLD];  // ldmatrix row addresses (relative to the stage) per group/chunk
+    int so0, so1, sb_sh;     // packed (scale, scale) words of rows r, r+8; shift for GPW == 1
+    uint32_t magic_a, magic_b;
+    const uint8_t* xl;       // B fragments of token slot r (lanes past the last slot repeat one)
+    const float4* rl;        // records of tokens 2c, 2c+1 (wrapped into the slots likewise)
+
+    __device__ __forceinline__ QtConsumer(int warp, int lane, const uint8_t* xf, const float4* rec) {
+        rt = warp % RT;
+        kq = warp / RT;
+        r = lane >> 2;
+        c = lane & 3;
+        const int row = 16 * rt + (lane & 15);
+#pragma unroll
+        for (int h = 0; h < GPW; ++h) {
+            const int gi = GPW * kq + h;
+            const int box = (gi * WPG) >> 5;
+            const int cbase = ((gi * WPG) & 31) >> 2;
+#pragma unroll
+            for (int j = 0; j < NLD; ++j) {
+                const int ch = cbase + 2 * j + (CPG > 1 ? (lane >> 4) : 0);
+                lmo[h][j] = box * (BR * 128) + row * 128 + ((ch ^ (row & 7)) << 4);
+            }
+        }
+        const int rr = 16 * rt + r;
+        so0 = W_BYTES + rr * 16 + ((GPW * kq) & ~1) * 2;
+        so1 = so0 + 8 * 16;
+        sb_sh = GPW == 1 ? 16 * (kq & 1) : 0;
+        magic_a = opaque(EH::template Magic<BITS>::kA);
+        magic_b = opaque(EH::template Magic<BITS>::kB);
+        // (n-tile nt's slots are 8 nt.. : its fragments sit 8 * 64 bytes further)
+        const int tr = r & (TS - 1);
+        xl = xf + (tr * 4 + c) * 16 + GPW * kq * TM * XG;
+        rl = rec + ((2 * c) & (TS - 1)) + GPW * kq * TM;
+    }
+    // staged activations of the stage at position lst (8 groups each) of the staged groups
+    __device__ __forceinline__ const uint8_t* x_at(int lst) const {
+        return xl + static_cast<size_t>(lst) * qt::SG * TM * XG;
+    }
+    __device__ __forceinline__ const float4* rec_at(int lst) const {
+        return rl + lst * qt::SG * TM;
+    }
+
+    __device__ __forceinline__ void stage(const uint8_t* stg, const uint8_t* xs, const float4* rs,
+                                          float (&acc)[NT][4]) const {
+        const uint32_t stg_s = smem_u32(stg);
+        uint32_t s_r0[SBW], s_r1[SBW], b_r0[SBW], b_r1[SBW];
+#pragma unroll
+        for (int q = 0; q < SBW; ++q) {
+            s_r0[q] = *reinterpret_cast<const uint32_t*>(stg + so0 + 4 * q);
+            s_r1[q] = *reinterpret_cast<const uint32_t*>(stg + so1 + 4 * q);
+            b_r0[q] = *reinterpret_cast<const uint32_t*>(stg + so0 + 4 * q + SB_BYTES);
+            b_r1[q] = *reinterpret_cast<const uint32_t*>(stg + so1 + 4 * q + SB_BYTES);
+        }
+        if constexpr (GPW == 1) {
+            s_r0[0] >>= sb_sh; s_r1[0] >>= sb_sh;
+            b_r0[0] >>= sb_sh; b_r1[0] >>= sb_sh;
+        }
+#pragma unroll
+        for (int h = 0; h < GPW; ++h) {
+            uint32_t wa[CPG], wb[CPG];
+            if constexpr (CPG == 1) {
+                ldmatrix_x2(stg_s + lmo[h][0], wa[0], wb[0]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < NLD; ++j)
+                    ldmatrix_x4(stg_s + lmo[h][j], wa[2 * j], wb[2 * j], wa[2 * j + 1],
+                                wb[2 * j + 1]);
+            }
+            const int hq = h >> 1;
+            const float s0 = (h & 1) ? ET::hi(s_r0[hq]) : ET::lo(s_r0[hq]);
+            const float s1 = (h & 1) ? ET::hi(s_r1[hq]) : ET::lo(s_r1[hq]);
+            const float b0 = (h & 1) ? ET::hi(b_r0[hq]) : ET::lo(b_r0[hq]);
+            const float b1 = (h & 1) ? ET::hi(b_r1[hq]) : ET::lo(b_r1[hq]);
+            uint32_t ta[CPG][4], tb[CPG][4];
+#pragma unroll
+            for (int w = 0; w < CPG; ++w) {
+                EH::template extract<BITS>(wa[w], ta[w], magic_a, magic_b);
+                EH::template extract<BITS>(wb[w], tb[w], magic_a, magic_b);
+            }
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+            uint32_t X[FR];
+#pragma unroll
+            for (int f = 0; f < FR / 4; ++f) {
+                const uint4 v = *reinterpret_cast<const uint4*>(xs + h * TM * XG + f * TM * 64 +
+                                                                nt * 8 * 64);
+                X[4 * f + 0] = v.x; X[4 * f + 1] = v.y;
+                X[4 * f + 2] = v.z; X[4 * f + 3] = v.w;
+            }
+            float d[4];
+#pragma unroll
+            for (int w = 0; w < CPG; ++w) {
+                if constexpr (BITS == 4) {
+                    if (w == 0)
+                        mma16816z<__half>(d, ta[w][0], tb[w][0], ta[w][1], tb[w][1],
+                                          X[4 * w + 0], X[4 * w + 1]);
+                    else
+                        mma16816<__half>(d, ta[w][0], tb[w][0], ta[w][1], tb[w][1],
+                                         X[4 * w + 0], X[4 * w + 1]);
+                    mma16816<__half>(d, ta[w][2], tb[w][2], ta[w][3], tb[w][3], X[4 * w + 2],
+                                     X[4 * w + 3]);
+                } else {
+                    if (w == 0)
+                        mma16816z<__half>(d, ta[w][0], tb[w][0], ta[w][1], tb[w][1],
+                                          X[2 * w + 0], X[2 * w + 0]);
+                    else
+                        mma16816<__half>(d, ta[w][0], tb[w][0], ta[w][1], tb[w][1],
+                                         X[2 * w + 0], X[2 * w + 0]);
+                    mma16816<__half>(d, ta[w][2], tb[w][2], ta[w][3], tb[w][3], X[2 * w + 1],
+                                     X[2 * w + 1]);
+                }
+            }
+            // fold this group into tokens 8 nt + 2c, 8 nt + 2c + 1 of rows r, r+8
+            const float4 q0 = rs[h * TM + 8 * nt];
+            acc[nt][0] = fmaf(s0 * q0.z, d[0] - q0.y, fmaf(b0, q0.x, acc[nt][0]));
+            acc[nt][2] = fmaf(s1 * q0.z, d[2] - q0.y, fmaf(b1, q0.x, acc[nt][2]));
+            if constexpr (ODD) {
+                const float4 q1 = rs[h * TM + 8 * nt + 1];
+                acc[nt][1] = fmaf(s0 * q1.z, d[1] - q1.y, fmaf(b0, q1.x, acc[nt][1]));
+                acc[nt][3] = fmaf(s1 * q1.z, d[3] - q1.y, fmaf(b1, q1.x, acc[nt][3]));
+            }
+            }
+        }
+    }
+
+    // Adds the KSW group-interleaved warps of each row tile into warp kq == 0's acc
+    // (fixed order). Starts and ends with a barrier of the consumer threads.
+    __device__ __forceinline__ void combine(float* red, int lane, float (&acc)[NT][4]) const {
+        named_bar_sync(1, qt::CTHREADS);
+        if (kq > 0) {
+            float* dst = red + ((kq - 1) * RT + rt) * NT * 4 * 32 + lane;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) dst[(nt * 4 + e) * 32] = acc[nt][e];
+        }
+        named_bar_sync(1, qt::CTHREADS);
+        if (kq == 0) {
+#pragma unroll
+            for (int h = 1; h < KSW; ++h) {
+                const float* src = red + ((h - 1) * RT + rt) * NT * 4 * 32 + lane;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) acc[nt][e] += src[(nt * 4 + e) * 32];
+            }
+        }
+    }
+};
 
 template <typename T, int BITS, int GS, int TM, int BR, bool HEADS, int EPI>
 __global__ void __launch_bounds__(qt::threads(HEADS), 1)
@@ -367,143 +655,20 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
 
     // x[M, K] -> f16 B fragments and records, for the groups this CTA's units use
-    // ([ga0, ga1) and [gb0, gb1) above). Item i = ((j * TM + t) * 4 + c), j the group's position in those ranges:
-    // lane c of token slot t holds words c, c+4, ... of the group (the words ldmatrix
-    // gives that lane). The ranges are whole stages (8 groups), so the item count is
-    // a multiple of 32: every warp runs whole iterations and the 4 lanes of an item
-    // share a warp.
+    // ([ga0, ga1) and [gb0, gb1) above), stored by the group's position in those ranges
+    // (at most p.GL of them), not by its index in K.
     {
         const T* xg = static_cast<const T*>(p.x);
-        constexpr int XW = BITS == 4 ? 8 : 4;  // activations per packed word
-        constexpr int PB = (CPG * XW / 2 <= 8) ? 4 : 2;  // items with loads in flight together
-        const int total = (na + gb1 - gb0) * TM * 4;
-        for (int i0 = ctid; i0 < total; i0 += PB * CTHREADS) {
-          uint32_t raw[PB][CPG][XW / 2];
-#pragma unroll
-          for (int b = 0; b < PB; ++b) {
-            const int i = i0 + b * CTHREADS;
-            const int cc = i & 3, t = (i >> 2) % TM, j = (i >> 2) / TM;
-            const int g = j < na ? ga0 + j : gb0 + (j - na);
-#pragma unroll
-            for (int w = 0; w < CPG; ++w) {
-                const long long off = static_cast<long long>(t) * p.K + g * GS + (4 * w + cc) * XW;
-                if constexpr (BITS == 4) {
-                    uint4 q = make_uint4(0u, 0u, 0u, 0u);
-                    if (i < total && t < M) q = *reinterpret_cast<const uint4*>(xg + off);
-                    raw[b][w][0] = q.x; raw[b][w][1] = q.y; raw[b][w][2] = q.z; raw[b][w][3] = q.w;
-                } else {
-                    uint2 q = make_uint2(0u, 0u);
-                    if (i < total && t < M) q = *reinterpret_cast<const uint2*>(xg + off);
-                    raw[b][w][0] = q.x; raw[b][w][1] = q.y;
-                }
-            }
-          }
-#pragma unroll
-          for (int b = 0; b < PB; ++b) {
-            const int i = i0 + b * CTHREADS;
-            if (i >= total) break;  // warp-uniform: total and CTHREADS are multiples of 32
-            const int cc = i & 3, t = (i >> 2) % TM, j = (i >> 2) / TM;
-            float v[CPG][XW];
-            float m = 0.f;
-#pragma unroll
-            for (int w = 0; w < CPG; ++w) {
-#pragma unroll
-                for (int k = 0; k < XW / 2; ++k) {
-                    v[w][2 * k] = ET::lo(raw[b][w][k]);
-                    v[w][2 * k + 1] = ET::hi(raw[b][w][k]);
-                    m = fmaxf(m, fmaxf(fabsf(v[w][2 * k]), fabsf(v[w][2 * k + 1])));
-                }
-            }
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-            // fmaxf drops NaN, and an infinite maximum keeps e = 0: NaN and inf
-            // activations reach D unchanged and propagate to the output.
-            const int e = slice_exponent(m);
-            const float sc = pow2i(e);
-            uint32_t fr[FR];
-            float s_all = 0.f, s_even = 0.f, s_odd = 0.f;
-#pragma unroll
-            for (int w = 0; w < CPG; ++w) {
-                float y[XW];
-#pragma unroll
-                for (int k = 0; k < XW; ++k) {
-                    y[k] = v[w][k] * sc;
-                    s_all += v[w][k];
-                    if (k & 1) s_odd += y[k]; else s_even += y[k];
-                }
-                if constexpr (BITS == 4) {
-                    // operands pair nibbles (0,4) (1,5) (2,6) (3,7) of the word
-                    fr[4 * w + 0] = pack_half2(y[0], y[4]);
-                    fr[4 * w + 1] = pack_half2(y[1], y[5]);
-                    fr[4 * w + 2] = pack_half2(y[2], y[6]);
-                    fr[4 * w + 3] = pack_half2(y[3], y[7]);
-                } else {
-                    // operands pair bytes (0,2) and (1,3) of the word
-                    fr[2 * w + 0] = pack_half2(y[0], y[2]);
-                    fr[2 * w + 1] = pack_half2(y[1], y[3]);
-                }
-            }
-#pragma unroll
-            for (int o = 1; o <= 2; o <<= 1) {
-                s_all += __shfl_xor_sync(0xffffffffu, s_all, o);
-                s_even += __shfl_xor_sync(0xffffffffu, s_even, o);
-                s_odd += __shfl_xor_sync(0xffffffffu, s_odd, o);
-            }
-            // fragments and records are stored by the group's position j in the CTA's
-            // ranges (at most p.GL of them), not by its index in K
-            uint4* dst = reinterpret_cast<uint4*>(xf + static_cast<size_t>(j) * TM * XG);
-#pragma unroll
-            for (int f = 0; f < FR / 4; ++f)
-                dst[(f * TM + t) * 4 + cc] =
-                    make_uint4(fr[4 * f], fr[4 * f + 1], fr[4 * f + 2], fr[4 * f + 3]);
-            if (cc == 0) {
-                // 4-bit: even code positions carry offset kOffE, odd ones kOffO (per
-                // MMA slot); 8-bit: every activation meets both nibble operands.
-                const float toff = (BITS == 4) ? OFF::kOffE * s_even + OFF::kOffO * s_odd
-                                               : OFF::kOff * (s_even + s_odd);
-                rec[j * TM + t] = make_float4(s_all, toff, pow2i(-e), 0.f);
-            }
-          }
-        }
+        qt_stage_activations<T, BITS, GS, TM>(
+            xf, rec, na + gb1 - gb0,
+            [&](int t) -> const T* { return t < M ? xg + static_cast<long long>(t) * p.K : nullptr; },
+            [&](int j) -> int { return j < na ? ga0 + j : gb0 + (j - na); }, ctid);
     }
     named_bar_sync(1, CTHREADS);
 
-    const uint32_t magic_a = opaque(EH::template Magic<BITS>::kA);
-    const uint32_t magic_b = opaque(EH::template Magic<BITS>::kB);
+    const QtConsumer<T, BITS, GS, TM, BR> cons(warp, lane, xf, rec);
     const T* biasg = static_cast<const T*>(p.bias);
     T* og = static_cast<T*>(p.out);
-
-    // Per-lane offsets, fixed for the whole kernel. Group gi = GPW*kq + h of a stage:
-    //   ldmatrix row addresses (relative to the stage) of its CPG chunks,
-    constexpr int NLD = CPG > 1 ? CPG / 2 : 1;
-    uint32_t lmo[GPW][NLD];
-    {
-        const int row = 16 * rt + (lane & 15);
-#pragma unroll
-        for (int h = 0; h < GPW; ++h) {
-            const int gi = GPW * kq + h;
-            const int box = (gi * WPG) >> 5;
-            const int cbase = ((gi * WPG) & 31) >> 2;
-#pragma unroll
-            for (int j = 0; j < NLD; ++j) {
-                const int ch = cbase + 2 * j + (CPG > 1 ? (lane >> 4) : 0);
-                lmo[h][j] = box * (BR * 128) + row * 128 + ((ch ^ (row & 7)) << 4);
-            }
-        }
-    }
-    //   packed (scale, scale) / (bias, bias) words of the warp's group pairs, rows r, r+8,
-    const int rr = 16 * rt + r;
-    //   (a warp with one group reads the word holding it and shifts it down),
-    constexpr int SBW = GPW >= 2 ? GPW / 2 : 1;
-    const int so0 = W_BYTES + rr * 16 + ((GPW * kq) & ~1) * 2, so1 = so0 + 8 * 16;
-    const int sb_sh = GPW == 1 ? 16 * (kq & 1) : 0;
-    //   the B fragments of token slot r (lanes past the last slot repeat a slot:
-    //   their MMA columns are never read),
-    //   (n-tile nt's slots are 8 nt.. : its fragments sit 8 * 64 bytes further)
-    const int tr = r & (TS - 1);
-    const uint8_t* xl = xf + (tr * 4 + c) * 16 + GPW * kq * TM * XG;
-    //   and the records of tokens 2c, 2c+1 (wrapped into the slots likewise).
-    const float4* rl = rec + ((2 * c) & (TS - 1)) + GPW * kq * TM;
 
     // Last contributor to row block rb_: adds the contributors' fp32 partials in CTA
     // order, writes the outputs and re-arms the ticket.
@@ -562,8 +727,8 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
         // local position of stage st0 in the staged ranges: range a holds stages
         // ga0/SG.., range b (a share that wraps into the next row block) stages 0..
         const int lst = st0 >= ga0 / SG ? st0 - ga0 / SG : na / SG + st0;
-        const uint8_t* xs = xl + static_cast<size_t>(lst) * SG * TM * XG;
-        const float4* rs = rl + lst * SG * TM;
+        const uint8_t* xs = cons.x_at(lst);
+        const float4* rs = cons.rec_at(lst);
 
         for (int st = st0; st < st_end; ++st, ++it) {
             if (!*s_abort) {
@@ -573,86 +738,7 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
                     *s_abort = 1;
                 }
             }
-            const uint8_t* stg = ring + slot * STAGE;
-            const uint32_t stg_s = smem_u32(stg);
-            uint32_t s_r0[SBW], s_r1[SBW], b_r0[SBW], b_r1[SBW];
-#pragma unroll
-            for (int q = 0; q < SBW; ++q) {
-                s_r0[q] = *reinterpret_cast<const uint32_t*>(stg + so0 + 4 * q);
-                s_r1[q] = *reinterpret_cast<const uint32_t*>(stg + so1 + 4 * q);
-                b_r0[q] = *reinterpret_cast<const uint32_t*>(stg + so0 + 4 * q + SB_BYTES);
-                b_r1[q] = *reinterpret_cast<const uint32_t*>(stg + so1 + 4 * q + SB_BYTES);
-            }
-            if constexpr (GPW == 1) {
-                s_r0[0] >>= sb_sh; s_r1[0] >>= sb_sh;
-                b_r0[0] >>= sb_sh; b_r1[0] >>= sb_sh;
-            }
-#pragma unroll
-            for (int h = 0; h < GPW; ++h) {
-                uint32_t wa[CPG], wb[CPG];
-                if constexpr (CPG == 1) {
-                    ldmatrix_x2(stg_s + lmo[h][0], wa[0], wb[0]);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < NLD; ++j)
-                        ldmatrix_x4(stg_s + lmo[h][j], wa[2 * j], wb[2 * j], wa[2 * j + 1],
-                                    wb[2 * j + 1]);
-                }
-                const int hq = h >> 1;
-                const float s0 = (h & 1) ? ET::hi(s_r0[hq]) : ET::lo(s_r0[hq]);
-                const float s1 = (h & 1) ? ET::hi(s_r1[hq]) : ET::lo(s_r1[hq]);
-                const float b0 = (h & 1) ? ET::hi(b_r0[hq]) : ET::lo(b_r0[hq]);
-                const float b1 = (h & 1) ? ET::hi(b_r1[hq]) : ET::lo(b_r1[hq]);
-                uint32_t ta[CPG][4], tb[CPG][4];
-#pragma unroll
-                for (int w = 0; w < CPG; ++w) {
-                    EH::template extract<BITS>(wa[w], ta[w], magic_a, magic_b);
-                    EH::template extract<BITS>(wb[w], tb[w], magic_a, magic_b);
-                }
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                uint32_t X[FR];
-#pragma unroll
-                for (int f = 0; f < FR / 4; ++f) {
-                    const uint4 v = *reinterpret_cast<const uint4*>(xs + h * TM * XG + f * TM * 64 +
-                                                                    nt * 8 * 64);
-                    X[4 * f + 0] = v.x; X[4 * f + 1] = v.y;
-                    X[4 * f + 2] = v.z; X[4 * f + 3] = v.w;
-                }
-                float d[4];
-#pragma unroll
-                for (int w = 0; w < CPG; ++w) {
-                    if constexpr (BITS == 4) {
-                        if (w == 0)
-                            mma16816z<__half>(d, ta[w][0], tb[w][0], ta[w][1], tb[w][1],
-                                              X[4 * w + 0], X[4 * w + 1]);
-                        else
-                            mma16816<__half>(d, ta[w][0], tb[w][0], ta[w][1], tb[w][1],
-                                             X[4 * w + 0], X[4 * w + 1]);
-                        mma16816<__half>(d, ta[w][2], tb[w][2], ta[w][3], tb[w][3], X[4 * w + 2],
-                                         X[4 * w + 3]);
-                    } else {
-                        if (w == 0)
-                            mma16816z<__half>(d, ta[w][0], tb[w][0], ta[w][1], tb[w][1],
-                                              X[2 * w + 0], X[2 * w + 0]);
-                        else
-                            mma16816<__half>(d, ta[w][0], tb[w][0], ta[w][1], tb[w][1],
-                                             X[2 * w + 0], X[2 * w + 0]);
-                        mma16816<__half>(d, ta[w][2], tb[w][2], ta[w][3], tb[w][3], X[2 * w + 1],
-                                         X[2 * w + 1]);
-                    }
-                }
-                // fold this group into tokens 8 nt + 2c, 8 nt + 2c + 1 of rows r, r+8
-                const float4 q0 = rs[h * TM + 8 * nt];
-                acc[nt][0] = fmaf(s0 * q0.z, d[0] - q0.y, fmaf(b0, q0.x, acc[nt][0]));
-                acc[nt][2] = fmaf(s1 * q0.z, d[2] - q0.y, fmaf(b1, q0.x, acc[nt][2]));
-                if constexpr (ODD) {
-                    const float4 q1 = rs[h * TM + 8 * nt + 1];
-                    acc[nt][1] = fmaf(s0 * q1.z, d[1] - q1.y, fmaf(b0, q1.x, acc[nt][1]));
-                    acc[nt][3] = fmaf(s1 * q1.z, d[3] - q1.y, fmaf(b1, q1.x, acc[nt][3]));
-                }
-                }
-            }
+            cons.stage(ring + slot * STAGE, xs, rs, acc);
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(empty + slot));
             xs += SG * TM * XG;
@@ -663,26 +749,8 @@ __global__ void __launch_bounds__(qt::threads(HEADS), 1)
             }
         }
 
-        // ---- combine the four group-interleaved warps of each row tile (fixed order)
-        named_bar_sync(1, CTHREADS);
-        if (kq > 0) {
-            float* dst = red + ((kq - 1) * RT + rt) * NT * 4 * 32 + lane;
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) dst[(nt * 4 + e) * 32] = acc[nt][e];
-        }
-        named_bar_sync(1, CTHREADS);
-        if (kq == 0) {
-#pragma unroll
-            for (int h = 1; h < KSW; ++h) {
-                const float* src = red + ((h - 1) * RT + rt) * NT * 4 * 32 + lane;
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) acc[nt][e] += src[(nt * 4 + e) * 32];
-            }
-        }
+        // ---- combine the group-interleaved warps of each row tile (fixed order)
+        cons.combine(red, lane, acc);
         const bool abort = *s_abort != 0;
         const int row0 = rb * BR;
         if (st0 == 0 && st_end == S) {

@@ -1,23 +1,93 @@
 // quantize / dequantize kernels (MLX affine layout), bit-exact with the CPU
 // restatement of MLX's algorithm.
 //
-// Layout: one thread owns one packed uint32 word (32/bits consecutive codes of
-// a row); the group_size/(32/bits) threads of a group sit in adjacent lanes of
-// one warp, so group min/max is a shuffle reduction and every load and store
-// is coalesced. Both kernels are pure HBM streams (load-time work in the
-// reference: mx.quantize at lfm2.py:112-117, nn.quantize at qwen2.py:318-324).
+// quantize: one thread owns one packed uint32 word (32/bits consecutive codes of a
+// row), loaded as one or two 16-byte vectors; the group_size/(32/bits) threads of a
+// group sit in adjacent lanes of one warp, so group min/max is a shuffle reduction.
+// dequantize: each lane expands four words strided by 32, so a warp's loads and its
+// vector stores cover contiguous spans. Both kernels are HBM streams (load-time work
+// in the reference: mx.quantize at lfm2.py:112-117, nn.quantize at qwen2.py:318-324).
 #include "common.cuh"
 #include "launch.h"
 
 namespace mlxq {
+
+// 32-bit words of packed elements: two 16-bit values (low half first) or one float.
+template <typename T>
+struct Packed {
+    static constexpr int kPerWord = sizeof(T) == 2 ? 2 : 1;
+    static __device__ __forceinline__ float get(uint32_t u, int i) {
+        if constexpr (sizeof(T) == 4) {
+            return __uint_as_float(u);
+        } else {
+            return i == 0 ? Elem<T>::lo(u) : Elem<T>::hi(u);
+        }
+    }
+    static __device__ __forceinline__ uint32_t bits(T v) {
+        if constexpr (sizeof(T) == 4) {
+            return __float_as_uint(v);
+        } else {
+            return static_cast<uint32_t>(*reinterpret_cast<const unsigned short*>(&v));
+        }
+    }
+};
+
+// N consecutive 32-bit words (N in {2, 4, 8, 16}) from / to an address aligned to
+// min(4 N, 16) bytes, as 8- or 16-byte accesses with the streaming cache hint: the
+// data is touched once.
+template <int N>
+__device__ __forceinline__ void load_words(const void* p, uint32_t (&r)[N]) {
+    if constexpr (N == 2) {
+        const uint2 v = __ldcs(reinterpret_cast<const uint2*>(p));
+        r[0] = v.x;
+        r[1] = v.y;
+    } else {
+#pragma unroll
+        for (int i = 0; i < N / 4; ++i) {
+            const uint4 v = __ldcs(reinterpret_cast<const uint4*>(p) + i);
+            r[4 * i] = v.x;
+            r[4 * i + 1] = v.y;
+            r[4 * i + 2] = v.z;
+            r[4 * i + 3] = v.w;
+        }
+    }
+}
+
+template <int N>
+__device__ __forceinline__ void store_words(void* p, const uint32_t (&r)[N]) {
+    if constexpr (N == 2) {
+        __stcs(reinterpret_cast<uint2*>(p), make_uint2(r[0], r[1]));
+    } else {
+#pragma unroll
+        for (int i = 0; i < N / 4; ++i)
+            __stcs(reinterpret_cast<uint4*>(p) + i,
+                   make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]));
+    }
+}
+
+// The code of one element, clamp(rint(RN(d / s)), 0, n_bins) with RN the IEEE
+// quotient. The fast quotient __fdividef(d, s) is within 2 ulp of d / s for
+// 2^-126 <= |s| <= 2^126 (CUDA's documented bound); a result within 1e-3 of a
+// half-integer, outside [-1024, 1024] or not a number is recomputed with the IEEE
+// division, so the rounding to an integer never differs from the exact quotient's
+// (2 ulp at |q| <= 1024 is below 2.5e-4). `fast` is false when |s| is outside the
+// bound's range.
+__device__ __forceinline__ float quant_code(float d, float s, float n_bins, bool fast) {
+    float q = __fdividef(d, s);
+    const float f = q - floorf(q);
+    if (!fast || !(fabsf(q) <= 1024.0f) || fabsf(f - 0.5f) < 1e-3f) q = __fdiv_rn(d, s);
+    return fminf(fmaxf(rintf(q), 0.0f), n_bins);
+}
 
 template <typename T, int BITS>
 __global__ void __launch_bounds__(256) quantize_kernel(const T* __restrict__ w,
                                                        uint32_t* __restrict__ wq,
                                                        T* __restrict__ scales,
                                                        T* __restrict__ biases,
-                                                       long long total_words, int lanes_per_group) {
+                                                       long long total_words, int lanes_per_group,
+                                                       int log2_lanes) {
     constexpr int EPW = 32 / BITS;
+    constexpr int NW = EPW / Packed<T>::kPerWord;  // input words per packed word
     const float n_bins = static_cast<float>((1 << BITS) - 1);
     const long long wi = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     const bool live = wi < total_words;
@@ -25,10 +95,11 @@ __global__ void __launch_bounds__(256) quantize_kernel(const T* __restrict__ w,
     float v[EPW];
     float lmax = -INFINITY, lmin = INFINITY;
     if (live) {
-        const T* src = w + wi * EPW;
+        uint32_t raw[NW];
+        load_words<NW>(w + wi * EPW, raw);
 #pragma unroll
         for (int e = 0; e < EPW; ++e) {
-            v[e] = Elem<T>::to_f(src[e]);
+            v[e] = Packed<T>::get(raw[e / Packed<T>::kPerWord], e % Packed<T>::kPerWord);
             lmax = fmaxf(lmax, v[e]);
             lmin = fminf(lmin, v[e]);
         }
@@ -52,20 +123,26 @@ __global__ void __launch_bounds__(256) quantize_kernel(const T* __restrict__ w,
         scale = __fdiv_rn(edge, q0);
         bias = edge;
     }
+    const float as = fabsf(scale);
+    const bool fast = as >= 0x1p-126f && as <= 0x1p126f;
     uint32_t word = 0;
 #pragma unroll
     for (int e = 0; e < EPW; ++e) {
-        float q = rintf(__fdiv_rn(__fsub_rn(v[e], bias), scale));
-        q = fminf(fmaxf(q, 0.0f), n_bins);
+        const float q = quant_code(__fsub_rn(v[e], bias), scale, n_bins, fast);
         word |= static_cast<uint32_t>(q) << (BITS * e);
     }
-    wq[wi] = word;
+    __stcs(wq + wi, word);
     if ((threadIdx.x & (lanes_per_group - 1)) == 0) {
-        const long long g = wi / lanes_per_group;
+        const long long g = wi >> log2_lanes;
         scales[g] = Elem<T>::from_f(scale);
         biases[g] = Elem<T>::from_f(bias);
     }
 }
+
+// Each warp expands 32 * WPT consecutive packed words; lane l takes words
+// l, l + 32, ... of that run, so every load (4 bytes a lane) and every store
+// (EPW elements a lane) of the warp covers one contiguous span.
+constexpr int kDequantWPT = 4;
 
 template <typename T, int BITS>
 __global__ void __launch_bounds__(256) dequantize_kernel(const uint32_t* __restrict__ wq,
@@ -73,25 +150,47 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const uint32_t* __restr
                                                          const T* __restrict__ biases,
                                                          T* __restrict__ out,
                                                          long long total_words,
-                                                         int words_per_group) {
+                                                         int log2_words_per_group) {
     constexpr int EPW = 32 / BITS;
-    const long long wi = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (wi >= total_words) return;
-    const long long g = wi / words_per_group;
-    const float s = Elem<T>::to_f(scales[g]);
-    const float b = Elem<T>::to_f(biases[g]);
-    const uint32_t word = wq[wi];
-    T res[EPW];
+    constexpr int NW = EPW / Packed<T>::kPerWord;  // output words per packed word
+    const int lane = threadIdx.x & 31;
+    const long long warp = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const long long base = warp * (32 * kDequantWPT) + lane;
+    uint32_t word[kDequantWPT];
+    float s[kDequantWPT], b[kDequantWPT];
 #pragma unroll
-    for (int e = 0; e < EPW; ++e) {
-        const float q = static_cast<float>((word >> (BITS * e)) & ((1u << BITS) - 1u));
-        // One rounding per operation, in the storage type: round(round(s*q) + b).
-        const float t = Elem<T>::to_f(Elem<T>::from_f(__fmul_rn(s, q)));
-        res[e] = Elem<T>::from_f(__fadd_rn(t, b));
+    for (int j = 0; j < kDequantWPT; ++j) {
+        const long long wi = base + 32 * j;
+        if (wi < total_words) {
+            const long long g = wi >> log2_words_per_group;
+            word[j] = __ldcs(wq + wi);
+            s[j] = Elem<T>::to_f(scales[g]);
+            b[j] = Elem<T>::to_f(biases[g]);
+        }
     }
-    T* dst = out + wi * EPW;
 #pragma unroll
-    for (int e = 0; e < EPW; ++e) dst[e] = res[e];
+    for (int j = 0; j < kDequantWPT; ++j) {
+        const long long wi = base + 32 * j;
+        if (wi >= total_words) break;
+        uint32_t res[NW];
+#pragma unroll
+        for (int i = 0; i < NW; ++i) res[i] = 0;
+#pragma unroll
+        for (int e = 0; e < EPW; ++e) {
+            const float q = static_cast<float>((word[j] >> (BITS * e)) & ((1u << BITS) - 1u));
+            // One rounding per operation, in the storage type: round(round(s*q) + b).
+            const float t = Elem<T>::to_f(Elem<T>::from_f(__fmul_rn(s[j], q)));
+            const uint32_t r = Packed<T>::bits(Elem<T>::from_f(__fadd_rn(t, b[j])));
+            res[e / Packed<T>::kPerWord] |= r << (16 * (e % Packed<T>::kPerWord));
+        }
+        store_words<NW>(out + wi * EPW, res);
+    }
+}
+
+static int log2_exact(int v) {
+    int l = 0;
+    while ((1 << l) < v) ++l;
+    return l;
 }
 
 template <typename T>
@@ -99,15 +198,16 @@ static cudaError_t launch_quantize_t(const void* w, uint32_t* wq, void* s, void*
                                      long long K, int gs, int bits, cudaStream_t st) {
     const long long words = rows * K * bits / 32;
     const int lanes = gs / (32 / bits);
+    const int ll = log2_exact(lanes);
     const unsigned blocks = static_cast<unsigned>((words + 255) / 256);
     if (words == 0) return cudaSuccess;
     const T* wt = static_cast<const T*>(w);
     T* st_ = static_cast<T*>(s);
     T* bt = static_cast<T*>(b);
     switch (bits) {
-        case 2: quantize_kernel<T, 2><<<blocks, 256, 0, st>>>(wt, wq, st_, bt, words, lanes); break;
-        case 4: quantize_kernel<T, 4><<<blocks, 256, 0, st>>>(wt, wq, st_, bt, words, lanes); break;
-        case 8: quantize_kernel<T, 8><<<blocks, 256, 0, st>>>(wt, wq, st_, bt, words, lanes); break;
+        case 2: quantize_kernel<T, 2><<<blocks, 256, 0, st>>>(wt, wq, st_, bt, words, lanes, ll); break;
+        case 4: quantize_kernel<T, 4><<<blocks, 256, 0, st>>>(wt, wq, st_, bt, words, lanes, ll); break;
+        case 8: quantize_kernel<T, 8><<<blocks, 256, 0, st>>>(wt, wq, st_, bt, words, lanes, ll); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
@@ -118,16 +218,17 @@ static cudaError_t launch_dequantize_t(const uint32_t* wq, const void* s, const 
                                        long long rows, long long K, int gs, int bits,
                                        cudaStream_t st) {
     const long long words = rows * K * bits / 32;
-    const int wpg = gs * bits / 32;
-    const unsigned blocks = static_cast<unsigned>((words + 255) / 256);
+    const int lw = log2_exact(gs * bits / 32);
+    const long long per_block = 256LL * kDequantWPT;
+    const unsigned blocks = static_cast<unsigned>((words + per_block - 1) / per_block);
     if (words == 0) return cudaSuccess;
     const T* stt = static_cast<const T*>(s);
     const T* bt = static_cast<const T*>(b);
     T* o = static_cast<T*>(out);
     switch (bits) {
-        case 2: dequantize_kernel<T, 2><<<blocks, 256, 0, st>>>(wq, stt, bt, o, words, wpg); break;
-        case 4: dequantize_kernel<T, 4><<<blocks, 256, 0, st>>>(wq, stt, bt, o, words, wpg); break;
-        case 8: dequantize_kernel<T, 8><<<blocks, 256, 0, st>>>(wq, stt, bt, o, words, wpg); break;
+        case 2: dequantize_kernel<T, 2><<<blocks, 256, 0, st>>>(wq, stt, bt, o, words, lw); break;
+        case 4: dequantize_kernel<T, 4><<<blocks, 256, 0, st>>>(wq, stt, bt, o, words, lw); break;
+        case 8: dequantize_kernel<T, 8><<<blocks, 256, 0, st>>>(wq, stt, bt, o, words, lw); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();

@@ -1,0 +1,122 @@
+"""gather_qmm at decode sizes on the TMA-fed grouped kernel (qmv_grouped.cuh): an
+expert's sorted rows taken TM at a time (experts with more rows than one chunk, empty
+experts), unsorted entries one at a time (several chunks per entry when an entry has
+more rows than the token slots), weight rows past N in the last row block, K whose
+group count is not a multiple of 8 (a zero-padded last stage; scales copied in 4- or
+8-byte pieces), and shapes the kernel does not take (an odd group count) on the
+cp.async kernel. Every case against the C oracle.
+
+Tolerance: max|d| <= 2e-2 * max|ref| (bf16/f16 outputs, fp32 accumulation)."""
+import numpy as np
+import pytest
+import torch
+
+import mlx_server_runtime_b200 as mxq
+from oracle import coracle
+
+from gpu_util import close, rand_weights, rand_x, to_dev, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+def _experts(rng, E, N, K, dt, gs, bits):
+    w = rand_weights(rng, (E * N, K), dt)
+    wq, s, b = coracle.quantize(w, dt, gs, bits)
+    return wq.reshape(E, N, -1), s.reshape(E, N, -1), b.reshape(E, N, -1)
+
+
+def _sorted_case(E, N, K, counts, dt="bfloat16", bits=4, gs=64, M=1, seed=0):
+    rng = np.random.default_rng(seed)
+    wq, s, b = _experts(rng, E, N, K, dt, gs, bits)
+    sel = np.repeat(np.arange(E, dtype=np.int32), counts)
+    x = rand_x(rng, (sel.size, M, K), dt)
+    ref = coracle.gather_qmm(x, wq, s, b, sel, dt, gs, bits)
+    y = mxq.gather_qmm(to_dev(x, dt), to_dev(wq), to_dev(s, dt), to_dev(b, dt),
+                       rhs_indices=to_dev(sel), group_size=gs, bits=bits, sorted_indices=True)
+    torch.cuda.synchronize()
+    close(to_np(y), ref, dt)
+
+
+@pytest.mark.parametrize("K", [768, 1024, 2048])
+def test_sorted_chunks(K):
+    # mean 6.5 rows per expert: 8-slot chunks; experts of 0, 1, 8, 9, 17 and 30 rows
+    counts = [0, 1, 8, 9, 17, 30, 3, 0, 5, 6, 4, 7, 2, 5, 6, 1]
+    _sorted_case(16, 200, K, counts, seed=K)
+
+
+@pytest.mark.parametrize("dt", ["bfloat16", "float16"])
+@pytest.mark.parametrize("bits,gs", [(4, 32), (4, 64), (4, 128), (8, 32), (8, 64)])
+def test_sorted_types(dt, bits, gs):
+    rng = np.random.default_rng(bits * gs)
+    counts = rng.integers(0, 6, size=24)
+    _sorted_case(24, 96, 768, counts, dt=dt, bits=bits, gs=gs, seed=bits + gs)
+
+
+def test_sorted_few_rows_per_expert():
+    # 64 entries over 128 experts (mean 0.5 rows): single-slot chunks
+    rng = np.random.default_rng(5)
+    counts = rng.multinomial(64, np.ones(128) / 128)
+    _sorted_case(128, 768, 2048, counts, seed=6)
+
+
+def test_sorted_two_rows_per_entry():
+    _sorted_case(6, 130, 512, [3, 0, 5, 1, 2, 4], M=2, seed=7)
+
+
+@pytest.mark.parametrize("M", [1, 3, 9])
+def test_unsorted_entries(M):
+    """Entries one at a time: lhs indices, repeated experts, M rows per entry (9 rows
+    take two chunks of 8 slots)."""
+    rng = np.random.default_rng(M)
+    E, N, K = 12, 80, 640
+    wq, s, b = _experts(rng, E, N, K, "bfloat16", 64, 4)
+    x = rand_x(rng, (7, M, K), "bfloat16")
+    lhs = rng.integers(0, 7, 10).astype(np.int32)
+    rhs = rng.integers(0, E, 10).astype(np.int32)
+    rhs[3] = rhs[4]
+    ref = coracle.gather_qmm(x, wq, s, b, rhs, "bfloat16", 64, 4, lhs=lhs)
+    y = mxq.gather_qmm(to_dev(x, "bfloat16"), to_dev(wq), to_dev(s, "bfloat16"),
+                       to_dev(b, "bfloat16"), lhs_indices=to_dev(lhs), rhs_indices=to_dev(rhs))
+    close(to_np(y), ref, "bfloat16")
+
+
+def test_odd_group_count_takes_cp_async_kernel():
+    # K = 192 at group 64: three groups (scale rows of 6 bytes) -> the cp.async kernel
+    _sorted_case(8, 64, 192, [2, 0, 3, 1, 4, 0, 2, 5], seed=11)
+
+
+def test_repeated_calls_and_graph_replay():
+    """The chunk table lives in shared memory: back-to-back calls with different
+    routings, and a CUDA graph replayed after its index array changed."""
+    rng = np.random.default_rng(13)
+    E, N, K = 32, 256, 1024
+    wq, s, b = _experts(rng, E, N, K, "bfloat16", 64, 4)
+    args = (to_dev(wq), to_dev(s, "bfloat16"), to_dev(b, "bfloat16"))
+    x = to_dev(rand_x(rng, (40, 1, K), "bfloat16"), "bfloat16")
+    sel = torch.zeros(40, dtype=torch.int32, device="cuda")
+    out = {}
+
+    def run():
+        out["y"] = mxq.gather_qmm(x, *args, rhs_indices=sel, sorted_indices=True)
+
+    for trial in range(3):
+        routing = np.sort(rng.integers(0, E, 40)).astype(np.int32)
+        sel.copy_(torch.from_numpy(routing))
+        run()
+        ref = coracle.gather_qmm(to_np(x), wq, s, b, routing, "bfloat16", 64, 4)
+        close(to_np(out["y"]), ref, "bfloat16")
+    g = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        run()
+        with torch.cuda.graph(g, stream=st):
+            run()
+    torch.cuda.synchronize()
+    routing = np.sort(rng.integers(0, E, 40)).astype(np.int32)
+    sel.copy_(torch.from_numpy(routing))
+    g.replay()
+    torch.cuda.synchronize()
+    ref = coracle.gather_qmm(to_np(x), wq, s, b, routing, "bfloat16", 64, 4)
+    close(to_np(out["y"]), ref, "bfloat16")
+    del g

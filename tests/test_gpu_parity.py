@@ -41,6 +41,29 @@ def test_quantize_dequantize_bit_exact(dt, bits, gs):
     assert to_np(d_got).tobytes() == np.asarray(d_ref).tobytes()
 
 
+@pytest.mark.parametrize("dt,bits", [("bfloat16", 4), ("float16", 4), ("float16", 8),
+                                     ("float32", 4), ("float32", 8)])
+def test_quantize_half_integer_quotients(dt, bits):
+    """Groups whose (w - bias) / scale land exactly on half-integers (ties, rounded to
+    even) and, in float32, one ulp either side of them: the kernel's fast quotient must
+    give the codes of the IEEE quotient."""
+    rng = np.random.default_rng(7 * bits)
+    n, gs, rows = (1 << bits) - 1, 64, 192
+    half = rng.integers(0, 2 * n + 1, (rows, gs)).astype(np.float32) / 2
+    half[:, 0], half[:, 1] = 0.0, n          # endpoints: scale -step, bias = max
+    step = (2.0 ** rng.integers(-10, 6, (rows, 1))).astype(np.float32)
+    w = half * step                          # exact in every dtype tested
+    if dt == "float32":
+        nudge = rng.integers(-1, 2, w.shape)
+        nudge[:, :2] = 0
+        w = np.where(nudge < 0, np.nextafter(w, -np.inf),
+                     np.where(nudge > 0, np.nextafter(w, np.inf), w)).astype(np.float32)
+    w = O.from_f32(w, dt)
+    ref, got = _quant_both(w, dt, gs, bits)
+    for r, g, name in zip(ref, got, ("wq", "scales", "biases")):
+        assert to_np(g).tobytes() == np.asarray(r).tobytes(), name
+
+
 def test_kat_on_gpu():
     import json
     with open(os.path.join(GOLDEN, "kat.json")) as f:
