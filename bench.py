@@ -407,11 +407,17 @@ def moe_sweep(torch, mxq, dev, stream, peak_gbs, peak_tf, nvtx_step=False):
     from mlx_server_runtime_b200 import nn
     ws = moe_weights(torch, mxq, dev)
     sw = switch_glu(mxq, ws)
+    # the same bank with gate/up interleaved per expert (SwitchGLU.fuse_gate_up):
+    # up, gate and the activation in one launch at decode sizes
+    sw_fused = switch_glu(mxq, ws)
+    sw_fused.fuse_gate_up()
     gen = torch.Generator(device=dev)
     gen.manual_seed(12)
     per_expert = sum(n * k * BITS // 8 + 4 * n * k // GS
                      for n, k in ((MOE_INTER, MOE_HID), (MOE_INTER, MOE_HID), (MOE_HID, MOE_INTER)))
-    out = {"what": "SwitchGLU block: sort by expert (T >= 8), up, gate, silu*up, down, unsort",
+    out = {"what": "SwitchGLU block: sort by expert (64 entries and up), up, gate, silu*up, "
+                   "down, unsort; fused_gate_up: the same with gate/up interleaved per expert "
+                   "(one launch for up, gate and the activation at decode sizes)",
            "peak_gbs": peak_gbs, "peak_tflops": peak_tf, "T": {}}
     for T in (1, 64, 4096):
         x = torch.randn(T, MOE_HID, device=dev, generator=gen).to(torch.bfloat16)
@@ -434,8 +440,12 @@ def moe_sweep(torch, mxq, dev, stream, peak_gbs, peak_tf, nvtx_step=False):
              "GB/s": round(gbs, 1), "TFLOP/s": round(tf, 2)}
         e["roofline"] = ({"bound": "hbm", "frac": round(gbs / peak_gbs, 4)} if T <= 64
                          else {"bound": "tensor", "frac": round(tf / peak_tf, 4)})
+        ms_f = graph_ms(torch, [lambda: sw_fused(x, idx)], 20 if T < 4096 else 10, stream)
+        gbs_f = byts / (ms_f * 1e-3) / 1e9
+        e["fused_gate_up"] = {"us": round(ms_f * 1e3, 1), "GB/s": round(gbs_f, 1),
+                              "TFLOP/s": round(flops / (ms_f * 1e-3) / 1e12, 2)}
         out["T"][str(T)] = e
-    del sw, ws
+    del sw, sw_fused, ws
     torch.cuda.empty_cache()
     return out
 

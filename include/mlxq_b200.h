@@ -171,6 +171,26 @@ int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const 
                     void* stream);
 
 /*
+ * gather_qmm with the SwiGLU activation in the epilogue, for the decode sizes of an
+ * MoE layer: w, scales, biases hold every expert's gate and up projections interleaved
+ * by 16-row tiles (tile j = gate rows 8j..8j+7, then up rows 8j..8j+7; N = 2 * the
+ * hidden size, a multiple of 16), and out [batch, M, N/2] receives silu(gate) * up,
+ * each projection rounded to dtype first (as SwitchGLU's separate up_proj, gate_proj
+ * and element-wise ops compute it, lfm2.py:202-218). Other arguments as
+ * mlxq_gather_qmm; no workspace. MLXQ_ERR_SHAPE when the decode kernel does not take
+ * the shape: mlxq_gather_swiglu_supported says which do (lhs_given: lhs_indices will
+ * be passed).
+ */
+int mlxq_gather_swiglu_supported(int64_t batch, int64_t M, int64_t N, int64_t K,
+                                 int64_t num_experts, int64_t x_batches, int group_size, int bits,
+                                 int dtype, int lhs_given, int sorted_indices);
+int mlxq_gather_qmm_swiglu(const void* x, const uint32_t* w, const void* scales,
+                           const void* biases, const int32_t* lhs_indices, int64_t lhs_div,
+                           const int32_t* rhs_indices, void* out, int64_t batch, int64_t M,
+                           int64_t N, int64_t K, int64_t num_experts, int64_t x_batches,
+                           int group_size, int bits, int dtype, int sorted_indices, void* stream);
+
+/*
  * quantized_matmul_argmax: greedy decoding's next token without the logits. The
  * reference computes the vocabulary logits with the lm_head (or the tied
  * embedding's as_linear) quantized_matmul, then takes their argmax per sequence
@@ -334,6 +354,19 @@ int mlxq_quantized_embedding(const int32_t* ids, int64_t n, const uint32_t* wq,
 int mlxq_moe_route(const void* logits, int logits_dtype, const float* expert_bias,
                    int32_t* indices, void* scores, int scores_dtype, int64_t tokens,
                    int num_experts, int top_k, int norm_topk_prob, void* stream);
+
+/*
+ * Stable sort of MoE routing entries by expert: replaces the argsort pair of the
+ * sorted SwitchGLU path (_gather_sort, lfm2.py:613-618: order = argsort(indices),
+ * inv_order = argsort(order)). For entries i < n with expert indices[i]:
+ * order[p] = the entry at sorted position p (equal experts keep entry order),
+ * sorted_indices[p] = indices[order[p]], inverse[i] = the sorted position of entry i.
+ * Negative values form one group before every expert and values >= num_experts one
+ * after, each in entry order (argsort would also order them by value).
+ * n <= 16384, num_experts <= 1024. One launch, nothing read back to the host.
+ */
+int mlxq_moe_sort(const int32_t* indices, int64_t n, int num_experts, int32_t* order,
+                  int32_t* sorted_indices, int32_t* inverse, void* stream);
 
 /*
  * Decode-loop bookkeeping on the device, so a captured decode step replays with no

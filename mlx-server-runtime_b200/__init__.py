@@ -10,11 +10,12 @@ tests/conftest.py, bench.py and __graft_entry__.py do. Operators live in
 from __future__ import annotations
 
 from . import _lib
-from .core import (Workspace, concat_quantized, dequantize, gather_qmm, interleave_gate_up,
-                   launch_overlap, quantize, quantized_matmul, quantized_matmul_argmax,
-                   quantized_matmul_swiglu)
+from .core import (Workspace, concat_quantized, dequantize, gather_qmm, gather_qmm_swiglu,
+                   interleave_gate_up, launch_overlap, quantize, quantized_matmul,
+                   quantized_matmul_argmax, quantized_matmul_swiglu)
 
-__all__ = ["quantize", "dequantize", "quantized_matmul", "gather_qmm", "concat_quantized",
+__all__ = ["quantize", "dequantize", "quantized_matmul", "gather_qmm", "gather_qmm_swiglu",
+           "concat_quantized",
            "interleave_gate_up", "quantized_matmul_swiglu", "quantized_matmul_argmax",
            "Workspace", "launch_overlap",
            "library_path", "load_library"]

@@ -47,6 +47,9 @@ EXPORTED = (
     "mlxq_quantized_embedding",
     "mlxq_decode_advance",
     "mlxq_moe_route",
+    "mlxq_moe_sort",
+    "mlxq_gather_swiglu_supported",
+    "mlxq_gather_qmm_swiglu",
 )
 
 _lock = threading.Lock()
@@ -129,6 +132,14 @@ def load(path: str | None = None):
         L.mlxq_decode_advance.restype = i32
         L.mlxq_moe_route.argtypes = [vp, i32, vp, vp, vp, i32, i64, i32, i32, i32, vp]
         L.mlxq_moe_route.restype = i32
+        L.mlxq_moe_sort.argtypes = [vp, i64, i32, vp, vp, vp, vp]
+        L.mlxq_moe_sort.restype = i32
+        L.mlxq_gather_swiglu_supported.argtypes = [i64, i64, i64, i64, i64, i64, i32, i32, i32,
+                                                   i32, i32]
+        L.mlxq_gather_swiglu_supported.restype = i32
+        L.mlxq_gather_qmm_swiglu.argtypes = [vp, vp, vp, vp, vp, i64, vp, vp, i64, i64, i64, i64,
+                                             i64, i64, i32, i32, i32, i32, vp]
+        L.mlxq_gather_qmm_swiglu.restype = i32
         v = L.mlxq_abi_version()
         if v != ABI_VERSION:
             raise LibraryError(f"{p} has ABI version {v}, expected {ABI_VERSION}; rebuild it")

@@ -28,8 +28,8 @@ from . import _lib
 
 _DT = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
 
-__all__ = ["quantize", "dequantize", "quantized_matmul", "gather_qmm", "concat_quantized",
-           "moe_route",
+__all__ = ["quantize", "dequantize", "quantized_matmul", "gather_qmm", "gather_qmm_swiglu",
+           "concat_quantized", "moe_route", "moe_sort",
            "interleave_gate_up", "quantized_matmul_swiglu", "quantized_matmul_argmax",
            "Workspace", "launch_overlap"]
 
@@ -277,22 +277,26 @@ def concat_quantized(parts, group_size: int = 64, bits: int = 4):
 
 
 def interleave_gate_up(gate, up, group_size: int = 64, bits: int = 4):
-    """The weight layout quantized_matmul_swiglu reads: the (w, scales, biases) of a
-    SwiGLU MLP's gate and up projections (same shape [I, ...], I a multiple of 8)
-    interleaved by 16-row tiles, tile j = gate rows 8j..8j+7 then up rows 8j..8j+7.
-    Rows are copied bit for bit (a load-time permutation, nothing is requantized)."""
+    """The weight layout quantized_matmul_swiglu (2-D, one matrix) and
+    gather_qmm_swiglu (3-D, [experts, rows, ...]) read: the (w, scales, biases) of a
+    SwiGLU MLP's gate and up projections (same shape [..., I, ...], I a multiple of 8)
+    interleaved by 16-row tiles within each matrix, tile j = gate rows 8j..8j+7 then up
+    rows 8j..8j+7. Rows are copied bit for bit (a load-time permutation, nothing is
+    requantized)."""
     (wg, sg, bg), (wu, su, bu) = gate, up
     for a, c in ((wg, wu), (sg, su), (bg, bu)):
-        if a.shape != c.shape or a.dtype != c.dtype or a.ndim != 2:
-            raise ValueError("gate and up must be 2-D quantized matrices of the same shape")
+        if a.shape != c.shape or a.dtype != c.dtype or a.ndim not in (2, 3):
+            raise ValueError("gate and up must be 2-D (or 3-D expert banks of) quantized "
+                             "matrices of the same shape")
     _check_qweights(wg, sg, bg, group_size, bits, sg.dtype)
-    inter = wg.shape[0]
+    lead, inter = tuple(wg.shape[:-2]), wg.shape[-2]
     if inter % 8:
         raise ValueError(f"gate/up rows ({inter}) must be a multiple of 8")
 
     def mix(a, c):
-        return torch.stack([a.reshape(inter // 8, 8, -1), c.reshape(inter // 8, 8, -1)],
-                           dim=1).reshape(2 * inter, -1).contiguous()
+        return torch.stack([a.reshape(*lead, inter // 8, 8, a.shape[-1]),
+                            c.reshape(*lead, inter // 8, 8, c.shape[-1])],
+                           dim=-3).reshape(*lead, 2 * inter, a.shape[-1]).contiguous()
     if wg.dtype == torch.uint32:  # (torch has no uint32 stack on every device: move as int32)
         w = mix(wg.view(torch.int32), wu.view(torch.int32)).view(torch.uint32)
     else:
@@ -415,20 +419,8 @@ def broadcast_divisor(bx: tuple, bshape: tuple) -> int | None:
     return tail if tuple(pad[:k]) == tuple(bshape[:k]) else None
 
 
-def gather_qmm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
-               biases: torch.Tensor | None = None, lhs_indices: torch.Tensor | None = None,
-               rhs_indices: torch.Tensor | None = None, transpose: bool = True,
-               group_size: int = 64, bits: int = 4, mode: str = "affine",
-               sorted_indices: bool = False) -> torch.Tensor:
-    """Batched quantized matmul with index-selected operands (MLX gather_qmm).
-
-    x [..., M, K] with batch dims Bx; w [..., N, K*bits/32] with batch dims Bw.
-    lhs_indices index flattened Bx, rhs_indices flattened Bw; both broadcast to
-    a common shape S and the result is [*S, M, N].
-    """
-    _mode(mode)
-    if not transpose:
-        raise ValueError("transpose=False is not supported; the model graphs use transpose=True")
+def _gather_args(x, w, scales, biases, lhs_indices, rhs_indices, group_size, bits):
+    """Checks and flattens gather_qmm's operands (shared by the gather entry points)."""
     dev = _cuda(x, w, scales, biases, lhs_indices, rhs_indices)
     dt = _dtype_code(x, "x")
     if x.ndim < 2 or w.ndim < 2:
@@ -450,37 +442,125 @@ def gather_qmm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
     except RuntimeError as e:
         raise ValueError(f"cannot broadcast index shapes {lhs_shape} and {rhs_shape}") from e
     batch = math.prod(bshape)
-    out = torch.empty(*bshape, M, N, dtype=x.dtype, device=dev)
-    if batch == 0 or M == 0:
-        return out
 
     def _flat(idx, natural):
         if idx is None:
             idx = torch.arange(math.prod(natural), device=dev, dtype=torch.int32).reshape(natural)
         return idx.to(torch.int32).expand(bshape).contiguous().reshape(-1)
 
-    rhs = _flat(rhs_indices, bw)
-    lhs, lhs_div = None, 1
-    if lhs_indices is None:
-        lhs_div = broadcast_divisor(bx, bshape)
-        if lhs_div is None:
-            lhs, lhs_div = _flat(None, bx), 1
-    else:
-        lhs = _flat(lhs_indices, bx)
+    rhs = lhs = None
+    lhs_div = 1
+    if batch and M:
+        rhs = _flat(rhs_indices, bw)
+        if lhs_indices is None:
+            lhs_div = broadcast_divisor(bx, bshape)
+            if lhs_div is None:
+                lhs, lhs_div = _flat(None, bx), 1
+        else:
+            lhs = _flat(lhs_indices, bx)
+    return dict(dev=dev, dt=dt, K=K, M=M, N=N, E=E, x_batches=x_batches, bshape=bshape,
+                batch=batch, lhs=lhs, lhs_div=lhs_div, rhs=rhs, x=x.contiguous(),
+                w=w.contiguous(), scales=scales.contiguous(), biases=biases.contiguous())
+
+
+def gather_qmm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
+               biases: torch.Tensor | None = None, lhs_indices: torch.Tensor | None = None,
+               rhs_indices: torch.Tensor | None = None, transpose: bool = True,
+               group_size: int = 64, bits: int = 4, mode: str = "affine",
+               sorted_indices: bool = False) -> torch.Tensor:
+    """Batched quantized matmul with index-selected operands (MLX gather_qmm).
+
+    x [..., M, K] with batch dims Bx; w [..., N, K*bits/32] with batch dims Bw.
+    lhs_indices index flattened Bx, rhs_indices flattened Bw; both broadcast to
+    a common shape S and the result is [*S, M, N].
+    """
+    _mode(mode)
+    if not transpose:
+        raise ValueError("transpose=False is not supported; the model graphs use transpose=True")
+    a = _gather_args(x, w, scales, biases, lhs_indices, rhs_indices, group_size, bits)
+    dev, batch, M, N, K = a["dev"], a["batch"], a["M"], a["N"], a["K"]
+    out = torch.empty(*a["bshape"], M, N, dtype=x.dtype, device=dev)
+    if batch == 0 or M == 0:
+        return out
     L = _lib.load()
-    x2 = x.contiguous()
-    w, scales, biases = w.contiguous(), scales.contiguous(), biases.contiguous()
     with torch.cuda.device(dev):
         st = torch.cuda.current_stream(dev)
-        need = L.mlxq_gather_qmm_workspace_size(batch, M, N, K, E, group_size, bits, dt,
+        need = L.mlxq_gather_qmm_workspace_size(batch, M, N, K, a["E"], group_size, bits, a["dt"],
                                                 int(bool(sorted_indices)))
         ws = Workspace.get(dev, st, need, "gather") if need else None
-        rc = L.mlxq_gather_qmm(_ptr(x2), _ptr(w), _ptr(scales), _ptr(biases), _ptr(lhs), lhs_div,
-                               _ptr(rhs), _ptr(out), batch, M, N, K, E, x_batches, group_size,
-                               bits, dt, int(bool(sorted_indices)), _ptr(ws),
+        rc = L.mlxq_gather_qmm(_ptr(a["x"]), _ptr(a["w"]), _ptr(a["scales"]), _ptr(a["biases"]),
+                               _ptr(a["lhs"]), a["lhs_div"], _ptr(a["rhs"]), _ptr(out), batch, M,
+                               N, K, a["E"], a["x_batches"], group_size, bits, a["dt"],
+                               int(bool(sorted_indices)), _ptr(ws),
                                0 if ws is None else ws.numel(), st.cuda_stream)
     _lib.check(rc, "gather_qmm")
     return out
+
+
+def gather_qmm_swiglu(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
+                      biases: torch.Tensor, lhs_indices: torch.Tensor | None = None,
+                      rhs_indices: torch.Tensor | None = None, group_size: int = 64,
+                      bits: int = 4, mode: str = "affine",
+                      sorted_indices: bool = False) -> torch.Tensor:
+    """silu(x @ gate_e^T) * (x @ up_e^T) per routed entry, from an expert bank in
+    interleave_gate_up's layout ([E, N, ...], N = 2 * hidden): [*S, M, N/2].
+
+    Decode sizes run as one launch with the activation in the grouped kernel's
+    epilogue; other sizes run gather_qmm and then the activation as torch element-wise
+    ops. Either way each projection is rounded to x's dtype before silu(g) * u is
+    formed in float32 and rounded once more."""
+    _mode(mode)
+    a = _gather_args(x, w, scales, biases, lhs_indices, rhs_indices, group_size, bits)
+    dev, batch, M, N, K = a["dev"], a["batch"], a["M"], a["N"], a["K"]
+    if N % 16:
+        raise ValueError(f"w must hold gate/up 16-row tiles (N={N} is not a multiple of 16)")
+    L = _lib.load()
+    if batch == 0 or M == 0 or not L.mlxq_gather_swiglu_supported(
+            batch, M, N, K, a["E"], a["x_batches"], group_size, bits, a["dt"],
+            int(a["lhs"] is not None), int(bool(sorted_indices))):
+        y = gather_qmm(x, w, scales, biases, lhs_indices, rhs_indices, True, group_size, bits,
+                       mode, sorted_indices)
+        y = y.reshape(*a["bshape"], M, N // 16, 2, 8).float()
+        g, u = y[..., 0, :], y[..., 1, :]
+        return (torch.nn.functional.silu(g) * u).to(x.dtype).reshape(*a["bshape"], M, N // 2)
+    out = torch.empty(*a["bshape"], M, N // 2, dtype=x.dtype, device=dev)
+    with torch.cuda.device(dev):
+        st = torch.cuda.current_stream(dev)
+        rc = L.mlxq_gather_qmm_swiglu(_ptr(a["x"]), _ptr(a["w"]), _ptr(a["scales"]),
+                                      _ptr(a["biases"]), _ptr(a["lhs"]), a["lhs_div"],
+                                      _ptr(a["rhs"]), _ptr(out), batch, M, N, K, a["E"],
+                                      a["x_batches"], group_size, bits, a["dt"],
+                                      int(bool(sorted_indices)), st.cuda_stream)
+    _lib.check(rc, "gather_qmm_swiglu")
+    return out
+
+
+def moe_sort(indices: torch.Tensor, num_experts: int):
+    """Stable sort of routing entries by expert on the device, the argsort pair of the
+    sorted SwitchGLU path (_gather_sort, lfm2.py:613-618 of the reference): for the
+    flattened int32 `indices` (n <= 16384 entries), returns int32 tensors (order,
+    sorted_indices, inverse) with order[p] the entry at sorted position p (equal
+    experts in entry order), sorted_indices[p] = indices[order[p]] and inverse[i] the
+    position of entry i. Values outside [0, num_experts) form a group before
+    (negative) or after (too large) every expert, in entry order."""
+    dev = _cuda(indices)
+    if indices.dtype != torch.int32:
+        raise ValueError(f"indices must be int32, got {indices.dtype}")
+    flat = indices.contiguous().reshape(-1)
+    n = flat.numel()
+    if not 1 <= num_experts <= 1024 or n > 16384:
+        raise ValueError(f"moe_sort takes n <= 16384 entries and 1 <= num_experts <= 1024 "
+                         f"(got n={n}, num_experts={num_experts})")
+    order = torch.empty(n, dtype=torch.int32, device=dev)
+    srt = torch.empty_like(order)
+    inv = torch.empty_like(order)
+    if n:
+        with torch.cuda.device(dev):
+            st = torch.cuda.current_stream(dev)
+            rc = _lib.load().mlxq_moe_sort(_ptr(flat), n, num_experts, _ptr(order), _ptr(srt),
+                                           _ptr(inv), st.cuda_stream)
+        _lib.check(rc, "moe_sort")
+    return order, srt, inv
 
 
 def moe_route(logits: torch.Tensor, top_k: int, norm_topk_prob: bool = True,

@@ -442,11 +442,12 @@ static bool gather_cpasync_forced() {
     return v;
 }
 
-int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const void* biases,
-                    const int32_t* lhs_indices, int64_t lhs_div, const int32_t* rhs_indices,
-                    void* out, int64_t batch, int64_t M, int64_t N, int64_t K,
-                    int64_t num_experts, int64_t x_batches, int group_size, int bits, int dtype,
-                    int sorted_indices, void* workspace, size_t workspace_bytes, void* stream) {
+// Argument checks shared by the gather_qmm entry points (`what` names the caller).
+static int check_gather(const char* what, const void* x, const uint32_t* w, const void* scales,
+                        const void* biases, const int32_t* lhs_indices, int64_t lhs_div,
+                        const int32_t* rhs_indices, const void* out, int64_t batch, int64_t M,
+                        int64_t N, int64_t K, int64_t num_experts, int64_t x_batches,
+                        int group_size, int bits, int dtype) {
     int rc = check_bits_gs(bits, group_size, true);
     if (rc) return rc;
     if ((rc = check_k(K, group_size))) return rc;
@@ -454,18 +455,48 @@ int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const 
         M > kIntMax || N > kIntMax || K > kIntMax || num_experts > kIntMax ||
         x_batches > kIntMax || batch * M > kIntMax || x_batches * M > kIntMax)
         return fail(MLXQ_ERR_SHAPE,
-                    "gather_qmm: bad shape batch=%lld M=%lld N=%lld K=%lld E=%lld x_batches=%lld",
+                    "%s: bad shape batch=%lld M=%lld N=%lld K=%lld E=%lld x_batches=%lld", what,
                     (long long)batch, (long long)M, (long long)N, (long long)K,
                     (long long)num_experts, (long long)x_batches);
     if (!lhs_indices && lhs_div < 1)
-        return fail(MLXQ_ERR_INDEX, "gather_qmm: lhs_div must be >= 1 without lhs_indices");
+        return fail(MLXQ_ERR_INDEX, "%s: lhs_div must be >= 1 without lhs_indices", what);
     if (dtype != MLXQ_BF16 && dtype != MLXQ_F16)
-        return fail(MLXQ_ERR_DTYPE, "gather_qmm: dtype=%d must be bfloat16 or float16", dtype);
+        return fail(MLXQ_ERR_DTYPE, "%s: dtype=%d must be bfloat16 or float16", what, dtype);
     if (!x || !w || !scales || !biases || !out || !rhs_indices)
-        return fail(MLXQ_ERR_NULL, "gather_qmm: NULL pointer");
+        return fail(MLXQ_ERR_NULL, "%s: NULL pointer", what);
     if (!aligned16(x) || !aligned16(w) || !aligned16(scales) || !aligned16(biases) ||
         !aligned16(out))
-        return fail(MLXQ_ERR_ALIGN, "gather_qmm: pointers must be 16-byte aligned");
+        return fail(MLXQ_ERR_ALIGN, "%s: pointers must be 16-byte aligned", what);
+    return MLXQ_OK;
+}
+
+// The grouped decode plan for a gather_qmm call; false when its kernel does not take
+// the shape (or MLXQ_GATHER_KERNEL=cpasync asks for the cp.async kernel).
+static bool gather_decode_plan(const DeviceInfo& di, bool lhs_given, int64_t lhs_div,
+                               int64_t batch, int64_t M, int64_t N, int64_t K,
+                               int64_t num_experts, int64_t x_batches, int group_size, int bits,
+                               int sorted_indices, mlxq::QgdPlan* plan) {
+    if (gather_cpasync_forced()) return false;
+    const bool rows_sorted = sorted_indices && !lhs_given && lhs_div == 1 && x_batches == batch;
+    // enough rows per expert for the grouped tcgen05 GEMM (mlxq_gather_qmm takes it first)
+    if (rows_sorted && batch * M >= kGroupedMinRows * num_experts &&
+        mlxq::qgemm_supported(static_cast<int>(batch * M), static_cast<int>(N),
+                              static_cast<int>(K), bits, group_size))
+        return false;
+    return mlxq::qmv_grouped_plan(bits, group_size, batch, static_cast<int>(M),
+                                  static_cast<int>(N), static_cast<int>(K),
+                                  static_cast<int>(num_experts), rows_sorted, di.num_sms,
+                                  di.max_smem, di.sm_smem, plan);
+}
+
+int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const void* biases,
+                    const int32_t* lhs_indices, int64_t lhs_div, const int32_t* rhs_indices,
+                    void* out, int64_t batch, int64_t M, int64_t N, int64_t K,
+                    int64_t num_experts, int64_t x_batches, int group_size, int bits, int dtype,
+                    int sorted_indices, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc = check_gather("gather_qmm", x, w, scales, biases, lhs_indices, lhs_div, rhs_indices,
+                          out, batch, M, N, K, num_experts, x_batches, group_size, bits, dtype);
+    if (rc) return rc;
     if (batch == 0 || M == 0) return MLXQ_OK;
     DeviceInfo di;
     if ((rc = device_info(&di, static_cast<cudaStream_t>(stream)))) return rc;
@@ -506,18 +537,16 @@ int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const 
     // Otherwise the TMA-fed grouped decode kernel: sorted rows of an expert taken
     // together, else one entry at a time (the cp.async kernel below when its plan does
     // not fit, or when MLXQ_GATHER_KERNEL=cpasync asks for it, for comparisons).
-    if (!gather_cpasync_forced()) {
-        const bool rows_sorted = mode == 2 && !lhs_indices && lhs_div == 1 && x_batches == batch;
+    {
         mlxq::QgdPlan gp;
-        if (mlxq::qmv_grouped_plan(bits, group_size, batch, static_cast<int>(M),
-                                   static_cast<int>(N), static_cast<int>(K),
-                                   static_cast<int>(num_experts), rows_sorted, di.num_sms,
-                                   di.max_smem, di.sm_smem, &gp)) {
+        if (gather_decode_plan(di, lhs_indices != nullptr, lhs_div, batch, M, N, K, num_experts, x_batches,
+                               group_size, bits, sorted_indices, &gp)) {
             cudaError_t e = mlxq::qmv_grouped_launch(
                 dtype, bits, group_size, gp, x, w, scales, biases, out, rhs_indices, lhs_indices,
                 static_cast<int>(lhs_div < 1 ? 1 : lhs_div), static_cast<int>(batch),
                 static_cast<int>(x_batches), static_cast<int>(M), static_cast<int>(N),
-                static_cast<int>(K), static_cast<int>(num_experts), false, st);
+                static_cast<int>(K), static_cast<int>(num_experts),
+                mlxq::launch_overlap_enabled(), st);
             if (e != cudaSuccess) return cuda_fail(e, "gather_qmm (grouped decode) launch");
             return MLXQ_OK;
         }
@@ -551,6 +580,54 @@ int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const 
     plan.overlap = false;  // index arrays come from the kernels just before
     cudaError_t e = mlxq::qmv_launch(dtype, bits, group_size, plan, p, st);
     if (e != cudaSuccess) return cuda_fail(e, "gather_qmm launch");
+    return MLXQ_OK;
+}
+
+int mlxq_gather_swiglu_supported(int64_t batch, int64_t M, int64_t N, int64_t K,
+                                 int64_t num_experts, int64_t x_batches, int group_size, int bits,
+                                 int dtype, int lhs_given, int sorted_indices) {
+    if (check_bits_gs(bits, group_size, true) || check_k(K, group_size)) return 0;
+    if (dtype != MLXQ_BF16 && dtype != MLXQ_F16) return 0;
+    if (batch < 1 || M < 1 || N < 16 || N % 16 || num_experts < 1 || x_batches < 1 ||
+        batch > kIntMax || M > kIntMax || N > kIntMax || K > kIntMax ||
+        num_experts > kIntMax || x_batches > kIntMax || batch * M > kIntMax ||
+        x_batches * M > kIntMax)
+        return 0;
+    DeviceInfo di;
+    if (device_info(&di, nullptr)) return 0;
+    mlxq::QgdPlan gp;
+    return gather_decode_plan(di, lhs_given != 0, 1, batch, M, N, K, num_experts, x_batches,
+                              group_size, bits, sorted_indices, &gp) ? 1 : 0;
+}
+
+int mlxq_gather_qmm_swiglu(const void* x, const uint32_t* w, const void* scales,
+                           const void* biases, const int32_t* lhs_indices, int64_t lhs_div,
+                           const int32_t* rhs_indices, void* out, int64_t batch, int64_t M,
+                           int64_t N, int64_t K, int64_t num_experts, int64_t x_batches,
+                           int group_size, int bits, int dtype, int sorted_indices, void* stream) {
+    int rc = check_gather("gather_qmm_swiglu", x, w, scales, biases, lhs_indices, lhs_div,
+                          rhs_indices, out, batch, M, N, K, num_experts, x_batches, group_size,
+                          bits, dtype);
+    if (rc) return rc;
+    if (N % 16)
+        return fail(MLXQ_ERR_SHAPE, "gather_qmm_swiglu: N=%lld must hold 16-row gate/up tiles",
+                    (long long)N);
+    if (batch == 0 || M == 0) return MLXQ_OK;
+    DeviceInfo di;
+    if ((rc = device_info(&di, static_cast<cudaStream_t>(stream)))) return rc;
+    mlxq::QgdPlan gp;
+    if (!gather_decode_plan(di, lhs_indices != nullptr, lhs_div, batch, M, N, K, num_experts, x_batches,
+                            group_size, bits, sorted_indices, &gp))
+        return fail(MLXQ_ERR_SHAPE,
+                    "gather_qmm_swiglu: no decode plan for this shape (call gather_qmm and "
+                    "apply the activation)");
+    cudaError_t e = mlxq::qmv_grouped_launch(
+        dtype, bits, group_size, gp, x, w, scales, biases, out, rhs_indices, lhs_indices,
+        static_cast<int>(lhs_div < 1 ? 1 : lhs_div), static_cast<int>(batch),
+        static_cast<int>(x_batches), static_cast<int>(M), static_cast<int>(N),
+        static_cast<int>(K), static_cast<int>(num_experts), mlxq::launch_overlap_enabled(),
+        static_cast<cudaStream_t>(stream), 1);
+    if (e != cudaSuccess) return cuda_fail(e, "gather_qmm_swiglu launch");
     return MLXQ_OK;
 }
 

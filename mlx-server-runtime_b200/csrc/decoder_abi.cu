@@ -196,6 +196,20 @@ int mlxq_moe_route(const void* logits, int logits_dtype, const float* expert_bia
     return e == cudaSuccess ? MLXQ_OK : cuda_fail(e, "moe_route launch");
 }
 
+int mlxq_moe_sort(const int32_t* indices, int64_t n, int num_experts, int32_t* order,
+                  int32_t* sorted_indices, int32_t* inverse, void* stream) {
+    if (n < 0 || n > 16384 || num_experts < 1 || num_experts > 1024)
+        return fail(MLXQ_ERR_SHAPE, "moe_sort: need n <= 16384 and 1 <= num_experts <= 1024");
+    if (!indices || !order || !sorted_indices || !inverse)
+        return fail(MLXQ_ERR_NULL, "moe_sort: NULL pointer");
+    if (n == 0) return MLXQ_OK;
+    cudaError_t e = mlxq::launch_moe_sort(indices, static_cast<int>(n), num_experts, order,
+                                          sorted_indices, inverse,
+                                          mlxq::launch_overlap_enabled(),
+                                          static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MLXQ_OK : cuda_fail(e, "moe_sort launch");
+}
+
 int mlxq_decode_advance(int32_t* positions, int32_t* kv_lens, int32_t* slots,
                         const int32_t* block_table, int64_t max_blocks, int64_t batch,
                         int page_size, void* stream) {

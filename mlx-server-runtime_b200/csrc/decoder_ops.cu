@@ -955,6 +955,105 @@ cudaError_t launch_moe_route(int logits_dtype, const void* logits, const float* 
 }
 
 // ------------------------------------------------------------------------------------
+// Stable sort of MoE routing entries by expert (the argsort pair of _gather_sort,
+// lfm2.py:613-618): order[p] = entry at sorted position p, sorted[p] = its expert,
+// inverse[i] = sorted position of entry i. One CTA, a counting sort: entries are
+// bucketed by clamp(v, -1, E) + 1 (values outside [0, E) form a bucket before and one
+// after the experts, each in entry order); warp w owns the contiguous slice w of the
+// entries and counts its buckets (shared-memory atomics), an exclusive scan over
+// (bucket, warp) gives each warp's first position per bucket, and the warp then
+// places its slice 32 entries at a time in order: lanes with the same bucket
+// (match_any) take consecutive positions by lane.
+constexpr int kMoeSortThreads = 1024;
+constexpr int kMoeSortWarps = kMoeSortThreads / 32;
+
+__global__ void __launch_bounds__(kMoeSortThreads) moe_sort_kernel(
+    const int32_t* __restrict__ idx, int n, int E, int32_t* __restrict__ order,
+    int32_t* __restrict__ sorted, int32_t* __restrict__ inverse) {
+    extern __shared__ int ms_smem[];
+    const int nb = E + 2;
+    int* cnt = ms_smem;                       // [nb][warps]: counts, then first positions
+    int* key = cnt + nb * kMoeSortWarps;      // [n] bucket of each entry
+    __shared__ int wsum[kMoeSortWarps];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int L = nb * kMoeSortWarps;
+    for (int i = tid; i < L; i += kMoeSortThreads) cnt[i] = 0;
+    __syncthreads();
+    const int per = (n + kMoeSortWarps - 1) / kMoeSortWarps;
+    const int lo = min(n, warp * per), hi = min(n, lo + per);
+    for (int i = lo + lane; i < hi; i += 32) {
+        const int k = max(-1, min(idx[i], E)) + 1;
+        key[i] = k;
+        atomicAdd(cnt + k * kMoeSortWarps + warp, 1);
+    }
+    __syncthreads();
+    // exclusive scan of cnt in (bucket, warp) order: thread t scans a contiguous run
+    {
+        const int run = (L + kMoeSortThreads - 1) / kMoeSortThreads;
+        const int r0 = min(L, tid * run), r1 = min(L, r0 + run);
+        int sum = 0;
+        for (int i = r0; i < r1; ++i) sum += cnt[i];
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        if (lane == 31) wsum[warp] = incl;
+        __syncthreads();
+        if (warp == 0) {
+            int w = wsum[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, w, o);
+                if (lane >= o) w += v;
+            }
+            wsum[lane] = w;  // inclusive over warps
+        }
+        __syncthreads();
+        int pos = incl - sum + (warp > 0 ? wsum[warp - 1] : 0);
+        for (int i = r0; i < r1; ++i) {
+            const int c = cnt[i];
+            cnt[i] = pos;
+            pos += c;
+        }
+    }
+    __syncthreads();
+    const unsigned below = (1u << lane) - 1u;
+    for (int base = lo; base < hi; base += 32) {
+        const int i = base + lane;
+        const bool live = i < hi;
+        const int k = live ? key[i] : -1 - lane;  // dead lanes match no one
+        const unsigned same = __match_any_sync(0xffffffffu, k);
+        if (live) {
+            int* slot = cnt + k * kMoeSortWarps + warp;
+            const int r = *slot + __popc(same & below);
+            order[r] = i;
+            sorted[r] = idx[i];
+            inverse[i] = r;
+        }
+        __syncwarp();
+        // the lowest lane of each bucket moves the warp's position on past its members
+        if (live && (same & below) == 0) cnt[k * kMoeSortWarps + warp] += __popc(same);
+        __syncwarp();
+    }
+}
+
+size_t moe_sort_smem(int n, int E) {
+    return static_cast<size_t>(n + (E + 2) * kMoeSortWarps) * sizeof(int);
+}
+
+cudaError_t launch_moe_sort(const int32_t* idx, int n, int E, int32_t* order, int32_t* sorted,
+                            int32_t* inverse, bool overlap, cudaStream_t st) {
+    void* args[] = {&idx, &n, &E, &order, &sorted, &inverse};
+    static PerDevice cfg;
+    return launch_ex(reinterpret_cast<const void*>(&moe_sort_kernel), cfg, dim3(1),
+                     dim3(kMoeSortThreads), moe_sort_smem(n, E), st, overlap, args);
+}
+
+// ------------------------------------------------------------------------------------
 // One decode step further for every sequence: the next token sits at position
 // p + 1, the cache then holds p + 2 keys, and its slot is that position's place in
 // the sequence's pages (-1 past the block table).

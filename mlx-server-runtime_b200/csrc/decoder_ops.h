@@ -35,6 +35,9 @@ cudaError_t launch_embed(int dtype, int bits, const int32_t* ids, int n, const u
 cudaError_t launch_moe_route(int logits_dtype, const void* logits, const float* bias,
                              int32_t* indices, int scores_dtype, void* scores, int T, int E, int K,
                              int norm, bool overlap, cudaStream_t st);
+size_t moe_sort_smem(int n, int E);
+cudaError_t launch_moe_sort(const int32_t* idx, int n, int E, int32_t* order, int32_t* sorted,
+                            int32_t* inverse, bool overlap, cudaStream_t st);
 cudaError_t launch_decode_advance(int32_t* positions, int32_t* kv_lens, int32_t* slots,
                                   const int32_t* block_table, int max_blocks, int B, int page,
                                   bool overlap, cudaStream_t st);

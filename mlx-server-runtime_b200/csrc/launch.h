@@ -174,7 +174,7 @@ cudaError_t qmv_grouped_launch(int dtype, int bits, int gs, const QgdPlan& plan,
                                const uint32_t* w, const void* s, const void* b, void* out,
                                const int32_t* rhs, const int32_t* lhs, int lhs_div, int batch,
                                int x_batches, int M, int N, int K, int E, bool overlap,
-                               cudaStream_t st);
+                               cudaStream_t st, int epi = 0);
 // A single bounded wait that runs out (mlxq_check_bounded_wait).
 cudaError_t launch_bounded_wait_check(uint32_t polls, cudaStream_t st);
 

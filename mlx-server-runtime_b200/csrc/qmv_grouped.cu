@@ -5,7 +5,7 @@
 
 namespace mlxq {
 
-template <typename T, int BITS, int GS, int TM, int BR>
+template <typename T, int BITS, int GS, int TM, int BR, int EPI>
 cudaError_t qgd_launch_t(const CUtensorMap& tw, const QgdParams& p, int grid, size_t smem,
                          bool overlap, cudaStream_t st);
 
@@ -61,23 +61,27 @@ bool qmv_grouped_plan(int bits, int gs, long long batch, int M, int N, int K, in
     return true;
 }
 
-#define QGD_CASE_TM(T, BITS, GS)                                                         \
-    switch (plan.TM) {                                                                   \
-        case 1: return qgd_launch_t<T, BITS, GS, 1, 64>(tw, p, plan.P, plan.smem, overlap, st); \
-        case 4: return qgd_launch_t<T, BITS, GS, 4, 64>(tw, p, plan.P, plan.smem, overlap, st); \
-        default: return qgd_launch_t<T, BITS, GS, 8, 64>(tw, p, plan.P, plan.smem, overlap, st); \
+#define QGD_CASE_TM(T, BITS, GS, EPI)                                                        \
+    switch (plan.TM) {                                                                       \
+        case 1: return qgd_launch_t<T, BITS, GS, 1, 64, EPI>(tw, p, plan.P, plan.smem, overlap, st); \
+        case 4: return qgd_launch_t<T, BITS, GS, 4, 64, EPI>(tw, p, plan.P, plan.smem, overlap, st); \
+        default: return qgd_launch_t<T, BITS, GS, 8, 64, EPI>(tw, p, plan.P, plan.smem, overlap, st); \
     }
+#define QGD_CASE(T, BITS, GS)                     \
+    if (epi == 1) { QGD_CASE_TM(T, BITS, GS, 1) } \
+    QGD_CASE_TM(T, BITS, GS, 0)
 
 template <typename T>
-static cudaError_t qgd_dispatch(int bits, int gs, const CUtensorMap& tw, const QgdParams& p,
-                                const QgdPlan& plan, bool overlap, cudaStream_t st) {
+static cudaError_t qgd_dispatch(int bits, int gs, int epi, const CUtensorMap& tw,
+                                const QgdParams& p, const QgdPlan& plan, bool overlap,
+                                cudaStream_t st) {
     if (bits == 4) {
-        if (gs == 32) { QGD_CASE_TM(T, 4, 32) }
-        if (gs == 64) { QGD_CASE_TM(T, 4, 64) }
-        if (gs == 128) { QGD_CASE_TM(T, 4, 128) }
+        if (gs == 32) { QGD_CASE(T, 4, 32) }
+        if (gs == 64) { QGD_CASE(T, 4, 64) }
+        if (gs == 128) { QGD_CASE(T, 4, 128) }
     } else if (bits == 8) {
-        if (gs == 32) { QGD_CASE_TM(T, 8, 32) }
-        if (gs == 64) { QGD_CASE_TM(T, 8, 64) }
+        if (gs == 32) { QGD_CASE(T, 8, 32) }
+        if (gs == 64) { QGD_CASE(T, 8, 64) }
     }
     return cudaErrorInvalidValue;
 }
@@ -86,7 +90,8 @@ cudaError_t qmv_grouped_launch(int dtype, int bits, int gs, const QgdPlan& plan,
                                const uint32_t* w, const void* s, const void* b, void* out,
                                const int32_t* rhs, const int32_t* lhs, int lhs_div, int batch,
                                int x_batches, int M, int N, int K, int E, bool overlap,
-                               cudaStream_t st) {
+                               cudaStream_t st, int epi) {
+    if (epi == 1 && N % 16) return cudaErrorInvalidValue;
     const unsigned long long kw = static_cast<unsigned long long>(K) * bits / 32;
     CUtensorMap tw;
     if (plan.BR != kQgdRows ||
@@ -102,8 +107,9 @@ cudaError_t qmv_grouped_launch(int dtype, int bits, int gs, const QgdPlan& plan,
     p.batch = batch; p.x_batches = x_batches; p.M = M;
     p.N = N; p.K = K; p.G = K / gs; p.E = E;
     p.S = plan.S; p.RB = plan.RB; p.stages = plan.stages; p.sorted = plan.sorted ? 1 : 0;
-    if (dtype == kBF16) return qgd_dispatch<__nv_bfloat16>(bits, gs, tw, p, plan, overlap, st);
-    if (dtype == kF16) return qgd_dispatch<__half>(bits, gs, tw, p, plan, overlap, st);
+    if (dtype == kBF16)
+        return qgd_dispatch<__nv_bfloat16>(bits, gs, epi, tw, p, plan, overlap, st);
+    if (dtype == kF16) return qgd_dispatch<__half>(bits, gs, epi, tw, p, plan, overlap, st);
     return cudaErrorInvalidValue;
 }
 

@@ -81,7 +81,10 @@ struct QgdParams {
     int* err;
 };
 
-template <typename T, int BITS, int GS, int TM, int BR>
+// EPI 0: the outputs out[row, n]. EPI 1: SwiGLU over gate/up rows interleaved by
+// 16-row tiles in every expert (as the dense decode kernel's epilogue 1): out[row, c]
+// = silu(gate) * up for the N / 2 columns, each projection rounded to T first.
+template <typename T, int BITS, int GS, int TM, int BR, int EPI>
 __global__ void __launch_bounds__(qgd::THREADS, 2)
     qmv_grouped_kernel(const __grid_constant__ CUtensorMap tw, const QgdParams p) {
     using namespace qt;
@@ -331,19 +334,33 @@ __global__ void __launch_bounds__(qgd::THREADS, 2)
         }
         cons.combine(red, lane, acc);
         if (cons.kq == 0 && !*s_abort) {
-            const int row0 = rb * BR + 16 * cons.rt + cons.r;
+            if constexpr (EPI == 1) {
+                // this lane holds gate row r and up row r + 8 of its 16-row tile
+                const int n = (rb * BR + 16 * cons.rt) / 2 + cons.r;
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    const int n = row0 + 8 * hh;
+                for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                     for (int q = 0; q < 2; ++q) {
                         const int t = 8 * nt + 2 * cons.c + q;
-                        if (t < ck.rows && n < N)
-                            og[(ck.orow + t) * N + n] = ET::from_f(acc[nt][2 * hh + q]);
+                        if (t < ck.rows && 2 * n < N)
+                            og[(ck.orow + t) * (N / 2) + n] =
+                                swiglu_out<T>(acc[nt][q], acc[nt][2 + q]);
                     }
-                }
+            } else {
+                const int row0 = rb * BR + 16 * cons.rt + cons.r;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        const int n = row0 + 8 * hh;
+#pragma unroll
+                        for (int q = 0; q < 2; ++q) {
+                            const int t = 8 * nt + 2 * cons.c + q;
+                            if (t < ck.rows && n < N)
+                                og[(ck.orow + t) * N + n] = ET::from_f(acc[nt][2 * hh + q]);
+                        }
+                    }
+            }
         }
     }
 }

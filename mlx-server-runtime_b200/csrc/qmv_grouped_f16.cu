@@ -1,4 +1,4 @@
 #include "qmv_grouped_inst.cuh"
 namespace mlxq {
-MLXQ_INSTANTIATE_QGD(__half)
+MLXQ_INSTANTIATE_QGD(__half, 0)
 }

@@ -6,10 +6,10 @@
 
 namespace mlxq {
 
-template <typename T, int BITS, int GS, int TM, int BR>
+template <typename T, int BITS, int GS, int TM, int BR, int EPI>
 cudaError_t qgd_launch_t(const CUtensorMap& tw, const QgdParams& p, int grid, size_t smem,
                          bool overlap, cudaStream_t st) {
-    auto kern = qmv_grouped_kernel<T, BITS, GS, TM, BR>;
+    auto kern = qmv_grouped_kernel<T, BITS, GS, TM, BR, EPI>;
     static PerDevice configured;
     int dev = 0;
     cudaError_t e = current_device(&dev);
@@ -29,20 +29,20 @@ cudaError_t qgd_launch_t(const CUtensorMap& tw, const QgdParams& p, int grid, si
     return cudaLaunchKernelEx(&cfg, kern, tw, p);
 }
 
-#define MLXQ_QGD_INST0(T, BITS, GS, TM, BR) \
-    template cudaError_t qgd_launch_t<T, BITS, GS, TM, BR>(const CUtensorMap&, const QgdParams&, \
-                                                           int, size_t, bool, cudaStream_t);
-#define MLXQ_QGD_INST1(T, BITS, GS)      \
-    MLXQ_QGD_INST0(T, BITS, GS, 1, 64)   \
-    MLXQ_QGD_INST0(T, BITS, GS, 4, 64)   \
-    MLXQ_QGD_INST0(T, BITS, GS, 8, 64)
+#define MLXQ_QGD_INST0(T, BITS, GS, TM, BR, EPI)                                              \
+    template cudaError_t qgd_launch_t<T, BITS, GS, TM, BR, EPI>(                              \
+        const CUtensorMap&, const QgdParams&, int, size_t, bool, cudaStream_t);
+#define MLXQ_QGD_INST1(T, BITS, GS, EPI)      \
+    MLXQ_QGD_INST0(T, BITS, GS, 1, 64, EPI)   \
+    MLXQ_QGD_INST0(T, BITS, GS, 4, 64, EPI)   \
+    MLXQ_QGD_INST0(T, BITS, GS, 8, 64, EPI)
 
-// Every (bits, group size) the plan accepts, for activation type T.
-#define MLXQ_INSTANTIATE_QGD(T)   \
-    MLXQ_QGD_INST1(T, 4, 32)      \
-    MLXQ_QGD_INST1(T, 4, 64)      \
-    MLXQ_QGD_INST1(T, 4, 128)     \
-    MLXQ_QGD_INST1(T, 8, 32)      \
-    MLXQ_QGD_INST1(T, 8, 64)
+// Every (bits, group size) the plan accepts, for activation type T and epilogue EPI.
+#define MLXQ_INSTANTIATE_QGD(T, EPI)   \
+    MLXQ_QGD_INST1(T, 4, 32, EPI)      \
+    MLXQ_QGD_INST1(T, 4, 64, EPI)      \
+    MLXQ_QGD_INST1(T, 4, 128, EPI)     \
+    MLXQ_QGD_INST1(T, 8, 32, EPI)      \
+    MLXQ_QGD_INST1(T, 8, 64, EPI)
 
 }  // namespace mlxq

@@ -66,20 +66,23 @@ __device__ __forceinline__ void store_words(void* p, const uint32_t (&r)[N]) {
 }
 
 // The code of one element, clamp(rint(RN(d / s)), 0, n_bins) with RN the IEEE
-// quotient. The fast quotient __fdividef(d, s) is within 2 ulp of d / s for
-// 2^-126 <= |s| <= 2^126 (CUDA's documented bound); a result within 1e-3 of a
-// half-integer, outside [-1024, 1024] or not a number is recomputed with the IEEE
-// division, so the rounding to an integer never differs from the exact quotient's
-// (2 ulp at |q| <= 1024 is below 2.5e-4). `fast` is false when |s| is outside the
-// bound's range.
-__device__ __forceinline__ float quant_code(float d, float s, float n_bins, bool fast) {
-    float q = __fdividef(d, s);
-    const float f = q - floorf(q);
-    if (!fast || !(fabsf(q) <= 1024.0f) || fabsf(f - 0.5f) < 1e-3f) q = __fdiv_rn(d, s);
-    return fminf(fmaxf(rintf(q), 0.0f), n_bins);
+// quotient, from r = RN(1 / s): q = RN(d * r) is within (2^-23 + 2^-48) |d / s| of
+// d / s, and RN(d / s) within 2^-24 |d / s|, so for |q| <= 1024 the two differ by
+// less than 2e-4. When q is more than 1e-3 from every half-integer, both round to
+// the same integer; otherwise (or when q is outside [-1024, 1024], not a number, or
+// r is not a normal float: `fast` false) the IEEE quotient is taken.
+__device__ __forceinline__ float quant_code(float d, float s, float r, float n_bins, bool fast) {
+    const float q = __fmul_rn(d, r);
+    float k = rintf(q);
+    if (!fast || !(fabsf(q) <= 1024.0f) || fabsf(q - k) > 0.499f) k = rintf(__fdiv_rn(d, s));
+    return fminf(fmaxf(k, 0.0f), n_bins);
 }
 
-template <typename T, int BITS>
+// One thread quantizes WPT consecutive packed words (WPT * 32/bits elements, all in
+// one group); the group_size / (WPT * 32/bits) threads of a group sit in adjacent
+// lanes, so group min/max is a shuffle reduction over them, and the group's scale
+// and bias (three IEEE divisions) are worked out once per WPT words.
+template <typename T, int BITS, int WPT>
 __global__ void __launch_bounds__(256) quantize_kernel(const T* __restrict__ w,
                                                        uint32_t* __restrict__ wq,
                                                        T* __restrict__ scales,
@@ -89,20 +92,24 @@ __global__ void __launch_bounds__(256) quantize_kernel(const T* __restrict__ w,
     constexpr int EPW = 32 / BITS;
     constexpr int NW = EPW / Packed<T>::kPerWord;  // input words per packed word
     const float n_bins = static_cast<float>((1 << BITS) - 1);
-    const long long wi = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const long long ti = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const long long wi = ti * WPT;  // first packed word (total_words is a multiple of WPT)
     const bool live = wi < total_words;
 
-    float v[EPW];
+    float v[WPT][EPW];
     float lmax = -INFINITY, lmin = INFINITY;
     if (live) {
-        uint32_t raw[NW];
-        load_words<NW>(w + wi * EPW, raw);
+        uint32_t raw[WPT][NW];
 #pragma unroll
-        for (int e = 0; e < EPW; ++e) {
-            v[e] = Packed<T>::get(raw[e / Packed<T>::kPerWord], e % Packed<T>::kPerWord);
-            lmax = fmaxf(lmax, v[e]);
-            lmin = fminf(lmin, v[e]);
-        }
+        for (int j = 0; j < WPT; ++j) load_words<NW>(w + (wi + j) * EPW, raw[j]);
+#pragma unroll
+        for (int j = 0; j < WPT; ++j)
+#pragma unroll
+            for (int e = 0; e < EPW; ++e) {
+                v[j][e] = Packed<T>::get(raw[j][e / Packed<T>::kPerWord], e % Packed<T>::kPerWord);
+                lmax = fmaxf(lmax, v[j][e]);
+                lmin = fminf(lmin, v[j][e]);
+            }
     }
     // Reduce over the lanes of this group (an aligned power-of-two segment of
     // the warp). Lanes past the end form whole segments of their own.
@@ -123,17 +130,21 @@ __global__ void __launch_bounds__(256) quantize_kernel(const T* __restrict__ w,
         scale = __fdiv_rn(edge, q0);
         bias = edge;
     }
-    const float as = fabsf(scale);
-    const bool fast = as >= 0x1p-126f && as <= 0x1p126f;
-    uint32_t word = 0;
+    const float r = __frcp_rn(scale);
+    const float ar = fabsf(r);
+    const bool fast = ar >= 0x1p-126f && ar <= 0x1p126f;
 #pragma unroll
-    for (int e = 0; e < EPW; ++e) {
-        const float q = quant_code(__fsub_rn(v[e], bias), scale, n_bins, fast);
-        word |= static_cast<uint32_t>(q) << (BITS * e);
+    for (int j = 0; j < WPT; ++j) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int e = 0; e < EPW; ++e) {
+            const float q = quant_code(__fsub_rn(v[j][e], bias), scale, r, n_bins, fast);
+            word |= static_cast<uint32_t>(q) << (BITS * e);
+        }
+        __stcs(wq + wi + j, word);
     }
-    __stcs(wq + wi, word);
     if ((threadIdx.x & (lanes_per_group - 1)) == 0) {
-        const long long g = wi >> log2_lanes;
+        const long long g = ti >> log2_lanes;
         scales[g] = Elem<T>::from_f(scale);
         biases[g] = Elem<T>::from_f(bias);
     }
@@ -193,24 +204,42 @@ static int log2_exact(int v) {
     return l;
 }
 
+// Packed words per quantize thread: four (one 64-byte span of bf16 weights at 4 bits)
+// unless a group has fewer.
+constexpr int kQuantWPT = 4;
+
+template <typename T, int BITS>
+static cudaError_t launch_quantize_b(const T* w, uint32_t* wq, T* s, T* b, long long words,
+                                     int gs, cudaStream_t st) {
+    const int wpg = gs / (32 / BITS);  // packed words per group
+    if (wpg >= kQuantWPT) {
+        const int lanes = wpg / kQuantWPT;
+        const long long threads = words / kQuantWPT;
+        const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
+        quantize_kernel<T, BITS, kQuantWPT>
+            <<<blocks, 256, 0, st>>>(w, wq, s, b, words, lanes, log2_exact(lanes));
+    } else {
+        const unsigned blocks = static_cast<unsigned>((words + 255) / 256);
+        quantize_kernel<T, BITS, 1><<<blocks, 256, 0, st>>>(w, wq, s, b, words, wpg,
+                                                            log2_exact(wpg));
+    }
+    return cudaGetLastError();
+}
+
 template <typename T>
 static cudaError_t launch_quantize_t(const void* w, uint32_t* wq, void* s, void* b, long long rows,
                                      long long K, int gs, int bits, cudaStream_t st) {
     const long long words = rows * K * bits / 32;
-    const int lanes = gs / (32 / bits);
-    const int ll = log2_exact(lanes);
-    const unsigned blocks = static_cast<unsigned>((words + 255) / 256);
     if (words == 0) return cudaSuccess;
     const T* wt = static_cast<const T*>(w);
     T* st_ = static_cast<T*>(s);
     T* bt = static_cast<T*>(b);
     switch (bits) {
-        case 2: quantize_kernel<T, 2><<<blocks, 256, 0, st>>>(wt, wq, st_, bt, words, lanes, ll); break;
-        case 4: quantize_kernel<T, 4><<<blocks, 256, 0, st>>>(wt, wq, st_, bt, words, lanes, ll); break;
-        case 8: quantize_kernel<T, 8><<<blocks, 256, 0, st>>>(wt, wq, st_, bt, words, lanes, ll); break;
+        case 2: return launch_quantize_b<T, 2>(wt, wq, st_, bt, words, gs, st);
+        case 4: return launch_quantize_b<T, 4>(wt, wq, st_, bt, words, gs, st);
+        case 8: return launch_quantize_b<T, 8>(wt, wq, st_, bt, words, gs, st);
         default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 
 template <typename T>

@@ -302,19 +302,58 @@ class QuantizedSwitchLinear(Module):
         return out
 
 
-def _gather_sort(x, indices):
-    """Rows sorted by expert (lfm2.py:613-618)."""
+def _gather_sort(x, indices, num_experts=None):
+    """Rows sorted by expert (lfm2.py:613-618): the rows of x for the routing entries
+    in expert order (stable), the sorted indices and the inverse permutation. With the
+    expert count known and at most 16384 entries, one device kernel (core.moe_sort)
+    gives both permutations; otherwise torch's stable argsort."""
     width = indices.shape[-1]
     flat = indices.reshape(-1)
+    xs = x.reshape(-1, *x.shape[-2:])
+    if num_experts is not None and 0 < flat.numel() <= 16384 and num_experts <= 1024:
+        order, srt, inverse = core.moe_sort(flat.to(torch.int32), num_experts)
+        rows = torch.div(order, width, rounding_mode="floor")
+        return xs.index_select(0, rows), srt, inverse
     order = torch.argsort(flat, stable=True)
     inverse = torch.argsort(order)
-    xs = x.reshape(-1, *x.shape[-2:])
     return xs[order // width], flat[order], inverse
 
 
 def _scatter_unsort(x, inverse, shape):
     """Inverse of _gather_sort (lfm2.py:621-622)."""
-    return x[inverse].reshape(*shape, *x.shape[1:])
+    return x.index_select(0, inverse).reshape(*shape, *x.shape[1:])
+
+
+class FusedSwitchGateUp(Module):
+    """An expert bank's gate and up projections in interleave_gate_up's layout (each
+    expert's rows interleaved by 16-row tiles): silu(gate) * up per routed entry from
+    one gather_qmm_swiglu call (one launch at decode sizes)."""
+
+    def __init__(self, weight, scales, biases, group_size: int, bits: int, mode: str):
+        self.weight, self.scales, self.biases = weight, scales, biases
+        self.group_size, self.bits, self.mode = group_size, bits, mode
+
+    @classmethod
+    def from_pair(cls, gate: "QuantizedSwitchLinear", up: "QuantizedSwitchLinear"):
+        for a in (gate, up):
+            if not isinstance(a, QuantizedSwitchLinear) or hasattr(a, "bias"):
+                raise ValueError("gate and up must be quantized expert banks without bias")
+        if (gate.group_size, gate.bits, gate.mode) != (up.group_size, up.bits, up.mode):
+            raise ValueError("gate and up must share group_size, bits and mode")
+        w, s, b = core.interleave_gate_up((gate.weight, gate.scales, gate.biases),
+                                          (up.weight, up.scales, up.biases),
+                                          gate.group_size, gate.bits)
+        return cls(w, s, b, gate.group_size, gate.bits, gate.mode)
+
+    @property
+    def num_experts(self) -> int:
+        return self.weight.shape[0]
+
+    def __call__(self, x, indices, *, sorted_indices: bool = False):
+        return core.gather_qmm_swiglu(x, self.weight, self.scales, self.biases,
+                                      rhs_indices=indices, group_size=self.group_size,
+                                      bits=self.bits, mode=self.mode,
+                                      sorted_indices=sorted_indices)
 
 
 class SwitchGLU(Module):
@@ -325,15 +364,28 @@ class SwitchGLU(Module):
         self.up_proj = SwitchLinear(input_dims, hidden_dims, num_experts, **kw)
         self.down_proj = SwitchLinear(hidden_dims, input_dims, num_experts, **kw)
 
+    def fuse_gate_up(self) -> None:
+        """Replace the quantized gate_proj and up_proj by one FusedSwitchGateUp (rows
+        copied bit for bit, no extra memory kept): up, gate and the activation then run
+        as one launch at decode sizes."""
+        self.gate_up_proj = FusedSwitchGateUp.from_pair(self.gate_proj, self.up_proj)
+        del self.gate_proj, self.up_proj
+
     def __call__(self, x, indices):
         x = x.unsqueeze(-2).unsqueeze(-3)
         do_sort = indices.numel() >= 64
         selected, inverse = indices, None
+        fused = getattr(self, "gate_up_proj", None)
         if do_sort:
-            x, selected, inverse = _gather_sort(x, indices)
-        up = self.up_proj(x, selected, sorted_indices=do_sort)
-        gate = self.gate_proj(x, selected, sorted_indices=do_sort)
-        out = self.down_proj(silu(gate) * up, selected, sorted_indices=do_sort)
+            experts = (fused or self.gate_proj).weight.shape[0]
+            x, selected, inverse = _gather_sort(x, indices, experts)
+        if fused is not None:
+            act = fused(x, selected, sorted_indices=do_sort)
+        else:
+            up = self.up_proj(x, selected, sorted_indices=do_sort)
+            gate = self.gate_proj(x, selected, sorted_indices=do_sort)
+            act = silu(gate) * up
+        out = self.down_proj(act, selected, sorted_indices=do_sort)
         if do_sort:
             out = _scatter_unsort(out, inverse, indices.shape)
         return out.squeeze(-2)

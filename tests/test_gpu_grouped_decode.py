@@ -12,7 +12,7 @@ import pytest
 import torch
 
 import mlx_server_runtime_b200 as mxq
-from oracle import coracle
+from oracle import coracle, oracle_np as O
 
 from gpu_util import close, rand_weights, rand_x, to_dev, to_np
 
@@ -120,3 +120,55 @@ def test_repeated_calls_and_graph_replay():
     ref = coracle.gather_qmm(to_np(x), wq, s, b, routing, "bfloat16", 64, 4)
     close(to_np(out["y"]), ref, "bfloat16")
     del g
+
+
+# ------------------------------------------------------------ SwiGLU epilogue ----
+def _swiglu_ref(g, u, dt):
+    """silu(g) * u from the two projections as the oracle writes them (rounded to dt)."""
+    gf, uf = O.to_f32(g, dt).astype(np.float64), O.to_f32(u, dt).astype(np.float64)
+    return O.from_f32((gf / (1.0 + np.exp(-gf)) * uf).astype(np.float32), dt)
+
+
+@pytest.mark.parametrize("sorted_rows", [True, False])
+@pytest.mark.parametrize("K", [768, 2048, 192])
+def test_gather_qmm_swiglu(sorted_rows, K):
+    """Gate and up banks interleaved per expert; K=192 (three groups) takes the
+    gather_qmm + element-wise form."""
+    dt, gs, bits = "bfloat16", 64, 4
+    rng = np.random.default_rng(K + sorted_rows)
+    E, I, T, k = 16, 96, 12, 4
+    gate, up = _experts(rng, E, I, K, dt, gs, bits), _experts(rng, E, I, K, dt, gs, bits)
+    idx = np.stack([rng.choice(E, k, replace=False) for _ in range(T)]).astype(np.int32)
+    x = rand_x(rng, (T, K), dt)
+    if sorted_rows:
+        flat = idx.reshape(-1)
+        order = np.argsort(flat, kind="stable")
+        xs, sel, lhs = x[order // k][:, None, :], flat[order].astype(np.int32), None
+    else:
+        xs, sel, lhs = x[:, None, :], idx.reshape(-1), np.repeat(np.arange(T, dtype=np.int32), k)
+    g = coracle.gather_qmm(xs, *gate, sel, dt, gs, bits, lhs=lhs)
+    u = coracle.gather_qmm(xs, *up, sel, dt, gs, bits, lhs=lhs)
+    ref = _swiglu_ref(g, u, dt)
+    dev = lambda t: tuple(to_dev(a, dt) if a.dtype != np.uint32 else to_dev(a) for a in t)
+    w, s, b = mxq.interleave_gate_up(dev(gate), dev(up), gs, bits)
+    y = mxq.gather_qmm_swiglu(to_dev(xs, dt), w, s, b,
+                              lhs_indices=None if lhs is None else to_dev(lhs),
+                              rhs_indices=to_dev(sel), sorted_indices=sorted_rows)
+    assert y.shape == (len(sel), 1, I)
+    close(to_np(y), ref, dt)
+
+
+@pytest.mark.parametrize("T", [1, 64])
+def test_fused_switch_glu_matches_unfused(T):
+    from mlx_server_runtime_b200 import nn
+    E, D, H = 32, 512, 256
+    g = torch.Generator(device="cuda").manual_seed(T)
+    sw = nn.SwitchGLU(D, H, E, generator=g)
+    nn.quantize(sw, 64, 4)
+    x = torch.randn(T, D, device="cuda", generator=g).to(torch.bfloat16)
+    idx = torch.stack([torch.randperm(E, device="cuda", generator=g)[:8] for _ in range(T)]).int()
+    y_ref = sw(x, idx)
+    sw.fuse_gate_up()
+    assert not hasattr(sw, "gate_proj") and hasattr(sw, "gate_up_proj")
+    y = sw(x, idx)
+    close(to_np(y), to_np(y_ref), "bfloat16")

@@ -50,3 +50,41 @@ def test_router_matches_reference(dtype, T, E, k, norm):
             ref_t = ref_t / (ref_t.sum() + 1e-20)
         np.testing.assert_allclose(got_s[t], ref_t, rtol=tol, atol=1e-6)
         assert np.all(np.diff(p[t, got_i[t]]) <= 1e-6)   # descending gates
+
+
+@pytest.mark.parametrize("n,E", [(1, 1), (8, 128), (512, 128), (4096, 128), (16384, 1024),
+                                 (333, 7)])
+def test_moe_sort_matches_stable_argsort(n, E):
+    """core.moe_sort against numpy's stable argsort (order, sorted indices, inverse)."""
+    from mlx_server_runtime_b200 import core
+    rng = np.random.default_rng(n + E)
+    idx = rng.integers(0, E, n).astype(np.int32)
+    order, srt, inv = (t.cpu().numpy() for t in core.moe_sort(torch.from_numpy(idx).cuda(), E))
+    ref = np.argsort(idx, kind="stable")
+    assert np.array_equal(order, ref)
+    assert np.array_equal(srt, idx[ref])
+    assert np.array_equal(inv, np.argsort(ref, kind="stable"))
+
+
+def test_moe_sort_out_of_range_groups():
+    from mlx_server_runtime_b200 import core
+    idx = np.array([3, -2, 9, 0, -1, 3, 12, 1], np.int32)     # E = 4
+    order, srt, inv = (t.cpu().numpy() for t in core.moe_sort(torch.from_numpy(idx).cuda(), 4))
+    # negatives first (entry order), then experts 0..3 (stable), then values >= 4
+    assert order.tolist() == [1, 4, 3, 7, 0, 5, 2, 6]
+    assert srt.tolist() == idx[order].tolist()
+    assert np.array_equal(inv[order], np.arange(8))
+
+
+def test_switch_glu_sorted_path_uses_device_sort():
+    """SwitchGLU at 64 entries sorts on the device; the result equals the unsorted
+    form (each entry through its expert) for the same routing."""
+    E, D, H = 16, 256, 128
+    g = torch.Generator(device="cuda").manual_seed(3)
+    sw = nn.SwitchGLU(D, H, E, generator=g)
+    nn.quantize(sw, 64, 4)
+    x = (torch.randn(8, D, device="cuda", generator=g)).to(torch.bfloat16)
+    idx = torch.stack([torch.randperm(E, device="cuda", generator=g)[:8] for _ in range(8)]).int()
+    y_sorted = sw(x, idx)                                   # 64 entries: sorted path
+    y_rows = torch.cat([sw(x[t:t + 1], idx[t:t + 1]) for t in range(8)])  # 8 entries each
+    assert torch.equal(y_sorted, y_rows)
