@@ -136,9 +136,10 @@ size_t mlxq_qmm_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, 
  * quantized_matmul: replaces mx.quantized_matmul(x, w, scales, biases,
  * transpose=True, group_size, bits) as called by nn.QuantizedLinear
  * (qwen2.py:58-61,123-134,227), plus QuantizedLinear's optional bias add.
- * Up to 32 rows of x use the decode kernel (HBM-bound); more rows with K a
+ * Up to 32 rows of x use the decode kernels (HBM-bound); more rows with K a
  * multiple of 64 use the tcgen05 prefill kernel (weights dequantized into
- * shared memory, rounded once to the activation dtype, fp32 accumulation).
+ * tensor memory as the MMA's A operand, rounded once to the activation dtype,
+ * fp32 accumulation).
  * x [M, K], w [N, K*bits/32], scales/biases [N, K/group_size], bias [N] or
  * NULL, out [M, N]; x/scales/biases/bias/out all of `dtype` (bf16 or f16).
  * out = round(x @ dequant(w)^T) with float32 accumulation; with bias,

@@ -285,8 +285,6 @@ __global__ void __launch_bounds__(attn::THREADS)
     __shared__ __align__(128) uint8_t qsm[16 * HD * 2];
     __shared__ __align__(128) uint8_t kv[2 * SK * HD * 2];  // keys, values; then warp O
     __shared__ float wm[NW][MAXG], wl[NW][MAXG];
-    __shared__ float mw[MAXG][MAXSPLIT], lw[MAXG][MAXSPLIT];
-    __shared__ float cinv[MAXG];
     __shared__ int pid[SK / 8 + 2];
     __shared__ int s_last;
     static_assert(NW * MAXG * HD * 4 <= 2 * SK * HD * 2, "warp outputs fit the tile buffer");
@@ -294,26 +292,42 @@ __global__ void __launch_bounds__(attn::THREADS)
     pdl_wait();
     const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int G = Hq / Hkv;
-    const int L = min(kv_lens[b], max_kv);  // max_kv <= the block table's reach
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int skeys = tps * SK;             // keys per split
+    const int ks0 = split * skeys;
+    const int32_t* bt = block_table + static_cast<size_t>(b) * max_blocks;
+    // The sequence length, the first tile's page ids and the queries do not depend on
+    // one another: their loads are issued together (page ids past the block table are
+    // not read).
+    constexpr int QPT = (16 * CH + THREADS - 1) / THREADS;  // query chunks per thread
+    int pid0 = 0;
+    const int p00 = ks0 / page;
+    if (tid < SK / 8 + 2 && p00 + tid < max_blocks) pid0 = bt[p00 + tid];
+    uint4 qv[QPT];
+#pragma unroll
+    for (int i = 0; i < QPT; ++i) {
+        const int c = tid + i * THREADS;
+        const int r = c / CH, ch = c % CH;
+        qv[i] = make_uint4(0u, 0u, 0u, 0u);
+        if (c < 16 * CH && r < G)
+            qv[i] = *reinterpret_cast<const uint4*>(
+                q + (static_cast<size_t>(b) * Hq + g * G + r) * HD + ch * 8);
+    }
+    const int L = min(kv_lens[b], max_kv);  // max_kv <= the block table's reach
     const int nsplit = (L + skeys - 1) / skeys;
     if (split >= nsplit) return;
-    const int ks0 = split * skeys, ke = min(L, ks0 + skeys);
+    const int ke = min(L, ks0 + skeys);
     const int ntile = (ke - ks0 + SK - 1) / SK;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int32_t* bt = block_table + static_cast<size_t>(b) * max_blocks;
     uint8_t* ksm = kv;
     uint8_t* vsm = kv + SK * HD * 2;
 
     // queries: rows = the group's heads, rows G..15 zero
-    for (int c = tid; c < 16 * CH; c += THREADS) {
-        const int r = c / CH, ch = c % CH;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (r < G)
-            v = *reinterpret_cast<const uint4*>(
-                q + (static_cast<size_t>(b) * Hq + g * G + r) * HD + ch * 8);
-        *reinterpret_cast<uint4*>(qsm + kv_swz<HD>(r, ch)) = v;
+#pragma unroll
+    for (int i = 0; i < QPT; ++i) {
+        const int c = tid + i * THREADS;
+        if (c < 16 * CH) *reinterpret_cast<uint4*>(qsm + kv_swz<HD>(c / CH, c % CH)) = qv[i];
     }
+    if (tid < SK / 8 + 2) pid[tid] = pid0;  // page sizes >= 8: a tile spans <= SK/8 + 1 pages
     __syncthreads();
     uint32_t qa[HD / 16][4];
     {
@@ -334,9 +348,11 @@ __global__ void __launch_bounds__(attn::THREADS)
         const int n = min(SK, ke - k0);
         const int p0 = k0 / page;
         const int np = (k0 + n - 1) / page - p0 + 1;
-        if (tile > 0) __syncthreads();  // the previous tile's buffers are free
-        if (tid < np) pid[tid] = bt[p0 + tid];
-        __syncthreads();
+        if (tile > 0) {
+            __syncthreads();  // the previous tile's buffers are free
+            if (tid < np) pid[tid] = bt[p0 + tid];
+            __syncthreads();
+        }
 #pragma unroll 4
         for (int c = tid; c < SK * CH; c += THREADS) {
             const int r = c / CH, ch = c % CH;
@@ -462,46 +478,33 @@ __global__ void __launch_bounds__(attn::THREADS)
                  static_cast<unsigned>(nsplit - 1);
     __syncthreads();
     if (!s_last) return;
-    // The last split merges them: every split's (max, sum) per head into shared memory
-    // at once, turned into weights exp2(m_s - M); then each thread reads its slice of
-    // every split's outputs with the loads in flight together.
-    for (int e = tid; e < G * nsplit; e += THREADS) {
-        const int hh = e / nsplit, sp = e % nsplit;
-        const float2 ml = __ldcg(&ws_ml[(base + sp) * MAXG + hh]);
-        mw[hh][sp] = ml.x;
-        lw[hh][sp] = ml.y;
-    }
-    __syncthreads();
-    for (int hh = tid; hh < G; hh += THREADS) {
-        float M = -INFINITY;
-        for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, mw[hh][sp]);
-        float den = 0.f;
-        for (int sp = 0; sp < nsplit; ++sp) {
-            const float c = exp2f(mw[hh][sp] - M);
-            mw[hh][sp] = c;
-            den = fmaf(c, lw[hh][sp], den);
-        }
-        cinv[hh] = 1.0f / den;
-    }
-    __syncthreads();
+    // The last split merges them in split order with a running maximum: each thread
+    // reads every split's (max, sum) of its head and its slice of the split's outputs,
+    // four splits' loads in flight together.
     if (h < G) {
         float acc[DPT];
 #pragma unroll
         for (int e = 0; e < DPT; ++e) acc[e] = 0.f;
+        float M = -INFINITY, den = 0.f;
 #pragma unroll 4
         for (int sp = 0; sp < nsplit; ++sp) {
-            const float c = mw[h][sp];
+            const float2 ml = __ldcg(&ws_ml[(base + sp) * MAXG + h]);
             const float* src = &ws_o[((base + sp) * MAXG + h) * HD + DPT * dd];
+            float v[DPT];
 #pragma unroll
             for (int e = 0; e < DPT; e += 4) {
-                const float4 v = __ldcg(reinterpret_cast<const float4*>(src + e));
-                acc[e] = fmaf(c, v.x, acc[e]);
-                acc[e + 1] = fmaf(c, v.y, acc[e + 1]);
-                acc[e + 2] = fmaf(c, v.z, acc[e + 2]);
-                acc[e + 3] = fmaf(c, v.w, acc[e + 3]);
+                const float4 t = __ldcg(reinterpret_cast<const float4*>(src + e));
+                v[e] = t.x; v[e + 1] = t.y; v[e + 2] = t.z; v[e + 3] = t.w;
             }
+            const float Mn = fmaxf(M, ml.x);
+            const float co = M == -INFINITY ? 0.f : exp2f(M - Mn);
+            const float cn = ml.x == -INFINITY ? 0.f : exp2f(ml.x - Mn);
+            den = fmaf(cn, ml.y, den * co);
+#pragma unroll
+            for (int e = 0; e < DPT; ++e) acc[e] = fmaf(cn, v[e], acc[e] * co);
+            M = Mn;
         }
-        const float inv = cinv[h];
+        const float inv = 1.0f / den;
         T* dst = out + (static_cast<size_t>(b) * Hq + g * G + h) * HD + DPT * dd;
 #pragma unroll
         for (int e = 0; e < DPT; e += 2)
