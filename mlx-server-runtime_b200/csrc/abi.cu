@@ -1,6 +1,7 @@
 // extern "C" entry points of libmlxq_b200.so (declared in include/mlxq_b200.h).
 // Host-side validation happens before anything is enqueued; every failure
 // returns a negative code and records a message for mlxq_last_error().
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -203,6 +204,44 @@ int mlxq_dequantize(const uint32_t* wq, const void* scales, const void* biases, 
     return MLXQ_OK;
 }
 
+// Rows the TMA-fed decode kernel takes in one launch (its token slots). 17-32 rows of a
+// small matrix run as two launches of it (rows 0-15, then the rest): each launch
+// streams the weights again, which pays only while they are small (k/v 512x3584 at 32
+// rows: 16.8 us against 30.1 us on the cp.async kernel; gate/up 18944x3584: 37.9 us
+// against 28.1 us). MLXQ_DECODE_CHUNKS=0 (read once per process) turns it off, for
+// comparisons.
+constexpr int64_t kTmaRows = 16;
+constexpr int64_t kChunkMaxWeightBytes = 4 << 20;
+
+static bool decode_chunks_enabled() {
+    static const bool v = [] {
+        const char* e = std::getenv("MLXQ_DECODE_CHUNKS");
+        return !(e && std::strcmp(e, "0") == 0);
+    }();
+    return v;
+}
+
+// Plans of the (at most two) row chunks of a decode-sized quantized_matmul on the TMA
+// kernel: plan[0] for the first kTmaRows rows (or all of M), plan[1] for the rest
+// (a copy of plan[0] when M <= kTmaRows). False when the kernel does not take the shape.
+static bool tma_row_chunks(int64_t M, int64_t N, int64_t K, int group_size, int bits, int dtype,
+                           const DeviceInfo& di, mlxq::QtPlan plan[2]) {
+    if (M < 1 || M > 2 * kTmaRows) return false;
+    if (M > kTmaRows && (!decode_chunks_enabled() || N * K * bits / 8 > kChunkMaxWeightBytes))
+        return false;
+    const int64_t m0 = std::min(M, kTmaRows);
+    if (!mlxq::qmv_tma_plan(dtype, bits, group_size, static_cast<int>(m0), static_cast<int>(N),
+                            static_cast<int>(K), di.num_sms, di.max_smem, di.sm_smem, &plan[0]))
+        return false;
+    plan[1] = plan[0];
+    if (M > kTmaRows &&
+        !mlxq::qmv_tma_plan(dtype, bits, group_size, static_cast<int>(M - kTmaRows),
+                            static_cast<int>(N), static_cast<int>(K), di.num_sms, di.max_smem,
+                            di.sm_smem, &plan[1]))
+        return false;
+    return true;
+}
+
 size_t mlxq_qmm_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, int bits,
                                int dtype) {
     if (check_bits_gs(bits, group_size, true) || check_k(K, group_size)) return 0;
@@ -217,10 +256,9 @@ size_t mlxq_qmm_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, 
                          di.num_sms, &gp);
         return gp.ws_bytes;
     }
-    mlxq::QtPlan tplan;
-    if (mlxq::qmv_tma_plan(dtype, bits, group_size, static_cast<int>(M), static_cast<int>(N),
-                           static_cast<int>(K), di.num_sms, di.max_smem, di.sm_smem, &tplan))
-        return tplan.ws_bytes;
+    mlxq::QtPlan tplan[2];
+    if (tma_row_chunks(M, N, K, group_size, bits, dtype, di, tplan))
+        return std::max(tplan[0].ws_bytes, tplan[1].ws_bytes);
     mlxq::QmvPlan plan;
     bool ok = false;
     return dense_plan(M, N, K, group_size, bits, dtype, di, &plan, &ok);
@@ -248,7 +286,7 @@ int mlxq_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
     if ((rc = device_info(&di, static_cast<cudaStream_t>(stream)))) return rc;
     if (mlxq::qgemm_supported(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), bits,
                               group_size)) {
-        // prefill: dequantize into shared memory + tcgen05 tensor cores
+        // prefill: dequantize into tensor memory + tcgen05 tensor cores
         mlxq::QgemmParams q{};
         q.x = x; q.w = w; q.s = scales; q.b = biases; q.bias = bias; q.out = out;
         q.M = static_cast<int>(M); q.N = static_cast<int>(N); q.K = static_cast<int>(K);
@@ -268,23 +306,27 @@ int mlxq_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
         if (e != cudaSuccess) return cuda_fail(e, "quantized_matmul (prefill) launch");
         return MLXQ_OK;
     }
-    mlxq::QtPlan tplan;
-    if (mlxq::qmv_tma_plan(dtype, bits, group_size, static_cast<int>(M), static_cast<int>(N),
-                           static_cast<int>(K), di.num_sms, di.max_smem, di.sm_smem, &tplan)) {
-        // decode, M <= 16: TMA-fed stream-K kernel
-        if (tplan.ws_bytes > 0) {
-            if (!workspace || workspace_bytes < tplan.ws_bytes)
+    mlxq::QtPlan tplan[2];
+    if (tma_row_chunks(M, N, K, group_size, bits, dtype, di, tplan)) {
+        // decode, M <= 32: the TMA-fed stream-K kernel, 16 rows per launch
+        const size_t need = std::max(tplan[0].ws_bytes, tplan[1].ws_bytes);
+        if (need > 0) {
+            if (!workspace || workspace_bytes < need)
                 return fail(MLXQ_ERR_WORKSPACE,
-                            "quantized_matmul: needs %zu workspace bytes, got %zu",
-                            tplan.ws_bytes, workspace ? workspace_bytes : (size_t)0);
+                            "quantized_matmul: needs %zu workspace bytes, got %zu", need,
+                            workspace ? workspace_bytes : (size_t)0);
             if (reinterpret_cast<uintptr_t>(workspace) & 255u)
                 return fail(MLXQ_ERR_ALIGN, "quantized_matmul: workspace must be 256-byte aligned");
         }
-        cudaError_t e = mlxq::qmv_tma_launch(
-            dtype, bits, group_size, tplan, x, w, scales, biases, bias, out, static_cast<int>(M),
-            static_cast<int>(N), static_cast<int>(K), workspace, mlxq::launch_overlap_enabled(),
-            static_cast<cudaStream_t>(stream));
-        if (e != cudaSuccess) return cuda_fail(e, "quantized_matmul (decode) launch");
+        for (int64_t r0 = 0, c = 0; r0 < M; r0 += kTmaRows, ++c) {
+            const int64_t mc = std::min(kTmaRows, M - r0);
+            cudaError_t e = mlxq::qmv_tma_launch(
+                dtype, bits, group_size, tplan[c], static_cast<const char*>(x) + r0 * K * 2, w,
+                scales, biases, bias, static_cast<char*>(out) + r0 * N * 2,
+                static_cast<int>(mc), static_cast<int>(N), static_cast<int>(K), workspace,
+                mlxq::launch_overlap_enabled(), static_cast<cudaStream_t>(stream));
+            if (e != cudaSuccess) return cuda_fail(e, "quantized_matmul (decode) launch");
+        }
         return MLXQ_OK;
     }
     mlxq::QmvPlan plan;

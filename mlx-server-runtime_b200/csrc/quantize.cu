@@ -71,11 +71,20 @@ __device__ __forceinline__ void store_words(void* p, const uint32_t (&r)[N]) {
 // less than 2e-4. When q is more than 1e-3 from every half-integer, both round to
 // the same integer; otherwise (or when q is outside [-1024, 1024], not a number, or
 // r is not a normal float: `fast` false) the IEEE quotient is taken.
-__device__ __forceinline__ float quant_code(float d, float s, float r, float n_bins, bool fast) {
+// Rounding to an integer adds and subtracts 1.5 * 2^23 (a float in [2^23, 2^24) has
+// unit spacing, and the add rounds to nearest even like rintf for |q| < 2^22), and the
+// clamped integer is read from the low mantissa bits of the same sum: no conversion
+// instructions on the common path.
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+constexpr uint32_t kRoundMagicBits = 0x4B400000u;
+
+__device__ __forceinline__ uint32_t quant_code(float d, float s, float r, float n_bins, bool fast) {
     const float q = __fmul_rn(d, r);
-    float k = rintf(q);
-    if (!fast || !(fabsf(q) <= 1024.0f) || fabsf(q - k) > 0.499f) k = rintf(__fdiv_rn(d, s));
-    return fminf(fmaxf(k, 0.0f), n_bins);
+    float k = __fsub_rn(__fadd_rn(q, kRoundMagic), kRoundMagic);
+    if (!fast || !(fabsf(q) <= 1024.0f) || fabsf(__fsub_rn(q, k)) > 0.499f)
+        k = rintf(__fdiv_rn(d, s));
+    k = fminf(fmaxf(k, 0.0f), n_bins);
+    return __float_as_uint(__fadd_rn(k, kRoundMagic)) - kRoundMagicBits;
 }
 
 // One thread quantizes WPT consecutive packed words (WPT * 32/bits elements, all in
@@ -138,8 +147,7 @@ __global__ void __launch_bounds__(256) quantize_kernel(const T* __restrict__ w,
         uint32_t word = 0;
 #pragma unroll
         for (int e = 0; e < EPW; ++e) {
-            const float q = quant_code(__fsub_rn(v[j][e], bias), scale, r, n_bins, fast);
-            word |= static_cast<uint32_t>(q) << (BITS * e);
+            word |= quant_code(__fsub_rn(v[j][e], bias), scale, r, n_bins, fast) << (BITS * e);
         }
         __stcs(wq + wi + j, word);
     }

@@ -30,9 +30,16 @@ def _case(dt, bits, gs, M, N, K, seed, bias=False, calls=1):
     return [to_np(y) for y in outs]
 
 
-@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 6, 7, 8, 9, 12, 16])
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 6, 7, 8, 9, 12, 16, 17, 24, 31, 32])
 def test_decode_token_counts(M):
     _case("bfloat16", 4, 64, M, 3584, 3584, seed=100 + M)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("M", [17, 24, 31, 32])
+def test_decode_two_launches(M, bits):
+    # small matrices at 17-32 rows: two launches of the 16-slot kernel
+    _case("bfloat16", bits, 64, M, 512, 3584, seed=300 + M + bits, bias=(M == 24))
 
 
 @pytest.mark.parametrize("dt", ["bfloat16", "float16"])
