@@ -90,3 +90,49 @@ def test_fused_gate_up_rejects_bias_and_mismatch():
         mnn.FusedGateUp(a, c)
     f = mnn.FusedGateUp(a, _layer(16, 256, False, 4))
     assert f.weight.shape == (32, 32)
+
+
+def _bank(E, N, K, seed):
+    w, s, b = _q(E * N, K, seed=seed)
+    return w.reshape(E, N, -1), s.reshape(E, N, -1), b.reshape(E, N, -1)
+
+
+def test_interleave_expert_banks_per_expert():
+    """3-D banks interleave within each expert: expert e of the result is the 2-D
+    interleave of expert e's gate and up."""
+    E, I, K = 3, 24, 256
+    gate, up = _bank(E, I, K, 11), _bank(E, I, K, 12)
+    w, s, b = mxq.interleave_gate_up(gate, up, 64, 4)
+    assert w.shape == (E, 2 * I, K // 8) and s.shape == (E, 2 * I, K // 64)
+    for e in range(E):
+        w2, s2, b2 = mxq.interleave_gate_up(tuple(t[e] for t in gate), tuple(t[e] for t in up),
+                                            64, 4)
+        assert torch.equal(w[e].view(torch.int32), w2.view(torch.int32))
+        assert torch.equal(s[e].view(torch.int16), s2.view(torch.int16))
+        assert torch.equal(b[e].view(torch.int16), b2.view(torch.int16))
+    # tile j of expert 1: gate rows 8j..8j+7, then up rows 8j..8j+7
+    assert torch.equal(w[1, 16:24].view(torch.int32), gate[0][1, 8:16].view(torch.int32))
+    assert torch.equal(w[1, 24:32].view(torch.int32), up[0][1, 8:16].view(torch.int32))
+
+
+def _switch(E, N, K, seed, bias=False):
+    q = mnn.QuantizedSwitchLinear.__new__(mnn.QuantizedSwitchLinear)
+    q.group_size, q.bits, q.mode = 64, 4, "affine"
+    q.weight, q.scales, q.biases = _bank(E, N, K, seed)
+    if bias:
+        q.bias = torch.zeros(E, N, dtype=torch.bfloat16)
+    return q
+
+
+def test_fuse_switch_gate_up_replaces_the_pair():
+    sw = mnn.SwitchGLU.__new__(mnn.SwitchGLU)
+    sw.gate_proj, sw.up_proj = _switch(4, 16, 128, 1), _switch(4, 16, 128, 2)
+    sw.down_proj = _switch(4, 128, 16 * 4, 3)
+    sw.fuse_gate_up()
+    f = sw.gate_up_proj
+    assert not hasattr(sw, "gate_proj") and not hasattr(sw, "up_proj")
+    assert f.weight.shape == (4, 32, 16) and f.num_experts == 4
+    with pytest.raises(ValueError):   # a bank with bias cannot fuse
+        mnn.FusedSwitchGateUp.from_pair(_switch(4, 16, 128, 4, bias=True), _switch(4, 16, 128, 5))
+    with pytest.raises(ValueError):
+        mxq.interleave_gate_up(_bank(4, 12, 128, 6), _bank(4, 12, 128, 7), 64, 4)  # 12 % 8
