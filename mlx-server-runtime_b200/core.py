@@ -506,9 +506,9 @@ def gather_qmm_swiglu(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
     interleave_gate_up's layout ([E, N, ...], N = 2 * hidden): [*S, M, N/2].
 
     Decode sizes run as one launch with the activation in the grouped kernel's
-    epilogue; other sizes run gather_qmm and then the activation as torch element-wise
-    ops. Either way each projection is rounded to x's dtype before silu(g) * u is
-    formed in float32 and rounded once more."""
+    epilogue (each projection rounded to x's dtype, silu(g) * u formed in float32 and
+    rounded once); other sizes run gather_qmm and then torch's silu and multiply in
+    x's dtype on the de-interleaved halves, as SwitchGLU's separate projections do."""
     _mode(mode)
     a = _gather_args(x, w, scales, biases, lhs_indices, rhs_indices, group_size, bits)
     dev, batch, M, N, K = a["dev"], a["batch"], a["M"], a["N"], a["K"]
@@ -520,9 +520,9 @@ def gather_qmm_swiglu(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
             int(a["lhs"] is not None), int(bool(sorted_indices))):
         y = gather_qmm(x, w, scales, biases, lhs_indices, rhs_indices, True, group_size, bits,
                        mode, sorted_indices)
-        y = y.reshape(*a["bshape"], M, N // 16, 2, 8).float()
+        y = y.reshape(*a["bshape"], M, N // 16, 2, 8)
         g, u = y[..., 0, :], y[..., 1, :]
-        return (torch.nn.functional.silu(g) * u).to(x.dtype).reshape(*a["bshape"], M, N // 2)
+        return (torch.nn.functional.silu(g) * u).reshape(*a["bshape"], M, N // 2)
     out = torch.empty(*a["bshape"], M, N // 2, dtype=x.dtype, device=dev)
     with torch.cuda.device(dev):
         st = torch.cuda.current_stream(dev)
