@@ -548,12 +548,15 @@ def expert_parallel_bench(torch, mxq, dist, dev, world, rank, stream):
     from mlx_server_runtime_b200 import distributed, nn
     e_local = MOE_E // world
     ws = moe_weights(torch, mxq, dev, seed=100 + rank, experts=e_local)
-    ep = distributed.ExpertParallelSwitchGLU(ws["gate"], ws["up"], ws["down"],
-                                             num_experts=MOE_E, group_size=GS, bits=BITS)
     gen = torch.Generator(device=dev)
     gen.manual_seed(200 + rank)
     res = {}
     for T in (64, 4096):
+        # decode size: fixed-capacity exchange (no host synchronisation); 4096 tokens:
+        # the counts first, then only the routed rows
+        ep = distributed.ExpertParallelSwitchGLU(
+            ws["gate"], ws["up"], ws["down"], num_experts=MOE_E, group_size=GS, bits=BITS,
+            capacity=T * MOE_TOPK if T <= 64 else None)
         x = torch.randn(T, MOE_HID, device=dev, generator=gen).to(torch.bfloat16)
         idx, _ = nn.route_topk(torch.randn(T, MOE_E, device=dev, generator=gen), MOE_TOPK)
         for _ in range(3):
@@ -574,7 +577,8 @@ def expert_parallel_bench(torch, mxq, dist, dev, world, rank, stream):
     del ep, ws
     torch.cuda.empty_cache()
     return {"what": "SwitchGLU with 128 experts split over the ranks, T tokens per rank, "
-                    "NCCL all-to-all dispatch and combine (host-synchronised split sizes)",
+                    "NCCL all-to-all dispatch and combine (T=64: fixed-capacity buffers, "
+                    "no host synchronisation; T=4096: host-synchronised split sizes)",
             "T_per_rank": res}
 
 

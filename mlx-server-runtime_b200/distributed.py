@@ -91,7 +91,8 @@ class ExpertParallelSwitchGLU:
     scales, biases) triples with a leading local-expert dimension."""
 
     def __init__(self, gate, up, down, *, num_experts: int, group_size=64, bits=4, group=None,
-                 local_gather: Callable | None = None, act: Callable | None = None):
+                 local_gather: Callable | None = None, act: Callable | None = None,
+                 capacity: int | None = None):
         self.gate, self.up, self.down = gate, up, down
         self.num_experts = num_experts
         self.group_size, self.bits = group_size, bits
@@ -103,10 +104,25 @@ class ExpertParallelSwitchGLU:
         self.e_local = num_experts // self.world
         self.local_gather = local_gather or _default_gather
         self.act = act or (lambda g, u: torch.nn.functional.silu(g) * u)
+        if capacity is not None and capacity < 1:
+            raise ValueError(f"capacity={capacity} must be >= 1 routed rows")
+        self.capacity = capacity
 
     def __call__(self, x: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
-        """x [T, D], indices [T, k] (global expert ids) -> [T, k, D] expert outputs."""
+        """x [T, D], indices [T, k] (global expert ids) -> [T, k, D] expert outputs.
+
+        With a `capacity` (routed rows per rank, the same on every rank; decode sizes)
+        every rank sends every rank a buffer of `capacity` rows, so the split sizes
+        are fixed: the call reads nothing back to the host and can be captured in a
+        CUDA graph, at the cost of sending world x capacity rows. Without one, the
+        ranks exchange their per-destination counts first (read back to the host) and
+        send only the routed rows. Every rank must use the same form."""
         T, D = x.shape
+        k = indices.shape[1]
+        if self.capacity is not None:
+            if T * k > self.capacity:
+                raise ValueError(f"{T * k} routed rows exceed the capacity {self.capacity}")
+            return self._call_fixed(x, indices)
         k = indices.shape[1]
         flat = indices.reshape(-1).to(torch.int64)
         dest = flat // self.e_local                              # owning rank per row
@@ -128,11 +144,7 @@ class ExpertParallelSwitchGLU:
         rows = recv_rows[lorder].unsqueeze(1)                     # [R, 1, D]
         sel = local_e[lorder].to(torch.int32)
         if rows.shape[0]:
-            g = self.local_gather(rows, *self.gate, sel, self.group_size, self.bits, True)
-            u = self.local_gather(rows, *self.up, sel, self.group_size, self.bits, True)
-            h = self.act(g, u)
-            y = self.local_gather(h, *self.down, sel, self.group_size, self.bits, True)
-            y = y.reshape(rows.shape[0], -1)
+            y = self._local_experts(rows, sel)
         else:
             y = x.new_empty(0, D)
         back = torch.empty_like(y)
@@ -142,4 +154,48 @@ class ExpertParallelSwitchGLU:
         dist.all_to_all_single(out_rows, back.contiguous(), sc, rc, group=self.group)
         out = torch.empty_like(out_rows)
         out[order] = out_rows
+        return out.reshape(T, k, D)
+
+    def _local_experts(self, rows, sel):
+        """The rank's experts on rows [R, D] sorted by local expert sel (entries with
+        sel < 0 first: padding, which the gathers leave unwritten)."""
+        g = self.local_gather(rows, *self.gate, sel, self.group_size, self.bits, True)
+        u = self.local_gather(rows, *self.up, sel, self.group_size, self.bits, True)
+        h = self.act(g, u)
+        y = self.local_gather(h, *self.down, sel, self.group_size, self.bits, True)
+        return y.reshape(rows.shape[0], -1)
+
+    def _call_fixed(self, x, indices):
+        T, D = x.shape
+        k = indices.shape[1]
+        W, C = self.world, self.capacity
+        dev = x.device
+        flat = indices.reshape(-1).to(torch.int64)
+        dest = flat // self.e_local
+        order = torch.argsort(dest * self.num_experts + flat, stable=True)
+        # slot of each routed row in the [W, C] send buffer: its destination's block,
+        # then its place among the rows for that destination (scatter_add: no host sync)
+        counts = torch.zeros(W, dtype=torch.int64, device=dev).scatter_add_(
+            0, dest, torch.ones_like(dest))
+        starts = torch.cumsum(counts, 0) - counts
+        sdest = dest[order]
+        slot = sdest * C + (torch.arange(T * k, device=dev) - starts[sdest])
+        send = x.new_zeros(W * C, D)
+        send[slot] = x[order // k]
+        send_e = torch.full((W * C,), -1, dtype=torch.int64, device=dev)
+        send_e[slot] = flat[order]
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=self.group)
+        recv_e = torch.empty_like(send_e)
+        dist.all_to_all_single(recv_e, send_e, group=self.group)
+        local_e = torch.where(recv_e >= 0, recv_e - self.rank * self.e_local,
+                              torch.full_like(recv_e, -1))
+        lorder = torch.argsort(local_e, stable=True)
+        y = self._local_experts(recv[lorder].unsqueeze(1), local_e[lorder].to(torch.int32))
+        back = torch.empty_like(y)
+        back[lorder] = y
+        ret = torch.empty_like(back)
+        dist.all_to_all_single(ret, back, group=self.group)
+        out = torch.empty(T * k, D, dtype=x.dtype, device=dev)
+        out[order] = ret[slot]
         return out.reshape(T, k, D)

@@ -92,7 +92,17 @@ def _sharded_linear_worker(rank, world, port, N, K, M, use_bias, q):
         q.put((rank, False, repr(e)))
 
 
-def _ep_worker(rank, world, port, E, D, I, tokens, k, q):
+def _oracle_gather_skip_padding(x, w, s, b, rhs, group_size, bits, sorted_indices):
+    """The oracle gather for rows with an expert; padding rows (rhs < 0) give zeros
+    (the GPU gathers leave them unwritten)."""
+    y = torch.zeros(rhs.shape[0], x.shape[1], w.shape[1], dtype=torch.bfloat16)
+    keep = (rhs >= 0).nonzero().reshape(-1)
+    if keep.numel():
+        y[keep] = _oracle_gather(x[keep], w, s, b, rhs[keep], group_size, bits, sorted_indices)
+    return y
+
+
+def _ep_worker(rank, world, port, E, D, I, tokens, k, capacity, q):
     try:
         dist = _setup(rank, world, port)
         from mlx_server_runtime_b200.distributed import ExpertParallelSwitchGLU
@@ -110,7 +120,8 @@ def _ep_worker(rank, world, port, E, D, I, tokens, k, q):
                        dtype=np.int32).reshape(T, k)
         idx = torch.from_numpy(idx)
         moe = ExpertParallelSwitchGLU(local(gate), local(up), local(down), num_experts=E,
-                                      group_size=64, bits=4, local_gather=_oracle_gather)
+                                      group_size=64, bits=4, capacity=capacity,
+                                      local_gather=_oracle_gather_skip_padding)
         got = moe(x, idx)
         # unsharded reference: every (token, slot) through its expert, one row at a time
         ref = torch.empty(T, k, D, dtype=torch.bfloat16)
@@ -157,9 +168,16 @@ def test_sharded_linear_allgather_matches_unsharded(N, use_bias):
 
 def test_expert_parallel_switchglu_matches_unsharded():
     # 4 experts over 2 ranks, rank 0 has 5 tokens and rank 1 has 3 (ragged dispatch)
-    res = _run(_ep_worker, 2, 4, 64, 128, (5, 3), 2)
+    res = _run(_ep_worker, 2, 4, 64, 128, (5, 3), 2, None)
     assert sorted(info for _, _, info in res) == [(3, 2, 64), (5, 2, 64)]
 
 
 def test_expert_parallel_rank_with_no_tokens():
-    _run(_ep_worker, 2, 4, 64, 128, (4, 0), 2)
+    _run(_ep_worker, 2, 4, 64, 128, (4, 0), 2, None)
+
+
+def test_expert_parallel_fixed_capacity():
+    # the same exchange with fixed [world, capacity] buffers (no host synchronisation);
+    # capacity above both ranks' routed rows, ragged token counts
+    res = _run(_ep_worker, 2, 4, 64, 128, (5, 3), 2, 12)
+    assert sorted(info for _, _, info in res) == [(3, 2, 64), (5, 2, 64)]

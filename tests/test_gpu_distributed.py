@@ -88,6 +88,13 @@ def _worker(rank, world, port, q):
         h = oracle_np.from_f32(act * u, "bfloat16")
         ref = coracle.gather_qmm(h, *host[2], flat, "bfloat16", 64, 4).reshape(T, k, D)
         close(to_np(got), ref, "bfloat16")
+        # the same with fixed-capacity buffers (no host synchronisation): 32 tokens x 2
+        # experts = 64 routed rows at most
+        moe_fixed = ExpertParallelSwitchGLU(*local, num_experts=E, group_size=64, bits=4,
+                                            capacity=64)
+        xd, idd = to_dev(x_np, "bfloat16", dev), torch.from_numpy(idx_np).to(dev)
+        close(to_np(moe_fixed(xd, idd)), ref, "bfloat16")
+        torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, True, ""))
