@@ -369,6 +369,24 @@ def prefill_sweep(torch, mxq, dev, stream, peak_tf):
         out["shapes"][name] = row
         del ws, w0
         torch.cuda.empty_cache()
+    # gate and up interleaved (37888 x 3584) with the SwiGLU epilogue: one launch writes
+    # silu(gate) * up, against gate_up above plus torch's element-wise activation
+    N, K = 2 * INTER, HIDDEN
+    w = (torch.randn(N, K, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+    w0 = mxq.quantize(w, GS, BITS)
+    del w
+    row = {}
+    for M in (512, 2048, 8192):
+        x = torch.randn(M, K, device=dev, generator=gen).to(torch.bfloat16)
+        ms = graph_ms(torch, [lambda: mxq.quantized_matmul_swiglu(x, *w0, GS, BITS)],
+                      4 if M == 8192 else 10, stream)
+        tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+        row[str(M)] = {"us": round(ms * 1e3, 1), "TFLOP/s": round(tf, 1),
+                       "frac": round(tf / peak_tf, 4)}
+        del x
+    out["shapes"]["gate_up_swiglu"] = row
+    del w0
+    torch.cuda.empty_cache()
     out["roofline"] = best
     return out
 

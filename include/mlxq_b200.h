@@ -212,16 +212,18 @@ int mlxq_quantized_matmul_argmax(const void* x, const uint32_t* w, const void* s
 
 /*
  * quantized_matmul_swiglu: the gate and up projections of a SwiGLU MLP and the
- * activation between them, silu(gate_proj(x)) * up_proj(x), in one decode launch.
+ * activation between them, silu(gate_proj(x)) * up_proj(x), in one launch.
  * The reference computes it as two quantized_matmul calls, a silu and a multiply
  * (qwen2.py:133-134, lfm2.py:212).
  * w / scales / biases hold the gate and up matrices interleaved by 16-row tiles:
  * tile j = gate rows 8j..8j+7 then up rows 8j..8j+7 (quantized rows copied as they
  * are; mlx_server_runtime_b200.interleave_gate_up builds it). N = 2 * intermediate
  * (a multiple of 16); out [M, N/2] = silu(g) * u with g, u each rounded to `dtype`
- * first, as the two separate matmuls would be. Decode shapes only: M <= 16 and
- * K/group_size a multiple of 8 (mlxq_swiglu_supported says so); workspace as
- * mlxq_qmm_workspace_size(M, N, K, ...).
+ * first, as the two separate matmuls would be. Decode shapes (M <= 16, K/group_size
+ * a multiple of 8) run the decode kernel's epilogue (workspace as
+ * mlxq_qmm_workspace_size(M, N, K, ...)); prefill shapes (M > 32, K a multiple of 64)
+ * the tensor-core kernel's, whole tiles, no workspace. mlxq_swiglu_supported says
+ * which shapes one of them takes.
  */
 int mlxq_swiglu_supported(int64_t M, int64_t N, int64_t K, int group_size, int bits, int dtype);
 int mlxq_quantized_matmul_swiglu(const void* x, const uint32_t* w, const void* scales,

@@ -309,11 +309,11 @@ def quantized_matmul_swiglu(x: torch.Tensor, w: torch.Tensor, scales: torch.Tens
                             mode: str = "affine") -> torch.Tensor:
     """silu(x @ gate^T) * (x @ up^T) from interleave_gate_up's layout: [..., N/2].
 
-    Decode shapes (up to 16 rows, K/group_size a multiple of 8) run as one launch
-    with the activation in the matmul's epilogue; other shapes run
-    quantized_matmul and then the activation as torch element-wise ops. Either
-    way each projection is rounded to x's dtype before silu(g) * u is formed in
-    float32 and rounded once more.
+    Decode shapes (up to 16 rows, K/group_size a multiple of 8) and prefill shapes
+    (more than 32 rows, K a multiple of 64) run as one launch with the activation in
+    the matmul's epilogue; other shapes run quantized_matmul and then the activation
+    as torch element-wise ops. Either way each projection is rounded to x's dtype
+    before silu(g) * u is formed in float32 and rounded once more.
     """
     _mode(mode)
     dev = _cuda(x, w, scales, biases)

@@ -363,6 +363,9 @@ int mlxq_swiglu_supported(int64_t M, int64_t N, int64_t K, int group_size, int b
     if (dtype != MLXQ_BF16 && dtype != MLXQ_F16) return 0;
     DeviceInfo di;
     if (device_info(&di, nullptr)) return 0;
+    if (mlxq::qgemm_supported(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), bits,
+                              group_size))
+        return 1;
     mlxq::QtPlan tplan;
     return mlxq::qmv_tma_plan(dtype, bits, group_size, static_cast<int>(M), static_cast<int>(N),
                               static_cast<int>(K), di.num_sms, di.max_smem, di.sm_smem, &tplan)
@@ -390,12 +393,25 @@ int mlxq_quantized_matmul_swiglu(const void* x, const uint32_t* w, const void* s
     if (M == 0) return MLXQ_OK;
     DeviceInfo di;
     if ((rc = device_info(&di, static_cast<cudaStream_t>(stream)))) return rc;
+    if (mlxq::qgemm_supported(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), bits,
+                              group_size)) {
+        // prefill: the tcgen05 kernel's whole tiles with the SwiGLU epilogue
+        mlxq::QgemmParams q{};
+        q.x = x; q.w = w; q.s = scales; q.b = biases; q.bias = nullptr; q.out = out;
+        q.M = static_cast<int>(M); q.N = static_cast<int>(N); q.K = static_cast<int>(K);
+        q.epi = 1;
+        cudaError_t e = mlxq::qgemm_launch(dtype, bits, group_size, q,
+                                           static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return cuda_fail(e, "quantized_matmul_swiglu (prefill) launch");
+        return MLXQ_OK;
+    }
     mlxq::QtPlan tplan;
     if (!mlxq::qmv_tma_plan(dtype, bits, group_size, static_cast<int>(M), static_cast<int>(N),
                             static_cast<int>(K), di.num_sms, di.max_smem, di.sm_smem, &tplan))
         return fail(MLXQ_ERR_SHAPE,
-                    "quantized_matmul_swiglu: decode shapes only (M <= 16, K/group_size a "
-                    "multiple of 8); see mlxq_swiglu_supported");
+                    "quantized_matmul_swiglu: no plan (decode kernel: M <= 16, K/group_size a "
+                    "multiple of 8; prefill kernel: M > 32, K a multiple of 64); see "
+                    "mlxq_swiglu_supported");
     if (tplan.ws_bytes > 0) {
         if (!workspace || workspace_bytes < tplan.ws_bytes)
             return fail(MLXQ_ERR_WORKSPACE,

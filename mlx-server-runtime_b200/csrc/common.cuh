@@ -188,4 +188,14 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     return r;
 }
 
+// silu(gate) * up of the SwiGLU epilogues from the fp32 accumulators of a gate row and
+// its up row: each projection rounded to T first (as two separate matmuls would write
+// them), the activation in fp32, one more rounding.
+template <typename T>
+__device__ __forceinline__ T swiglu_out(float g, float u) {
+    using ET = Elem<T>;
+    const float gr = ET::to_f(ET::from_f(g)), ur = ET::to_f(ET::from_f(u));
+    return ET::from_f(gr / (1.0f + expf(-gr)) * ur);
+}
+
 }  // namespace mlxq

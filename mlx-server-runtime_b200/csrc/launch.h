@@ -198,6 +198,8 @@ struct QgemmParams {
     unsigned* counter; // stream-K tickets, one per tile, zero at entry and exit
     float* partial;    // stream-K fp32 partial tiles, two slots per CTA
     int narrow;        // dense whole tiles of 128 tokens instead of 192 (more tiles)
+    int epi;           // 1: SwiGLU over gate/up rows interleaved by 16-row tiles (dense
+                       // whole tiles), out [M, N / 2]
 };
 
 // Plan of the prefill kernel for a dense problem: data-parallel whole tiles, or

@@ -276,7 +276,10 @@ __device__ __forceinline__ uint4 dequant_chunk(const uint32_t* wds, uint32_t s2,
 //   warps 2-5 (epilogue) drain the other accumulator (thread = weight row, columns =
 //                      tokens) while the next tile accumulates; optional bias as a
 //                      second rounding.
-template <typename T, int BITS, int GS, int BT, bool SK>
+// EPI 1: SwiGLU over gate/up rows interleaved by 16-row tiles (whole tiles only): the
+// gate row r and up row r + 8 of a tile are tensor-memory lanes l and l ^ 8 of one warp;
+// the gate lane writes silu(gate) * up to column 8 j + r of the N / 2 outputs.
+template <typename T, int BITS, int GS, int BT, bool SK, int EPI = 0>
 __global__ void __launch_bounds__(qg::THREADS, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw,
                  const QgemmParams p) {
@@ -616,7 +619,20 @@ __global__ void __launch_bounds__(qg::THREADS, 1)
                     uint32_t v[32];
                     tmem_ld32(tacc + i * 32, v);
                     const int tok0 = tl.row0 + i * 32;
-                    if (col_ok) {
+                    if constexpr (EPI == 1) {
+                        // gate lanes (row r < 8 of their 16-row tile) pair with lane ^ 8
+                        const bool gate_lane = (lane & 8) == 0;
+                        const int nh = (tl.nb * BW + q * 32 + (lane & 16)) / 2 + (lane & 7);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const float mine = __uint_as_float(v[j]);
+                            const float other = __shfl_xor_sync(0xffffffffu, mine, 8);
+                            const int tok = tok0 + j;
+                            if (gate_lane && col_ok && tok < tl.row_end)
+                                og[static_cast<long long>(tok) * (N / 2) + nh] =
+                                    swiglu_out<T>(mine, other);
+                        }
+                    } else if (col_ok) {
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
                             const int tok = tok0 + j;
@@ -754,9 +770,9 @@ bool qg_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esize,
 
 // SK: the stream-K instance (a separate kernel, so the whole-tile one keeps its
 // registers and schedule).
-template <typename T, int BITS, int GS, int BT, bool SK>
+template <typename T, int BITS, int GS, int BT, bool SK, int EPI = 0>
 static cudaError_t qgemm_launch_bt(const QgemmParams& p, cudaStream_t st) {
-    auto kern = qgemm_kernel<T, BITS, GS, BT, SK>;
+    auto kern = qgemm_kernel<T, BITS, GS, BT, SK, EPI>;
     constexpr int smem = qg::smem_bytes<BITS, BT>();
     static_assert(smem <= 232448, "at most 227 KB of dynamic shared memory per CTA");
     static PerDevice configured;
@@ -790,6 +806,10 @@ static cudaError_t qgemm_launch_bt(const QgemmParams& p, cudaStream_t st) {
 // dense shape with few tiles (see qgemm_plan) also gets more of them at 128 tokens.
 template <typename T, int BITS, int GS>
 static cudaError_t qgemm_launch_t(const QgemmParams& p, cudaStream_t st) {
+    if (p.epi == 1) {  // dense whole tiles only
+        if (p.E > 0 || p.sk) return cudaErrorInvalidValue;
+        return qgemm_launch_bt<T, BITS, GS, qg::BT_DENSE, false, 1>(p, st);
+    }
     if (p.E > 0 || p.narrow) return qgemm_launch_bt<T, BITS, GS, qg::BT_GROUPED, false>(p, st);
     if (p.sk) return qgemm_launch_bt<T, BITS, GS, qg::BT_DENSE, true>(p, st);
     return qgemm_launch_bt<T, BITS, GS, qg::BT_DENSE, false>(p, st);

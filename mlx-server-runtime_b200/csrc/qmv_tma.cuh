@@ -195,12 +195,6 @@ struct QtParams {
 //    the first n); the CTA keeps its best key per token in shared memory, then one
 //    global atomicMax per token; the last CTA to finish (a done counter) writes the
 //    winning n per token to int32 out[t] and re-arms the keys and the counter.
-template <typename T>
-__device__ __forceinline__ T swiglu_out(float g, float u) {
-    using ET = Elem<T>;
-    const float gr = ET::to_f(ET::from_f(g)), ur = ET::to_f(ET::from_f(u));
-    return ET::from_f(gr / (1.0f + expf(-gr)) * ur);
-}
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, int n) {
     uint32_t u = __float_as_uint(v);

@@ -113,3 +113,24 @@ def test_fused_gate_up_module_repeat():
     outs = [f(x) for _ in range(3)]
     assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
     close(to_np(outs[0]), to_np(ref), "bfloat16")
+
+
+@pytest.mark.parametrize("bits,gs,dt", [(4, 64, "bfloat16"), (8, 32, "float16"),
+                                        (4, 128, "bfloat16")])
+@pytest.mark.parametrize("M", [33, 333])
+def test_swiglu_prefill_epilogue(bits, gs, dt, M):
+    """More than 32 rows: the tensor-core kernel's SwiGLU epilogue (gate lane and up
+    lane of each 16-row tile paired in the epilogue warp); I = 520 leaves a partial
+    last weight block."""
+    rng = np.random.default_rng(M + bits + gs)
+    I, K = 520, 2048
+    gate = coracle.quantize(rand_weights(rng, (I, K), dt), dt, gs, bits)
+    up = coracle.quantize(rand_weights(rng, (I, K), dt), dt, gs, bits)
+    x = rand_x(rng, (M, K), dt)
+    ref = _swiglu_ref(x, gate, up, dt, gs, bits)
+    dev = lambda t: (to_dev(t[0]), to_dev(t[1], dt), to_dev(t[2], dt))
+    w, s, b = mxq.interleave_gate_up(dev(gate), dev(up), gs, bits)
+    y = mxq.quantized_matmul_swiglu(to_dev(x, dt), w, s, b, gs, bits)
+    torch.cuda.synchronize()
+    assert y.shape == (M, I)
+    close(to_np(y), ref, dt)
