@@ -178,9 +178,11 @@ int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const 
  * hidden size, a multiple of 16), and out [batch, M, N/2] receives silu(gate) * up,
  * each projection rounded to dtype first (as SwitchGLU's separate up_proj, gate_proj
  * and element-wise ops compute it, lfm2.py:202-218). Other arguments as
- * mlxq_gather_qmm; no workspace. MLXQ_ERR_SHAPE when the decode kernel does not take
- * the shape: mlxq_gather_swiglu_supported says which do (lhs_given: lhs_indices will
- * be passed).
+ * mlxq_gather_qmm: decode sizes run the grouped decode kernel's epilogue (no workspace
+ * used), sorted batches with enough rows per expert the grouped tensor-core kernel's
+ * (workspace as mlxq_gather_qmm_workspace_size). MLXQ_ERR_SHAPE when neither takes the
+ * shape: mlxq_gather_swiglu_supported says which do (lhs_given: lhs_indices will be
+ * passed).
  */
 int mlxq_gather_swiglu_supported(int64_t batch, int64_t M, int64_t N, int64_t K,
                                  int64_t num_experts, int64_t x_batches, int group_size, int bits,
@@ -189,7 +191,8 @@ int mlxq_gather_qmm_swiglu(const void* x, const uint32_t* w, const void* scales,
                            const void* biases, const int32_t* lhs_indices, int64_t lhs_div,
                            const int32_t* rhs_indices, void* out, int64_t batch, int64_t M,
                            int64_t N, int64_t K, int64_t num_experts, int64_t x_batches,
-                           int group_size, int bits, int dtype, int sorted_indices, void* stream);
+                           int group_size, int bits, int dtype, int sorted_indices,
+                           void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * quantized_matmul_argmax: greedy decoding's next token without the logits. The

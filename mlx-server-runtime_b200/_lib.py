@@ -138,7 +138,7 @@ def load(path: str | None = None):
                                                    i32, i32]
         L.mlxq_gather_swiglu_supported.restype = i32
         L.mlxq_gather_qmm_swiglu.argtypes = [vp, vp, vp, vp, vp, i64, vp, vp, i64, i64, i64, i64,
-                                             i64, i64, i32, i32, i32, i32, vp]
+                                             i64, i64, i32, i32, i32, i32, vp, sz, vp]
         L.mlxq_gather_qmm_swiglu.restype = i32
         v = L.mlxq_abi_version()
         if v != ABI_VERSION:

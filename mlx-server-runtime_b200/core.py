@@ -505,10 +505,11 @@ def gather_qmm_swiglu(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
     """silu(x @ gate_e^T) * (x @ up_e^T) per routed entry, from an expert bank in
     interleave_gate_up's layout ([E, N, ...], N = 2 * hidden): [*S, M, N/2].
 
-    Decode sizes run as one launch with the activation in the grouped kernel's
-    epilogue (each projection rounded to x's dtype, silu(g) * u formed in float32 and
-    rounded once); other sizes run gather_qmm and then torch's silu and multiply in
-    x's dtype on the de-interleaved halves, as SwitchGLU's separate projections do."""
+    Decode sizes and sorted batches with enough rows per expert run as one launch with
+    the activation in the grouped (decode or tensor-core) kernel's epilogue (each
+    projection rounded to x's dtype, silu(g) * u formed in float32 and rounded once);
+    other sizes run gather_qmm and then torch's silu and multiply in x's dtype on the
+    de-interleaved halves, as SwitchGLU's separate projections do."""
     _mode(mode)
     a = _gather_args(x, w, scales, biases, lhs_indices, rhs_indices, group_size, bits)
     dev, batch, M, N, K = a["dev"], a["batch"], a["M"], a["N"], a["K"]
@@ -526,11 +527,15 @@ def gather_qmm_swiglu(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
     out = torch.empty(*a["bshape"], M, N // 2, dtype=x.dtype, device=dev)
     with torch.cuda.device(dev):
         st = torch.cuda.current_stream(dev)
+        need = L.mlxq_gather_qmm_workspace_size(batch, M, N, K, a["E"], group_size, bits, a["dt"],
+                                                int(bool(sorted_indices)))
+        ws = Workspace.get(dev, st, need, "gather") if need else None
         rc = L.mlxq_gather_qmm_swiglu(_ptr(a["x"]), _ptr(a["w"]), _ptr(a["scales"]),
                                       _ptr(a["biases"]), _ptr(a["lhs"]), a["lhs_div"],
                                       _ptr(a["rhs"]), _ptr(out), batch, M, N, K, a["E"],
                                       a["x_batches"], group_size, bits, a["dt"],
-                                      int(bool(sorted_indices)), st.cuda_stream)
+                                      int(bool(sorted_indices)), _ptr(ws),
+                                      0 if ws is None else ws.numel(), st.cuda_stream)
     _lib.check(rc, "gather_qmm_swiglu")
     return out
 

@@ -528,6 +528,17 @@ static int check_gather(const char* what, const void* x, const uint32_t* w, cons
     return MLXQ_OK;
 }
 
+// Sorted rows (no lhs, one x row block per entry) with enough rows per expert for the
+// grouped tcgen05 GEMM.
+static bool grouped_prefill_applies(bool lhs_given, int64_t lhs_div, int64_t batch, int64_t M,
+                                    int64_t N, int64_t K, int64_t num_experts, int64_t x_batches,
+                                    int group_size, int bits, int sorted_indices) {
+    return sorted_indices && !lhs_given && lhs_div == 1 && x_batches == batch &&
+           batch * M >= kGroupedMinRows * num_experts &&
+           mlxq::qgemm_supported(static_cast<int>(batch * M), static_cast<int>(N),
+                                 static_cast<int>(K), bits, group_size);
+}
+
 // The grouped decode plan for a gather_qmm call; false when its kernel does not take
 // the shape (or MLXQ_GATHER_KERNEL=cpasync asks for the cp.async kernel).
 static bool gather_decode_plan(const DeviceInfo& di, bool lhs_given, int64_t lhs_div,
@@ -537,14 +548,39 @@ static bool gather_decode_plan(const DeviceInfo& di, bool lhs_given, int64_t lhs
     if (gather_cpasync_forced()) return false;
     const bool rows_sorted = sorted_indices && !lhs_given && lhs_div == 1 && x_batches == batch;
     // enough rows per expert for the grouped tcgen05 GEMM (mlxq_gather_qmm takes it first)
-    if (rows_sorted && batch * M >= kGroupedMinRows * num_experts &&
-        mlxq::qgemm_supported(static_cast<int>(batch * M), static_cast<int>(N),
-                              static_cast<int>(K), bits, group_size))
+    if (grouped_prefill_applies(lhs_given, lhs_div, batch, M, N, K, num_experts, x_batches,
+                                group_size, bits, sorted_indices))
         return false;
     return mlxq::qmv_grouped_plan(bits, group_size, batch, static_cast<int>(M),
                                   static_cast<int>(N), static_cast<int>(K),
                                   static_cast<int>(num_experts), rows_sorted, di.num_sms,
                                   di.max_smem, di.sm_smem, plan);
+}
+
+// The grouped tcgen05 GEMM: the segment table and per-expert tile offsets in the
+// workspace (mlxq_gather_qmm_workspace_size), then the kernel (epi 1: SwiGLU epilogue).
+static int launch_grouped_prefill(const void* x, const uint32_t* w, const void* scales,
+                                  const void* biases, void* out, const int32_t* rhs_indices,
+                                  int64_t batch, int64_t M, int64_t N, int64_t K,
+                                  int64_t num_experts, int group_size, int bits, int dtype,
+                                  void* workspace, cudaStream_t st, int epi) {
+    int32_t* seg = static_cast<int32_t*>(workspace);
+    int32_t* tile_start = seg + (num_experts + 1);
+    cudaError_t e = mlxq::launch_segments(rhs_indices, static_cast<int>(batch),
+                                          static_cast<int>(num_experts), seg, st);
+    if (e == cudaSuccess)
+        e = mlxq::launch_group_tiles(seg, static_cast<int>(num_experts), static_cast<int>(M),
+                                     static_cast<int>(N), tile_start, st);
+    if (e != cudaSuccess) return cuda_fail(e, "gather_qmm segment table");
+    mlxq::QgemmParams q{};
+    q.x = x; q.w = w; q.s = scales; q.b = biases; q.bias = nullptr; q.out = out;
+    q.M = static_cast<int>(batch * M); q.N = static_cast<int>(N); q.K = static_cast<int>(K);
+    q.E = static_cast<int>(num_experts); q.rpe = static_cast<int>(M);
+    q.seg = seg; q.tile_start = tile_start;
+    q.epi = epi;
+    e = mlxq::qgemm_launch(dtype, bits, group_size, q, st);
+    if (e != cudaSuccess) return cuda_fail(e, "gather_qmm (grouped) launch");
+    return MLXQ_OK;
 }
 
 int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const void* biases,
@@ -571,26 +607,11 @@ int mlxq_gather_qmm(const void* x, const uint32_t* w, const void* scales, const 
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     // Sorted, one x row block per entry, enough rows per expert: grouped tcgen05 GEMM
     // over the experts' contiguous row segments.
-    if (mode == 2 && !lhs_indices && lhs_div == 1 && x_batches == batch &&
-        batch * M >= kGroupedMinRows * num_experts &&
-        mlxq::qgemm_supported(static_cast<int>(batch * M), static_cast<int>(N),
-                              static_cast<int>(K), bits, group_size)) {
-        int32_t* seg = static_cast<int32_t*>(workspace);
-        int32_t* tile_start = seg + (num_experts + 1);
-        cudaError_t e = mlxq::launch_segments(rhs_indices, static_cast<int>(batch),
-                                              static_cast<int>(num_experts), seg, st);
-        if (e == cudaSuccess)
-            e = mlxq::launch_group_tiles(seg, static_cast<int>(num_experts), static_cast<int>(M),
-                                         static_cast<int>(N), tile_start, st);
-        if (e != cudaSuccess) return cuda_fail(e, "gather_qmm segment table");
-        mlxq::QgemmParams q{};
-        q.x = x; q.w = w; q.s = scales; q.b = biases; q.bias = nullptr; q.out = out;
-        q.M = static_cast<int>(batch * M); q.N = static_cast<int>(N); q.K = static_cast<int>(K);
-        q.E = static_cast<int>(num_experts); q.rpe = static_cast<int>(M);
-        q.seg = seg; q.tile_start = tile_start;
-        e = mlxq::qgemm_launch(dtype, bits, group_size, q, st);
-        if (e != cudaSuccess) return cuda_fail(e, "gather_qmm (grouped) launch");
-        return MLXQ_OK;
+    if (grouped_prefill_applies(lhs_indices != nullptr, lhs_div, batch, M, N, K, num_experts,
+                                x_batches, group_size, bits, sorted_indices)) {
+        rc = launch_grouped_prefill(x, w, scales, biases, out, rhs_indices, batch, M, N, K,
+                                    num_experts, group_size, bits, dtype, workspace, st, 0);
+        return rc;
     }
     // Otherwise the TMA-fed grouped decode kernel: sorted rows of an expert taken
     // together, else one entry at a time (the cp.async kernel below when its plan does
@@ -651,6 +672,9 @@ int mlxq_gather_swiglu_supported(int64_t batch, int64_t M, int64_t N, int64_t K,
         num_experts > kIntMax || x_batches > kIntMax || batch * M > kIntMax ||
         x_batches * M > kIntMax)
         return 0;
+    if (grouped_prefill_applies(lhs_given != 0, 1, batch, M, N, K, num_experts, x_batches,
+                                group_size, bits, sorted_indices))
+        return 1;
     DeviceInfo di;
     if (device_info(&di, nullptr)) return 0;
     mlxq::QgdPlan gp;
@@ -662,7 +686,8 @@ int mlxq_gather_qmm_swiglu(const void* x, const uint32_t* w, const void* scales,
                            const void* biases, const int32_t* lhs_indices, int64_t lhs_div,
                            const int32_t* rhs_indices, void* out, int64_t batch, int64_t M,
                            int64_t N, int64_t K, int64_t num_experts, int64_t x_batches,
-                           int group_size, int bits, int dtype, int sorted_indices, void* stream) {
+                           int group_size, int bits, int dtype, int sorted_indices,
+                           void* workspace, size_t workspace_bytes, void* stream) {
     int rc = check_gather("gather_qmm_swiglu", x, w, scales, biases, lhs_indices, lhs_div,
                           rhs_indices, out, batch, M, N, K, num_experts, x_batches, group_size,
                           bits, dtype);
@@ -673,12 +698,25 @@ int mlxq_gather_qmm_swiglu(const void* x, const uint32_t* w, const void* scales,
     if (batch == 0 || M == 0) return MLXQ_OK;
     DeviceInfo di;
     if ((rc = device_info(&di, static_cast<cudaStream_t>(stream)))) return rc;
+    if (grouped_prefill_applies(lhs_indices != nullptr, lhs_div, batch, M, N, K, num_experts,
+                                x_batches, group_size, bits, sorted_indices)) {
+        const size_t need = mlxq_gather_qmm_workspace_size(batch, M, N, K, num_experts,
+                                                           group_size, bits, dtype, 1);
+        if (!workspace || workspace_bytes < need)
+            return fail(MLXQ_ERR_WORKSPACE, "gather_qmm_swiglu: needs %zu workspace bytes, got %zu",
+                        need, workspace ? workspace_bytes : (size_t)0);
+        if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+            return fail(MLXQ_ERR_ALIGN, "gather_qmm_swiglu: workspace must be 256-byte aligned");
+        return launch_grouped_prefill(x, w, scales, biases, out, rhs_indices, batch, M, N, K,
+                                      num_experts, group_size, bits, dtype, workspace,
+                                      static_cast<cudaStream_t>(stream), 1);
+    }
     mlxq::QgdPlan gp;
-    if (!gather_decode_plan(di, lhs_indices != nullptr, lhs_div, batch, M, N, K, num_experts, x_batches,
-                            group_size, bits, sorted_indices, &gp))
+    if (!gather_decode_plan(di, lhs_indices != nullptr, lhs_div, batch, M, N, K, num_experts,
+                            x_batches, group_size, bits, sorted_indices, &gp))
         return fail(MLXQ_ERR_SHAPE,
-                    "gather_qmm_swiglu: no decode plan for this shape (call gather_qmm and "
-                    "apply the activation)");
+                    "gather_qmm_swiglu: no plan for this shape (call gather_qmm and apply the "
+                    "activation)");
     cudaError_t e = mlxq::qmv_grouped_launch(
         dtype, bits, group_size, gp, x, w, scales, biases, out, rhs_indices, lhs_indices,
         static_cast<int>(lhs_div < 1 ? 1 : lhs_div), static_cast<int>(batch),

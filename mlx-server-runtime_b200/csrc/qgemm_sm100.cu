@@ -806,8 +806,9 @@ static cudaError_t qgemm_launch_bt(const QgemmParams& p, cudaStream_t st) {
 // dense shape with few tiles (see qgemm_plan) also gets more of them at 128 tokens.
 template <typename T, int BITS, int GS>
 static cudaError_t qgemm_launch_t(const QgemmParams& p, cudaStream_t st) {
-    if (p.epi == 1) {  // dense whole tiles only
-        if (p.E > 0 || p.sk) return cudaErrorInvalidValue;
+    if (p.epi == 1) {  // whole tiles only
+        if (p.sk) return cudaErrorInvalidValue;
+        if (p.E > 0) return qgemm_launch_bt<T, BITS, GS, qg::BT_GROUPED, false, 1>(p, st);
         return qgemm_launch_bt<T, BITS, GS, qg::BT_DENSE, false, 1>(p, st);
     }
     if (p.E > 0 || p.narrow) return qgemm_launch_bt<T, BITS, GS, qg::BT_GROUPED, false>(p, st);

@@ -158,8 +158,9 @@ def test_gather_qmm_swiglu(sorted_rows, K):
     close(to_np(y), ref, dt)
 
 
-@pytest.mark.parametrize("T", [1, 64])
+@pytest.mark.parametrize("T", [1, 64, 512])
 def test_fused_switch_glu_matches_unfused(T):
+    # 512 tokens x 8 = 4096 rows over 32 experts: the grouped tensor-core kernel's epilogue
     from mlx_server_runtime_b200 import nn
     E, D, H = 32, 512, 256
     g = torch.Generator(device="cuda").manual_seed(T)
@@ -172,3 +173,24 @@ def test_fused_switch_glu_matches_unfused(T):
     assert not hasattr(sw, "gate_proj") and hasattr(sw, "gate_up_proj")
     y = sw(x, idx)
     close(to_np(y), to_np(y_ref), "bfloat16")
+
+
+def test_gather_qmm_swiglu_grouped_prefill():
+    """Sorted rows with enough per expert (>= 24 on average) take the grouped tensor-core
+    kernel with the SwiGLU epilogue; an empty expert and a ragged one included."""
+    dt, gs, bits = "bfloat16", 64, 4
+    rng = np.random.default_rng(99)
+    E, I, K = 8, 200, 1024
+    counts = [50, 0, 131, 64, 1, 70, 90, 40]
+    gate, up = _experts(rng, E, I, K, dt, gs, bits), _experts(rng, E, I, K, dt, gs, bits)
+    sel = np.repeat(np.arange(E, dtype=np.int32), counts)
+    xs = rand_x(rng, (sel.size, 1, K), dt)
+    g = coracle.gather_qmm(xs, *gate, sel, dt, gs, bits)
+    u = coracle.gather_qmm(xs, *up, sel, dt, gs, bits)
+    ref = _swiglu_ref(g, u, dt)
+    dev = lambda t: tuple(to_dev(a, dt) if a.dtype != np.uint32 else to_dev(a) for a in t)
+    w, s, b = mxq.interleave_gate_up(dev(gate), dev(up), gs, bits)
+    y = mxq.gather_qmm_swiglu(to_dev(xs, dt), w, s, b, rhs_indices=to_dev(sel),
+                              sorted_indices=True)
+    assert y.shape == (sel.size, 1, I)
+    close(to_np(y), ref, dt)
