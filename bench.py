@@ -888,7 +888,9 @@ def run(args):
 
 
 CASES = {"q": (HIDDEN, HIDDEN), "kv": (KV, HIDDEN), "gate": (INTER, HIDDEN),
-         "down": (HIDDEN, INTER), "lm_head": (VOCAB, HIDDEN)}
+         "down": (HIDDEN, INTER), "lm_head": (VOCAB, HIDDEN),
+         # the epilogue instances: gate and up interleaved with SwiGLU, lm_head with argmax
+         "gate_up_swiglu": (2 * INTER, HIDDEN), "lm_head_argmax": (VOCAB, HIDDEN)}
 
 
 def run_quantize_case(args):
@@ -942,15 +944,23 @@ def run_case(args):
         ws.append(mxq.quantize(w, GS, BITS))
         del w
     x = torch.randn(M, K, device=dev, generator=gen).to(torch.bfloat16)
+    fn = {"gate_up_swiglu": mxq.quantized_matmul_swiglu,
+          "lm_head_argmax": mxq.quantized_matmul_argmax}.get(args.case)
+    if fn is None:
+        def fn(x, w, s, b, group_size, bits):
+            return mxq.quantized_matmul(x, w, s, b, group_size=group_size, bits=bits)
+    out_bytes = {"gate_up_swiglu": 2 * M * (N // 2), "lm_head_argmax": 4 * M}.get(args.case)
+    if out_bytes is not None:
+        per = per - 2 * M * N + out_bytes
     mxq.launch_overlap(not args.no_overlap)
     for i in range(max(3, args.warmup)):
-        mxq.quantized_matmul(x, *ws[i % copies], group_size=GS, bits=BITS)
+        fn(x, *ws[i % copies], group_size=GS, bits=BITS)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if args.eager:
         e0.record()
         for i in range(args.steps):
-            mxq.quantized_matmul(x, *ws[i % copies], group_size=GS, bits=BITS)
+            fn(x, *ws[i % copies], group_size=GS, bits=BITS)
         e1.record()
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / args.steps
@@ -960,12 +970,12 @@ def run_case(args):
         st.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(st):
             for i in range(copies):
-                mxq.quantized_matmul(x, *ws[i], group_size=GS, bits=BITS)
+                fn(x, *ws[i], group_size=GS, bits=BITS)
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=st):
             for i in range(copies):
-                mxq.quantized_matmul(x, *ws[i], group_size=GS, bits=BITS)
+                fn(x, *ws[i], group_size=GS, bits=BITS)
         for _ in range(3):
             g.replay()
         reps = max(1, args.steps // copies)
