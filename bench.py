@@ -747,6 +747,27 @@ def run(args):
         barrier()
         return max_over_ranks(e0.elapsed_time(e1) / steps)
 
+    def step_distribution(fn, steps):
+        """Per-step ms of fn from an event between consecutive steps on the current
+        stream (outside the timed region): median, p10 and p90, each the max over ranks."""
+        cur = torch.cuda.current_stream(dev)
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+        barrier()
+        evs[0].record(cur)
+        for i in range(steps):
+            fn()
+            evs[i + 1].record(cur)
+        barrier()
+        d = sorted(evs[i].elapsed_time(evs[i + 1]) for i in range(steps))
+
+        def q(f):
+            return d[min(steps - 1, int(round(f * (steps - 1))))]
+
+        out = {k: round(max_over_ranks(q(f)), 4) for k, f in (("median", 0.5), ("p10", 0.1),
+                                                               ("p90", 0.9))}
+        out["steps"] = steps
+        return out
+
     for _ in range(max(3, args.warmup)):
         step()
     barrier()
@@ -758,6 +779,7 @@ def run(args):
     with ClockSampler(dev.index) as clk:
         ms = timed(step, args.steps)
     value = total_bytes / (ms * 1e-3) / 1e9
+    dist_ms = step_distribution(step, max(10, min(args.steps, 50)))
     # the matmuls alone (the step without its all-gather), for N > 1
     ms_kernels = timed(graph.replay, args.steps) if world > 1 else ms
 
@@ -864,6 +886,7 @@ def run(args):
             "e2e": {"value": round(e2e, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 4)},
             "clocks": clk.summary(),
+            "step_ms_distribution": dist_ms,
             "fused_projections": {
                 "value": round(fused_total / (ms_fused * 1e-3) / 1e9, 1), "unit": "GB/s",
                 "ms_per_step": round(ms_fused, 4),
