@@ -298,6 +298,7 @@ int mlxq_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
         if (gp.stream_k && workspace && workspace_bytes >= gp.ws_bytes &&
             !(reinterpret_cast<uintptr_t>(workspace) & 255u)) {
             q.sk = 1;
+            q.grid = gp.grid;
             q.counter = static_cast<unsigned*>(workspace);
             q.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + mlxq::kTicketBytes);
         }

@@ -198,6 +198,7 @@ struct QgemmParams {
     unsigned* counter; // stream-K tickets, one per tile, zero at entry and exit
     float* partial;    // stream-K fp32 partial tiles, two slots per CTA
     int narrow;        // dense whole tiles of 128 tokens instead of 192 (more tiles)
+    int grid;          // stream-K CTAs (0: one per SM)
     int epi;           // 1: SwiGLU over gate/up rows interleaved by 16-row tiles (dense
                        // whole tiles), out [M, N / 2]
 };
@@ -207,6 +208,7 @@ struct QgemmParams {
 struct QgemmPlan {
     bool stream_k;
     bool narrow;      // whole tiles of 128 tokens: more tiles for a shape that has few
+    int grid;         // stream-K CTAs: one per SM, or fewer when K is short
     size_t ws_bytes;  // workspace (tickets + partial tiles) for stream-K, else 0
 };
 bool qgemm_plan(int M, int N, int K, int num_sms, QgemmPlan* plan);

@@ -30,6 +30,7 @@
 // waited for (bounded), tensor memory is freed and the kernel returns.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -797,7 +798,8 @@ static cudaError_t qgemm_launch_bt(const QgemmParams& p, cudaStream_t st) {
     // is at most ceil(M / BT) + E
     const long long mblocks = (p.M + BT - 1) / BT + (p.E > 0 ? p.E : 0);
     const long long tiles = mblocks * ((p.N + qg::BW - 1) / qg::BW);
-    const int grid = SK ? sms : static_cast<int>(tiles < sms ? tiles : sms);
+    const int grid = SK ? (p.grid > 0 && p.grid < sms ? p.grid : sms)
+                        : static_cast<int>(tiles < sms ? tiles : sms);
     kern<<<grid, qg::THREADS, smem, st>>>(tx, tw, p);
     return cudaGetLastError();
 }
@@ -874,6 +876,7 @@ static cudaError_t qgemm_dtype(int bits, int gs, const QgemmParams& p, cudaStrea
 // one's pass over their partials cost more than the idle SMs (k/v at 512 tokens: 12
 // tiles split 12 ways ran at 32 TFLOP/s).
 constexpr double kStreamKBelow = 0.85;
+constexpr long long kStreamKShare = 3;
 
 bool qgemm_plan(int M, int N, int K, int num_sms, QgemmPlan* plan) {
     QgemmPlan pl{};
@@ -883,19 +886,27 @@ bool qgemm_plan(int M, int N, int K, int num_sms, QgemmPlan* plan) {
     const long long waves = (tiles + num_sms - 1) / num_sms;
     const double fill = static_cast<double>(tiles) / static_cast<double>(waves * num_sms);
     const long long units = tiles * KB;
-    if (num_sms > 0 && fill < kStreamKBelow && units >= num_sms && 3 * units >= KB * num_sms &&
+    const long long tiles128 = static_cast<long long>((M + qg::BT_GROUPED - 1) /
+                                                      qg::BT_GROUPED) *
+                               ((N + qg::BW - 1) / qg::BW);
+    // Stream-K CTAs: each takes at least KB / kStreamKShare K blocks, so at most about
+    // that many CTAs add partials to one tile (the last one reads them all, which is
+    // what bounds a short-K stream-K); one per SM when the K blocks allow, else fewer,
+    // as long as they outnumber the whole 128-token tiles (k/v at 512-2048 tokens:
+    // 36-132 CTAs instead of 16-64 tiles, 32.1 against 34.8 µs at 512 tokens).
+    const long long sk_grid =
+        num_sms > 0 ? std::min<long long>(num_sms, kStreamKShare * units / KB) : 0;
+    if (num_sms > 0 && fill < kStreamKBelow && (sk_grid == num_sms || sk_grid > tiles128) &&
+        units >= sk_grid && sk_grid > 0 &&
         tiles * 4 <= static_cast<long long>(kArgmaxOffset) &&
         units * (num_sms + 1) < (1LL << 31)) {
         pl.stream_k = true;
+        pl.grid = static_cast<int>(sk_grid);
         pl.ws_bytes = kTicketBytes + static_cast<size_t>(num_sms) * 2 * qg::BW *
                                          qg::BT_DENSE * sizeof(float);
     } else if (fill < kStreamKBelow) {
-        // too few tiles and too short a K for stream-K (k/v at a few thousand tokens):
-        // 128-token tiles give the SMs more of them (a tile's pipeline, not its width,
-        // sets its time)
-        const long long tiles128 = static_cast<long long>((M + qg::BT_GROUPED - 1) /
-                                                          qg::BT_GROUPED) *
-                                   ((N + qg::BW - 1) / qg::BW);
+        // too few tiles and too short a K for stream-K: 128-token tiles give the SMs
+        // more of them (a tile's pipeline, not its width, sets its time)
         pl.narrow = tiles128 > tiles && tiles < num_sms;
     }
     *plan = pl;
