@@ -301,6 +301,10 @@ int mlxq_quantized_matmul(const void* x, const uint32_t* w, const void* scales,
             q.grid = gp.grid;
             q.counter = static_cast<unsigned*>(workspace);
             q.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + mlxq::kTicketBytes);
+        } else if (gp.stream_k && gp.grid < di.num_sms) {
+            // a short-K shape with few tiles and no room for its partials: 128-token
+            // tiles, more of them than 192-token ones
+            q.narrow = (M + 127) / 128 > (M + 191) / 192 ? 1 : 0;
         }
         cudaError_t e = mlxq::qgemm_launch(dtype, bits, group_size, q,
                                            static_cast<cudaStream_t>(stream));

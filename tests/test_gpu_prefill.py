@@ -105,3 +105,31 @@ def test_prefill_stream_k_repeat_and_whole_tiles_agree():
     torch.cuda.synchronize()
     assert _lib.device_error() == 0
     close(to_np(outs[0]), to_np(whole), "bfloat16")
+
+
+def test_prefill_stream_k_reduced_grid_and_fallback():
+    """A short-K shape with few tiles (k/v at 512 tokens: 12 tiles of 56 K blocks) runs
+    stream-K on fewer CTAs than SMs: matches the oracle, repeats bit for bit, and the
+    form without a workspace (128-token whole tiles) agrees within tolerance."""
+    import ctypes
+    rng = np.random.default_rng(31)
+    M, N, K = 512, 512, 3584
+    w = rand_weights(rng, (N, K), "bfloat16")
+    xh = rand_x(rng, (M, K), "bfloat16")
+    wq, s, b = coracle.quantize(w, "bfloat16", 64, 4)
+    ref = coracle.quantized_matmul(xh, wq, s, b, "bfloat16", 64, 4)
+    x, wd, sd, bd = to_dev(xh, "bfloat16"), to_dev(wq), to_dev(s, "bfloat16"), to_dev(b, "bfloat16")
+    outs = [mxq.quantized_matmul(x, wd, sd, bd) for _ in range(2)]
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    assert torch.equal(outs[0], outs[1])
+    close(to_np(outs[0]), ref, "bfloat16")
+    L = _lib.load()
+    whole = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    rc = L.mlxq_quantized_matmul(x.data_ptr(), wd.data_ptr(), sd.data_ptr(), bd.data_ptr(), None,
+                                 whole.data_ptr(), M, N, K, 64, 4, _lib.BF16, None, 0,
+                                 ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0, _lib.last_error()
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    close(to_np(whole), ref, "bfloat16")
