@@ -48,20 +48,20 @@ def load_weight_index(model_path: str) -> dict[str, str]:
             from safetensors import safe_open
             with safe_open(single, framework="pt") as f:
                 return {k: "model.safetensors" for k in f.keys()}
-        raise WeightArtifactError(f"missing weight index: {os.path.basename(index_path)}")
+        raise WeightArtifactError(f"{model_path}: neither {os.path.basename(index_path)} nor model.safetensors exists")
     try:
         with open(index_path) as f:
             payload = json.load(f)
     except (OSError, json.JSONDecodeError) as e:
-        raise WeightArtifactError(f"could not parse {os.path.basename(index_path)}: {e}") from e
+        raise WeightArtifactError(f"{os.path.basename(index_path)} is not readable JSON ({e})") from e
     wmap = payload.get("weight_map")
     if not isinstance(wmap, dict) or not wmap:
-        raise WeightArtifactError("model.safetensors.index.json has no weight_map")
+        raise WeightArtifactError("model.safetensors.index.json: weight_map is absent or empty")
     if not all(isinstance(k, str) and isinstance(v, str) for k, v in wmap.items()):
-        raise WeightArtifactError("weight_map entries must be strings")
+        raise WeightArtifactError("model.safetensors.index.json: weight_map must map tensor names to file names")
     missing = sorted({v for v in wmap.values() if not os.path.exists(os.path.join(model_path, v))})
     if missing:
-        raise WeightArtifactError("missing weight files: " + ", ".join(missing))
+        raise WeightArtifactError(f"{len(missing)} shard file(s) named by the index are not in {model_path}: " + ", ".join(missing))
     return dict(wmap)
 
 

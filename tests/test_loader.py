@@ -88,7 +88,7 @@ def test_load_checkpoint_quantizes_where_scales_exist(tmp_path):
 def test_load_errors(tmp_path):
     _checkpoint(tmp_path)
     os.remove(tmp_path / "model-00002-of-00002.safetensors")
-    with pytest.raises(loader.WeightArtifactError, match="missing weight files"):
+    with pytest.raises(loader.WeightArtifactError, match="shard file"):
         loader.load_checkpoint(Tiny(), str(tmp_path))
 
 
