@@ -181,3 +181,17 @@ def test_expert_parallel_fixed_capacity():
     # capacity above both ranks' routed rows, ragged token counts
     res = _run(_ep_worker, 2, 4, 64, 128, (5, 3), 2, 12)
     assert sorted(info for _, _, info in res) == [(3, 2, 64), (5, 2, 64)]
+
+
+def test_sharded_linear_allgather_four_ranks():
+    # 200 rows over 4 ranks: shards of 50, the same all-gather as at 8 GPUs
+    res = _run(_sharded_linear_worker, 4, 200, 128, 3, True)
+    assert all(info == (1, 3, 200) for _, _, info in res)
+
+
+@pytest.mark.parametrize("capacity", [None, 24])
+def test_expert_parallel_four_ranks(capacity):
+    # 8 experts over 4 ranks (2 each), ragged token counts and an empty rank, both
+    # exchange forms (split sizes read back, or fixed [world, capacity] buffers)
+    res = _run(_ep_worker, 4, 8, 64, 128, (5, 3, 0, 6), 2, capacity)
+    assert sorted(info for _, _, info in res) == [(0, 2, 64), (3, 2, 64), (5, 2, 64), (6, 2, 64)]
