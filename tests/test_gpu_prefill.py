@@ -133,3 +133,12 @@ def test_prefill_stream_k_reduced_grid_and_fallback():
     torch.cuda.synchronize()
     assert _lib.device_error() == 0
     close(to_np(whole), ref, "bfloat16")
+
+
+@pytest.mark.parametrize("dt", ["bfloat16", "float16"])
+@pytest.mark.parametrize("bits,gs", [(4, 32), (8, 64), (4, 128)])
+@pytest.mark.parametrize("M", [512, 2048])
+def test_prefill_stream_k_reduced_grid_types(dt, bits, gs, M):
+    # k/v-shaped (N=512, K=3584): stream-K on 36 (M=512) or 132 (M=2048) CTAs, with bias
+    y, ref = _case(dt, bits, gs, M, 512, 3584, seed=M + bits * 13 + gs, bias=True)
+    close(y, ref, dt)
